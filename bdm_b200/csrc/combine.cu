@@ -1,0 +1,147 @@
+// Read combine + output normalisation + sigmoid gate (one CTA per token).
+//
+// Restates the token-order readout (gdn2_banks.py:265-283 scatter_bank_outputs,
+// role_bank_dispatch.py:201-231 _readout) and the normalisation and gate of
+// _project_bank_output (_parameters.py:222-232).  The KR read rows of a token
+// are summed in ascending bank order -- the packed (bank) order the reference
+// visits -- then LayerNorm (or RMS), then times dtype(sigmoid(gate)).
+#include "common.cuh"
+
+namespace bdm {
+namespace {
+
+constexpr int kCols = 8;  // columns per thread
+constexpr int kMaxKR = 64;
+
+__device__ __forceinline__ float block_sum(float x, float *red) {
+    x = warp_sum(x);
+    const int warp = threadIdx.x >> 5, lane = (int)lane_id();
+    const int nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = x;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : 0.f;
+    return warp_sum(t);
+}
+
+template <typename T>
+__global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int64_t *__restrict__ ri, int64_t ntok,
+                                         int kr, int64_t width, const T *__restrict__ gate, int64_t ld_gate,
+                                         const T *__restrict__ nw, const T *__restrict__ nb, float eps, int norm_mode,
+                                         int round_each, T *__restrict__ out) {
+    __shared__ int64_t banks[kMaxKR];
+    __shared__ int slot_at[kMaxKR];
+    __shared__ float red[32];
+    const int64_t t = blockIdx.x;
+    if (t >= ntok) return;
+    if (ri) {
+        if ((int)threadIdx.x < kr) banks[threadIdx.x] = ri[t * kr + threadIdx.x];
+        __syncthreads();
+        if ((int)threadIdx.x < kr) {
+            const int j = threadIdx.x;
+            const int64_t bj = banks[j];
+            int rank = 0;
+            for (int i = 0; i < kr; ++i) rank += (banks[i] < bj) || (banks[i] == bj && i < j);
+            slot_at[rank] = j;
+        }
+        __syncthreads();
+    }
+    const int64_t c0 = (int64_t)threadIdx.x * kCols;
+    float x[kCols];
+#pragma unroll
+    for (int i = 0; i < kCols; ++i) x[i] = 0.f;
+    const bool act = c0 < width;
+    if (act) {
+        if (ri) {
+            for (int r = 0; r < kr; ++r) {
+                const T *row = reads + (t * kr + slot_at[r]) * width + c0;
+#pragma unroll
+                for (int i = 0; i < kCols; ++i) {
+                    if (c0 + i < width) {
+                        const float y = x[i] + Elem<T>::to_float(row[i]);
+                        x[i] = round_each ? rnd<T>(y) : y;
+                    }
+                }
+            }
+            if (!round_each) {
+#pragma unroll
+                for (int i = 0; i < kCols; ++i) x[i] = rnd<T>(x[i]);
+            }
+        } else {
+            const T *row = reads + t * width + c0;
+#pragma unroll
+            for (int i = 0; i < kCols; ++i)
+                if (c0 + i < width) x[i] = Elem<T>::to_float(row[i]);
+        }
+    }
+    const float inv_w = 1.0f / (float)width;
+    float n[kCols];
+    if (norm_mode == 1) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) s += x[i];
+        const float mean = block_sum(s, red) * inv_w;
+        float sq = 0.f;
+#pragma unroll
+        for (int i = 0; i < kCols; ++i)
+            if (act && c0 + i < width) sq += (x[i] - mean) * (x[i] - mean);
+        const float var = block_sum(sq, red) * inv_w;
+        const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) {
+            float y = 0.f;
+            if (act && c0 + i < width) {
+                y = (x[i] - mean) * rstd * Elem<T>::to_float(nw[c0 + i]);
+                if (nb) y += Elem<T>::to_float(nb[c0 + i]);
+            }
+            n[i] = rnd<T>(y);
+        }
+    } else {
+        float sq = 0.f;
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) sq += x[i] * x[i];
+        const float var = block_sum(sq, red) * inv_w;
+        const float sc = rnd<T>(1.0f / sqrtf(var + eps));
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) {
+            n[i] = 0.f;
+            if (act && c0 + i < width) n[i] = rnd<T>(rnd<T>(x[i] * sc) * Elem<T>::to_float(nw[c0 + i]));
+        }
+    }
+    if (act) {
+        const T *grow = gate + t * ld_gate + c0;
+        T *orow = out + t * width + c0;
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) {
+            if (c0 + i < width) {
+                const float gt = rnd<T>(1.0f / (1.0f + expf(-Elem<T>::to_float(grow[i]))));
+                orow[i] = Elem<T>::from_float(n[i] * gt);
+            }
+        }
+    }
+}
+
+}  // namespace
+}  // namespace bdm
+
+extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                     const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
+                                     float eps, int norm_mode, int round_each, int dtype, void *out, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || width <= 0 || ld_gate < width) return BDM_ERR_INVALID;
+    if (read_idx && (kr <= 0 || kr > kMaxKR)) return BDM_ERR_UNSUPPORTED;
+    if (ntok == 0) return BDM_OK;
+    if (!reads || !gate || !norm_weight || !out) return BDM_ERR_INVALID;
+    if (norm_mode != 0 && norm_mode != 1) return BDM_ERR_INVALID;
+    int64_t threads = ceil_div(ceil_div(width, kCols), 32) * 32;
+    if (threads < 64) threads = 64;
+    if (threads > 1024) return BDM_ERR_UNSUPPORTED;
+    if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        combine_norm_gate_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
+            static_cast<const T *>(reads), read_idx, ntok, read_idx ? kr : 1, width, static_cast<const T *>(gate),
+            ld_gate, static_cast<const T *>(norm_weight), static_cast<const T *>(norm_bias), eps, norm_mode,
+            round_each, static_cast<T *>(out));
+    });
+    return launch_status();
+}

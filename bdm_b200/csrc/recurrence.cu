@@ -1,0 +1,413 @@
+// Per-bank GDN2 delta-rule recurrence over dispatched events.
+//
+// Restates the reference recurrence (gdn2_banks.py:22-43 reference_packed_gdn2,
+// role_bank_kernel.py:46-73 _role_forward, forward_rows.py:9-149) together with
+// the route-weighted packing it consumes (gdn2_banks.py:196-224,
+// role_bank_dispatch.py:41-73, routed_update.py:5-13), without materialising
+// packed event tensors: every event is gathered from token storage by id.
+//
+// Work unit = one warp = (batch*bank sequence, head, tile of 32*NC value
+// columns).  The S x dv bank state is column-separable: each lane owns NC
+// columns and keeps all S rows of them in FP32 registers, so the erase
+// reduction over rows needs no shuffles.  Per write event, per column pair
+// (f32x2 packed FMA on sm_100):
+//   hd = M * exp(g_e) ; erase = sum_s a_s hd_s ; u = w_e*v - erase ; M = hd + k u
+// Per read event: out = scale * sum_s q_e,s M_s.
+// Per-event row controls (exp(g_e), a = dtype(b*p)*k, k, or q_e = dtype(q*r))
+// are computed once per event by the warp's lanes and staged in shared memory
+// as duplicated pairs for the packed math; value rows v and w are gathered in
+// mini-batches so several loads are in flight per lane.
+#include "common.cuh"
+
+namespace bdm {
+namespace {
+
+constexpr int kScanWarps = 4;
+
+struct ScanParams {
+    const void *q, *k, *v;
+    const float *g;
+    const void *b, *w;
+    const int64_t *wi, *ri;
+    const void *ww, *rw;
+    const int64_t *order, *cu;
+    int64_t batch, time, J, nt, nw, E;
+    int H, dv, kw, kr, routed_decay, ctiles;
+    float scale;
+    const void *row_factor, *col_factor;
+    int64_t factor_cols;
+    int factor_dtype;
+    void *cache;
+    int cache_dtype, store_final, interval;
+    void *reads;
+    int64_t units;
+};
+
+template <typename T, int NC> struct Row {
+    // NC consecutive elements of T loaded / stored as one vector.
+    static constexpr int kBytes = NC * (int)sizeof(T);
+    T x[NC];
+};
+
+template <int BYTES> struct VecOf;
+template <> struct VecOf<4> { using type = uint32_t; };
+template <> struct VecOf<8> { using type = uint2; };
+template <> struct VecOf<16> { using type = uint4; };
+template <> struct VecOf<32> { using type = uint4; };
+
+template <typename T, int NC>
+__device__ __forceinline__ void load_row(Row<T, NC> &r, const T *p) {
+    constexpr int B = Row<T, NC>::kBytes;
+    if constexpr (B == 32) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(p);
+        uint4 *dst = reinterpret_cast<uint4 *>(r.x);
+        dst[0] = __ldg(src);
+        dst[1] = __ldg(src + 1);
+    } else {
+        using V = typename VecOf<B>::type;
+        *reinterpret_cast<V *>(r.x) = __ldg(reinterpret_cast<const V *>(p));
+    }
+}
+
+template <typename T, int NC>
+__device__ __forceinline__ void store_row(T *p, const Row<T, NC> &r) {
+    constexpr int B = Row<T, NC>::kBytes;
+    if constexpr (B == 32) {
+        uint4 *dst = reinterpret_cast<uint4 *>(p);
+        const uint4 *src = reinterpret_cast<const uint4 *>(r.x);
+        dst[0] = src[0];
+        dst[1] = src[1];
+    } else {
+        using V = typename VecOf<B>::type;
+        *reinterpret_cast<V *>(p) = *reinterpret_cast<const V *>(r.x);
+    }
+}
+
+__device__ __forceinline__ float2 dup(float x) { return make_float2(x, x); }
+
+// Round a pair to T and back (RNE); one packed convert for BF16.
+template <typename T> __device__ __forceinline__ float2 round_pair(float2 x);
+template <> __device__ __forceinline__ float2 round_pair<float>(float2 x) { return x; }
+template <> __device__ __forceinline__ float2 round_pair<bf16>(float2 x) {
+    return __bfloat1622float2(__floats2bfloat162_rn(x.x, x.y));
+}
+
+template <typename T> __device__ __forceinline__ float2 load_pair(const T *x);
+template <> __device__ __forceinline__ float2 load_pair<float>(const float *x) { return make_float2(x[0], x[1]); }
+template <> __device__ __forceinline__ float2 load_pair<bf16>(const bf16 *x) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(x));
+}
+
+template <typename T> __device__ __forceinline__ void store_pair(T *x, float2 v);
+template <> __device__ __forceinline__ void store_pair<float>(float *x, float2 v) {
+    x[0] = v.x;
+    x[1] = v.y;
+}
+template <> __device__ __forceinline__ void store_pair<bf16>(bf16 *x, float2 v) {
+    *reinterpret_cast<__nv_bfloat162 *>(x) = __floats2bfloat162_rn(v.x, v.y);
+}
+
+__device__ __forceinline__ float2 bf16_round_pair(float2 x) { return round_pair<bf16>(x); }
+
+// Events staged per batch and value-row mini-batch size (prefetch depth).
+template <int S> struct EvBatch { static constexpr int value = S >= 16 ? 16 : 32; };
+template <typename T, int NC> struct MiniBatch {
+    static constexpr int raw = 64 / (NC * (int)sizeof(T));
+    static constexpr int value = raw > 8 ? 8 : (raw < 2 ? 2 : raw);
+};
+
+template <typename T, int S, int NC>
+__global__ void __launch_bounds__(kScanWarps * 32)
+bank_scan_kernel(const ScanParams p) {
+    constexpr int NP = NC / 2;
+    constexpr int EB = EvBatch<S>::value;
+    constexpr int MB = MiniBatch<T, NC>::value;
+    static_assert(EB % MB == 0, "mini-batches tile the event batch");
+    // Per warp: controls [EB][3][S] duplicated pairs, token ids and weights.
+    __shared__ float2 ctl_all[kScanWarps][EB][3 * S];
+    __shared__ int64_t tok_all[kScanWarps][EB];
+    __shared__ int64_t rid_all[kScanWarps][EB];
+    __shared__ float wgt_all[kScanWarps][EB];
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = (int)lane_id();
+    const int64_t unit = (int64_t)blockIdx.x * kScanWarps + warp;
+    if (unit >= p.units) return;  // warp-uniform
+    float2(*ctl)[3 * S] = ctl_all[warp];
+    int64_t *tok_s = tok_all[warp];
+    int64_t *rid_s = rid_all[warp];
+    float *wgt_s = wgt_all[warp];
+
+    const int64_t per_seq = (int64_t)p.H * p.ctiles;
+    const int64_t seq = unit / per_seq;
+    const int hh = (int)((unit % per_seq) / p.ctiles);
+    const int ct = (int)(unit % p.ctiles);
+    const int64_t bidx = seq / p.J, bank = seq % p.J;
+    const int col0 = ct * 32 * NC + lane * NC;
+    const bool active = col0 < p.dv;
+    const int HS = p.H * S;
+    const int64_t V = (int64_t)p.H * p.dv;
+
+    const T *qp = static_cast<const T *>(p.q);
+    const T *kp = static_cast<const T *>(p.k);
+    const T *vp = static_cast<const T *>(p.v);
+    const T *bp = static_cast<const T *>(p.b);
+    const T *wp = static_cast<const T *>(p.w);
+    const T *wwp = static_cast<const T *>(p.ww);
+    const T *rwp = static_cast<const T *>(p.rw);
+    T *outp = static_cast<T *>(p.reads);
+
+    // ---------------------------------------------------------- initial state
+    float2 M[S][NP];
+    const int64_t state_off = ((bidx * p.J + bank) * p.H + hh) * (int64_t)S * p.dv + col0;
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int j = 0; j < NP; ++j) M[s][j] = make_float2(0.f, 0.f);
+    if (active) {
+        if (p.cache) {
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+#pragma unroll
+                for (int j = 0; j < NP; ++j) {
+                    const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
+                    M[s][j] = p.cache_dtype == BDM_BF16 ? load_pair<bf16>(static_cast<const bf16 *>(p.cache) + o)
+                                                        : load_pair<float>(static_cast<const float *>(p.cache) + o);
+                }
+        } else if (p.row_factor) {
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                const int64_t r = (bank * p.H + hh) * S + s;
+                const int64_t ou = (r / p.factor_cols) * p.dv + col0, oz = (r % p.factor_cols) * p.dv + col0;
+#pragma unroll
+                for (int j = 0; j < NP; ++j) {
+                    float2 u, z;
+                    if (p.factor_dtype == BDM_BF16) {
+                        u = load_pair<bf16>(static_cast<const bf16 *>(p.row_factor) + ou + 2 * j);
+                        z = load_pair<bf16>(static_cast<const bf16 *>(p.col_factor) + oz + 2 * j);
+                        M[s][j] = bf16_round_pair(make_float2(u.x + z.x, u.y + z.y));
+                    } else {
+                        u = load_pair<float>(static_cast<const float *>(p.row_factor) + ou + 2 * j);
+                        z = load_pair<float>(static_cast<const float *>(p.col_factor) + oz + 2 * j);
+                        M[s][j] = make_float2(u.x + z.x, u.y + z.y);
+                    }
+                }
+            }
+        }
+        if (p.interval > 0) {
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+#pragma unroll
+                for (int j = 0; j < NP; ++j) M[s][j] = bf16_round_pair(M[s][j]);
+        }
+    }
+
+    // Clamp caller-provided bounds so a malformed cu_seqlens cannot index past `order`.
+    const int64_t start = min(max(p.cu[seq], (int64_t)0), p.E);
+    const int64_t end = min(max(p.cu[seq + 1], start), p.E);
+    int since_round = 0;  // events since the last stored-state rounding
+
+    for (int64_t base = start; base < end; base += EB) {
+        const int n = (int)((end - base) < EB ? (end - base) : EB);
+        // ------------------------------------------------ decode event ids
+        bool is_write = false;
+        if (lane < n) {
+            int64_t id = p.order[base + lane];
+            int64_t tok = -1, rid = -1;
+            float wt = 0.f;
+            if (id >= 0 && id < p.nw) {
+                tok = id / p.kw;
+                wt = Elem<T>::to_float(wwp[id]);
+                is_write = true;
+            } else if (id >= p.nw && id < p.E) {
+                rid = id - p.nw;
+                tok = rid / p.kr;
+                wt = Elem<T>::to_float(rwp[rid]);
+            }
+            if (tok < 0 || tok >= p.nt) {  // corrupt id: make the event a no-op
+                tok = -1;
+                is_write = false;
+                rid = -1;
+            }
+            tok_s[lane] = tok;
+            rid_s[lane] = rid;
+            wgt_s[lane] = wt;
+        }
+        const unsigned wmask = __ballot_sync(0xffffffffu, is_write);
+        __syncwarp();
+        // ------------------------------------- per-event row controls (lanes)
+        for (int task = lane; task < n * S; task += 32) {
+            const int ev = task / S, s = task % S;
+            const int64_t tok = tok_s[ev];
+            if (tok < 0) continue;
+            const int64_t o = tok * HS + (int64_t)hh * S + s;
+            const float wt = wgt_s[ev];
+            if ((wmask >> ev) & 1u) {
+                const float kk = Elem<T>::to_float(kp[o]);
+                const float gg = p.g[o];
+                const float ge = p.routed_decay ? gg * wt : gg;
+                const float a = rnd<T>(Elem<T>::to_float(bp[o]) * wt) * kk;
+                ctl[ev][s] = dup(expf(ge));
+                ctl[ev][S + s] = dup(a);
+                ctl[ev][2 * S + s] = dup(kk);
+            } else {
+                ctl[ev][s] = dup(rnd<T>(Elem<T>::to_float(qp[o]) * wt));
+            }
+        }
+        __syncwarp();
+        // --------------------------------------------------- event stream
+        for (int mb = 0; mb < n; mb += MB) {
+            Row<T, NC> vr[MB], wr[MB];
+#pragma unroll
+            for (int j = 0; j < MB; ++j) {
+                const int ev = mb + j;
+                if (ev < n && ((wmask >> ev) & 1u) && active) {
+                    const int64_t o = tok_s[ev] * V + (int64_t)hh * p.dv + col0;
+                    load_row<T, NC>(vr[j], vp + o);
+                    load_row<T, NC>(wr[j], wp + o);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < MB; ++j) {
+                const int ev = mb + j;
+                if (ev >= n) break;
+                if (p.interval > 0 && since_round == p.interval) {
+#pragma unroll
+                    for (int s = 0; s < S; ++s)
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) M[s][c] = bf16_round_pair(M[s][c]);
+                    since_round = 0;
+                }
+                ++since_round;
+                if (tok_s[ev] < 0) continue;
+                if ((wmask >> ev) & 1u) {
+                    const float wt = wgt_s[ev];
+                    float2 er[NP];
+#pragma unroll
+                    for (int s = 0; s < S; ++s) {
+                        const float2 e2 = ctl[ev][s];
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) M[s][c] = __fmul2_rn(M[s][c], e2);
+                    }
+#pragma unroll
+                    for (int c = 0; c < NP; ++c) {
+                        float2 lo = __fmul2_rn(ctl[ev][S + 0], M[0][c]);
+                        float2 hi = __fmul2_rn(ctl[ev][S + 1], M[1][c]);
+#pragma unroll
+                        for (int s = 2; s < S; s += 2) {
+                            lo = __ffma2_rn(ctl[ev][S + s], M[s][c], lo);
+                            hi = __ffma2_rn(ctl[ev][S + s + 1], M[s + 1][c], hi);
+                        }
+                        er[c] = make_float2(lo.x + hi.x, lo.y + hi.y);
+                    }
+                    float2 u[NP];
+#pragma unroll
+                    for (int c = 0; c < NP; ++c) {
+                        const float2 vv = load_pair<T>(vr[j].x + 2 * c);
+                        const float2 wv = load_pair<T>(wr[j].x + 2 * c);
+                        const float2 we = round_pair<T>(__fmul2_rn(wv, dup(wt)));
+                        const float2 x = __fmul2_rn(we, vv);
+                        u[c] = make_float2(x.x - er[c].x, x.y - er[c].y);
+                    }
+#pragma unroll
+                    for (int s = 0; s < S; ++s) {
+                        const float2 k2 = ctl[ev][2 * S + s];
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) M[s][c] = __ffma2_rn(k2, u[c], M[s][c]);
+                    }
+                } else {
+                    float2 acc[NP];
+#pragma unroll
+                    for (int c = 0; c < NP; ++c) acc[c] = __fmul2_rn(ctl[ev][0], M[0][c]);
+#pragma unroll
+                    for (int s = 1; s < S; ++s)
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) acc[c] = __ffma2_rn(ctl[ev][s], M[s][c], acc[c]);
+                    if (active) {
+                        Row<T, NC> out;
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) store_pair<T>(out.x + 2 * c, __fmul2_rn(acc[c], dup(p.scale)));
+                        store_row<T, NC>(outp + rid_s[ev] * V + (int64_t)hh * p.dv + col0, out);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+
+    if (p.store_final && p.cache && active) {
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
+                if (p.cache_dtype == BDM_BF16) store_pair<bf16>(static_cast<bf16 *>(p.cache) + o, M[s][j]);
+                else store_pair<float>(static_cast<float *>(p.cache) + o, M[s][j]);
+            }
+    }
+}
+
+template <typename T, int S, int NC>
+int launch_scan(const ScanParams &p, cudaStream_t st) {
+    ScanParams q = p;
+    q.ctiles = (int)ceil_div(p.dv, 32 * NC);
+    q.units = p.batch * p.J * p.H * q.ctiles;
+    if (q.units == 0) return BDM_OK;
+    const int64_t blocks = ceil_div(q.units, kScanWarps);
+    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    bank_scan_kernel<T, S, NC><<<(unsigned)blocks, kScanWarps * 32, 0, st>>>(q);
+    return launch_status();
+}
+
+template <typename T>
+int launch_scan_shape(const ScanParams &p, int S, cudaStream_t st) {
+    const bool narrow = p.dv < 128;
+    switch (S) {
+        case 4: return narrow ? launch_scan<T, 4, 2>(p, st) : launch_scan<T, 4, 8>(p, st);
+        case 8: return narrow ? launch_scan<T, 8, 2>(p, st) : launch_scan<T, 8, 4>(p, st);
+        case 16: return launch_scan<T, 16, 2>(p, st);
+        default: return BDM_ERR_UNSUPPORTED;
+    }
+}
+
+}  // namespace
+}  // namespace bdm
+
+extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
+                             const int64_t *write_idx, const void *write_w, const int64_t *read_idx,
+                             const void *read_w, const int64_t *order, const int64_t *cu_seqlens, int64_t batch,
+                             int64_t time, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw,
+                             int kr, int dtype, int routed_decay, float scale, const void *row_factor,
+                             const void *col_factor, int64_t factor_cols, int factor_dtype, void *cache,
+                             int cache_dtype, int store_final, int state_interval, void *reads, void *stream) {
+    using namespace bdm;
+    if (batch <= 0 || time <= 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0)
+        return BDM_ERR_INVALID;
+    if (!q || !k || !v || !g || !b || !w || !write_idx || !write_w || !read_idx || !read_w || !order || !cu_seqlens ||
+        !reads)
+        return BDM_ERR_INVALID;
+    if (bank_size != 4 && bank_size != 8 && bank_size != 16) return BDM_ERR_UNSUPPORTED;
+    if (head_value_width % 8) return BDM_ERR_UNSUPPORTED;
+    if (state_interval < 0 || (store_final && !cache)) return BDM_ERR_INVALID;
+    if (!valid_dtype(dtype) || (cache && !valid_dtype(cache_dtype))) return BDM_ERR_DTYPE;
+    if (!cache && row_factor) {
+        if (!col_factor || factor_cols <= 0 || !valid_dtype(factor_dtype)) return BDM_ERR_INVALID;
+        if ((bank_count * heads * bank_size) % factor_cols) return BDM_ERR_INVALID;
+    }
+    ScanParams p{};
+    p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w;
+    p.wi = write_idx; p.ri = read_idx; p.ww = write_w; p.rw = read_w;
+    p.order = order; p.cu = cu_seqlens;
+    p.batch = batch; p.time = time; p.J = bank_count; p.nt = batch * time; p.nw = p.nt * kw;
+    p.E = p.nt * (kw + kr);
+    p.H = heads; p.dv = head_value_width; p.kw = kw; p.kr = kr; p.routed_decay = routed_decay;
+    p.scale = scale;
+    p.row_factor = cache ? nullptr : row_factor;
+    p.col_factor = cache ? nullptr : col_factor;
+    p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
+    p.cache = cache; p.cache_dtype = cache_dtype; p.store_final = store_final; p.interval = state_interval;
+    p.reads = reads;
+    cudaStream_t st = as_stream(stream);
+    BDM_DISPATCH_DTYPE(dtype, T, { return launch_scan_shape<T>(p, bank_size, st); });
+    return BDM_OK;
+}

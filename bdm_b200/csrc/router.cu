@@ -1,0 +1,132 @@
+// Product-key top-B router (one warp per token).
+//
+// Restates product_key_route (implementation/bdm/gdn2_banks.py:74-114):
+//   top-sub per factor -> sub x sub pair sums in the logits dtype -> top-count
+//   -> softmax in FP32, index = row * J2 + col.
+// Selection is a sequence of warp arg-max rounds over 64-bit keys
+// (order-preserving value bits : inverted index), so equal scores resolve to
+// the lower index -- the tie rule the reference leaves to torch.topk.
+#include "common.cuh"
+
+namespace bdm {
+namespace {
+
+constexpr int kRouteWarps = 8;
+
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Warp arg-max of (hi, lo) keys; every lane gets the winning key.
+__device__ __forceinline__ void warp_argmax(uint32_t hi, uint32_t lo, uint32_t &wh, uint32_t &wl) {
+    wh = __reduce_max_sync(0xffffffffu, hi);
+    wl = __reduce_max_sync(0xffffffffu, hi == wh ? lo : 0u);
+}
+
+// Local best of the elements this lane owns (i = lane + 32*m), skipping taken ones.
+__device__ __forceinline__ void lane_best(const float *vals, int n, uint32_t taken, uint32_t &bh, uint32_t &bl) {
+    bh = 0u;
+    bl = 0u;
+    const int lane = (int)lane_id();
+    for (int m = 0, i = lane; i < n; ++m, i += 32) {
+        if (taken & (1u << m)) continue;
+        uint32_t h = ordered_bits(vals[i]);
+        uint32_t l = ~(uint32_t)i;
+        if (h > bh || (h == bh && l > bl)) {
+            bh = h;
+            bl = l;
+        }
+    }
+}
+
+// Top-k of vals[0..n) (n <= 1024, k <= n) ordered by (value desc, index asc).
+__device__ void warp_topk(const float *vals, int n, int k, float *out_v, int *out_i) {
+    const int lane = (int)lane_id();
+    uint32_t taken = 0u, bh, bl;
+    lane_best(vals, n, taken, bh, bl);
+    for (int r = 0; r < k; ++r) {
+        uint32_t wh, wl;
+        warp_argmax(bh, bl, wh, wl);
+        int i = (int)(~wl);
+        if (lane == 0) {
+            out_v[r] = vals[i];
+            out_i[r] = i;
+        }
+        if ((i & 31) == lane) {
+            taken |= 1u << (i >> 5);
+            lane_best(vals, n, taken, bh, bl);
+        }
+    }
+    __syncwarp();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRouteWarps * 32)
+route_kernel(const T *__restrict__ logits, int64_t ntok, int64_t ld, int j1, int j2, int sub, int count,
+             int64_t *__restrict__ out_idx, T *__restrict__ out_w) {
+    extern __shared__ float smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = (int)lane_id();
+    const int per_warp = j1 + j2 + 4 * sub + sub * sub + 2 * count;
+    float *z = smem + warp * per_warp;
+    float *fv = z + j1 + j2;
+    float *sv = fv + sub;
+    int *fi = reinterpret_cast<int *>(sv + sub);
+    int *si = fi + sub;
+    float *pv = reinterpret_cast<float *>(si + sub);
+    float *cv = pv + sub * sub;
+    int *ci = reinterpret_cast<int *>(cv + count);
+
+    for (int64_t t = (int64_t)blockIdx.x * kRouteWarps + warp; t < ntok; t += (int64_t)gridDim.x * kRouteWarps) {
+        const T *row = logits + t * ld;
+        for (int i = lane; i < j1 + j2; i += 32) z[i] = Elem<T>::to_float(row[i]);
+        __syncwarp();
+        warp_topk(z, j1, sub, fv, fi);
+        warp_topk(z + j1, j2, sub, sv, si);
+        // Pair scores in the logits dtype, pair p = i*sub + l (gdn2_banks.py:106-110).
+        for (int p = lane; p < sub * sub; p += 32) pv[p] = rnd<T>(fv[p / sub] + sv[p % sub]);
+        __syncwarp();
+        warp_topk(pv, sub * sub, count, cv, ci);
+        // Softmax in FP32 over the descending selection: cv[0] is the maximum.
+        float e = 0.f;
+        if (lane < count) e = expf(cv[lane] - cv[0]);
+        float sum = warp_sum(e);
+        if (lane < count) {
+            int p = ci[lane];
+            out_idx[t * count + lane] = (int64_t)fi[p / sub] * j2 + si[p % sub];
+            out_w[t * count + lane] = Elem<T>::from_float(e / sum);
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace
+}  // namespace bdm
+
+extern "C" int bdm_route(const void *logits, int64_t ntok, int64_t ld, int j1, int j2, int selected, int dtype,
+                         int64_t *indices, void *weights, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || j1 <= 0 || j2 <= 0 || selected <= 0 || ld < j1 + j2) return BDM_ERR_INVALID;
+    if (ntok == 0) return BDM_OK;
+    if (!logits || !indices || !weights) return BDM_ERR_INVALID;
+    int sub = selected < j1 ? selected : j1;
+    sub = sub < j2 ? sub : j2;
+    int count = selected < sub * sub ? selected : sub * sub;
+    if (j1 > 1024 || j2 > 1024 || sub > 32 || count > 32) return BDM_ERR_UNSUPPORTED;
+    size_t per_warp = (size_t)(j1 + j2 + 4 * sub + sub * sub + 2 * count) * sizeof(float);
+    size_t smem = per_warp * kRouteWarps;
+    if (smem > 200 * 1024) return BDM_ERR_UNSUPPORTED;
+    int64_t blocks = ceil_div(ntok, kRouteWarps);
+    if (blocks > 16 * kNumSMs) blocks = 16 * kNumSMs;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        auto kern = route_kernel<T>;
+        if (smem > 48 * 1024) {
+            int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            if (rc) return rc;
+        }
+        kern<<<(unsigned)blocks, kRouteWarps * 32, smem, as_stream(stream)>>>(
+            static_cast<const T *>(logits), ntok, ld, j1, j2, sub, count, indices, static_cast<T *>(weights));
+    });
+    return launch_status();
+}

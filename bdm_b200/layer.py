@@ -1,0 +1,372 @@
+"""Drop-in BDM layer whose bank path runs on hand-written sm_100a kernels.
+
+``BankedDeltaMemory`` (alias ``BlockSparseDeltaMemory``) keeps the reference
+module's constructor, parameter names, shapes and seeded initialisation
+(implementation/bdm/model.py:15-78, _parameters.py:69-177, routing.py:12-68),
+so ``state_dict``s move between the two unchanged, and its entry points:
+
+* ``forward(hidden)``                      model.py:88-140   (prefill / training forward)
+* ``prefill(hidden, state=None, *, state_dtype=None)``  inference.py:110-131
+* ``step(hidden, state)``                  inference.py:161-194
+* ``create_state(batch, dtype=...)``       inference.py:100-107
+
+Per forward: ONE projection GEMM (all controllers, both routers and the output
+gate, biases in its epilogue), then the CUDA kernels of ``ops`` -- controller
+epilogue, router, dispatch, bank recurrence, combine + norm + gate -- and the
+o_proj GEMM.  There is no backend switch and no CPU path; CPU inputs raise.
+The backward pass is not implemented: forward / prefill / step run without
+autograd, and a forward that would need gradients raises.
+"""
+from __future__ import annotations
+
+import hashlib
+import math
+
+import torch
+from torch import nn
+from torch.nn import functional as F
+
+from . import ops
+from .config import BDMConfig, near_square_factors, state_interval
+
+
+class SharedResidualRouter(nn.Module):
+    """Routing base plus learned read / write residuals (routing.py:12-35).
+
+    ``read``/``write`` are kept for API parity; the layer folds both into its
+    fused projection instead of calling them.
+    """
+
+    def __init__(self, input_width: int, output_width: int) -> None:
+        super().__init__()
+        if input_width <= 0 or output_width <= 0:
+            raise ValueError('router widths must be positive')
+        self.base = nn.Linear(input_width, output_width)
+        self.read_residual = nn.Linear(input_width, output_width)
+        self.write_residual = nn.Linear(input_width, output_width)
+
+    def read_params(self):
+        return self.base.weight + self.read_residual.weight, self.base.bias + self.read_residual.bias
+
+    def write_params(self):
+        return self.base.weight + self.write_residual.weight, self.base.bias + self.write_residual.bias
+
+    def read(self, hidden):
+        return F.linear(hidden, *self.read_params())
+
+    def write(self, hidden):
+        return F.linear(hidden, *self.write_params())
+
+    @torch.no_grad()
+    def initialize_from_independent(self, *, std: float, read_generator=None, write_generator=None) -> None:
+        """Base = mean of two matched truncated-normal draws; residuals and biases zero (routing.py:37-68)."""
+        if std <= 0:
+            raise ValueError('router initialization scale must be positive')
+        draws = []
+        for generator in (read_generator, write_generator):
+            weight = torch.empty_like(self.base.weight)
+            nn.init.trunc_normal_(weight, mean=0.0, std=std, a=-3.0 * std, b=3.0 * std, generator=generator)
+            draws.append(weight)
+        self.base.weight.copy_(0.5 * (draws[0] + draws[1]))
+        for t in (self.base.bias, self.read_residual.weight, self.read_residual.bias, self.write_residual.weight,
+                  self.write_residual.bias):
+            t.zero_()
+
+
+class BankedDeltaMemory(nn.Module):
+    """Shared-residual product routing around GDN2 memory banks, on B200 kernels."""
+
+    def __init__(self, config: BDMConfig, *, layer_id=0, seed=0, backend='role', compact_replay=None):
+        super().__init__()
+        if backend != 'role':
+            raise ValueError("bdm_b200 runs only its CUDA path (backend='role'); there is no CPU or FLA backend")
+        if seed < 0 or layer_id < 0:
+            raise ValueError('seed and layer_id must be nonnegative')
+        if compact_replay is not None and type(compact_replay) is not bool:
+            raise ValueError('compact_replay must be None, True, or False')
+        self.compact_replay = compact_replay
+        self.config, self.backend = config, backend
+        self.hidden_size, self.bank_count, self.bank_size = config.dim, config.bank_count, config.bank_size
+        self.value_width, self.kernel_key_width = config.value_width, config.bank_size
+        self.num_heads = config.num_heads
+        self.head_value_width = config.head_value_width
+        key_width = config.num_heads * config.bank_size
+        self.num_reads = self.num_writes = config.selected_banks
+        self.layer_id, self.initialization_seed = layer_id, seed * 100_000 + 6000 + layer_id
+        self.norm_eps = config.norm_eps
+        self.shared_residual_router = True
+        self.initial_state_mode = 'product_key'
+        self.routing_mode = 'product_topk'
+        self.factors = near_square_factors(config.bank_count)
+        route_width = sum(self.factors)
+        self.factor_route_width = self.route_projection_width = route_width
+        # Module creation order matches the reference, so the global RNG
+        # draws of nn.Linear's default init (overwritten below) line up too.
+        self.q_proj = nn.Linear(config.dim, key_width, bias=False)
+        self.k_proj = nn.Linear(config.dim, key_width, bias=False)
+        self.v_proj = nn.Linear(config.dim, config.value_width, bias=False)
+        self.shared_router = SharedResidualRouter(config.dim, route_width)
+        self.read_route_proj = self.write_route_proj = None
+        self.f_proj = nn.Sequential(nn.Linear(config.dim, config.head_value_width, bias=False),
+                                    nn.Linear(config.head_value_width, key_width, bias=False))
+        self.b_proj = nn.Linear(config.dim, key_width, bias=False)
+        self.w_proj = nn.Linear(config.dim, config.value_width, bias=False)
+        self.A_log = nn.Parameter(torch.empty(config.num_heads, dtype=torch.float32))
+        self.dt_bias = nn.Parameter(torch.empty(key_width, dtype=torch.float32))
+        self.A_log._no_weight_decay = self.dt_bias._no_weight_decay = True
+        rows, columns = near_square_factors(config.logical_rows)
+        self.register_parameter('initial_state', None)
+        self.initial_row_factor = nn.Parameter(torch.zeros(rows, config.head_value_width))
+        self.initial_column_factor = nn.Parameter(torch.zeros(columns, config.head_value_width))
+        self.initial_row_factor._sdm_memory_bank = self.initial_column_factor._sdm_memory_bank = True
+        self.output_gate = nn.Linear(config.dim, config.value_width, bias=True)
+        self.output_norm_weight = nn.Parameter(torch.ones(config.value_width))
+        if config.output_normalization == 'layer':
+            self.output_norm_bias = nn.Parameter(torch.zeros(config.value_width))
+        self.o_proj = nn.Linear(config.value_width, config.dim, bias=config.output_bias)
+        self._fused_cache = None
+        # Optional list; when set, (start, end) CUDA events bracket every bank-recurrence launch.
+        self.scan_events = None
+        self.init_weights(initialization_seed=self.initialization_seed)
+
+    # ---------------------------------------------------------- initialisation
+    def _role_generator(self, role, parameter, initialization_seed):
+        """Per-role generator seeded by blake2b of the role name (_parameters.py:69-84)."""
+        if initialization_seed is None:
+            return None
+        digest = hashlib.blake2b(f'bank_sparse_gdn2.{self.layer_id}.{role}'.encode(), digest_size=8).digest()
+        generator = torch.Generator(device=parameter.device)
+        generator.manual_seed((initialization_seed ^ int.from_bytes(digest, byteorder='little')) % (1 << 63))
+        return generator
+
+    def init_weights(self, init_std=None, factor=1.0, width_scaling=None, *, initialization_seed=None):
+        """Seeded initialisation identical to the reference (_parameters.py:86-177)."""
+        del width_scaling
+        if initialization_seed is None:
+            initialization_seed = self.initialization_seed
+        if initialization_seed is not None and initialization_seed < 0:
+            raise ValueError('initialization_seed must be non-negative')
+        for name, module in self.named_modules():
+            if isinstance(module, nn.Linear) and not name.startswith('shared_router.'):
+                nn.init.xavier_uniform_(module.weight, gain=2 ** -2.5,
+                                        generator=self._role_generator(f'{name}.weight', module.weight,
+                                                                       initialization_seed))
+                if module.bias is not None:
+                    nn.init.zeros_(module.bias)
+        base_std = (init_std or self.hidden_size ** -0.5) / factor
+        self.shared_router.initialize_from_independent(
+            std=base_std,
+            read_generator=self._role_generator('read_router.weight', self.shared_router.base.weight,
+                                                initialization_seed),
+            write_generator=self._role_generator('write_router.weight', self.shared_router.base.weight,
+                                                 initialization_seed))
+        with torch.no_grad():
+            self.A_log.uniform_(1.0, 16.0, generator=self._role_generator('decay_rate', self.A_log,
+                                                                          initialization_seed)).log_()
+            log_dt = torch.empty_like(self.dt_bias).uniform_(
+                math.log(0.001), math.log(0.1),
+                generator=self._role_generator('time_step', self.dt_bias, initialization_seed))
+            dt = log_dt.exp().clamp_min(1e-4)
+            self.dt_bias.copy_(dt + torch.log(-torch.expm1(-dt)))  # inverse softplus
+            for role, parameter in (('initial_state.row', self.initial_row_factor),
+                                    ('initial_state.column', self.initial_column_factor)):
+                nn.init.trunc_normal_(parameter, mean=0.0, std=base_std, a=-3 * base_std, b=3 * base_std,
+                                      generator=self._role_generator(role, parameter, initialization_seed))
+                # two additive factors share one row's variance budget
+                parameter.mul_(1 / math.sqrt(2))
+            self.output_norm_weight.fill_(1.0)
+            if hasattr(self, 'output_norm_bias'):
+                self.output_norm_bias.zero_()
+        self._fused_cache = None
+
+    def reset_parameters(self) -> None:
+        self.init_weights(initialization_seed=self.initialization_seed)
+
+    # ------------------------------------------------------------- properties
+    @property
+    def total_rows(self) -> int:
+        return self.bank_count * self.num_heads * self.bank_size
+
+    @property
+    def touched_rows(self) -> int:
+        return self.num_writes * self.num_heads * self.bank_size
+
+    @property
+    def logical_reads(self) -> int:
+        return self.num_reads * self.num_heads * self.bank_size
+
+    @property
+    def logical_writes(self) -> int:
+        return self.num_writes * self.num_heads * self.bank_size
+
+    @property
+    def initial_state_parameter_count(self) -> int:
+        return self.initial_row_factor.numel() + self.initial_column_factor.numel()
+
+    # ------------------------------------------------------- fused projection
+    def _fused_projection(self):
+        """Concatenated [W; bias] of every projection that reads ``hidden``.
+
+        Column blocks: q | k | v | f1 | b | w | read router | write router | gate.
+        Router weights are base + residual in the parameter dtype, as
+        SharedResidualRouter.read/write form them.  Rebuilt when a parameter changes.
+        """
+        params = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.f_proj[0].weight,
+                  self.b_proj.weight, self.w_proj.weight, *self.shared_router.parameters(), self.output_gate.weight,
+                  self.output_gate.bias]
+        key = tuple((p.data_ptr(), p._version, p.dtype, p.device) for p in params)
+        if self._fused_cache is not None and self._fused_cache[0] == key:
+            return self._fused_cache[1]
+        with torch.no_grad():
+            rw, rb = self.shared_router.read_params()
+            ww, wb = self.shared_router.write_params()
+            blocks = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.f_proj[0].weight,
+                      self.b_proj.weight, self.w_proj.weight, rw, ww, self.output_gate.weight]
+            weight = torch.cat([b.detach() for b in blocks], 0).contiguous()
+            widths = [b.shape[0] for b in blocks]
+            offsets = [0]
+            for wdt in widths:
+                offsets.append(offsets[-1] + wdt)
+            bias = torch.zeros(weight.shape[0], dtype=weight.dtype, device=weight.device)
+            bias[offsets[6]:offsets[7]] = rb.detach()
+            bias[offsets[7]:offsets[8]] = wb.detach()
+            bias[offsets[8]:offsets[9]] = self.output_gate.bias.detach()
+            names = ['q', 'k', 'v', 'f', 'b', 'w', 'read', 'write', 'gate']
+            cols = dict(zip(names, offsets[:-1]))
+        fused = (weight, bias, cols)
+        self._fused_cache = (key, fused)
+        return fused
+
+    def _project(self, hidden2d):
+        weight, bias, cols = self._fused_projection()
+        return torch.addmm(bias, hidden2d, weight.t()), cols
+
+    # ------------------------------------------------------------------ steps
+    def _check_hidden(self, hidden):
+        if hidden.ndim != 3 or hidden.shape[-1] != self.hidden_size or hidden.shape[1] == 0:
+            raise ValueError('hidden must be [batch, positive time, dim]')
+        if not hidden.is_cuda:
+            raise ValueError('bdm_b200 requires CUDA tensors; there is no CPU path')
+        if hidden.dtype != self.q_proj.weight.dtype:
+            raise ValueError(f'hidden dtype {hidden.dtype} does not match the parameters ({self.q_proj.weight.dtype})')
+        ops.dtype_code(hidden.dtype)
+
+    def _controls_and_routes(self, hidden):
+        batch, time, _ = hidden.shape
+        proj, cols = self._project(hidden.reshape(batch * time, self.hidden_size))
+        q, k, v, g, b, w = ops.controllers(proj, cols, self.f_proj[1].weight, self.A_log, self.dt_bias,
+                                           heads=self.num_heads, bank_size=self.bank_size,
+                                           head_value_width=self.head_value_width,
+                                           qk_norm=self.config.qk_normalization)
+        width = sum(self.factors)
+        ww, wi = ops.route(proj[:, cols['write']:cols['write'] + width], bank_count=self.bank_count,
+                           selected_banks=self.num_writes, factors=self.factors)
+        rw, ri = ops.route(proj[:, cols['read']:cols['read'] + width], bank_count=self.bank_count,
+                           selected_banks=self.num_reads, factors=self.factors)
+        shape = (batch, time, -1)
+        routes = (ww.reshape(shape), wi.reshape(shape), rw.reshape(shape), ri.reshape(shape))
+        gate = proj[:, cols['gate']:cols['gate'] + self.value_width]
+        return (q, k, v, g, b, w), routes, gate
+
+    def _output(self, hidden, reads, read_idx, gate, *, round_each):
+        batch, time, _ = hidden.shape
+        normed = ops.combine_norm_gate(reads, read_idx, gate, self.output_norm_weight,
+                                       getattr(self, 'output_norm_bias', None), eps=self.norm_eps,
+                                       layer_norm=self.config.output_normalization == 'layer', round_each=round_each)
+        return F.linear(normed, self.o_proj.weight, self.o_proj.bias).reshape(batch, time, self.hidden_size)
+
+    def _bank_pass(self, controls, routes, batch, time, **state_args):
+        ww, wi, rw, ri = routes
+        meta = ops.dispatch(wi, ri, self.bank_count)
+        timing = self.scan_events is not None
+        if timing:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+        reads = ops.bank_scan(*controls, wi, ww, ri, rw, meta['order'], meta['cu_seqlens'], batch=batch, time=time,
+                              bank_count=self.bank_count, heads=self.num_heads, bank_size=self.bank_size,
+                              head_value_width=self.head_value_width, routed_decay=self.config.routed_decay,
+                              scale=self.bank_size ** -0.5, **state_args)
+        if timing:
+            end.record()
+            self.scan_events.append((start, end))
+        return reads
+
+    def forward(self, hidden):
+        """Full-sequence forward (model.py:88-140): training-state BF16 storage policy, FP32 combine."""
+        self._check_hidden(hidden)
+        if torch.is_grad_enabled() and (hidden.requires_grad or any(p.requires_grad for p in self.parameters())):
+            raise NotImplementedError('bdm_b200 implements the forward pass only; call it under torch.no_grad() '
+                                      'or torch.inference_mode()')
+        batch, time, _ = hidden.shape
+        controls, routes, gate = self._controls_and_routes(hidden)
+        interval = state_interval(self.bank_size) if self.config.training_state_dtype == 'bfloat16' else 0
+        reads = self._bank_pass(controls, routes, batch, time, row_factor=self.initial_row_factor,
+                                col_factor=self.initial_column_factor, state_interval=interval)
+        ri = routes[3].reshape(batch * time, -1)
+        return self._output(hidden, reads, ri, gate, round_each=False)
+
+    # ---------------------------------------------------- stateful inference
+    def _state_shape(self, batch):
+        if self.num_heads == 1:
+            return (batch, self.bank_count, self.bank_size, self.value_width)
+        return (batch, self.bank_count, self.num_heads, self.bank_size, self.head_value_width)
+
+    def create_state(self, batch, *, dtype=torch.bfloat16):
+        """Product-key initial cache [batch, J, S, V] (H = 1) or [batch, J, H, S, dv] (inference.py:100-107)."""
+        if dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError('cache dtype must be FP32 or BF16')
+        state = ops.product_state(self.initial_row_factor, self.initial_column_factor, batch=batch,
+                                  bank_count=self.bank_count, heads=self.num_heads, bank_size=self.bank_size,
+                                  dtype=dtype)
+        return state.reshape(self._state_shape(batch))
+
+    def _validate_state(self, hidden, state):
+        if state is not None and (tuple(state.shape) != self._state_shape(hidden.shape[0])
+                                  or state.dtype not in (torch.float32, torch.bfloat16)
+                                  or state.device != hidden.device or not state.is_contiguous()):
+            raise ValueError(f'state must be contiguous FP32 or BF16 {self._state_shape(hidden.shape[0])} '
+                             'on the input device')
+
+    @torch.no_grad()
+    def _prefill(self, hidden, state, state_dtype):
+        batch, time, _ = hidden.shape
+        cache_dtype = state_dtype or (state.dtype if state is not None else torch.bfloat16)
+        if cache_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError('cache dtype must be FP32 or BF16')
+        if state is None:
+            # Wider factors are not rounded early to a narrower cache (inference.py:117-121).
+            work = torch.float32 if self.initial_row_factor.dtype != cache_dtype else cache_dtype
+            state = self.create_state(batch, dtype=work)
+        elif state_dtype is not None and state_dtype != state.dtype:
+            raise ValueError('state_dtype must match the supplied cache')
+        controls, routes, gate = self._controls_and_routes(hidden)
+        reads = self._bank_pass(controls, routes, batch, time, cache=state, store_final=True, state_interval=0)
+        if state.dtype != cache_dtype:
+            state = state.to(cache_dtype)
+        ri = routes[3].reshape(batch * time, -1)
+        return self._output(hidden, reads, ri, gate, round_each=True), state
+
+    def prefill(self, hidden, state=None, *, state_dtype=None):
+        """Process a prefix (inference.py:110-131); BF16 cache storage rounds once, at handoff."""
+        self._check_hidden(hidden)
+        self._validate_state(hidden, state)
+        if torch.is_grad_enabled():
+            raise RuntimeError('Stateful inference requires no_grad or inference_mode')
+        return self._prefill(hidden, state, state_dtype)
+
+    def step(self, hidden, state):
+        """Advance the cache by one token per row (inference.py:161-194); mutates and returns ``state``."""
+        self._check_hidden(hidden)
+        self._validate_state(hidden, state)
+        if torch.is_grad_enabled() or hidden.shape[1] != 1:
+            raise ValueError('step requires one token under no_grad/inference_mode')
+        batch = hidden.shape[0]
+        controls, routes, gate = self._controls_and_routes(hidden)
+        ww, wi, rw, ri = (r.reshape(batch, -1) for r in routes)
+        raw = ops.decode_step(*controls, wi, ww, ri, rw, state, bank_count=self.bank_count, heads=self.num_heads,
+                              bank_size=self.bank_size, head_value_width=self.head_value_width,
+                              routed_decay=self.config.routed_decay, scale=self.bank_size ** -0.5)
+        return self._output(hidden, raw, None, gate, round_each=True), state
+
+
+BlockSparseDeltaMemory = BankedDeltaMemory

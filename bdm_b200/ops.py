@@ -1,0 +1,232 @@
+"""Torch-facing wrappers of the sm_100a kernels.
+
+Each function validates shapes, allocates outputs with the PyTorch caching
+allocator, and calls one C-ABI entry point on the current CUDA stream.
+Nothing here computes on the host; a CPU tensor is an error.
+
+Reference interfaces each op replaces (p0rc314in/bdm, implementation/bdm/):
+  route            gdn2_banks.py:74-114          product_key_route
+  dispatch         role_bank_dispatch.py:143-153 metadata (keys, sort, bounds)
+  controllers      _parameters.py:189-220        _controllers (after the GEMM)
+  product_state    _parameters.py:40-67          materialize_initial_state
+  bank_scan        routed_update.py:16-32, role_bank_kernel.py:177-202, inference.py:134-158
+  combine_norm_gate role_bank_dispatch.py:219-231, _parameters.py:222-232
+  decode_step      inference.py:161-194
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .config import near_square_factors
+
+_DT = {torch.float32: _lib.BDM_F32, torch.bfloat16: _lib.BDM_BF16}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DT[dtype]
+    except KeyError:
+        raise ValueError(f'unsupported dtype {dtype}; bdm_b200 computes in float32 or bfloat16') from None
+
+
+def _cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError('bdm_b200 ops require CUDA tensors (there is no CPU path)')
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def route(logits: torch.Tensor, *, bank_count: int, selected_banks: int, factors=None):
+    """Product-key top-B routing of ``logits[..., J1+J2]`` (last dim may be a strided view).
+
+    Returns (weights [..., count] in the logits dtype, indices [..., count] int64),
+    ordered by descending pair score, ties to the lower index.
+    """
+    _cuda(logits)
+    j1, j2 = factors or near_square_factors(bank_count)
+    if logits.shape[-1] != j1 + j2:
+        raise ValueError('projected route width does not match the bank table')
+    if not 1 <= selected_banks <= bank_count:
+        raise ValueError('selected bank count is outside the bank table')
+    lead = logits.shape[:-1]
+    z = logits.reshape(-1, logits.shape[-1])
+    if z.stride(-1) != 1:
+        z = z.contiguous()
+    ntok = z.shape[0]
+    sub = min(selected_banks, j1, j2)
+    count = min(selected_banks, sub * sub)
+    idx = torch.empty((ntok, count), dtype=torch.int64, device=z.device)
+    w = torch.empty((ntok, count), dtype=z.dtype, device=z.device)
+    ld = z.stride(0) if ntok > 1 else j1 + j2
+    _lib.check(_lib.load().bdm_route(_ptr(z), ntok, ld, j1, j2, selected_banks, dtype_code(z.dtype), _ptr(idx),
+                                     _ptr(w), _stream(z.device)), 'bdm_route')
+    return w.reshape(*lead, count), idx.reshape(*lead, count)
+
+
+def dispatch(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int, *, want_inverse=False,
+             want_tokens=False, error_word: torch.Tensor | None = None):
+    """Stable (batch, bank) counting sort of all routed events.
+
+    write_idx [B,T,KW], read_idx [B,T,KR] int64 -> dict(order [E], cu_seqlens [B*J+1], inverse?, tokens?).
+    """
+    _cuda(write_idx, read_idx)
+    if write_idx.dtype != torch.long or read_idx.dtype != torch.long:
+        raise ValueError('bank indices must be int64')
+    if write_idx.ndim != 3 or read_idx.ndim != 3 or write_idx.shape[:2] != read_idx.shape[:2]:
+        raise ValueError('routes must be [batch, time, banks] with matching batch and time')
+    batch, time, kw = write_idx.shape
+    kr = read_idx.shape[-1]
+    dev = write_idx.device
+    wi, ri = write_idx.contiguous(), read_idx.contiguous()
+    e = batch * time * (kw + kr)
+    order = torch.empty(e, dtype=torch.int64, device=dev)
+    cu = torch.empty(batch * bank_count + 1, dtype=torch.int64, device=dev)
+    inverse = torch.empty(e, dtype=torch.int64, device=dev) if want_inverse else None
+    tokens = torch.empty(e, dtype=torch.int64, device=dev) if want_tokens else None
+    lib = _lib.load()
+    nbytes = lib.bdm_dispatch_workspace_bytes(batch, time, kw, kr, bank_count)
+    if nbytes < 0:
+        raise ValueError('invalid dispatch geometry')
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+    _lib.check(lib.bdm_dispatch(_ptr(wi), _ptr(ri), batch, time, kw, kr, bank_count, _ptr(order), _ptr(cu),
+                                _ptr(inverse), _ptr(tokens), _ptr(error_word), _ptr(ws), nbytes, _stream(dev)),
+               'bdm_dispatch')
+    out = dict(order=order, cu_seqlens=cu)
+    if want_inverse:
+        out['inverse'] = inverse
+    if want_tokens:
+        out['tokens'] = tokens
+    return out
+
+
+def controllers(proj: torch.Tensor, cols: dict, f2_weight: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
+                *, heads: int, bank_size: int, head_value_width: int, qk_norm: str):
+    """Controller epilogue over the fused projection ``proj [NT, ld]`` (column offsets in ``cols``).
+
+    Returns q, k, v, g, b, w as [NT, H*S] / [NT, V] tensors (g float32).
+    """
+    _cuda(proj, f2_weight)
+    if proj.ndim != 2 or proj.stride(1) != 1:
+        raise ValueError('proj must be a row-major [tokens, width] matrix')
+    nt = proj.shape[0]
+    hs, v_width = heads * bank_size, heads * head_value_width
+    dev, dt = proj.device, proj.dtype
+    q = torch.empty((nt, hs), dtype=dt, device=dev)
+    k = torch.empty_like(q)
+    b = torch.empty_like(q)
+    g = torch.empty((nt, hs), dtype=torch.float32, device=dev)
+    v = torch.empty((nt, v_width), dtype=dt, device=dev)
+    w = torch.empty_like(v)
+    f2 = f2_weight.to(dt).contiguous()
+    al = a_log.detach().float().contiguous()
+    dtb = dt_bias.detach().float().contiguous()
+    _lib.check(_lib.load().bdm_controllers(
+        _ptr(proj), nt, proj.stride(0) if nt > 1 else proj.shape[1], cols['q'], cols['k'], cols['v'], cols['f'],
+        cols['b'], cols['w'], _ptr(f2), _ptr(al), _ptr(dtb), heads, bank_size, head_value_width,
+        1 if qk_norm == 'nvidia' else 0, dtype_code(dt), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w),
+        _stream(dev)), 'bdm_controllers')
+    return q, k, v, g, b, w
+
+
+def product_state(row_factor, col_factor, *, batch: int, bank_count: int, heads: int, bank_size: int,
+                  dtype: torch.dtype):
+    """Product-key initial memory [batch, J, H, S, dv] in ``dtype``."""
+    _cuda(row_factor, col_factor)
+    u, z = row_factor.detach().contiguous(), col_factor.detach().contiguous()
+    dv = u.shape[-1]
+    out = torch.empty((batch, bank_count, heads, bank_size, dv), dtype=dtype, device=u.device)
+    _lib.check(_lib.load().bdm_product_state(_ptr(u), _ptr(z), u.shape[0], z.shape[0], dtype_code(u.dtype), batch,
+                                             bank_count, heads, bank_size, dv, _ptr(out), dtype_code(dtype),
+                                             _stream(u.device)), 'bdm_product_state')
+    return out
+
+
+def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_seqlens, *, batch: int, time: int,
+              bank_count: int, heads: int, bank_size: int, head_value_width: int, routed_decay: bool, scale: float,
+              row_factor=None, col_factor=None, cache=None, store_final=False, state_interval=0):
+    """Per-bank recurrence over dispatched events; returns reads [NT, KR, V] in the activation dtype.
+
+    With ``cache`` ([batch, J, H, S, dv]) the state starts from it and, with
+    ``store_final``, ends in it; otherwise it starts from the product-key factors
+    (or zero when they are None).
+    """
+    _cuda(q, k, v, g, b, w, write_idx, read_idx, order, cu_seqlens, cache)
+    dt = q.dtype
+    nt = batch * time
+    kw, kr = write_idx.shape[-1], read_idx.shape[-1]
+    v_width = heads * head_value_width
+    for name, t, shape in (('q', q, (nt, heads * bank_size)), ('k', k, (nt, heads * bank_size)),
+                           ('b', b, (nt, heads * bank_size)), ('g', g, (nt, heads * bank_size)),
+                           ('v', v, (nt, v_width)), ('w', w, (nt, v_width))):
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f'{name} must be contiguous {shape}, got {tuple(t.shape)}')
+    if g.dtype != torch.float32 or any(t.dtype != dt for t in (k, v, b, w, write_w, read_w)):
+        raise ValueError('controllers and route weights must share the activation dtype (g is float32)')
+    reads = torch.empty((nt, kr, v_width), dtype=dt, device=q.device)
+    if cache is not None and not cache.is_contiguous():
+        raise ValueError('cache must be contiguous')
+    u = z = None
+    if cache is None and row_factor is not None:
+        u, z = row_factor.detach().contiguous(), col_factor.detach().contiguous()
+    # keep contiguous copies alive across the asynchronous call
+    wi, ww, ri, rw = (t.contiguous() for t in (write_idx, write_w, read_idx, read_w))
+    _lib.check(_lib.load().bdm_bank_scan(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(wi), _ptr(ww), _ptr(ri), _ptr(rw), _ptr(order),
+        _ptr(cu_seqlens), batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt),
+        int(routed_decay), float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
+        dtype_code(u.dtype) if u is not None else 0, _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
+        int(store_final), int(state_interval), _ptr(reads), _stream(q.device)), 'bdm_bank_scan')
+    return reads
+
+
+def combine_norm_gate(reads, read_idx, gate, norm_weight, norm_bias, *, eps: float, layer_norm: bool,
+                      round_each: bool):
+    """Ascending-bank read combine, LayerNorm/RMS and sigmoid gate -> [NT, V].
+
+    ``reads`` [NT, KR, V] with ``read_idx`` [NT, KR], or an already combined
+    [NT, V] with ``read_idx=None``; ``gate`` [NT, >=V] (row stride honoured).
+    """
+    _cuda(reads, gate, norm_weight)
+    dt = reads.dtype
+    nt, width = reads.shape[0], reads.shape[-1]
+    kr = read_idx.shape[-1] if read_idx is not None else 1
+    if gate.stride(-1) != 1:
+        raise ValueError('gate rows must be contiguous')
+    out = torch.empty((nt, width), dtype=dt, device=reads.device)
+    nw = norm_weight.detach().to(dt).contiguous()
+    nb = norm_bias.detach().to(dt).contiguous() if norm_bias is not None else None
+    rd = reads.contiguous()
+    ri = read_idx.contiguous() if read_idx is not None else None
+    _lib.check(_lib.load().bdm_combine_norm_gate(
+        _ptr(rd), _ptr(ri), nt, kr, width,
+        _ptr(gate), gate.stride(0) if nt > 1 else gate.shape[-1], _ptr(nw), _ptr(nb), float(eps),
+        1 if layer_norm else 0, int(round_each), dtype_code(dt), _ptr(out), _stream(reads.device)),
+        'bdm_combine_norm_gate')
+    return out
+
+
+def decode_step(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, state, *, bank_count: int, heads: int,
+                bank_size: int, head_value_width: int, routed_decay: bool, scale: float):
+    """One decode token per batch row; ``state`` [B, J, H, S, dv] updated in place. Returns raw [B, V]."""
+    _cuda(q, state)
+    if not state.is_contiguous():
+        raise ValueError('state must be contiguous')
+    batch = q.shape[0]
+    kw, kr = write_idx.shape[-1], read_idx.shape[-1]
+    raw = torch.empty((batch, heads * head_value_width), dtype=q.dtype, device=q.device)
+    wi, ww, ri, rw = (t.contiguous() for t in (write_idx, write_w, read_idx, read_w))
+    q, k, v, g, b, w = (t.contiguous() for t in (q, k, v, g, b, w))
+    _lib.check(_lib.load().bdm_decode_step(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(wi), _ptr(ww), _ptr(ri), _ptr(rw), batch,
+        bank_count, heads,
+        bank_size, head_value_width, kw, kr, dtype_code(q.dtype), int(routed_decay), float(scale), _ptr(state),
+        dtype_code(state.dtype), _ptr(raw), _stream(q.device)), 'bdm_decode_step')
+    return raw

@@ -1,0 +1,376 @@
+"""Benchmark: BDM layer prefill tokens/s on B200 (BASELINE config c2), plus c3 decode.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU; every rank runs its own
+replica of the c2 workload (batch shards trivially: weak scaling, no
+data-path collective).  Rank 0 prints ONE JSON line.
+
+Timed region (value): K forward steps of the public module call
+``layer(hidden)`` with the input already in HBM; an L2 flush (256 MiB write)
+runs between steps, outside the per-step CUDA events.  Time is the sum of
+per-step event times, maximised over ranks.  ``e2e`` times the same call with
+the input copied from pinned host memory and the output copied back inside
+each step.  ``roofline`` is for the dominant kernel, the bank recurrence
+(bdm_bank_scan), timed with CUDA events on its launch stream in the same steps.
+``cpu_baseline`` times the CPU restatement of the reference (oracle/) on the
+host cores on a bounded sample.  ``--impl reference`` runs only that CPU
+restatement (rank 0; other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# ----------------------------------------------------------------- workloads
+C2 = dict(dim=1024, bank_count=256, bank_size=8, selected_banks=8, value_width=1024, num_heads=8)
+C2_BATCH, C2_TIME, C2_CHUNK = 8, 4096, 64
+C3 = dict(dim=1024, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
+C3_BATCH, C3_PREFIX, C3_STEPS = 64, 2048, 1024
+METRIC = 'BDM layer prefill tokens/sec (c2: batch 8 x seq 4096, d_model 1024, H=8, J=256, S=8, B=8, d_v=128)'
+
+
+def c2_bytes_per_token(cfg=C2, batch=C2_BATCH, time_=C2_TIME):
+    """Algorithmic bytes per token of the bank recurrence (fixed per-token definition).
+
+    write events B*(3*H*S*2 + 2*V*2) + read events B*(H*S*2 + V*4) + bank state in/out
+    2*(batch*J*H*S*dv*2)/(batch*T).  The layer-level figure adds hidden in/out 2*D*2.
+    """
+    B, H, S, V, J = cfg['selected_banks'], cfg['num_heads'], cfg['bank_size'], cfg['value_width'], cfg['bank_count']
+    dv = V // H
+    kernel = B * (3 * H * S * 2 + 2 * V * 2) + B * (H * S * 2 + V * 4) + 2 * (batch * J * H * S * dv * 2) / (batch * time_)
+    return kernel, kernel + 2 * cfg['dim'] * 2
+
+
+def c2_flops_per_token(cfg=C2, chunk=C2_CHUNK):
+    """Chunked-form FLOPs per token: 2*B*H*[2(3CS + 2C dv + 3S dv) + (2/3)C^2]."""
+    B, H, S, V = cfg['selected_banks'], cfg['num_heads'], cfg['bank_size'], cfg['value_width']
+    dv = V // H
+    return 2 * B * H * (2 * (3 * chunk * S + 2 * chunk * dv + 3 * S * dv) + (2 / 3) * chunk * chunk)
+
+
+def c3_bytes_per_token(cfg=C3, batch=C3_BATCH, weight_bytes=0):
+    """Decode bytes per token: 3*B*H*S*dv*2 (write tiles in+out, read tiles) + 2*D*2 + weights/batch."""
+    B, H, S, V = cfg['selected_banks'], cfg['num_heads'], cfg['bank_size'], cfg['value_width']
+    return 3 * B * H * S * (V // H) * 2 + 2 * cfg['dim'] * 2 + weight_bytes / batch
+
+
+def load_peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p['hbm_gbs'], p['bf16_tflops'], 'measured'
+    return 6650.0, 1590.0, 'fallback'
+
+
+def load_traffic():
+    """DRAM bytes per bank-recurrence launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, 'profiles', 'bank_scan_c2.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get('dram_bytes_per_launch')
+    return None
+
+
+# -------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device_index):
+        self.index = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ''
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        if self.proc is None or not self.out:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        rows = [r for r in csv.reader(io.StringIO(self.out)) if len(r) >= 9]
+        sm, mx, reasons = [], None, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == 'active':
+                    reasons.add(name)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': mx, 'samples': len(sm),
+                'reasons': sorted(reasons)}
+
+
+# ------------------------------------------------------------- distributed
+def dist_setup(gpus):
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device('cuda', local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device='cuda')
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_forward_sample(batch, time_, seed=1):
+    """Time the CPU restatement (oracle/) of the c2 layer forward on batch x time_ tokens."""
+    import numpy as np
+
+    import oracle
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
+    threads = oracle.set_threads(0)
+    cfg = BSDMConfig(**C2)
+    m = BlockSparseDeltaMemory(cfg, seed=1).to(torch.bfloat16)
+    params = {k: v.float().numpy() for k, v in m.state_dict().items()}
+    params['initial_row_factor'][:] = 0
+    params['initial_column_factor'][:] = 0
+    layer = oracle.OracleLayer({k: getattr(cfg, k) for k in cfg.__dataclass_fields__}, params, bf16=True)
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, time_, cfg.dim, generator=gen).to(torch.bfloat16).float().numpy()
+    t0 = time.perf_counter()
+    y = layer.forward(x)
+    dt = time.perf_counter() - t0
+    assert np.isfinite(y).all()
+    return batch * time_ / dt, dt, threads
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    batch, time_ = C2_BATCH, 512
+    for _ in range(args.warmup):
+        cpu_forward_sample(batch, time_)
+    total_tok, total_s, threads = 0, 0.0, 1
+    for i in range(args.steps):
+        tps, dt, threads = cpu_forward_sample(batch, time_, seed=1 + i)
+        total_tok += batch * time_
+        total_s += dt
+    value = total_tok / total_s
+    sample = f'c2 geometry truncated to batch {batch} x seq {time_} per step (CPU restatement oracle/, BF16 emulated)'
+    line = {
+        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': args.gpus,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': 1000 * total_s / args.steps,
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': 'c2 prefill (truncated sample)', 'global_batch': batch, 'seq_len': time_,
+                   'parallelism': 'cpu'},
+        'cpu_baseline': {'value': value, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port', 'sample': sample},
+        'e2e': {'value': value, 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours
+def run_ours(args, world, rank, local):
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, _lib
+    dev = torch.device('cuda', local)
+    lib = _lib.load()
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+
+    cfg = BSDMConfig(**C2)
+    layer = BlockSparseDeltaMemory(cfg, seed=1).to(torch.bfloat16).to(dev)
+    with torch.no_grad():  # c2: bank states start at zero
+        layer.initial_row_factor.zero_()
+        layer.initial_column_factor.zero_()
+    gen = torch.Generator().manual_seed(1 + rank)
+    x_host = torch.randn(C2_BATCH, C2_TIME, cfg.dim, generator=gen).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev)
+    y_host = torch.empty_like(x_host).pin_memory()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    tokens = C2_BATCH * C2_TIME
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            layer(x)
+        torch.cuda.synchronize()
+        # ------------------------------------------------------- value
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        layer.scan_events = []
+        barrier(world)
+        torch.cuda.synchronize()
+        launches0 = lib.bdm_kernel_launches()
+        with ClockSampler(dev.index) as clocks:
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record()
+                layer(x)
+                ends[i].record()
+            torch.cuda.synchronize()
+        barrier(world)
+        launches = lib.bdm_kernel_launches() - launches0
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        scan_ms = [s.elapsed_time(e) for s, e in layer.scan_events]
+        layer.scan_events = None
+        total_ms = max_over_ranks(sum(step_ms), world)
+        scan_mean = max_over_ranks(statistics.mean(scan_ms), world)
+        # --------------------------------------------------------- e2e
+        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier(world)
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            e_starts[i].record()
+            x.copy_(x_host, non_blocking=True)
+            y = layer(x)
+            y_host.copy_(y, non_blocking=True)
+            e_ends[i].record()
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)), world)
+
+    value = world * tokens * args.steps / (total_ms / 1000)
+    kernel_bytes, layer_bytes = c2_bytes_per_token()
+    achieved = kernel_bytes * tokens / (scan_mean / 1000) / 1e9
+    flops = c2_flops_per_token() * tokens
+    roof_ms = max(flops / (bf16_peak * 1e12), layer_bytes * tokens / (hbm_peak * 1e9)) * 1000
+    line = {
+        'metric': METRIC, 'value': value, 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': total_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (x ~ N(0,1), seed 1 + rank; random-init weights, seed 1)',
+        'config': {'workload': 'c2 BDM layer prefill forward: BSDMConfig(dim=1024, bank_count=256, bank_size=8, '
+                               'selected_banks=8, value_width=1024, num_heads=8), zero initial banks',
+                   'global_batch': C2_BATCH * world, 'seq_len': C2_TIME, 'parallelism': f'dp{world} replicas',
+                   'l2': 'flushed between timed steps (256 MiB write, outside the step events)'},
+        'gpu_launches': int(launches),
+        'e2e': {'value': world * tokens * args.steps / (e2e_ms / 1000), 'unit': 'tokens/s',
+                'h2d_bytes_per_step': x_host.numel() * x_host.element_size(),
+                'd2h_bytes_per_step': y_host.numel() * y_host.element_size()},
+        'roofline': {'kernel': 'bdm_bank_scan (bank_scan_kernel<bf16,8,4>)', 'bound': 'hbm',
+                     'achieved': achieved, 'peak': hbm_peak, 'unit': 'GB/s', 'frac': achieved / hbm_peak,
+                     'peak_source': peak_kind, 'kernel_ms': scan_mean, 'bytes_per_token': kernel_bytes,
+                     'traffic': load_traffic(),
+                     'layer_frac': roof_ms / (total_ms / args.steps), 'layer_roofline_ms': roof_ms},
+        'clocks': clocks.summary(),
+    }
+    if not args.skip_decode:
+        try:
+            line['decode'] = run_decode(dev, rank, world, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['decode'] = {'error': repr(e)[:300]}
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        tps, dt, threads = cpu_forward_sample(C2_BATCH, args.cpu_time)
+        line['cpu_baseline'] = {'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+                                'sample': f'full c2 layer forward, batch {C2_BATCH} x seq {args.cpu_time} '
+                                          f'({dt:.1f} s) with the CPU restatement oracle/'}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_decode(dev, rank, world, args):
+    """c3: 1024 single-token steps at batch 64 on a state pre-filled by a 2048-token prefill."""
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
+    cfg = BSDMConfig(**C3)
+    layer = BlockSparseDeltaMemory(cfg, seed=2).to(torch.bfloat16).to(dev)
+    gen = torch.Generator().manual_seed(2 + rank)
+    prefix = torch.randn(C3_BATCH, C3_PREFIX, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
+    steps = args.decode_steps
+    toks = torch.randn(steps + 8, C3_BATCH, 1, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
+    with torch.inference_mode():
+        _, state = layer.prefill(prefix)
+        for i in range(8):
+            layer.step(toks[steps + i], state)
+        torch.cuda.synchronize()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(steps):
+            layer.step(toks[i], state)
+        end.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    weight_bytes = sum(p.numel() * p.element_size() for p in layer.parameters())
+    hbm_peak, _, _ = load_peaks()
+    bpt = c3_bytes_per_token(weight_bytes=weight_bytes)
+    tps = world * C3_BATCH * steps / (ms / 1000)
+    return {'metric': 'BDM decode tokens/sec (c3: batch 64, J=2048, S=8, B=8, d_v=128, 2048-token prefill)',
+            'value': tps, 'unit': 'tokens/s', 'steps': steps, 'ms_per_step': ms / steps,
+            'state_bytes': state.numel() * state.element_size(),
+            'roofline': {'bound': 'hbm', 'bytes_per_token': bpt, 'achieved': bpt * tps / world / 1e9,
+                         'peak': hbm_peak, 'unit': 'GB/s', 'frac': bpt * tps / world / 1e9 / hbm_peak}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--decode-steps', type=int, default=C3_STEPS)
+    ap.add_argument('--cpu-time', type=int, default=C2_TIME, help='sequence length of the CPU baseline sample')
+    ap.add_argument('--skip-decode', action='store_true')
+    ap.add_argument('--skip-cpu', action='store_true')
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == 'ours':
+        args.warmup = 3
+    if args.impl == 'reference':
+        world = int(os.environ.get('WORLD_SIZE', '1'))
+        rank = int(os.environ.get('RANK', '0'))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,182 @@
+/*
+ * bdm_b200.h -- C ABI of the B200-native Block Delta Memory (BDM) layer hot path.
+ *
+ * Plain pointers and sizes only.  Every device pointer is memory the caller
+ * owns (PyTorch allocations in the bundled Python module); the library
+ * allocates nothing.  Every call is asynchronous on the given CUDA stream
+ * (`stream` is a cudaStream_t passed as void*, NULL = legacy default stream)
+ * and returns a status code; BDM_ERR_CUDA means a launch failed (details in
+ * bdm_last_cuda_error()).  Kernels never trap: an index read from memory that
+ * is out of range is skipped and counted in the optional device error word.
+ *
+ * Element types: BDM_F32 (float) and BDM_BF16 (__nv_bfloat16, RNE rounding).
+ * Index tensors are int64, as in the reference.
+ *
+ * Tensor layouts (row-major, contiguous unless a leading dimension `ld*` is
+ * given):  NT = batch*time tokens, H heads, S = bank_size rows per bank,
+ * dv = head_value_width, V = H*dv, KW / KR = write / read banks per token.
+ *   q, k, b    [NT, H, S]  activation dtype        g [NT, H, S] float
+ *   v, w       [NT, V]     activation dtype
+ *   routes     write_idx/write_w [NT, KW], read_idx/read_w [NT, KR]
+ *   bank state [batch, J, H, S, dv] (H = 1 is the reference's [batch, J, S, V])
+ *   reads      [NT, KR, V] read output of every read event, by route slot
+ *
+ * Each entry point names the reference interface it replaces
+ * (p0rc314in/bdm, implementation/bdm/<file>:<lines>).
+ */
+#ifndef BDM_B200_H
+#define BDM_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BDM_API __attribute__((visibility("default")))
+#else
+#define BDM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum bdm_status {
+    BDM_OK = 0,
+    BDM_ERR_INVALID = 1,     /* bad size, shape or null pointer */
+    BDM_ERR_DTYPE = 2,       /* unsupported element type */
+    BDM_ERR_UNSUPPORTED = 3, /* geometry outside what the kernels implement */
+    BDM_ERR_CUDA = 4,        /* a CUDA call failed; see bdm_last_cuda_error() */
+    BDM_ERR_WORKSPACE = 5    /* workspace missing or too small */
+};
+
+enum bdm_dtype { BDM_F32 = 0, BDM_BF16 = 1 };
+
+/* Human-readable status text (static storage). */
+BDM_API const char *bdm_status_string(int status);
+/* cudaError_t of the last call that returned BDM_ERR_CUDA on this host thread. */
+BDM_API int bdm_last_cuda_error(void);
+/* ABI revision of this header. */
+BDM_API int bdm_abi_version(void);
+/* Kernels launched by this library since it was loaded (all threads). */
+BDM_API long long bdm_kernel_launches(void);
+
+/*
+ * Product-key top-B routing.  Replaces product_key_route
+ * (gdn2_banks.py:74-114), also in its batch_factors form (gdn2_banks.py:93-102).
+ *   logits  [ntok, ld] (dtype); factor scores at columns [0, j1) and [j1, j1+j2)
+ *   indices [ntok, count] int64, weights [ntok, count] (dtype), count = min(selected, sub^2),
+ *   sub = min(selected, j1, j2).  Ordered by descending pair score; ties go to
+ *   the lower index at both top-k stages.  Pair scores are summed in the
+ *   logits dtype; the softmax is FP32 and rounded to dtype.
+ */
+BDM_API int bdm_route(const void *logits, int64_t ntok, int64_t ld, int j1, int j2, int selected, int dtype,
+              int64_t *indices, void *weights, void *stream);
+
+/*
+ * Causal bank dispatch: a stable counting sort of all events by (batch, bank).
+ * Replaces role_bank_dispatch.metadata (role_bank_dispatch.py:143-153: _keys,
+ * torch.sort, _bounds) and the ordering of pack_bank_events
+ * (gdn2_banks.py:174-185, 237-246).
+ *   Event ids: write (token, slot) -> token*kw + slot; read -> NT*kw + token*kr + slot.
+ *   order      [E] int64, E = NT*(kw+kr): event id at each packed position, sorted
+ *              by ((batch*J + bank)*T + t)*2 + role; equal keys keep id order.
+ *   cu_seqlens [batch*J + 1] int64.
+ *   inverse    [E] int64 or NULL: packed position of each event id.
+ *   tokens     [E] int64 or NULL: token of each packed position.
+ *   error_word int32 device pointer or NULL: incremented for each out-of-range bank.
+ * The workspace (device memory, bdm_dispatch_workspace_bytes) is scratch.
+ */
+BDM_API int64_t bdm_dispatch_workspace_bytes(int64_t batch, int64_t time, int kw, int kr, int64_t bank_count);
+BDM_API int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time, int kw, int kr,
+                 int64_t bank_count, int64_t *order, int64_t *cu_seqlens, int64_t *inverse, int64_t *tokens,
+                 int32_t *error_word, void *workspace, int64_t workspace_bytes, void *stream);
+
+/*
+ * Controller epilogue over the fused input projection.  Replaces the
+ * element-wise part of _parameters._controllers (_parameters.py:189-220) and
+ * heads.controllers (heads.py:11-22); the projections themselves are one GEMM
+ * (proj = hidden @ [Wq;Wk;Wv;Wf1;Wb;Ww;...]^T) done by the caller.
+ *   proj [ntok, ld] (dtype) with the q, k, v, f1, b, w blocks at the given column offsets
+ *   f2_weight [H*S, dv] (dtype): second f_proj layer; a_log [H], dt_bias [H*S] float
+ *   qk_norm: 0 = F.normalize (original), 1 = x*rsqrt(sum x^2 + 1e-6) (nvidia)
+ *   out: q, k, b [ntok, H, S] (dtype), g [ntok, H, S] float, v, w [ntok, V] (dtype)
+ */
+BDM_API int bdm_controllers(const void *proj, int64_t ntok, int64_t ld, int64_t col_q, int64_t col_k, int64_t col_v,
+                    int64_t col_f, int64_t col_b, int64_t col_w, const void *f2_weight, const float *a_log,
+                    const float *dt_bias, int heads, int bank_size, int head_value_width, int qk_norm, int dtype,
+                    void *q, void *k, void *v, float *g, void *b, void *w, void *stream);
+
+/*
+ * Product-key initial bank memory.  Replaces materialize_initial_state
+ * (_parameters.py:40-67) and product_routed_update.materialize
+ * (product_routed_update.py:10-21).
+ *   out[n, j, h, s, :] = round_param(U[r / Q] + Z[r % Q]),  r = (j*H + h)*S + s,
+ *   U [P, dv], Z [Q, dv] in factor dtype; out [batch, J, H, S, dv] in out dtype.
+ */
+BDM_API int bdm_product_state(const void *row_factor, const void *col_factor, int64_t rows_p, int64_t cols_q,
+                      int factor_dtype, int64_t batch, int64_t bank_count, int heads, int bank_size,
+                      int head_value_width, void *out, int out_dtype, void *stream);
+
+/*
+ * Per-bank delta-rule recurrence over dispatched events (one pass over every
+ * (batch, bank, head) sequence).  Replaces routed_update.RoutedUpdate.forward
+ * -> role_bank_dispatch.pack + decay_transform + role_bank_kernel.forward
+ * (routed_update.py:5-32, role_bank_dispatch.py:156-185, role_bank_kernel.py:46-73,177-202)
+ * and, with a cache, inference._bank_prefill (inference.py:134-158).
+ *
+ * Per write event (token t, slot j, p = write_w[t,j]) and head h, in FP32:
+ *   M <- diag(exp(g_e)) M ;  u = w_e * v - (b_e * k)^T M ;  M <- M + k u^T
+ *   g_e = routed_decay ? g*p : g,  b_e = dtype(b*p),  w_e = dtype(w*p)
+ * Per read event (token t, slot j, r = read_w[t,j]):
+ *   reads[t*kr + j, h*dv:(h+1)*dv] = dtype(scale * M^T dtype(q*r))
+ * Initial state: `cache` when non-NULL ([batch,J,H,S,dv], cache_dtype), else the
+ * product-key factors (row_factor/col_factor as in bdm_product_state).
+ * state_interval > 0 rounds the FP32 state to BF16 before every
+ * state_interval-th event of a sequence and rounds the initial state
+ * (gdn2_banks.py:33-36); 0 keeps FP32 throughout (prefill).
+ * store_final writes the final state into `cache` (cache must be non-NULL).
+ * Supported: bank_size in {4, 8, 16}; head_value_width a multiple of 8.
+ */
+BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
+                  const int64_t *write_idx, const void *write_w, const int64_t *read_idx, const void *read_w,
+                  const int64_t *order, const int64_t *cu_seqlens, int64_t batch, int64_t time, int64_t bank_count,
+                  int heads, int bank_size, int head_value_width, int kw, int kr, int dtype, int routed_decay,
+                  float scale, const void *row_factor, const void *col_factor, int64_t factor_cols,
+                  int factor_dtype, void *cache, int cache_dtype, int store_final, int state_interval, void *reads,
+                  void *stream);
+
+/*
+ * Read combine + output normalisation + sigmoid gate.  Replaces
+ * role_bank_dispatch.readout / scatter_bank_outputs (role_bank_dispatch.py:219-231,
+ * gdn2_banks.py:265-283) and the normalisation and gate of _project_bank_output
+ * (_parameters.py:222-232); the o_proj GEMM follows in the caller.
+ *   reads [ntok, kr, width] (dtype) summed per token in ascending bank order of
+ *   read_idx [ntok, kr]; round_each = 1 rounds to dtype after every add (GPU
+ *   reference readouts), 0 accumulates in FP32 and rounds once (CPU reference).
+ *   With read_idx == NULL, `reads` is an already combined [ntok, width] tensor.
+ *   gate [ntok, ld_gate] (dtype): output_gate pre-activation including its bias.
+ *   norm_mode 1 = LayerNorm(weight, bias, eps), 0 = RMS (weight, eps).
+ *   out [ntok, width] (dtype) = dtype(norm(raw) * dtype(sigmoid(gate))).
+ */
+BDM_API int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                          const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
+                          float eps, int norm_mode, int round_each, int dtype, void *out, void *stream);
+
+/*
+ * One decode token per batch row.  Replaces inference.step's bank kernels
+ * _decode_write, _decode_read and _decode_sum (inference.py:21-67,175-193).
+ *   controls q,k,b,g [batch, H, S], v,w [batch, V]; routes [batch, kw|kr]
+ *   state [batch, J, H, S, dv] (state_dtype) updated in place: every write
+ *   bank of a row is rewritten in state_dtype, then reads (scale * M^T dtype(q*r),
+ *   rounded to dtype) see the updated banks and are summed in ascending bank
+ *   order with a rounding after each add into raw [batch, V] (dtype).
+ */
+BDM_API int bdm_decode_step(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
+                    const int64_t *write_idx, const void *write_w, const int64_t *read_idx, const void *read_w,
+                    int64_t batch, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw, int kr,
+                    int dtype, int routed_decay, float scale, void *state, int state_dtype, void *raw, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BDM_B200_H */

@@ -1,0 +1,65 @@
+"""The C-ABI library loads without a GPU and exports every entry point of include/bdm_b200.h.
+
+Only host-side paths run here (status text, workspace sizing, argument
+validation that returns before any CUDA call); nothing launches a kernel.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+from bdm_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, 'include', 'bdm_b200.h')
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r'^BDM_API\s+[\w\s\*]*?\b(bdm_\w+)\s*\(', text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert len(names) >= 11
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_lib.SIGNATURES), 'ctypes signatures must mirror the header'
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.bdm_abi_version() == 1
+    assert lib.bdm_status_string(0) == b'ok'
+    for code in range(1, 6):
+        assert lib.bdm_status_string(code) != b'unknown status'
+
+
+def test_dispatch_workspace_sizing():
+    lib = _lib.load()
+    small = lib.bdm_dispatch_workspace_bytes(2, 64, 8, 8, 256)
+    big = lib.bdm_dispatch_workspace_bytes(16, 8192, 16, 16, 16384)
+    assert 0 < small < big
+    assert lib.bdm_dispatch_workspace_bytes(0, 64, 8, 8, 256) == -1
+
+
+@pytest.mark.parametrize('call', [
+    lambda lib: lib.bdm_route(None, -1, 32, 16, 16, 8, 1, None, None, None),
+    lambda lib: lib.bdm_route(None, 4, 8, 16, 16, 8, 1, None, None, None),        # ld < j1 + j2
+    lambda lib: lib.bdm_dispatch(None, None, 2, 4, 8, 8, 256, None, None, None, None, None, None, 0, None),
+    lambda lib: lib.bdm_combine_norm_gate(None, None, 4, 8, 0, None, 0, None, None, 1e-5, 1, 0, 1, None, None),
+])
+def test_invalid_arguments_are_rejected_on_the_host(call):
+    assert call(_lib.load()) == _lib.BDM_ERR_INVALID
+
+
+def test_unsupported_geometry_is_reported():
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(16)
+    rc = lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 32, 64, 8, 8, 1, 1, 0.25, None, None, 0, 0, None, 0, 0,
+                           0, dummy, None)
+    assert rc == _lib.BDM_ERR_UNSUPPORTED  # bank_size 32 is not implemented
+    with pytest.raises(NotImplementedError):
+        _lib.check(rc, 'bdm_bank_scan')

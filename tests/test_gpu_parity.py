@@ -1,0 +1,332 @@
+"""CUDA path vs the CPU oracle (and the reference's golden vectors), through the C ABI.
+
+Bit-exact: routing indices, dispatch order / cu_seqlens / inverse / tokens.
+Floating point, max-relative error max|a-b| / max|b|:
+  FP32 runs            1e-4   ("within 1e-4 against an FP32 run")
+  BF16 runs            2e-2   (north star: "2e-2 max-relative error in BF16")
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, near_square_factors, ops, state_interval
+
+pytestmark = pytest.mark.gpu
+
+DEV = 'cuda'
+FP32_TOL, BF16_TOL = 1e-4, 2e-2
+
+
+def npf(t):
+    return t.detach().float().cpu().numpy()
+
+
+def max_rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def _logits(gen, ntok, width, dtype, ties=False):
+    if ties:
+        return torch.randint(-3, 4, (ntok, width), generator=gen).to(dtype)
+    return torch.randn(ntok, width, generator=gen).to(dtype)
+
+
+# ------------------------------------------------------------------ router
+@pytest.mark.parametrize('bank_count,selected', [(256, 8), (2048, 8), (16384, 16), (64, 4), (512, 8)])
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize('ties', [False, True])
+def test_router_bit_exact(bank_count, selected, dtype, ties):
+    gen = torch.Generator().manual_seed(bank_count + selected + int(ties))
+    j1, j2 = near_square_factors(bank_count)
+    z = _logits(gen, 3000, j1 + j2, dtype, ties)
+    w, i = ops.route(z.to(DEV), bank_count=bank_count, selected_banks=selected)
+    ow, oi = oracle.oracle_route(npf(z), bank_count=bank_count, selected_banks=selected,
+                                 bf16=dtype == torch.bfloat16)
+    np.testing.assert_array_equal(i.cpu().numpy(), oi)
+    if dtype == torch.bfloat16:
+        # the softmax sum order differs (warp tree vs sequential): at most one BF16 ulp
+        assert np.abs(npf(w) - ow).max() <= 2 ** -8
+    else:
+        np.testing.assert_allclose(npf(w), ow, rtol=2e-6, atol=1e-7)
+
+
+def test_router_strided_logits_and_golden(golden_dir):
+    data = torch.load(os.path.join(golden_dir, 'router.pt'), weights_only=False)
+    for case in data['cases']:
+        if case['kind'] != 'random' or case['logits'].dtype != torch.float32:
+            continue
+        z = case['logits'][0]
+        wide = torch.zeros(z.shape[0], z.shape[1] + 40, dtype=z.dtype)
+        wide[:, 24:24 + z.shape[1]] = z
+        w, i = ops.route(wide.to(DEV)[:, 24:24 + z.shape[1]], bank_count=case['bank_count'],
+                         selected_banks=case['selected'])
+        ref_i = case['indices'][0]
+        agree = (i.cpu() == ref_i).all(-1).float().mean().item()
+        assert agree > 0.99, agree  # FP32 ties are vanishingly rare
+        ow, oi = oracle.oracle_route(npf(z), bank_count=case['bank_count'], selected_banks=case['selected'],
+                                     bf16=False)
+        np.testing.assert_array_equal(i.cpu().numpy(), oi)
+
+
+# ----------------------------------------------------------------- dispatch
+def _random_routes(gen, batch, time, bank_count, selected):
+    j1, j2 = near_square_factors(bank_count)
+    wl = torch.randn(batch * time, j1 + j2, generator=gen)
+    rl = torch.randn(batch * time, j1 + j2, generator=gen)
+    ww, wi = oracle.oracle_route(wl.numpy(), bank_count=bank_count, selected_banks=selected, bf16=False)
+    rw, ri = oracle.oracle_route(rl.numpy(), bank_count=bank_count, selected_banks=selected, bf16=False)
+    shape = (batch, time, -1)
+    return (torch.from_numpy(ww).reshape(shape), torch.from_numpy(wi).reshape(shape),
+            torch.from_numpy(rw).reshape(shape), torch.from_numpy(ri).reshape(shape))
+
+
+@pytest.mark.parametrize('batch,time,bank_count,selected', [
+    (8, 4096, 256, 8),       # c2 geometry: one 11-bit pass
+    (16, 512, 16384, 16),    # c4 bank table: two passes
+    (2, 512, 256, 8),        # c1
+    (64, 16, 131072, 2),     # 23-bit sequence ids: three passes
+    (3, 5, 16, 2),           # ragged tiny
+])
+def test_dispatch_bit_exact(batch, time, bank_count, selected):
+    gen = torch.Generator().manual_seed(batch * 7 + time)
+    ww, wi, rw, ri = _random_routes(gen, batch, time, bank_count, selected)
+    out = ops.dispatch(wi.to(DEV), ri.to(DEV), bank_count, want_inverse=True, want_tokens=True)
+    ref = oracle.oracle_dispatch(wi.numpy(), ri.numpy(), bank_count)
+    for key in ('order', 'cu_seqlens', 'inverse', 'tokens'):
+        np.testing.assert_array_equal(out[key].cpu().numpy(), ref[key], err_msg=key)
+
+
+def test_dispatch_edge_cases_and_golden(golden_dir):
+    # every event in one bank: a single maximal sequence per batch row
+    wi = torch.zeros(2, 300, 3, dtype=torch.long)
+    ri = torch.zeros(2, 300, 3, dtype=torch.long)
+    out = ops.dispatch(wi.to(DEV), ri.to(DEV), 64, want_inverse=True, want_tokens=True)
+    ref = oracle.oracle_dispatch(wi.numpy(), ri.numpy(), 64)
+    for key in ('order', 'cu_seqlens', 'inverse', 'tokens'):
+        np.testing.assert_array_equal(out[key].cpu().numpy(), ref[key], err_msg=key)
+    # out-of-range banks are counted, never written out of bounds
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    bad = torch.tensor([[[0, 70]]], dtype=torch.long)
+    out = ops.dispatch(bad.to(DEV), torch.tensor([[[1, -3]]]).to(DEV), 64, error_word=err)
+    torch.cuda.synchronize()
+    assert err.item() == 2
+    assert sorted(out['order'].cpu().tolist()) == [0, 1, 2, 3]
+    for case in torch.load(os.path.join(golden_dir, 'dispatch.pt'), weights_only=False)['cases']:
+        out = ops.dispatch(case['wi'].to(DEV), case['ri'].to(DEV), case['bank_count'], want_tokens=True)
+        np.testing.assert_array_equal(out['order'].cpu().numpy(), case['order'].numpy())
+        np.testing.assert_array_equal(out['cu_seqlens'].cpu().numpy(), case['cu_seqlens'].numpy())
+        np.testing.assert_array_equal(out['tokens'].cpu().numpy(), case['tokens'].numpy())
+
+
+# -------------------------------------------------------------- recurrence
+def _controls(gen, nt, heads, s, dv, dtype):
+    q = torch.nn.functional.normalize(torch.randn(nt, heads, s, generator=gen), dim=-1).to(dtype)
+    k = torch.nn.functional.normalize(torch.randn(nt, heads, s, generator=gen), dim=-1).to(dtype)
+    v = torch.randn(nt, heads * dv, generator=gen).to(dtype)
+    g = -torch.rand(nt, heads, s, generator=gen) * 0.3
+    b = torch.rand(nt, heads, s, generator=gen).to(dtype)
+    w = torch.rand(nt, heads * dv, generator=gen).to(dtype)
+    return q.reshape(nt, -1), k.reshape(nt, -1), v, g.reshape(nt, -1), b.reshape(nt, -1), w
+
+
+def _run_scan(batch, time, bank_count, selected, heads, s, dv, dtype, *, interval, routed, cache_dtype=None,
+              seed=0):
+    gen = torch.Generator().manual_seed(seed)
+    nt = batch * time
+    ctl = _controls(gen, nt, heads, s, dv, dtype)
+    ww, wi, rw, ri = _random_routes(gen, batch, time, bank_count, selected)
+    ww, rw = ww.to(dtype), rw.to(dtype)
+    rows, cols = near_square_factors(bank_count * heads * s)
+    u = (0.05 * torch.randn(rows, dv, generator=gen)).to(dtype)
+    z = (0.05 * torch.randn(cols, dv, generator=gen)).to(dtype)
+    meta = ops.dispatch(wi.to(DEV), ri.to(DEV), bank_count)
+    args = [t.to(DEV) for t in ctl] + [wi.to(DEV), ww.to(DEV), ri.to(DEV), rw.to(DEV), meta['order'],
+                                       meta['cu_seqlens']]
+    init = npf(u)[:, None, :] + npf(z)[None, :, :]
+    init = (oracle.bf16_round(init) if dtype == torch.bfloat16 else init).reshape(bank_count, heads, s, dv)
+    kw = dict(batch=batch, time=time, bank_count=bank_count, heads=heads, bank_size=s, head_value_width=dv,
+              routed_decay=routed, scale=s ** -0.5)
+    if cache_dtype is None:
+        reads = ops.bank_scan(*args, **kw, row_factor=u.to(DEV), col_factor=z.to(DEV), state_interval=interval)
+        final = None
+        init_b = init[None]
+    else:
+        cache = torch.from_numpy(np.broadcast_to(init, (batch,) + init.shape).copy()).to(cache_dtype).to(DEV)
+        init_b = npf(cache)
+        reads = ops.bank_scan(*args, **kw, cache=cache, store_final=True, state_interval=interval)
+        final = cache
+    q, k, v, g, b, w = (npf(t) for t in ctl)
+    sh = lambda x, last: x.reshape(batch, time, heads, last)
+    oreads, ofinal = oracle.oracle_recurrence(sh(q, s), sh(k, s), sh(v, dv), sh(g, s), sh(b, s), sh(w, dv),
+                                              wi.numpy(), npf(ww), ri.numpy(), npf(rw), init_b,
+                                              bank_count=bank_count, bf16=dtype == torch.bfloat16,
+                                              routed_decay=routed, interval=interval, scale=s ** -0.5)
+    return npf(reads).reshape(oreads.shape), oreads, (npf(final) if final is not None else None), ofinal
+
+
+@pytest.mark.parametrize('s,dv,heads', [(8, 128, 1), (8, 64, 2), (4, 128, 1), (16, 128, 2), (8, 128, 3)])
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_bank_scan_forward(s, dv, heads, dtype):
+    interval = state_interval(s) if dtype == torch.bfloat16 else 0
+    ours, ref, _, _ = _run_scan(2, 200, 64, 4, heads, s, dv, dtype, interval=interval, routed=True, seed=s + dv)
+    tol = BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
+    assert max_rel(ours, ref) <= tol, max_rel(ours, ref)
+
+
+@pytest.mark.parametrize('cache_dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_bank_scan_prefill_final_state(cache_dtype, dtype):
+    ours, ref, final, ofinal = _run_scan(3, 150, 256, 8, 1, 8, 128, dtype, interval=0, routed=True,
+                                         cache_dtype=cache_dtype, seed=7)
+    tol = BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
+    assert max_rel(ours, ref) <= tol
+    ofinal_c = oracle.bf16_round(ofinal) if cache_dtype == torch.bfloat16 else ofinal
+    assert max_rel(final.reshape(ofinal_c.shape), ofinal_c) <= (tol if cache_dtype == torch.float32 else BF16_TOL)
+
+
+def test_bank_scan_plain_decay_and_fp32_against_golden(golden_dir):
+    # routed_decay=False path
+    ours, ref, _, _ = _run_scan(2, 100, 64, 4, 1, 8, 128, torch.float32, interval=0, routed=False, seed=3)
+    assert max_rel(ours, ref) <= FP32_TOL
+    # the reference's own serial equation oracle (FP32)
+    case = torch.load(os.path.join(golden_dir, 'recurrence.pt'), weights_only=False)['cases'][0]
+    batch, time, J, s, dv = case['batch'], case['time'], case['bank_count'], case['bank_size'], case['dv']
+    nt = batch * time
+    meta = ops.dispatch(case['wi'].to(DEV), case['ri'].to(DEV), J)
+    ctl = [case[n].reshape(nt, -1).float().to(DEV) for n in 'qkvgbw']
+    cache = case['init'].float().unsqueeze(0).expand(batch, -1, -1, -1).contiguous().to(DEV)
+    reads = ops.bank_scan(*ctl, case['wi'].to(DEV), case['ww'].float().to(DEV), case['ri'].to(DEV),
+                          case['rw'].float().to(DEV), meta['order'], meta['cu_seqlens'], batch=batch, time=time,
+                          bank_count=J, heads=1, bank_size=s, head_value_width=dv, routed_decay=True,
+                          scale=s ** -0.5, cache=cache, store_final=True)
+    out = reads.reshape(batch, time, -1, dv).sum(2)  # FP32: summation order is within tolerance
+    assert max_rel(npf(out), npf(case['serial_out'])) <= FP32_TOL
+    assert max_rel(npf(cache), npf(case['serial_state'])) <= FP32_TOL
+
+
+def test_bank_scan_c2_full_size_bf16():
+    """BASELINE c2 geometry (8 x 4096 tokens, H=8, S=8, dv=128, J=256, B=8) against the oracle."""
+    ours, ref, _, _ = _run_scan(8, 4096, 256, 8, 8, 8, 128, torch.bfloat16, interval=16, routed=True, seed=11)
+    assert max_rel(ours, ref) <= BF16_TOL, max_rel(ours, ref)
+    assert np.mean(ours == ref) > 0.5
+
+
+# ------------------------------------------------------------------ layer
+LAYER_GOLDEN = [('h1_fp32', 2e-2), ('h1_fp32_state32', FP32_TOL), ('h2_fp32_state32', FP32_TOL),
+                ('c1_t64', 2e-2)]
+
+
+def _module_from_golden(data):
+    cfg = BSDMConfig(**data['config'])
+    m = BlockSparseDeltaMemory(cfg, seed=data['seed'])
+    if data['dtype'] == 'torch.bfloat16':
+        m = m.to(torch.bfloat16)
+    m.load_state_dict(data['state_dict'])
+    return m.to(DEV)
+
+
+@pytest.mark.parametrize('name,tol', LAYER_GOLDEN)
+def test_layer_forward_matches_reference_golden(golden_dir, name, tol):
+    data = torch.load(os.path.join(golden_dir, f'layer_{name}.pt'), weights_only=False)
+    m = _module_from_golden(data)
+    with torch.no_grad():
+        y = m(data['x'].to(DEV))
+    assert max_rel(npf(y), npf(data['out'])) <= tol, max_rel(npf(y), npf(data['out']))
+
+
+@pytest.mark.parametrize('name', ['h1_bf16', 'h2_bf16'])
+def test_layer_bf16_with_reference_routes(golden_dir, name):
+    """BF16 logits tie often; drive our kernels with the reference's own routes."""
+    data = torch.load(os.path.join(golden_dir, f'layer_{name}.pt'), weights_only=False)
+    m = _module_from_golden(data)
+    x = data['x'].to(DEV)
+    batch, time, _ = x.shape
+    with torch.no_grad():
+        controls, _, gate = m._controls_and_routes(x)
+        r = data['routes']
+        routes = tuple(t.to(DEV) for t in (r['ww'], r['wi'], r['rw'], r['ri']))
+        interval = state_interval(m.bank_size)
+        reads = m._bank_pass(controls, routes, batch, time, row_factor=m.initial_row_factor,
+                             col_factor=m.initial_column_factor, state_interval=interval)
+        y = m._output(x, reads, routes[3].reshape(batch * time, -1), gate, round_each=False)
+    assert max_rel(npf(y), npf(data['out'])) <= BF16_TOL, max_rel(npf(y), npf(data['out']))
+
+
+def _oracle_layer(m):
+    params = {k: npf(v) for k, v in m.state_dict().items()}
+    cfg = {k: getattr(m.config, k) for k in m.config.__dataclass_fields__}
+    return oracle.OracleLayer(cfg, params, bf16=m.q_proj.weight.dtype == torch.bfloat16)
+
+
+def _our_controls_routes(m, x):
+    batch, time, _ = x.shape
+    controls, routes, _ = m._controls_and_routes(x)
+    H, S, dv = m.num_heads, m.bank_size, m.head_value_width
+    q, k, v, g, b, w = (npf(t) for t in controls)
+    sh = lambda t, last: t.reshape(batch, time, H, last)
+    ctl = (sh(q, S), sh(k, S), sh(v, dv), sh(g, S), sh(b, S), sh(w, dv))
+    ww, wi, rw, ri = routes
+    return ctl, ((npf(ww), wi.cpu().numpy()), (npf(rw), ri.cpu().numpy()))
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize('heads', [1, 2])
+def test_prefill_and_decode_steps_match_oracle(dtype, heads):
+    cfg = BSDMConfig(dim=128, bank_count=256, bank_size=8, selected_banks=8, value_width=64 * heads,
+                     num_heads=heads)
+    torch.manual_seed(5)
+    m = BlockSparseDeltaMemory(cfg, seed=1).to(dtype).to(DEV)
+    ol = _oracle_layer(m)
+    tol = BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
+    x = torch.randn(4, 48, 128).to(dtype).to(DEV)
+    with torch.no_grad():
+        ctl, routes = _our_controls_routes(m, x)
+        # the router on our own logits equals the oracle's router on the same logits
+        proj, cols = m._project(x.reshape(-1, 128))
+        width = sum(m.factors)
+        for role in ('write', 'read'):
+            lg = npf(proj[:, cols[role]:cols[role] + width])
+            _, oi = oracle.oracle_route(lg, bank_count=256, selected_banks=8, bf16=dtype == torch.bfloat16)
+            got = routes[0][1] if role == 'write' else routes[1][1]
+            np.testing.assert_array_equal(got.reshape(oi.shape), oi)
+        y, state = m.prefill(x, state_dtype=torch.bfloat16)
+        oy, ostate = ol.prefill(npf(x), controls=ctl, routes=routes, cache_bf16=True)
+        assert max_rel(npf(y), oy) <= max(tol, 2e-3 if dtype == torch.float32 else tol)
+        assert max_rel(npf(state).reshape(ostate.shape), ostate) <= BF16_TOL
+        ostate = np.ascontiguousarray(npf(state).reshape(ostate.shape))  # continue both from the same cache
+        for i in range(4):
+            xt = torch.randn(4, 1, 128).to(dtype).to(DEV)
+            ctl, routes = _our_controls_routes(m, xt)
+            y, state = m.step(xt, state)
+            oy, ostate = ol.step(npf(xt), ostate, controls=ctl, routes=routes, cache_bf16=True)
+            assert max_rel(npf(y), oy) <= max(tol, 2e-3 if dtype == torch.float32 else tol), i
+            assert max_rel(npf(state).reshape(ostate.shape), ostate) <= BF16_TOL, i
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_layer_forward_matches_oracle_with_same_routes(dtype):
+    cfg = BSDMConfig(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=256, num_heads=2,
+                     training_state_dtype='float32' if dtype == torch.float32 else 'bfloat16')
+    torch.manual_seed(9)
+    m = BlockSparseDeltaMemory(cfg, seed=2).to(dtype).to(DEV)
+    ol = _oracle_layer(m)
+    x = torch.randn(2, 96, 256).to(dtype).to(DEV)
+    with torch.no_grad():
+        y = m(x)
+        ctl, routes = _our_controls_routes(m, x)
+    oy = ol.forward(npf(x), controls=ctl, routes=routes)
+    tol = BF16_TOL if dtype == torch.bfloat16 else 2e-3  # FP32 GEMMs differ in accumulation order
+    assert max_rel(npf(y), oy) <= tol, max_rel(npf(y), oy)
+
+
+def test_forward_is_deterministic():
+    cfg = BSDMConfig(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=256, num_heads=2)
+    m = BlockSparseDeltaMemory(cfg, seed=4).to(torch.bfloat16).to(DEV)
+    x = torch.randn(2, 300, 256).to(torch.bfloat16).to(DEV)
+    with torch.no_grad():
+        a, b = m(x), m(x)
+    assert torch.equal(a, b)
