@@ -13,6 +13,26 @@ namespace {
 constexpr int kCols = 8;  // columns per thread
 constexpr int kMaxKR = 64;
 
+// Load 8 consecutive elements (one 16-byte access for bf16 when `vec`).
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float *x, int64_t n_valid, bool vec) {
+    if constexpr (sizeof(T) == 2) {
+        if (vec && n_valid >= 8) {
+            uint4 u = *reinterpret_cast<const uint4 *>(p);
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float2 f = __bfloat1622float2(h[i]);
+                x[2 * i] = f.x;
+                x[2 * i + 1] = f.y;
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kCols; ++i) x[i] = i < n_valid ? Elem<T>::to_float(p[i]) : 0.f;
+}
+
 __device__ __forceinline__ float block_sum(float x, float *red) {
     x = warp_sum(x);
     const int warp = threadIdx.x >> 5, lane = (int)lane_id();
@@ -28,7 +48,7 @@ template <typename T>
 __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int64_t *__restrict__ ri, int64_t ntok,
                                          int kr, int64_t width, const T *__restrict__ gate, int64_t ld_gate,
                                          const T *__restrict__ nw, const T *__restrict__ nb, float eps, int norm_mode,
-                                         int round_each, T *__restrict__ out) {
+                                         int round_each, int vec, T *__restrict__ out) {
     __shared__ int64_t banks[kMaxKR];
     __shared__ int slot_at[kMaxKR];
     __shared__ float red[32];
@@ -51,27 +71,21 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
 #pragma unroll
     for (int i = 0; i < kCols; ++i) x[i] = 0.f;
     const bool act = c0 < width;
+    const int64_t nv = width - c0;
     if (act) {
         if (ri) {
+            float y[kCols];
             for (int r = 0; r < kr; ++r) {
-                const T *row = reads + (t * kr + slot_at[r]) * width + c0;
+                load8<T>(reads + (t * kr + slot_at[r]) * width + c0, y, nv, vec);
 #pragma unroll
-                for (int i = 0; i < kCols; ++i) {
-                    if (c0 + i < width) {
-                        const float y = x[i] + Elem<T>::to_float(row[i]);
-                        x[i] = round_each ? rnd<T>(y) : y;
-                    }
-                }
+                for (int i = 0; i < kCols; ++i) x[i] = round_each ? rnd<T>(x[i] + y[i]) : x[i] + y[i];
             }
             if (!round_each) {
 #pragma unroll
                 for (int i = 0; i < kCols; ++i) x[i] = rnd<T>(x[i]);
             }
         } else {
-            const T *row = reads + t * width + c0;
-#pragma unroll
-            for (int i = 0; i < kCols; ++i)
-                if (c0 + i < width) x[i] = Elem<T>::to_float(row[i]);
+            load8<T>(reads + t * width + c0, x, nv, vec);
         }
     }
     const float inv_w = 1.0f / (float)width;
@@ -109,12 +123,27 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
         }
     }
     if (act) {
-        const T *grow = gate + t * ld_gate + c0;
+        float gv[kCols];
+        load8<T>(gate + t * ld_gate + c0, gv, nv, vec);
         T *orow = out + t * width + c0;
+        if constexpr (sizeof(T) == 2) {
+            if (vec && nv >= 8) {
+                uint4 u;
+                __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float g0 = rnd<T>(1.0f / (1.0f + expf(-gv[2 * i])));
+                    const float g1 = rnd<T>(1.0f / (1.0f + expf(-gv[2 * i + 1])));
+                    h[i] = __floats2bfloat162_rn(n[2 * i] * g0, n[2 * i + 1] * g1);
+                }
+                *reinterpret_cast<uint4 *>(orow) = u;
+                return;
+            }
+        }
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
             if (c0 + i < width) {
-                const float gt = rnd<T>(1.0f / (1.0f + expf(-Elem<T>::to_float(grow[i]))));
+                const float gt = rnd<T>(1.0f / (1.0f + expf(-gv[i])));
                 orow[i] = Elem<T>::from_float(n[i] * gt);
             }
         }
@@ -137,11 +166,14 @@ extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx,
     if (threads < 64) threads = 64;
     if (threads > 1024) return BDM_ERR_UNSUPPORTED;
     if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    const uintptr_t mis =
+        (reinterpret_cast<uintptr_t>(reads) | reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(out)) & 15;
+    const int vec = !mis && width % 8 == 0 && ld_gate % 8 == 0;
     BDM_DISPATCH_DTYPE(dtype, T, {
         combine_norm_gate_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
             static_cast<const T *>(reads), read_idx, ntok, read_idx ? kr : 1, width, static_cast<const T *>(gate),
             ld_gate, static_cast<const T *>(norm_weight), static_cast<const T *>(norm_bias), eps, norm_mode,
-            round_each, static_cast<T *>(out));
+            round_each, vec, static_cast<T *>(out));
     });
     return launch_status();
 }

@@ -109,34 +109,61 @@ template <> __device__ __forceinline__ void store_pair<bf16>(bf16 *x, float2 v) 
 
 __device__ __forceinline__ float2 bf16_round_pair(float2 x) { return round_pair<bf16>(x); }
 
-// Events staged per batch and value-row mini-batch size (prefetch depth).
+// Events staged per batch; value-row prefetch distance (events).
 template <int S> struct EvBatch { static constexpr int value = S >= 16 ? 16 : 32; };
-template <typename T, int NC> struct MiniBatch {
-    static constexpr int raw = 64 / (NC * (int)sizeof(T));
-    static constexpr int value = raw > 8 ? 8 : (raw < 2 ? 2 : raw);
+constexpr int kPrefetch = 4;
+
+// Asynchronous global -> shared copy of BYTES (a multiple of 4; 16-byte chunks when possible).
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void *smem, const void *gmem) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    const char *g = static_cast<const char *>(gmem);
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+        for (int i = 0; i < BYTES / 16; ++i)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s + 16 * i), "l"(g + 16 * i));
+    } else if constexpr (BYTES == 8) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(g));
+    } else {
+        static_assert(BYTES == 4, "unsupported copy size");
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(g));
+    }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Raw per-event control rows copied from token storage: k | b (dtype) and g (float) for a
+// write, q (dtype) in the k slot for a read.
+template <typename T, int S> struct RawLayout {
+    static constexpr int kBytes = S * (int)sizeof(T);
+    static constexpr int gBytes = S * 4;
+    static constexpr int kOff = 0, bOff = kBytes, gOff = 2 * kBytes;
+    static constexpr int size = 2 * kBytes + gBytes;  // multiple of 16 for S >= 4
 };
 
 template <typename T, int S, int NC>
-__global__ void __launch_bounds__(kScanWarps * 32)
+__global__ void __launch_bounds__(kScanWarps * 32, 5)
 bank_scan_kernel(const ScanParams p) {
     constexpr int NP = NC / 2;
     constexpr int EB = EvBatch<S>::value;
-    constexpr int MB = MiniBatch<T, NC>::value;
-    static_assert(EB % MB == 0, "mini-batches tile the event batch");
-    // Per warp: controls [EB][3][S] duplicated pairs, token ids and weights.
-    __shared__ float2 ctl_all[kScanWarps][EB][3 * S];
-    __shared__ int64_t tok_all[kScanWarps][EB];
-    __shared__ int64_t rid_all[kScanWarps][EB];
-    __shared__ float wgt_all[kScanWarps][EB];
+    constexpr int PD = kPrefetch;
+    using Raw = RawLayout<T, S>;
+    static_assert(EB % PD == 0 && 32 % EB == 0, "batch layout");
+    // Per warp: controls of the current batch as duplicated pairs ([e | a | k | p] for a
+    // write, [q] for a read), raw rows of the next batch, token / read-slot ids.
+    __shared__ float2 ctl_all[kScanWarps][EB][3 * S + 1];
+    __shared__ __align__(16) unsigned char raw_all[kScanWarps][EB][Raw::size];
+    __shared__ int tok_all[kScanWarps][EB];
+    __shared__ int rid_all[kScanWarps][EB];
 
     const int warp = threadIdx.x >> 5;
     const int lane = (int)lane_id();
     const int64_t unit = (int64_t)blockIdx.x * kScanWarps + warp;
     if (unit >= p.units) return;  // warp-uniform
-    float2(*ctl)[3 * S] = ctl_all[warp];
-    int64_t *tok_s = tok_all[warp];
-    int64_t *rid_s = rid_all[warp];
-    float *wgt_s = wgt_all[warp];
+    float2(*ctl)[3 * S + 1] = ctl_all[warp];
+    unsigned char(*raw)[Raw::size] = raw_all[warp];
+    int *tok_s = tok_all[warp];
+    int *rid_s = rid_all[warp];
 
     const int64_t per_seq = (int64_t)p.H * p.ctiles;
     const int64_t seq = unit / per_seq;
@@ -147,15 +174,16 @@ bank_scan_kernel(const ScanParams p) {
     const bool active = col0 < p.dv;
     const int HS = p.H * S;
     const int64_t V = (int64_t)p.H * p.dv;
+    const int nw = (int)p.nw, kw = p.kw, kr = p.kr, nt = (int)p.nt, E = (int)p.E;
 
     const T *qp = static_cast<const T *>(p.q);
     const T *kp = static_cast<const T *>(p.k);
-    const T *vp = static_cast<const T *>(p.v);
+    const T *vp = static_cast<const T *>(p.v) + (int64_t)hh * p.dv + col0;
     const T *bp = static_cast<const T *>(p.b);
-    const T *wp = static_cast<const T *>(p.w);
+    const T *wp = static_cast<const T *>(p.w) + (int64_t)hh * p.dv + col0;
     const T *wwp = static_cast<const T *>(p.ww);
     const T *rwp = static_cast<const T *>(p.rw);
-    T *outp = static_cast<T *>(p.reads);
+    T *outp = static_cast<T *>(p.reads) + (int64_t)hh * p.dv + col0;
 
     // ---------------------------------------------------------- initial state
     float2 M[S][NP];
@@ -181,14 +209,13 @@ bank_scan_kernel(const ScanParams p) {
                 const int64_t ou = (r / p.factor_cols) * p.dv + col0, oz = (r % p.factor_cols) * p.dv + col0;
 #pragma unroll
                 for (int j = 0; j < NP; ++j) {
-                    float2 u, z;
                     if (p.factor_dtype == BDM_BF16) {
-                        u = load_pair<bf16>(static_cast<const bf16 *>(p.row_factor) + ou + 2 * j);
-                        z = load_pair<bf16>(static_cast<const bf16 *>(p.col_factor) + oz + 2 * j);
+                        const float2 u = load_pair<bf16>(static_cast<const bf16 *>(p.row_factor) + ou + 2 * j);
+                        const float2 z = load_pair<bf16>(static_cast<const bf16 *>(p.col_factor) + oz + 2 * j);
                         M[s][j] = bf16_round_pair(make_float2(u.x + z.x, u.y + z.y));
                     } else {
-                        u = load_pair<float>(static_cast<const float *>(p.row_factor) + ou + 2 * j);
-                        z = load_pair<float>(static_cast<const float *>(p.col_factor) + oz + 2 * j);
+                        const float2 u = load_pair<float>(static_cast<const float *>(p.row_factor) + ou + 2 * j);
+                        const float2 z = load_pair<float>(static_cast<const float *>(p.col_factor) + oz + 2 * j);
                         M[s][j] = make_float2(u.x + z.x, u.y + z.y);
                     }
                 }
@@ -205,71 +232,103 @@ bank_scan_kernel(const ScanParams p) {
     // Clamp caller-provided bounds so a malformed cu_seqlens cannot index past `order`.
     const int64_t start = min(max(p.cu[seq], (int64_t)0), p.E);
     const int64_t end = min(max(p.cu[seq + 1], start), p.E);
-    int since_round = 0;  // events since the last stored-state rounding
 
-    for (int64_t base = start; base < end; base += EB) {
-        const int n = (int)((end - base) < EB ? (end - base) : EB);
-        // ------------------------------------------------ decode event ids
-        bool is_write = false;
-        if (lane < n) {
-            int64_t id = p.order[base + lane];
-            int64_t tok = -1, rid = -1;
-            float wt = 0.f;
-            if (id >= 0 && id < p.nw) {
-                tok = id / p.kw;
-                wt = Elem<T>::to_float(wwp[id]);
-                is_write = true;
-            } else if (id >= p.nw && id < p.E) {
-                rid = id - p.nw;
-                tok = rid / p.kr;
-                wt = Elem<T>::to_float(rwp[rid]);
+    // ------------------------------------------------------ batch staging
+    // Lane i owns event i of a batch: decode its id, start the async copy of its
+    // control rows, and later turn them into the duplicated-pair controls.
+    int my_tok = -1, my_rid = -1;
+    bool my_write = false;
+    float my_wt = 0.f;
+    auto stage_issue = [&](int64_t bbase, int bn) {
+        my_tok = -1;
+        my_rid = -1;
+        my_write = false;
+        if (lane < bn) {
+            const int64_t id = p.order[bbase + lane];
+            if (id >= 0 && id < nw) {
+                my_tok = (int)id / kw;
+                my_write = true;
+                my_wt = Elem<T>::to_float(wwp[id]);
+            } else if (id >= nw && id < E) {
+                my_rid = (int)id - nw;
+                my_tok = my_rid / kr;
+                my_wt = Elem<T>::to_float(rwp[my_rid]);
             }
-            if (tok < 0 || tok >= p.nt) {  // corrupt id: make the event a no-op
-                tok = -1;
-                is_write = false;
-                rid = -1;
+            if (my_tok >= nt) {
+                my_tok = -1;
+                my_write = false;
+                my_rid = -1;
             }
-            tok_s[lane] = tok;
-            rid_s[lane] = rid;
-            wgt_s[lane] = wt;
         }
-        const unsigned wmask = __ballot_sync(0xffffffffu, is_write);
-        __syncwarp();
-        // ------------------------------------- per-event row controls (lanes)
-        for (int task = lane; task < n * S; task += 32) {
-            const int ev = task / S, s = task % S;
-            const int64_t tok = tok_s[ev];
-            if (tok < 0) continue;
-            const int64_t o = tok * HS + (int64_t)hh * S + s;
-            const float wt = wgt_s[ev];
-            if ((wmask >> ev) & 1u) {
-                const float kk = Elem<T>::to_float(kp[o]);
-                const float gg = p.g[o];
-                const float ge = p.routed_decay ? gg * wt : gg;
-                const float a = rnd<T>(Elem<T>::to_float(bp[o]) * wt) * kk;
-                ctl[ev][s] = dup(expf(ge));
-                ctl[ev][S + s] = dup(a);
-                ctl[ev][2 * S + s] = dup(kk);
+        if (my_tok >= 0) {
+            const int64_t o = (int64_t)my_tok * HS + (int64_t)hh * S;
+            if (my_write) {
+                cp_async<Raw::kBytes>(raw[lane] + Raw::kOff, kp + o);
+                cp_async<Raw::kBytes>(raw[lane] + Raw::bOff, bp + o);
+                cp_async<Raw::gBytes>(raw[lane] + Raw::gOff, p.g + o);
             } else {
-                ctl[ev][s] = dup(rnd<T>(Elem<T>::to_float(qp[o]) * wt));
+                cp_async<Raw::kBytes>(raw[lane] + Raw::kOff, qp + o);
             }
         }
-        __syncwarp();
-        // --------------------------------------------------- event stream
-        for (int mb = 0; mb < n; mb += MB) {
-            Row<T, NC> vr[MB], wr[MB];
+        cp_async_commit();
+    };
+    auto stage_finish = [&]() -> unsigned {
+        cp_async_wait_all();
+        if (my_tok >= 0) {
+            const T *rk = reinterpret_cast<const T *>(raw[lane] + Raw::kOff);
+            if (my_write) {
+                const T *rb = reinterpret_cast<const T *>(raw[lane] + Raw::bOff);
+                const float *rg = reinterpret_cast<const float *>(raw[lane] + Raw::gOff);
 #pragma unroll
-            for (int j = 0; j < MB; ++j) {
-                const int ev = mb + j;
-                if (ev < n && ((wmask >> ev) & 1u) && active) {
-                    const int64_t o = tok_s[ev] * V + (int64_t)hh * p.dv + col0;
-                    load_row<T, NC>(vr[j], vp + o);
-                    load_row<T, NC>(wr[j], wp + o);
+                for (int s = 0; s < S; ++s) {
+                    const float kk = Elem<T>::to_float(rk[s]);
+                    const float ge = p.routed_decay ? rg[s] * my_wt : rg[s];
+                    ctl[lane][s] = dup(expf(ge));
+                    ctl[lane][S + s] = dup(rnd<T>(Elem<T>::to_float(rb[s]) * my_wt) * kk);
+                    ctl[lane][2 * S + s] = dup(kk);
                 }
-            }
+                ctl[lane][3 * S] = dup(my_wt);
+            } else {
 #pragma unroll
-            for (int j = 0; j < MB; ++j) {
-                const int ev = mb + j;
+                for (int s = 0; s < S; ++s) ctl[lane][s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * my_wt));
+            }
+        }
+        if (lane < EB) {
+            tok_s[lane] = my_tok;
+            rid_s[lane] = my_rid;
+        }
+        const unsigned wm = __ballot_sync(0xffffffffu, my_write);
+        __syncwarp();
+        return wm;
+    };
+
+    int bn = (int)min((int64_t)EB, end - start);
+    unsigned wmask = 0;
+    if (bn > 0) {
+        stage_issue(start, bn);
+        wmask = stage_finish();
+    }
+    int since_round = 0;  // events since the last stored-state rounding
+    Row<T, NC> vr[PD], wr[PD];
+
+    for (int64_t base = start; base < end;) {
+        const int n = bn;
+        const int64_t nbase = base + n;
+        const int nn = (int)min((int64_t)EB, end - nbase);
+        auto prefetch = [&](int ev, int slot) {
+            if (ev < n && ((wmask >> ev) & 1u) && active) {
+                const int64_t o = (int64_t)tok_s[ev] * V;
+                load_row<T, NC>(vr[slot], vp + o);
+                load_row<T, NC>(wr[slot], wp + o);
+            }
+        };
+#pragma unroll
+        for (int j = 0; j < PD; ++j) prefetch(j, j);
+        for (int e0 = 0; e0 < n; e0 += PD) {
+            if (e0 == (EB / 2) && nn > 0) stage_issue(nbase, nn);  // next batch, overlapped with the second half
+#pragma unroll
+            for (int j = 0; j < PD; ++j) {
+                const int ev = e0 + j;
                 if (ev >= n) break;
                 if (p.interval > 0 && since_round == p.interval) {
 #pragma unroll
@@ -279,60 +338,70 @@ bank_scan_kernel(const ScanParams p) {
                     since_round = 0;
                 }
                 ++since_round;
-                if (tok_s[ev] < 0) continue;
-                if ((wmask >> ev) & 1u) {
-                    const float wt = wgt_s[ev];
-                    float2 er[NP];
+                const int tk = tok_s[ev];
+                if (tk >= 0) {
+                    if ((wmask >> ev) & 1u) {
+                        float2 er[NP];
 #pragma unroll
-                    for (int s = 0; s < S; ++s) {
-                        const float2 e2 = ctl[ev][s];
+                        for (int s = 0; s < S; ++s) {
+                            const float2 e2 = ctl[ev][s];
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) M[s][c] = __fmul2_rn(M[s][c], e2);
-                    }
-#pragma unroll
-                    for (int c = 0; c < NP; ++c) {
-                        float2 lo = __fmul2_rn(ctl[ev][S + 0], M[0][c]);
-                        float2 hi = __fmul2_rn(ctl[ev][S + 1], M[1][c]);
-#pragma unroll
-                        for (int s = 2; s < S; s += 2) {
-                            lo = __ffma2_rn(ctl[ev][S + s], M[s][c], lo);
-                            hi = __ffma2_rn(ctl[ev][S + s + 1], M[s + 1][c], hi);
+                            for (int c = 0; c < NP; ++c) M[s][c] = __fmul2_rn(M[s][c], e2);
                         }
-                        er[c] = make_float2(lo.x + hi.x, lo.y + hi.y);
-                    }
-                    float2 u[NP];
 #pragma unroll
-                    for (int c = 0; c < NP; ++c) {
-                        const float2 vv = load_pair<T>(vr[j].x + 2 * c);
-                        const float2 wv = load_pair<T>(wr[j].x + 2 * c);
-                        const float2 we = round_pair<T>(__fmul2_rn(wv, dup(wt)));
-                        const float2 x = __fmul2_rn(we, vv);
-                        u[c] = make_float2(x.x - er[c].x, x.y - er[c].y);
-                    }
+                        for (int c = 0; c < NP; ++c) {
+                            float2 lo = __fmul2_rn(ctl[ev][S + 0], M[0][c]);
+                            float2 hi = __fmul2_rn(ctl[ev][S + 1], M[1][c]);
 #pragma unroll
-                    for (int s = 0; s < S; ++s) {
-                        const float2 k2 = ctl[ev][2 * S + s];
+                            for (int s = 2; s < S; s += 2) {
+                                lo = __ffma2_rn(ctl[ev][S + s], M[s][c], lo);
+                                hi = __ffma2_rn(ctl[ev][S + s + 1], M[s + 1][c], hi);
+                            }
+                            er[c] = make_float2(lo.x + hi.x, lo.y + hi.y);
+                        }
+                        const float2 pw = ctl[ev][3 * S];
+                        float2 u[NP];
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) M[s][c] = __ffma2_rn(k2, u[c], M[s][c]);
-                    }
-                } else {
-                    float2 acc[NP];
+                        for (int c = 0; c < NP; ++c) {
+                            const float2 vv = load_pair<T>(vr[j].x + 2 * c);
+                            const float2 wv = load_pair<T>(wr[j].x + 2 * c);
+                            const float2 we = round_pair<T>(__fmul2_rn(wv, pw));
+                            const float2 x = __fmul2_rn(we, vv);
+                            u[c] = make_float2(x.x - er[c].x, x.y - er[c].y);
+                        }
 #pragma unroll
-                    for (int c = 0; c < NP; ++c) acc[c] = __fmul2_rn(ctl[ev][0], M[0][c]);
+                        for (int s = 0; s < S; ++s) {
+                            const float2 k2 = ctl[ev][2 * S + s];
 #pragma unroll
-                    for (int s = 1; s < S; ++s)
+                            for (int c = 0; c < NP; ++c) M[s][c] = __ffma2_rn(k2, u[c], M[s][c]);
+                        }
+                    } else {
+                        float2 acc[NP];
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) acc[c] = __ffma2_rn(ctl[ev][s], M[s][c], acc[c]);
-                    if (active) {
-                        Row<T, NC> out;
+                        for (int c = 0; c < NP; ++c) acc[c] = __fmul2_rn(ctl[ev][0], M[0][c]);
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) store_pair<T>(out.x + 2 * c, __fmul2_rn(acc[c], dup(p.scale)));
-                        store_row<T, NC>(outp + rid_s[ev] * V + (int64_t)hh * p.dv + col0, out);
+                        for (int s = 1; s < S; ++s)
+#pragma unroll
+                            for (int c = 0; c < NP; ++c) acc[c] = __ffma2_rn(ctl[ev][s], M[s][c], acc[c]);
+                        if (active) {
+                            Row<T, NC> out;
+#pragma unroll
+                            for (int c = 0; c < NP; ++c)
+                                store_pair<T>(out.x + 2 * c, __fmul2_rn(acc[c], dup(p.scale)));
+                            store_row<T, NC>(outp + (int64_t)rid_s[ev] * V, out);
+                        }
                     }
                 }
+                prefetch(ev + PD, j);
             }
         }
-        __syncwarp();
+        if (nn > 0) {
+            if (n <= EB / 2) stage_issue(nbase, nn);  // short batch: the midpoint was never reached
+            __syncwarp();
+            wmask = stage_finish();
+        }
+        base = nbase;
+        bn = nn;
     }
 
     if (p.store_final && p.cache && active) {
@@ -390,6 +459,7 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     if (head_value_width % 8) return BDM_ERR_UNSUPPORTED;
     if (state_interval < 0 || (store_final && !cache)) return BDM_ERR_INVALID;
     if (!valid_dtype(dtype) || (cache && !valid_dtype(cache_dtype))) return BDM_ERR_DTYPE;
+    if (batch * time * (int64_t)(kw + kr) >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
     if (!cache && row_factor) {
         if (!col_factor || factor_cols <= 0 || !valid_dtype(factor_dtype)) return BDM_ERR_INVALID;
         if ((bank_count * heads * bank_size) % factor_cols) return BDM_ERR_INVALID;

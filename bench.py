@@ -87,34 +87,52 @@ def load_traffic():
 
 # -------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks / throttle reasons while the GPU is under load.
+
+    Sampling starts before the warm-up steps (nvidia-smi needs a few hundred ms
+    to produce its first line) and stops after the timed steps; every sample
+    taken in between is under load.
+    """
 
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
 
-    def __init__(self, device_index):
+    def __init__(self, device_index, interval_ms=50):
         self.index = device_index
+        self.interval_ms = interval_ms
         self.proc = None
+        self.out = ''
 
-    def __enter__(self):
+    def start(self):
+        import tempfile
+        self.file = tempfile.TemporaryFile(mode='w+')
         try:
-            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.index}', f'--query-gpu={self.FIELDS}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.index), f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', str(self.interval_ms)],
+                                         stdout=self.file, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
+            return self
+        deadline = time.time() + 5.0
+        while time.time() < deadline:  # wait for the first sample
+            self.file.flush()
+            if os.fstat(self.file.fileno()).st_size > 0:
+                break
+            time.sleep(0.05)
         return self
 
-    def __exit__(self, *exc):
-        self.out = ''
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                self.proc.wait()
+            self.file.seek(0)
+            self.out = self.file.read()
+            self.file.close()
 
     def summary(self):
         if self.proc is None or not self.out:
@@ -227,12 +245,13 @@ def run_ours(args, world, rank, local):
         layer.initial_row_factor.zero_()
         layer.initial_column_factor.zero_()
     gen = torch.Generator().manual_seed(1 + rank)
-    x_host = torch.randn(C2_BATCH, C2_TIME, cfg.dim, generator=gen).to(torch.bfloat16).pin_memory()
+    x_host = torch.randn(args.batch, C2_TIME, cfg.dim, generator=gen).to(torch.bfloat16).pin_memory()
     x = x_host.to(dev)
     y_host = torch.empty_like(x_host).pin_memory()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    tokens = C2_BATCH * C2_TIME
+    tokens = args.batch * C2_TIME
 
+    clocks = ClockSampler(dev.index).start()
     with torch.inference_mode():
         for _ in range(args.warmup):
             layer(x)
@@ -244,13 +263,13 @@ def run_ours(args, world, rank, local):
         barrier(world)
         torch.cuda.synchronize()
         launches0 = lib.bdm_kernel_launches()
-        with ClockSampler(dev.index) as clocks:
-            for i in range(args.steps):
-                flush.zero_()
-                starts[i].record()
-                layer(x)
-                ends[i].record()
-            torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            layer(x)
+            ends[i].record()
+        torch.cuda.synchronize()
+        clocks.stop()
         barrier(world)
         launches = lib.bdm_kernel_launches() - launches0
         step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -275,7 +294,7 @@ def run_ours(args, world, rank, local):
         e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)), world)
 
     value = world * tokens * args.steps / (total_ms / 1000)
-    kernel_bytes, layer_bytes = c2_bytes_per_token()
+    kernel_bytes, layer_bytes = c2_bytes_per_token(batch=args.batch)
     achieved = kernel_bytes * tokens / (scan_mean / 1000) / 1e9
     flops = c2_flops_per_token() * tokens
     roof_ms = max(flops / (bf16_peak * 1e12), layer_bytes * tokens / (hbm_peak * 1e9)) * 1000
@@ -285,7 +304,7 @@ def run_ours(args, world, rank, local):
         'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (x ~ N(0,1), seed 1 + rank; random-init weights, seed 1)',
         'config': {'workload': 'c2 BDM layer prefill forward: BSDMConfig(dim=1024, bank_count=256, bank_size=8, '
                                'selected_banks=8, value_width=1024, num_heads=8), zero initial banks',
-                   'global_batch': C2_BATCH * world, 'seq_len': C2_TIME, 'parallelism': f'dp{world} replicas',
+                   'global_batch': args.batch * world, 'seq_len': C2_TIME, 'parallelism': f'dp{world} replicas',
                    'l2': 'flushed between timed steps (256 MiB write, outside the step events)'},
         'gpu_launches': int(launches),
         'e2e': {'value': world * tokens * args.steps / (e2e_ms / 1000), 'unit': 'tokens/s',
@@ -351,6 +370,7 @@ def main():
     ap.add_argument('--steps', type=int, default=10)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--batch', type=int, default=C2_BATCH, help='c2 batch (8 is the benchmark; smaller for profiling)')
     ap.add_argument('--decode-steps', type=int, default=C3_STEPS)
     ap.add_argument('--cpu-time', type=int, default=C2_TIME, help='sequence length of the CPU baseline sample')
     ap.add_argument('--skip-decode', action='store_true')
