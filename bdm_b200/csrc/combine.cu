@@ -74,11 +74,23 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
     const int64_t nv = width - c0;
     if (act) {
         if (ri) {
-            float y[kCols];
-            for (int r = 0; r < kr; ++r) {
-                load8<T>(reads + (t * kr + slot_at[r]) * width + c0, y, nv, vec);
+            // up to kBatchRows rows in flight per thread, summed in bank order
+#ifndef BDM_COMBINE_ROWS
+#define BDM_COMBINE_ROWS 1
+#endif
+            constexpr int kBatchRows = BDM_COMBINE_ROWS;
+            for (int r0 = 0; r0 < kr; r0 += kBatchRows) {
+                float y[kBatchRows][kCols];
 #pragma unroll
-                for (int i = 0; i < kCols; ++i) x[i] = round_each ? rnd<T>(x[i] + y[i]) : x[i] + y[i];
+                for (int r = 0; r < kBatchRows; ++r)
+                    if (r0 + r < kr) load8<T>(reads + (t * kr + slot_at[r0 + r]) * width + c0, y[r], nv, vec);
+#pragma unroll
+                for (int r = 0; r < kBatchRows; ++r) {
+                    if (r0 + r < kr) {
+#pragma unroll
+                        for (int i = 0; i < kCols; ++i) x[i] = round_each ? rnd<T>(x[i] + y[r][i]) : x[i] + y[r][i];
+                    }
+                }
             }
             if (!round_each) {
 #pragma unroll
@@ -132,8 +144,8 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
                 __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float g0 = rnd<T>(1.0f / (1.0f + expf(-gv[2 * i])));
-                    const float g1 = rnd<T>(1.0f / (1.0f + expf(-gv[2 * i + 1])));
+                    const float g0 = rnd<T>(__fdividef(1.0f, 1.0f + __expf(-gv[2 * i])));
+                    const float g1 = rnd<T>(__fdividef(1.0f, 1.0f + __expf(-gv[2 * i + 1])));
                     h[i] = __floats2bfloat162_rn(n[2 * i] * g0, n[2 * i + 1] * g1);
                 }
                 *reinterpret_cast<uint4 *>(orow) = u;

@@ -389,3 +389,4 @@ extern "C" int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, i
     seq_bounds<<<(unsigned)blocks, 256, 0, st>>>(final_keys, p.E, p.nseq, cu_seqlens);
     return launch_status();
 }
+

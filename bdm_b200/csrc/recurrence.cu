@@ -8,21 +8,35 @@
 //
 // Work unit = one warp = (batch*bank sequence, head, tile of 32*NC value
 // columns).  The S x dv bank state is column-separable: each lane owns NC
-// columns and keeps all S rows of them in FP32 registers, so the erase
-// reduction over rows needs no shuffles.  Per write event, per column pair
-// (f32x2 packed FMA on sm_100):
-//   hd = M * exp(g_e) ; erase = sum_s a_s hd_s ; u = w_e*v - erase ; M = hd + k u
-// Per read event: out = scale * sum_s q_e,s M_s.
-// Per-event row controls (exp(g_e), a = dtype(b*p)*k, k, or q_e = dtype(q*r))
-// are computed once per event by the warp's lanes and staged in shared memory
-// as duplicated pairs for the packed math; value rows v and w are gathered in
-// mini-batches so several loads are in flight per lane.
+// columns and keeps all S rows of them in FP32 registers (f32x2 packed math on
+// sm_100), so reductions over rows need no shuffles.
+//
+// Deferred decay.  Reference step for a write event (per row s, per column):
+//     M = e * M ;  u = w_e*v - sum_s a_s M_s ;  M = M + k u
+// with e = exp(g_e), a = dtype(b*p)*k.  Inside a segment of events the kernel
+// keeps N = M / D, D_s = prod of e_s since the segment start, so one event is
+//     u = w_e*v - sum_s (a_s D_s) N_s ;  N_s += (k_s / D_s) u
+// and a read is  out = scale * sum_s (q_s D_s) N_s.  The per-event row
+// coefficients a*D, k/D, q*D come from a segmented prefix sum of log-decays
+// across the lanes of the warp (lane = event), computed while the previous
+// batch runs.  N is multiplied back by D (materialised) at every segment end:
+// the end of a batch, a BF16 state-storage point (gdn2_banks.py:35-36), or
+// where the cumulative log-decay would leave the FP32 range (the batch is cut).
 #include "common.cuh"
 
 namespace bdm {
 namespace {
 
+#ifndef BDM_SCAN_MIN_BLOCKS
+#define BDM_SCAN_MIN_BLOCKS 4  // resident CTAs per SM the register allocation targets (measured best)
+#endif
+#ifndef BDM_SCAN_PREFETCH
+#define BDM_SCAN_PREFETCH 4  // value-row prefetch distance (events)
+#endif
+
 constexpr int kScanWarps = 4;
+constexpr int kPrefetch = BDM_SCAN_PREFETCH;
+constexpr float kMinLogDecay = -60.0f;   // per-segment floor of the cumulative log-decay
 
 struct ScanParams {
     const void *q, *k, *v;
@@ -43,17 +57,16 @@ struct ScanParams {
     int64_t units;
 };
 
-template <typename T, int NC> struct Row {
-    // NC consecutive elements of T loaded / stored as one vector.
-    static constexpr int kBytes = NC * (int)sizeof(T);
-    T x[NC];
-};
-
 template <int BYTES> struct VecOf;
 template <> struct VecOf<4> { using type = uint32_t; };
 template <> struct VecOf<8> { using type = uint2; };
 template <> struct VecOf<16> { using type = uint4; };
-template <> struct VecOf<32> { using type = uint4; };
+
+// NC consecutive elements of T moved as one vector (two for 32 bytes).
+template <typename T, int NC> struct Row {
+    static constexpr int kBytes = NC * (int)sizeof(T);
+    T x[NC];
+};
 
 template <typename T, int NC>
 __device__ __forceinline__ void load_row(Row<T, NC> &r, const T *p) {
@@ -85,13 +98,6 @@ __device__ __forceinline__ void store_row(T *p, const Row<T, NC> &r) {
 
 __device__ __forceinline__ float2 dup(float x) { return make_float2(x, x); }
 
-// Round a pair to T and back (RNE); one packed convert for BF16.
-template <typename T> __device__ __forceinline__ float2 round_pair(float2 x);
-template <> __device__ __forceinline__ float2 round_pair<float>(float2 x) { return x; }
-template <> __device__ __forceinline__ float2 round_pair<bf16>(float2 x) {
-    return __bfloat1622float2(__floats2bfloat162_rn(x.x, x.y));
-}
-
 template <typename T> __device__ __forceinline__ float2 load_pair(const T *x);
 template <> __device__ __forceinline__ float2 load_pair<float>(const float *x) { return make_float2(x[0], x[1]); }
 template <> __device__ __forceinline__ float2 load_pair<bf16>(const bf16 *x) {
@@ -107,13 +113,40 @@ template <> __device__ __forceinline__ void store_pair<bf16>(bf16 *x, float2 v) 
     *reinterpret_cast<__nv_bfloat162 *>(x) = __floats2bfloat162_rn(v.x, v.y);
 }
 
-__device__ __forceinline__ float2 bf16_round_pair(float2 x) { return round_pair<bf16>(x); }
+__device__ __forceinline__ float2 bf16_round_pair(float2 x) {
+    return __bfloat1622float2(__floats2bfloat162_rn(x.x, x.y));
+}
 
-// Events staged per batch; value-row prefetch distance (events).
-template <int S> struct EvBatch { static constexpr int value = S >= 16 ? 16 : 32; };
-constexpr int kPrefetch = 4;
+// u = dtype(w * p) * v - erase for a column pair.  The product of two BF16
+// values is exact in FP32, so one packed BF16 multiply (RNE) reproduces the
+// reference's rounded w*p, and one FMA forms u exactly as mul-then-subtract does.
+template <typename T> struct WriteValue;
+template <> struct WriteValue<bf16> {
+    __device__ __forceinline__ static float2 apply(const bf16 *w, const bf16 *v, float2 pp, float2 minus_erase) {
+        const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162 *>(&pp.x);
+        const __nv_bfloat162 we = __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(w), p2);
+        return __ffma2_rn(__bfloat1622float2(we), load_pair<bf16>(v), minus_erase);
+    }
+};
+template <> struct WriteValue<float> {
+    __device__ __forceinline__ static float2 apply(const float *w, const float *v, float2 pp, float2 minus_erase) {
+        const float2 we = __fmul2_rn(load_pair<float>(w), pp);
+        return __ffma2_rn(we, load_pair<float>(v), minus_erase);
+    }
+};
 
-// Asynchronous global -> shared copy of BYTES (a multiple of 4; 16-byte chunks when possible).
+// Route weight as the pair operand WriteValue expects (BF16: bf16x2 bits in .x).
+template <typename T> __device__ __forceinline__ float2 weight_pair(float p);
+template <> __device__ __forceinline__ float2 weight_pair<float>(float p) { return dup(p); }
+template <> __device__ __forceinline__ float2 weight_pair<bf16>(float p) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(p, p);
+    float2 r;
+    r.x = *reinterpret_cast<const float *>(&h);
+    r.y = 0.f;
+    return r;
+}
+
+// Asynchronous global -> shared copy of BYTES (16-byte chunks when possible).
 template <int BYTES>
 __device__ __forceinline__ void cp_async(void *smem, const void *gmem) {
     const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
@@ -132,26 +165,33 @@ __device__ __forceinline__ void cp_async(void *smem, const void *gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
-// Raw per-event control rows copied from token storage: k | b (dtype) and g (float) for a
-// write, q (dtype) in the k slot for a read.
+// Raw control rows of one event copied from token storage: k | b (dtype) and
+// g (float) for a write; q (dtype) in the k slot for a read.
 template <typename T, int S> struct RawLayout {
     static constexpr int kBytes = S * (int)sizeof(T);
     static constexpr int gBytes = S * 4;
     static constexpr int kOff = 0, bOff = kBytes, gOff = 2 * kBytes;
-    static constexpr int size = 2 * kBytes + gBytes;  // multiple of 16 for S >= 4
+    static constexpr int size = 2 * kBytes + gBytes;
 };
 
+// Per-event controls as duplicated pairs: [a*D or q_e*D | k/D | p, pad | D before the event].
+template <int S> struct CtlLayout {
+    static constexpr int c = 0, kd = S, p = 2 * S, dprev = 2 * S + 2, size = 3 * S + 2;
+};
+
+template <int S> struct EvBatch { static constexpr int value = S >= 16 ? 16 : 32; };
+
 template <typename T, int S, int NC>
-__global__ void __launch_bounds__(kScanWarps * 32, 5)
+__global__ void __launch_bounds__(kScanWarps * 32, BDM_SCAN_MIN_BLOCKS)
 bank_scan_kernel(const ScanParams p) {
     constexpr int NP = NC / 2;
     constexpr int EB = EvBatch<S>::value;
     constexpr int PD = kPrefetch;
     using Raw = RawLayout<T, S>;
-    static_assert(EB % PD == 0 && 32 % EB == 0, "batch layout");
-    // Per warp: controls of the current batch as duplicated pairs ([e | a | k | p] for a
-    // write, [q] for a read), raw rows of the next batch, token / read-slot ids.
-    __shared__ float2 ctl_all[kScanWarps][EB][3 * S + 1];
+    using Ctl = CtlLayout<S>;
+    static_assert(EB % PD == 0 && 32 % EB == 0 && S % 2 == 0, "batch layout");
+    __shared__ __align__(16) float2 ctl_all[kScanWarps][EB][Ctl::size];
+    __shared__ __align__(16) float2 dend_all[kScanWarps][S];
     __shared__ __align__(16) unsigned char raw_all[kScanWarps][EB][Raw::size];
     __shared__ int tok_all[kScanWarps][EB];
     __shared__ int rid_all[kScanWarps][EB];
@@ -160,7 +200,8 @@ bank_scan_kernel(const ScanParams p) {
     const int lane = (int)lane_id();
     const int64_t unit = (int64_t)blockIdx.x * kScanWarps + warp;
     if (unit >= p.units) return;  // warp-uniform
-    float2(*ctl)[3 * S + 1] = ctl_all[warp];
+    float2(*ctl)[Ctl::size] = ctl_all[warp];
+    float2 *dend = dend_all[warp];
     unsigned char(*raw)[Raw::size] = raw_all[warp];
     int *tok_s = tok_all[warp];
     int *rid_s = rid_all[warp];
@@ -186,12 +227,12 @@ bank_scan_kernel(const ScanParams p) {
     T *outp = static_cast<T *>(p.reads) + (int64_t)hh * p.dv + col0;
 
     // ---------------------------------------------------------- initial state
-    float2 M[S][NP];
+    float2 N[S][NP];
     const int64_t state_off = ((bidx * p.J + bank) * p.H + hh) * (int64_t)S * p.dv + col0;
 #pragma unroll
     for (int s = 0; s < S; ++s)
 #pragma unroll
-        for (int j = 0; j < NP; ++j) M[s][j] = make_float2(0.f, 0.f);
+        for (int j = 0; j < NP; ++j) N[s][j] = make_float2(0.f, 0.f);
     if (active) {
         if (p.cache) {
 #pragma unroll
@@ -199,7 +240,7 @@ bank_scan_kernel(const ScanParams p) {
 #pragma unroll
                 for (int j = 0; j < NP; ++j) {
                     const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
-                    M[s][j] = p.cache_dtype == BDM_BF16 ? load_pair<bf16>(static_cast<const bf16 *>(p.cache) + o)
+                    N[s][j] = p.cache_dtype == BDM_BF16 ? load_pair<bf16>(static_cast<const bf16 *>(p.cache) + o)
                                                         : load_pair<float>(static_cast<const float *>(p.cache) + o);
                 }
         } else if (p.row_factor) {
@@ -212,11 +253,11 @@ bank_scan_kernel(const ScanParams p) {
                     if (p.factor_dtype == BDM_BF16) {
                         const float2 u = load_pair<bf16>(static_cast<const bf16 *>(p.row_factor) + ou + 2 * j);
                         const float2 z = load_pair<bf16>(static_cast<const bf16 *>(p.col_factor) + oz + 2 * j);
-                        M[s][j] = bf16_round_pair(make_float2(u.x + z.x, u.y + z.y));
+                        N[s][j] = bf16_round_pair(make_float2(u.x + z.x, u.y + z.y));
                     } else {
                         const float2 u = load_pair<float>(static_cast<const float *>(p.row_factor) + ou + 2 * j);
                         const float2 z = load_pair<float>(static_cast<const float *>(p.col_factor) + oz + 2 * j);
-                        M[s][j] = make_float2(u.x + z.x, u.y + z.y);
+                        N[s][j] = make_float2(u.x + z.x, u.y + z.y);
                     }
                 }
             }
@@ -225,7 +266,7 @@ bank_scan_kernel(const ScanParams p) {
 #pragma unroll
             for (int s = 0; s < S; ++s)
 #pragma unroll
-                for (int j = 0; j < NP; ++j) M[s][j] = bf16_round_pair(M[s][j]);
+                for (int j = 0; j < NP; ++j) N[s][j] = bf16_round_pair(N[s][j]);
         }
     }
 
@@ -234,8 +275,9 @@ bank_scan_kernel(const ScanParams p) {
     const int64_t end = min(max(p.cu[seq + 1], start), p.E);
 
     // ------------------------------------------------------ batch staging
-    // Lane i owns event i of a batch: decode its id, start the async copy of its
-    // control rows, and later turn them into the duplicated-pair controls.
+    // Lane i owns event i of a batch.  stage_issue decodes its id and starts the
+    // asynchronous copy of its control rows; stage_finish turns them into the
+    // deferred-decay coefficients.
     int my_tok = -1, my_rid = -1;
     bool my_write = false;
     float my_wt = 0.f;
@@ -243,6 +285,7 @@ bank_scan_kernel(const ScanParams p) {
         my_tok = -1;
         my_rid = -1;
         my_write = false;
+        my_wt = 0.f;
         if (lane < bn) {
             const int64_t id = p.order[bbase + lane];
             if (id >= 0 && id < nw) {
@@ -272,47 +315,92 @@ bank_scan_kernel(const ScanParams p) {
         }
         cp_async_commit();
     };
-    auto stage_finish = [&]() -> unsigned {
+    // pos0 = position of the batch's first event in its sequence.  Sets the
+    // number of events to run (<= bn, cut where the log-decay range ends), the
+    // storage-point mask, and returns the write mask.
+    auto stage_finish = [&](int64_t pos0, int bn, int &n_out, unsigned &round_out) -> unsigned {
         cp_async_wait_all();
-        if (my_tok >= 0) {
-            const T *rk = reinterpret_cast<const T *>(raw[lane] + Raw::kOff);
+        const bool valid = lane < bn;
+        const int64_t pos = pos0 + lane;
+        const bool head = valid && p.interval > 0 && pos > 0 && (pos % p.interval) == 0;
+        const T *rk = reinterpret_cast<const T *>(raw[lane] + Raw::kOff);
+        const float *rg = reinterpret_cast<const float *>(raw[lane] + Raw::gOff);
+        // segmented inclusive scan of log-decays; segments start at lane 0 and at storage points
+        float L[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            float ge = 0.f;
+            if (my_write && my_tok >= 0) ge = fmaxf(p.routed_decay ? rg[s] * my_wt : rg[s], kMinLogDecay);
+            L[s] = ge;
+        }
+        bool f = head || lane == 0;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const bool fu = __shfl_up_sync(0xffffffffu, f, d);
+            const bool take = lane >= d && !f;
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                const float lu = __shfl_up_sync(0xffffffffu, L[s], d);
+                if (take) L[s] += lu;
+            }
+            f = f || (lane >= d && fu);
+        }
+        // cut the batch before the first event whose segment would leave the FP32 range
+        float lmin = 0.f;
+#pragma unroll
+        for (int s = 0; s < S; ++s) lmin = fminf(lmin, L[s]);
+        const unsigned over = __ballot_sync(0xffffffffu, valid && lmin < kMinLogDecay);
+        const int n = over ? (__ffs(over) - 1) : bn;  // >= 1: a single event is floored above
+        const bool use = lane < n;
+        float D[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) D[s] = expf(L[s]);
+        if (use && my_tok >= 0) {
             if (my_write) {
                 const T *rb = reinterpret_cast<const T *>(raw[lane] + Raw::bOff);
-                const float *rg = reinterpret_cast<const float *>(raw[lane] + Raw::gOff);
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
                     const float kk = Elem<T>::to_float(rk[s]);
-                    const float ge = p.routed_decay ? rg[s] * my_wt : rg[s];
-                    ctl[lane][s] = dup(expf(ge));
-                    ctl[lane][S + s] = dup(rnd<T>(Elem<T>::to_float(rb[s]) * my_wt) * kk);
-                    ctl[lane][2 * S + s] = dup(kk);
+                    const float a = rnd<T>(Elem<T>::to_float(rb[s]) * my_wt) * kk;
+                    ctl[lane][Ctl::c + s] = dup(a * D[s]);
+                    ctl[lane][Ctl::kd + s] = dup(kk * expf(-L[s]));
                 }
-                ctl[lane][3 * S] = dup(my_wt);
+                ctl[lane][Ctl::p] = weight_pair<T>(my_wt);
             } else {
 #pragma unroll
-                for (int s = 0; s < S; ++s) ctl[lane][s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * my_wt));
+                for (int s = 0; s < S; ++s) ctl[lane][Ctl::c + s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * my_wt) * D[s]);
             }
         }
-        if (lane < EB) {
-            tok_s[lane] = my_tok;
-            rid_s[lane] = my_rid;
+        // D before a storage point (materialise there), D after the last event (batch end)
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const float before = __shfl_up_sync(0xffffffffu, D[s], 1);
+            if (use && head) ctl[lane][Ctl::dprev + s] = dup(lane == 0 ? 1.0f : before);
+            if (lane == n - 1) dend[s] = dup(D[s]);
         }
-        const unsigned wm = __ballot_sync(0xffffffffu, my_write);
+        if (lane < EB) {
+            tok_s[lane] = use ? my_tok : -1;
+            rid_s[lane] = use ? my_rid : -1;
+        }
+        n_out = n;
+        round_out = __ballot_sync(0xffffffffu, use && head);
+        const unsigned wm = __ballot_sync(0xffffffffu, use && my_write && my_tok >= 0);
         __syncwarp();
         return wm;
     };
 
-    int bn = (int)min((int64_t)EB, end - start);
-    unsigned wmask = 0;
-    if (bn > 0) {
-        stage_issue(start, bn);
-        wmask = stage_finish();
+    int n = 0;
+    unsigned wmask = 0, rmask = 0;
+    {
+        const int bn = (int)min((int64_t)EB, end - start);
+        if (bn > 0) {
+            stage_issue(start, bn);
+            wmask = stage_finish(0, bn, n, rmask);
+        }
     }
-    int since_round = 0;  // events since the last stored-state rounding
     Row<T, NC> vr[PD], wr[PD];
 
     for (int64_t base = start; base < end;) {
-        const int n = bn;
         const int64_t nbase = base + n;
         const int nn = (int)min((int64_t)EB, end - nbase);
         auto prefetch = [&](int ev, int slot) {
@@ -324,84 +412,79 @@ bank_scan_kernel(const ScanParams p) {
         };
 #pragma unroll
         for (int j = 0; j < PD; ++j) prefetch(j, j);
+        bool issued = false;
         for (int e0 = 0; e0 < n; e0 += PD) {
-            if (e0 == (EB / 2) && nn > 0) stage_issue(nbase, nn);  // next batch, overlapped with the second half
+            if (e0 == EB / 2 && nn > 0) {  // stage the next batch under the second half
+                stage_issue(nbase, nn);
+                issued = true;
+            }
 #pragma unroll
             for (int j = 0; j < PD; ++j) {
                 const int ev = e0 + j;
                 if (ev >= n) break;
-                if (p.interval > 0 && since_round == p.interval) {
+                if ((rmask >> ev) & 1u) {  // storage point: materialise, round to BF16
 #pragma unroll
-                    for (int s = 0; s < S; ++s)
+                    for (int s = 0; s < S; ++s) {
+                        const float2 d2 = ctl[ev][Ctl::dprev + s];
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) M[s][c] = bf16_round_pair(M[s][c]);
-                    since_round = 0;
+                        for (int c = 0; c < NP; ++c) N[s][c] = bf16_round_pair(__fmul2_rn(N[s][c], d2));
+                    }
                 }
-                ++since_round;
-                const int tk = tok_s[ev];
-                if (tk >= 0) {
-                    if ((wmask >> ev) & 1u) {
-                        float2 er[NP];
+                if ((wmask >> ev) & 1u) {
+                    float2 mer[NP];
 #pragma unroll
-                        for (int s = 0; s < S; ++s) {
-                            const float2 e2 = ctl[ev][s];
+                    for (int c = 0; c < NP; ++c) {
+                        float2 lo = __fmul2_rn(ctl[ev][Ctl::c + 0], N[0][c]);
+                        float2 hi = __fmul2_rn(ctl[ev][Ctl::c + 1], N[1][c]);
 #pragma unroll
-                            for (int c = 0; c < NP; ++c) M[s][c] = __fmul2_rn(M[s][c], e2);
+                        for (int s = 2; s < S; s += 2) {
+                            lo = __ffma2_rn(ctl[ev][Ctl::c + s], N[s][c], lo);
+                            hi = __ffma2_rn(ctl[ev][Ctl::c + s + 1], N[s + 1][c], hi);
                         }
+                        mer[c] = make_float2(-(lo.x + hi.x), -(lo.y + hi.y));
+                    }
+                    const float2 pw = ctl[ev][Ctl::p];
+                    float2 u[NP];
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) {
-                            float2 lo = __fmul2_rn(ctl[ev][S + 0], M[0][c]);
-                            float2 hi = __fmul2_rn(ctl[ev][S + 1], M[1][c]);
+                    for (int c = 0; c < NP; ++c)
+                        u[c] = WriteValue<T>::apply(wr[j].x + 2 * c, vr[j].x + 2 * c, pw, mer[c]);
 #pragma unroll
-                            for (int s = 2; s < S; s += 2) {
-                                lo = __ffma2_rn(ctl[ev][S + s], M[s][c], lo);
-                                hi = __ffma2_rn(ctl[ev][S + s + 1], M[s + 1][c], hi);
-                            }
-                            er[c] = make_float2(lo.x + hi.x, lo.y + hi.y);
-                        }
-                        const float2 pw = ctl[ev][3 * S];
-                        float2 u[NP];
+                    for (int s = 0; s < S; ++s) {
+                        const float2 k2 = ctl[ev][Ctl::kd + s];
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) {
-                            const float2 vv = load_pair<T>(vr[j].x + 2 * c);
-                            const float2 wv = load_pair<T>(wr[j].x + 2 * c);
-                            const float2 we = round_pair<T>(__fmul2_rn(wv, pw));
-                            const float2 x = __fmul2_rn(we, vv);
-                            u[c] = make_float2(x.x - er[c].x, x.y - er[c].y);
-                        }
+                        for (int c = 0; c < NP; ++c) N[s][c] = __ffma2_rn(k2, u[c], N[s][c]);
+                    }
+                } else if (tok_s[ev] >= 0) {
+                    float2 acc[NP];
 #pragma unroll
-                        for (int s = 0; s < S; ++s) {
-                            const float2 k2 = ctl[ev][2 * S + s];
+                    for (int c = 0; c < NP; ++c) acc[c] = __fmul2_rn(ctl[ev][Ctl::c + 0], N[0][c]);
 #pragma unroll
-                            for (int c = 0; c < NP; ++c) M[s][c] = __ffma2_rn(k2, u[c], M[s][c]);
-                        }
-                    } else {
-                        float2 acc[NP];
+                    for (int s = 1; s < S; ++s)
 #pragma unroll
-                        for (int c = 0; c < NP; ++c) acc[c] = __fmul2_rn(ctl[ev][0], M[0][c]);
+                        for (int c = 0; c < NP; ++c) acc[c] = __ffma2_rn(ctl[ev][Ctl::c + s], N[s][c], acc[c]);
+                    if (active) {
+                        Row<T, NC> out;
 #pragma unroll
-                        for (int s = 1; s < S; ++s)
-#pragma unroll
-                            for (int c = 0; c < NP; ++c) acc[c] = __ffma2_rn(ctl[ev][s], M[s][c], acc[c]);
-                        if (active) {
-                            Row<T, NC> out;
-#pragma unroll
-                            for (int c = 0; c < NP; ++c)
-                                store_pair<T>(out.x + 2 * c, __fmul2_rn(acc[c], dup(p.scale)));
-                            store_row<T, NC>(outp + (int64_t)rid_s[ev] * V, out);
-                        }
+                        for (int c = 0; c < NP; ++c) store_pair<T>(out.x + 2 * c, __fmul2_rn(acc[c], dup(p.scale)));
+                        store_row<T, NC>(outp + (int64_t)rid_s[ev] * V, out);
                     }
                 }
                 prefetch(ev + PD, j);
             }
         }
+        // segment end: materialise N = D * N for the next batch (or the final state)
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const float2 d2 = dend[s];
+#pragma unroll
+            for (int c = 0; c < NP; ++c) N[s][c] = __fmul2_rn(N[s][c], d2);
+        }
         if (nn > 0) {
-            if (n <= EB / 2) stage_issue(nbase, nn);  // short batch: the midpoint was never reached
+            if (!issued) stage_issue(nbase, nn);
             __syncwarp();
-            wmask = stage_finish();
+            wmask = stage_finish(nbase - start, nn, n, rmask);
         }
         base = nbase;
-        bn = nn;
     }
 
     if (p.store_final && p.cache && active) {
@@ -410,8 +493,8 @@ bank_scan_kernel(const ScanParams p) {
 #pragma unroll
             for (int j = 0; j < NP; ++j) {
                 const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
-                if (p.cache_dtype == BDM_BF16) store_pair<bf16>(static_cast<bf16 *>(p.cache) + o, M[s][j]);
-                else store_pair<float>(static_cast<float *>(p.cache) + o, M[s][j]);
+                if (p.cache_dtype == BDM_BF16) store_pair<bf16>(static_cast<bf16 *>(p.cache) + o, N[s][j]);
+                else store_pair<float>(static_cast<float *>(p.cache) + o, N[s][j]);
             }
     }
 }

@@ -3,15 +3,19 @@
 // Restates product_key_route (implementation/bdm/gdn2_banks.py:74-114):
 //   top-sub per factor -> sub x sub pair sums in the logits dtype -> top-count
 //   -> softmax in FP32, index = row * J2 + col.
-// Selection is a sequence of warp arg-max rounds over 64-bit keys
-// (order-preserving value bits : inverted index), so equal scores resolve to
-// the lower index -- the tie rule the reference leaves to torch.topk.
+// Every selection orders by (value desc, index asc), so equal scores resolve to
+// the lower index -- the tie rule the reference leaves to torch.topk.  Short
+// lists (factor widths <= 128, the pair "staircase") are ranked directly; wide
+// factors use warp arg-max rounds over 64-bit keys (order-preserving value
+// bits : inverted index).
 #include "common.cuh"
 
 namespace bdm {
 namespace {
 
 constexpr int kRouteWarps = 8;
+constexpr int kRankMax = 128;  // factor widths ranked directly
+constexpr int kMaxCand = 128;  // staircase pair candidates handled by ranking
 
 __device__ __forceinline__ uint32_t ordered_bits(float f) {
     uint32_t u = __float_as_uint(f);
@@ -61,13 +65,55 @@ __device__ void warp_topk(const float *vals, int n, int k, float *out_v, int *ou
     __syncwarp();
 }
 
+// Rank selection for short lists: element i's rank is the number of elements
+// ordered before it by (value desc, index asc); ranks < k are written to
+// out[rank].  n <= 4 * 32.
+__device__ void warp_rank_select(const float *vals, int n, int k, float *out_v, int *out_i) {
+    const int lane = (int)lane_id();
+    for (int i = lane; i < n; i += 32) {
+        const float x = vals[i];
+        int rank = 0;
+        for (int j = 0; j < n; ++j) {
+            const float y = vals[j];
+            rank += (y > x) || (y == x && j < i);
+        }
+        if (rank < k) {
+            out_v[rank] = x;
+            out_i[rank] = i;
+        }
+    }
+    __syncwarp();
+}
+
+// Pairs (i, l) that can reach the top `count`: a pair is outranked by every
+// (i', l') <= (i, l) componentwise (sums of descending lists, lower pair index),
+// so only pairs with (i + 1) * (l + 1) <= count are candidates.  Returns the
+// candidate count, or cap + 1 (list not filled) when more than `cap` exist.
+__device__ int staircase_candidates(int sub, int count, int *cand, int cap) {
+    int m = 0;
+    for (int i = 0; i < sub; ++i) {
+        const int width = min(sub, count / (i + 1));
+        for (int l = 0; l < width; ++l) {
+            if (m == cap) return cap + 1;
+            cand[m++] = i * sub + l;
+        }
+    }
+    return m;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kRouteWarps * 32)
 route_kernel(const T *__restrict__ logits, int64_t ntok, int64_t ld, int j1, int j2, int sub, int count,
              int64_t *__restrict__ out_idx, T *__restrict__ out_w) {
     extern __shared__ float smem[];
+    __shared__ int cand[kMaxCand];
+    __shared__ int ncand_s;
     const int warp = threadIdx.x >> 5;
     const int lane = (int)lane_id();
+    if (threadIdx.x == 0) ncand_s = staircase_candidates(sub, count, cand, kMaxCand);
+    __syncthreads();
+    const int ncand = ncand_s;
+    const bool fast_pairs = ncand <= kMaxCand && ncand > 0;
     const int per_warp = j1 + j2 + 4 * sub + sub * sub + 2 * count;
     float *z = smem + warp * per_warp;
     float *fv = z + j1 + j2;
@@ -82,12 +128,36 @@ route_kernel(const T *__restrict__ logits, int64_t ntok, int64_t ld, int j1, int
         const T *row = logits + t * ld;
         for (int i = lane; i < j1 + j2; i += 32) z[i] = Elem<T>::to_float(row[i]);
         __syncwarp();
-        warp_topk(z, j1, sub, fv, fi);
-        warp_topk(z + j1, j2, sub, sv, si);
+        if (j1 <= kRankMax) warp_rank_select(z, j1, sub, fv, fi);
+        else warp_topk(z, j1, sub, fv, fi);
+        if (j2 <= kRankMax) warp_rank_select(z + j1, j2, sub, sv, si);
+        else warp_topk(z + j1, j2, sub, sv, si);
         // Pair scores in the logits dtype, pair p = i*sub + l (gdn2_banks.py:106-110).
-        for (int p = lane; p < sub * sub; p += 32) pv[p] = rnd<T>(fv[p / sub] + sv[p % sub]);
-        __syncwarp();
-        warp_topk(pv, sub * sub, count, cv, ci);
+        if (fast_pairs) {
+            for (int c = lane; c < ncand; c += 32) {
+                const int p = cand[c];
+                pv[c] = rnd<T>(fv[p / sub] + sv[p % sub]);
+            }
+            __syncwarp();
+            for (int c = lane; c < ncand; c += 32) {
+                const float x = pv[c];
+                const int pc = cand[c];
+                int rank = 0;
+                for (int d = 0; d < ncand; ++d) {
+                    const float y = pv[d];
+                    rank += (y > x) || (y == x && cand[d] < pc);
+                }
+                if (rank < count) {
+                    cv[rank] = x;
+                    ci[rank] = pc;
+                }
+            }
+            __syncwarp();
+        } else {
+            for (int p = lane; p < sub * sub; p += 32) pv[p] = rnd<T>(fv[p / sub] + sv[p % sub]);
+            __syncwarp();
+            warp_topk(pv, sub * sub, count, cv, ci);
+        }
         // Softmax in FP32 over the descending selection: cv[0] is the maximum.
         float e = 0.f;
         if (lane < count) e = expf(cv[lane] - cv[0]);
