@@ -390,3 +390,56 @@ extern "C" int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, i
     return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Dispatch without caller-provided scratch.
+//
+// Some callers cannot hand the library a workspace: code that runs while a
+// CUDA graph is being captured (a cudaMalloc there breaks the capture),
+// runtimes that plan every device allocation up front or own the only
+// allocator in the process, and latency-critical servers that must not
+// allocate on the request path.  This entry point sorts with a fixed scratch
+// array that lives in the library itself, so it needs no allocation at all.
+//
+// The array is a file-scope __device__ variable of kNoAllocScratchBytes
+// (32 MiB).  Every GPU that loads the library holds it until the process
+// exits.  Host code cannot use the array's name as a device address; the
+// first call on each device looks the address up with cudaGetSymbolAddress
+// while that device is current and caches it, so make that first call before
+// any stream capture.  All calls share the one array: calls whose kernels can
+// overlap on the GPU (different streams, or different host threads on one
+// device) race on it and must be ordered by the caller.  The sort writes every
+// scratch byte it reads, so no clearing is needed between calls.
+// ---------------------------------------------------------------------------
+namespace bdm {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = (int64_t)32 << 20;
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_dispatch_scratch[kNoAllocScratchBytes];
+
+void *g_scratch_ptr[kMaxDevices] = {};
+
+}  // namespace
+}  // namespace bdm
+
+extern "C" int bdm_dispatch_noalloc(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time,
+                                    int kw, int kr, int64_t bank_count, int64_t *order, int64_t *cu_seqlens,
+                                    int64_t *inverse, int64_t *tokens, int32_t *error_word, void *stream) {
+    using namespace bdm;
+    if (batch <= 0 || time <= 0 || kw <= 0 || kr <= 0 || bank_count <= 0) return BDM_ERR_INVALID;
+    const int64_t need = make_plan(batch, time, kw, kr, bank_count).bytes;
+    if (need > kNoAllocScratchBytes) return BDM_ERR_WORKSPACE;  // beyond the fixed 32 MiB scratch
+    int dev = 0;
+    int rc = cuda_status(cudaGetDevice(&dev));
+    if (rc) return rc;
+    if (dev < 0 || dev >= kMaxDevices) return BDM_ERR_UNSUPPORTED;
+    void *ptr = __atomic_load_n(&g_scratch_ptr[dev], __ATOMIC_ACQUIRE);
+    if (!ptr) {
+        rc = cuda_status(cudaGetSymbolAddress(&ptr, g_dispatch_scratch));
+        if (rc) return rc;
+        __atomic_store_n(&g_scratch_ptr[dev], ptr, __ATOMIC_RELEASE);
+    }
+    return bdm_dispatch(write_idx, read_idx, batch, time, kw, kr, bank_count, order, cu_seqlens, inverse, tokens,
+                        error_word, ptr, kNoAllocScratchBytes, stream);
+}

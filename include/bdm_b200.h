@@ -91,6 +91,21 @@ BDM_API int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, int6
                  int32_t *error_word, void *workspace, int64_t workspace_bytes, void *stream);
 
 /*
+ * bdm_dispatch for callers that cannot allocate device memory -- code running
+ * under CUDA graph capture, runtimes that own every device allocation, or
+ * request paths that must not allocate.  No counterpart in the reference.
+ * Same arguments and results as bdm_dispatch minus the workspace: scratch is a
+ * fixed 32 MiB array inside the library (held on every GPU that loads it until
+ * exit).  Needs bdm_dispatch_workspace_bytes(...) <= 32 MiB, else returns
+ * BDM_ERR_WORKSPACE.  The first call on a device looks the array up (make it
+ * before any stream capture).  Calls share the array: calls that may overlap
+ * on the GPU race and must be ordered by the caller.
+ */
+BDM_API int bdm_dispatch_noalloc(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time,
+                                 int kw, int kr, int64_t bank_count, int64_t *order, int64_t *cu_seqlens,
+                                 int64_t *inverse, int64_t *tokens, int32_t *error_word, void *stream);
+
+/*
  * Controller epilogue over the fused input projection.  Replaces the
  * element-wise part of _parameters._controllers (_parameters.py:189-220) and
  * heads.controllers (heads.py:11-22); the projections themselves are one GEMM
