@@ -32,7 +32,7 @@ SIGNATURES = {
     'bdm_dispatch_workspace_bytes': (_i64, [_i64, _i64, _int, _int, _i64]),
     'bdm_dispatch': (_int, [_vp, _vp, _i64, _i64, _int, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     'bdm_dispatch_noalloc': (_int, [_vp, _vp, _i64, _i64, _int, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
-    'bdm_controllers': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _int, _int, _int,
+    'bdm_controllers': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _int, _int, _int,
                                _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'bdm_product_state': (_int, [_vp, _vp, _i64, _i64, _int, _i64, _i64, _int, _int, _int, _vp, _int, _vp]),
     'bdm_bank_scan': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int,

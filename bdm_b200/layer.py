@@ -11,9 +11,9 @@ so ``state_dict``s move between the two unchanged, and its entry points:
 * ``create_state(batch, dtype=...)``       inference.py:100-107
 
 Per forward: ONE projection GEMM (all controllers, both routers and the output
-gate, biases in its epilogue), then the CUDA kernels of ``ops`` -- controller
-epilogue, router, dispatch, bank recurrence, combine + norm + gate -- and the
-o_proj GEMM.  There is no backend switch and no CPU path; CPU inputs raise.
+gate, biases in its epilogue) and the small f_proj.1 GEMM, then the CUDA kernels
+of ``ops`` -- controller epilogue, router, dispatch, bank recurrence, combine +
+norm + gate -- and the o_proj GEMM.  There is no backend switch and no CPU path; CPU inputs raise.
 The backward pass is not implemented: forward / prefill / step run without
 autograd, and a forward that would need gradients raises.
 """
@@ -254,7 +254,9 @@ class BankedDeltaMemory(nn.Module):
     def _controls_and_routes(self, hidden):
         batch, time, _ = hidden.shape
         proj, cols = self._project(hidden.reshape(batch * time, self.hidden_size))
-        q, k, v, g, b, w = ops.controllers(proj, cols, self.f_proj[1].weight, self.A_log, self.dt_bias,
+        f1 = proj[:, cols['f']:cols['f'] + self.head_value_width]
+        f = torch.mm(f1, self.f_proj[1].weight.t())  # f_proj.1, rounded to the activation dtype
+        q, k, v, g, b, w = ops.controllers(proj, cols, f, self.A_log, self.dt_bias,
                                            heads=self.num_heads, bank_size=self.bank_size,
                                            head_value_width=self.head_value_width,
                                            qk_norm=self.config.qk_normalization)
@@ -367,6 +369,41 @@ class BankedDeltaMemory(nn.Module):
                               bank_size=self.bank_size, head_value_width=self.head_value_width,
                               routed_decay=self.config.routed_decay, scale=self.bank_size ** -0.5)
         return self._output(hidden, raw, None, gate, round_each=True), state
+
+    def capture_step(self, state, *, warmup=2):
+        """CUDA-graph one decode step bound to ``state`` (a cache from ``prefill``/``create_state``).
+
+        Returns ``run(hidden[B,1,D]) -> out[B,1,D]``; each call copies ``hidden`` into the graph's
+        input buffer, replays the step (``state`` is advanced in place exactly as ``step`` does)
+        and returns the graph's output buffer, which the next call overwrites.  Warm-up runs on a
+        clone of ``state``, so capturing does not advance the cache.  Parameters must not change
+        afterwards (the graph holds their fused copy).
+        """
+        if torch.is_grad_enabled():
+            raise RuntimeError('capture_step requires no_grad or inference_mode')
+        batch = state.shape[0]
+        dev, dt = state.device, self.q_proj.weight.dtype
+        hidden_in = torch.zeros(batch, 1, self.hidden_size, dtype=dt, device=dev)
+        self._validate_state(hidden_in, state)
+        scratch = state.clone()
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(hidden_in, scratch)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        del scratch
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out, _ = self.step(hidden_in, state)
+
+        def run(hidden):
+            hidden_in.copy_(hidden)
+            graph.replay()
+            return out
+
+        run.graph = graph  # keep the graph (and its memory pool) alive with the callable
+        return run
 
 
 BlockSparseDeltaMemory = BankedDeltaMemory

@@ -107,32 +107,34 @@ def dispatch(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int, *
     return out
 
 
-def controllers(proj: torch.Tensor, cols: dict, f2_weight: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
+def controllers(proj: torch.Tensor, cols: dict, f: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
                 *, heads: int, bank_size: int, head_value_width: int, qk_norm: str):
-    """Controller epilogue over the fused projection ``proj [NT, ld]`` (column offsets in ``cols``).
+    """Controller epilogue over the fused projection ``proj [NT, ld]`` (column offsets in ``cols``)
+    and the f_proj output ``f [NT, H*S]``.
 
     Returns q, k, v, g, b, w as [NT, H*S] / [NT, V] tensors (g float32).
     """
-    _cuda(proj, f2_weight)
-    if proj.ndim != 2 or proj.stride(1) != 1:
-        raise ValueError('proj must be a row-major [tokens, width] matrix')
+    _cuda(proj, f)
+    if proj.ndim != 2 or proj.stride(1) != 1 or f.ndim != 2 or f.stride(1) != 1:
+        raise ValueError('proj and f must be row-major [tokens, width] matrices')
     nt = proj.shape[0]
     hs, v_width = heads * bank_size, heads * head_value_width
     dev, dt = proj.device, proj.dtype
+    if f.dtype != dt or f.shape != (nt, hs):
+        raise ValueError(f'f must be [{nt}, {hs}] in {dt}')
     q = torch.empty((nt, hs), dtype=dt, device=dev)
     k = torch.empty_like(q)
     b = torch.empty_like(q)
     g = torch.empty((nt, hs), dtype=torch.float32, device=dev)
     v = torch.empty((nt, v_width), dtype=dt, device=dev)
     w = torch.empty_like(v)
-    f2 = f2_weight.to(dt).contiguous()
     al = a_log.detach().float().contiguous()
     dtb = dt_bias.detach().float().contiguous()
     _lib.check(_lib.load().bdm_controllers(
-        _ptr(proj), nt, proj.stride(0) if nt > 1 else proj.shape[1], cols['q'], cols['k'], cols['v'], cols['f'],
-        cols['b'], cols['w'], _ptr(f2), _ptr(al), _ptr(dtb), heads, bank_size, head_value_width,
-        1 if qk_norm == 'nvidia' else 0, dtype_code(dt), _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w),
-        _stream(dev)), 'bdm_controllers')
+        _ptr(proj), nt, proj.stride(0) if nt > 1 else proj.shape[1], cols['q'], cols['k'], cols['v'], cols['b'],
+        cols['w'], _ptr(f), f.stride(0) if nt > 1 else f.shape[1], _ptr(al), _ptr(dtb), heads, bank_size,
+        head_value_width, 1 if qk_norm == 'nvidia' else 0, dtype_code(dt), _ptr(q), _ptr(k), _ptr(v), _ptr(g),
+        _ptr(b), _ptr(w), _stream(dev)), 'bdm_controllers')
     return q, k, v, g, b, w
 
 

@@ -332,7 +332,11 @@ def run_ours(args, world, rank, local):
 
 
 def run_decode(dev, rank, world, args):
-    """c3: 1024 single-token steps at batch 64 on a state pre-filled by a 2048-token prefill."""
+    """c3: 1024 single-token steps at batch 64 on a state pre-filled by a 2048-token prefill.
+
+    The timed loop replays the CUDA-graphed step (``capture_step``); the per-call ``step``
+    path is timed on a short loop beside it.
+    """
     from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
     cfg = BSDMConfig(**C3)
     layer = BlockSparseDeltaMemory(cfg, seed=2).to(torch.bfloat16).to(dev)
@@ -342,24 +346,34 @@ def run_decode(dev, rank, world, args):
     toks = torch.randn(steps + 8, C3_BATCH, 1, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
     with torch.inference_mode():
         _, state = layer.prefill(prefix)
+        run = layer.capture_step(state)
         for i in range(8):
-            layer.step(toks[steps + i], state)
+            run(toks[steps + i])
         torch.cuda.synchronize()
         barrier(world)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for i in range(steps):
-            layer.step(toks[i], state)
+            run(toks[i])
         end.record()
         torch.cuda.synchronize()
+        eager_n = 64
+        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        es.record()
+        for i in range(eager_n):
+            layer.step(toks[i], state)
+        ee.record()
+        torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end), world)
+    eager_ms = es.elapsed_time(ee) / eager_n
     weight_bytes = sum(p.numel() * p.element_size() for p in layer.parameters())
     hbm_peak, _, _ = load_peaks()
     bpt = c3_bytes_per_token(weight_bytes=weight_bytes)
     tps = world * C3_BATCH * steps / (ms / 1000)
     return {'metric': 'BDM decode tokens/sec (c3: batch 64, J=2048, S=8, B=8, d_v=128, 2048-token prefill)',
             'value': tps, 'unit': 'tokens/s', 'steps': steps, 'ms_per_step': ms / steps,
-            'state_bytes': state.numel() * state.element_size(),
+            'path': 'CUDA-graphed step (BlockSparseDeltaMemory.capture_step)',
+            'eager_step_ms': eager_ms, 'state_bytes': state.numel() * state.element_size(),
             'roofline': {'bound': 'hbm', 'bytes_per_token': bpt, 'achieved': bpt * tps / world / 1e9,
                          'peak': hbm_peak, 'unit': 'GB/s', 'frac': bpt * tps / world / 1e9 / hbm_peak}}
 

@@ -108,17 +108,18 @@ BDM_API int bdm_dispatch_noalloc(const int64_t *write_idx, const int64_t *read_i
 /*
  * Controller epilogue over the fused input projection.  Replaces the
  * element-wise part of _parameters._controllers (_parameters.py:189-220) and
- * heads.controllers (heads.py:11-22); the projections themselves are one GEMM
- * (proj = hidden @ [Wq;Wk;Wv;Wf1;Wb;Ww;...]^T) done by the caller.
- *   proj [ntok, ld] (dtype) with the q, k, v, f1, b, w blocks at the given column offsets
- *   f2_weight [H*S, dv] (dtype): second f_proj layer; a_log [H], dt_bias [H*S] float
+ * heads.controllers (heads.py:11-22); the projections themselves are GEMMs
+ * done by the caller: proj = hidden @ [Wq;Wk;Wv;Wf1;Wb;Ww;...]^T and
+ * f = f1 @ Wf2^T (the second f_proj layer, rounded to dtype like the reference's Linear).
+ *   proj [ntok, ld] (dtype) with the q, k, v, b, w blocks at the given column offsets
+ *   f [ntok, ldf] (dtype, H*S columns); a_log [H], dt_bias [H*S] float
  *   qk_norm: 0 = F.normalize (original), 1 = x*rsqrt(sum x^2 + 1e-6) (nvidia)
  *   out: q, k, b [ntok, H, S] (dtype), g [ntok, H, S] float, v, w [ntok, V] (dtype)
  */
 BDM_API int bdm_controllers(const void *proj, int64_t ntok, int64_t ld, int64_t col_q, int64_t col_k, int64_t col_v,
-                    int64_t col_f, int64_t col_b, int64_t col_w, const void *f2_weight, const float *a_log,
-                    const float *dt_bias, int heads, int bank_size, int head_value_width, int qk_norm, int dtype,
-                    void *q, void *k, void *v, float *g, void *b, void *w, void *stream);
+                            int64_t col_b, int64_t col_w, const void *f, int64_t ldf, const float *a_log,
+                            const float *dt_bias, int heads, int bank_size, int head_value_width, int qk_norm,
+                            int dtype, void *q, void *k, void *v, float *g, void *b, void *w, void *stream);
 
 /*
  * Product-key initial bank memory.  Replaces materialize_initial_state

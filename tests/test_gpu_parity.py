@@ -330,3 +330,20 @@ def test_forward_is_deterministic():
     with torch.no_grad():
         a, b = m(x), m(x)
     assert torch.equal(a, b)
+
+
+def test_captured_decode_step_matches_eager_step():
+    cfg = BSDMConfig(dim=256, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
+    m = BlockSparseDeltaMemory(cfg, seed=2).to(torch.bfloat16).to(DEV)
+    prefix = torch.randn(16, 40, 256).to(torch.bfloat16).to(DEV)
+    toks = torch.randn(5, 16, 1, 256).to(torch.bfloat16).to(DEV)
+    with torch.inference_mode():
+        _, state = m.prefill(prefix)
+        eager_state = state.clone()
+        run = m.capture_step(state)
+        assert torch.equal(state, eager_state), 'capturing must not advance the cache'
+        for i in range(5):
+            y_graph = run(toks[i]).clone()
+            y_eager, _ = m.step(toks[i], eager_state)
+            assert torch.equal(y_graph, y_eager), i
+            assert torch.equal(state, eager_state), i
