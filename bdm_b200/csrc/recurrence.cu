@@ -54,8 +54,19 @@ struct ScanParams {
     void *cache;
     int cache_dtype, store_final, interval;
     void *reads;
-    int64_t units;
+    int64_t units;        // (sequence, head, column tile) units when every sequence runs
+    // Work list: non-empty sequences grouped by length class, longest class first.
+    const int *lists;     // kLenClasses lists of capacity nseq
+    const int *counts;    // [kLenClasses] list lengths
+    unsigned long long *next;  // dynamic work counter (zero at launch)
+    int64_t nseq;
 };
+
+// Length classes of the work list (events per sequence, lower bounds), longest first.
+// Inside a class sequences keep ascending (batch, bank) order, so warps running
+// at the same time mostly read the same batch row's token rows (L2 locality).
+constexpr int kLenClasses = 4;
+__device__ __constant__ int kLenLower[kLenClasses] = {8192, 2048, 512, 1};
 
 template <int BYTES> struct VecOf;
 template <> struct VecOf<4> { using type = uint32_t; };
@@ -198,18 +209,35 @@ bank_scan_kernel(const ScanParams p) {
 
     const int warp = threadIdx.x >> 5;
     const int lane = (int)lane_id();
-    const int64_t unit = (int64_t)blockIdx.x * kScanWarps + warp;
-    if (unit >= p.units) return;  // warp-uniform
     float2(*ctl)[Ctl::size] = ctl_all[warp];
     float2 *dend = dend_all[warp];
     unsigned char(*raw)[Raw::size] = raw_all[warp];
     int *tok_s = tok_all[warp];
     int *rid_s = rid_all[warp];
-
     const int64_t per_seq = (int64_t)p.H * p.ctiles;
-    const int64_t seq = unit / per_seq;
-    const int hh = (int)((unit % per_seq) / p.ctiles);
-    const int ct = (int)(unit % p.ctiles);
+    int64_t total = 0;
+#pragma unroll
+    for (int c = 0; c < kLenClasses; ++c) total += p.counts[c];
+    total *= per_seq;
+
+    // Persistent CTAs take kScanWarps consecutive (sequence, head, column tile)
+    // units at a time, so the warps of a CTA work on the heads of one sequence
+    // and share its control rows in L1.
+    __shared__ unsigned long long item_s;
+    for (;;) {
+    __syncthreads();
+    if (threadIdx.x == 0) item_s = atomicAdd(p.next, 1ull);
+    __syncthreads();
+    const int64_t item = (int64_t)item_s * kScanWarps + warp;
+    if ((int64_t)item_s * kScanWarps >= total) break;  // CTA-uniform
+    if (item >= total) continue;
+    int64_t local = (int64_t)item / per_seq;
+    int cls = 0;
+    while (cls < kLenClasses - 1 && local >= p.counts[cls]) local -= p.counts[cls++];
+    const int64_t seq = p.lists[(int64_t)cls * p.nseq + local];
+    const int64_t rem = (int64_t)item % per_seq;
+    const int hh = (int)(rem / p.ctiles);
+    const int ct = (int)(rem % p.ctiles);
     const int64_t bidx = seq / p.J, bank = seq % p.J;
     const int col0 = ct * 32 * NC + lane * NC;
     const bool active = col0 < p.dv;
@@ -497,6 +525,69 @@ bank_scan_kernel(const ScanParams p) {
                 else store_pair<float>(static_cast<float *>(p.cache) + o, N[s][j]);
             }
     }
+    __syncwarp();  // staging buffers are reused by the next unit
+    }
+}
+
+// Work list: every non-empty sequence goes to the list of its length class, in
+// ascending sequence order (one CTA: per-thread contiguous chunks + block scans).
+constexpr int kListThreads = 1024;
+
+__device__ __forceinline__ int len_class(const int64_t *cu, int64_t s, int64_t E) {
+    const int64_t a = min(max(cu[s], (int64_t)0), E), b = min(max(cu[s + 1], a), E);
+    const int64_t len = b - a;
+    if (len <= 0) return -1;
+    int c = 0;
+    while (c < kLenClasses - 1 && len < kLenLower[c]) ++c;
+    return c;
+}
+
+__global__ void __launch_bounds__(kListThreads)
+build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int *__restrict__ lists,
+               int *__restrict__ counts) {
+    __shared__ int warp_tot[kLenClasses][32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t chunk = (nseq + kListThreads - 1) / kListThreads;
+    const int64_t lo = min((int64_t)tid * chunk, nseq), hi = min(lo + chunk, nseq);
+    int cnt[kLenClasses] = {0, 0, 0, 0};
+    for (int64_t s = lo; s < hi; ++s) {
+        const int c = len_class(cu, s, E);
+        if (c >= 0) ++cnt[c];
+    }
+    int off[kLenClasses];
+#pragma unroll
+    for (int c = 0; c < kLenClasses; ++c) {  // exclusive scan of cnt[c] over threads
+        int x = cnt[c];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, d);
+            if (lane >= d) x += y;
+        }
+        if (lane == 31) warp_tot[c][warp] = x;
+        off[c] = x - cnt[c];
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int c = 0; c < kLenClasses; ++c) {
+            const int t = warp_tot[c][lane];
+            int x = t;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, d);
+                if (lane >= d) x += y;
+            }
+            warp_tot[c][lane] = x - t;
+            if (lane == 31) counts[c] = x;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < kLenClasses; ++c) off[c] += warp_tot[c][warp];
+    for (int64_t s = lo; s < hi; ++s) {
+        const int c = len_class(cu, s, E);
+        if (c >= 0) lists[(int64_t)c * nseq + off[c]++] = (int)s;
+    }
 }
 
 template <typename T, int S, int NC>
@@ -505,8 +596,16 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     q.ctiles = (int)ceil_div(p.dv, 32 * NC);
     q.units = p.batch * p.J * p.H * q.ctiles;
     if (q.units == 0) return BDM_OK;
-    const int64_t blocks = ceil_div(q.units, kScanWarps);
-    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    int dev = 0, sms = kNumSMs, per_sm = 1;
+    int rc = cuda_status(cudaGetDevice(&dev));
+    if (rc) return rc;
+    rc = cuda_status(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (rc) return rc;
+    rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bank_scan_kernel<T, S, NC>,
+                                                                   kScanWarps * 32, 0));
+    if (rc) return rc;
+    const int64_t want = ceil_div(q.units, kScanWarps);
+    const int64_t blocks = min((int64_t)sms * (per_sm > 0 ? per_sm : 1), want);
     bank_scan_kernel<T, S, NC><<<(unsigned)blocks, kScanWarps * 32, 0, st>>>(q);
     return launch_status();
 }
@@ -525,13 +624,27 @@ int launch_scan_shape(const ScanParams &p, int S, cudaStream_t st) {
 }  // namespace
 }  // namespace bdm
 
+namespace bdm {
+namespace {
+// Workspace: [counts (kLenClasses int32) | dynamic counter (uint64)] then the lists.
+constexpr int64_t kWsHeader = 256;
+inline int64_t scan_workspace_bytes(int64_t nseq) { return kWsHeader + (int64_t)kLenClasses * nseq * 4; }
+}  // namespace
+}  // namespace bdm
+
+extern "C" int64_t bdm_bank_scan_workspace_bytes(int64_t batch, int64_t bank_count) {
+    if (batch <= 0 || bank_count <= 0) return -1;
+    return bdm::scan_workspace_bytes(batch * bank_count);
+}
+
 extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
                              const int64_t *write_idx, const void *write_w, const int64_t *read_idx,
                              const void *read_w, const int64_t *order, const int64_t *cu_seqlens, int64_t batch,
                              int64_t time, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw,
                              int kr, int dtype, int routed_decay, float scale, const void *row_factor,
                              const void *col_factor, int64_t factor_cols, int factor_dtype, void *cache,
-                             int cache_dtype, int store_final, int state_interval, void *reads, void *stream) {
+                             int cache_dtype, int store_final, int state_interval, void *reads, void *workspace,
+                             int64_t workspace_bytes, void *stream) {
     using namespace bdm;
     if (batch <= 0 || time <= 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0)
         return BDM_ERR_INVALID;
@@ -543,10 +656,13 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     if (state_interval < 0 || (store_final && !cache)) return BDM_ERR_INVALID;
     if (!valid_dtype(dtype) || (cache && !valid_dtype(cache_dtype))) return BDM_ERR_DTYPE;
     if (batch * time * (int64_t)(kw + kr) >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
+    if (batch * bank_count >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
     if (!cache && row_factor) {
         if (!col_factor || factor_cols <= 0 || !valid_dtype(factor_dtype)) return BDM_ERR_INVALID;
         if ((bank_count * heads * bank_size) % factor_cols) return BDM_ERR_INVALID;
     }
+    const int64_t nseq = batch * bank_count;
+    if (!workspace || workspace_bytes < scan_workspace_bytes(nseq)) return BDM_ERR_WORKSPACE;
     ScanParams p{};
     p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w;
     p.wi = write_idx; p.ri = read_idx; p.ww = write_w; p.rw = read_w;
@@ -560,7 +676,19 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
     p.cache = cache; p.cache_dtype = cache_dtype; p.store_final = store_final; p.interval = state_interval;
     p.reads = reads;
+    char *ws = static_cast<char *>(workspace);
+    int *counts = reinterpret_cast<int *>(ws);
+    int *lists = reinterpret_cast<int *>(ws + kWsHeader);
+    p.counts = counts;
+    p.next = reinterpret_cast<unsigned long long *>(ws + 64);
+    p.lists = lists;
+    p.nseq = nseq;
     cudaStream_t st = as_stream(stream);
+    int rc = cuda_status(cudaMemsetAsync(workspace, 0, kWsHeader, st));
+    if (rc) return rc;
+    build_worklist<<<1, kListThreads, 0, st>>>(cu_seqlens, nseq, p.E, lists, counts);
+    rc = launch_status();
+    if (rc) return rc;
     BDM_DISPATCH_DTYPE(dtype, T, { return launch_scan_shape<T>(p, bank_size, st); });
     return BDM_OK;
 }

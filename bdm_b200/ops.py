@@ -180,12 +180,15 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         u, z = row_factor.detach().contiguous(), col_factor.detach().contiguous()
     # keep contiguous copies alive across the asynchronous call
     wi, ww, ri, rw = (t.contiguous() for t in (write_idx, write_w, read_idx, read_w))
-    _lib.check(_lib.load().bdm_bank_scan(
+    lib = _lib.load()
+    nbytes = lib.bdm_bank_scan_workspace_bytes(batch, bank_count)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    _lib.check(lib.bdm_bank_scan(
         _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(wi), _ptr(ww), _ptr(ri), _ptr(rw), _ptr(order),
         _ptr(cu_seqlens), batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt),
         int(routed_decay), float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
         dtype_code(u.dtype) if u is not None else 0, _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
-        int(store_final), int(state_interval), _ptr(reads), _stream(q.device)), 'bdm_bank_scan')
+        int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _stream(q.device)), 'bdm_bank_scan')
     return reads
 
 

@@ -39,6 +39,10 @@ C2 = dict(dim=1024, bank_count=256, bank_size=8, selected_banks=8, value_width=1
 C2_BATCH, C2_TIME, C2_CHUNK = 8, 4096, 64
 C3 = dict(dim=1024, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
 C3_BATCH, C3_PREFIX, C3_STEPS = 64, 2048, 1024
+C4 = dict(dim=2048, bank_count=16384, bank_size=16, selected_banks=16, value_width=2048, num_heads=16)
+C4_BATCH, C4_TIME, C4_ZIPF = 16, 8192, 1.1
+C4_METRIC = ('BDM layer prefill tokens/sec, bank-sharded large memory (c4: batch 16 x seq 8192, d_model 2048, '
+             'H=16, J=16384, S=16, B=16, d_v=128, Zipf(1.1) bank popularity)')
 METRIC = 'BDM layer prefill tokens/sec (c2: batch 8 x seq 4096, d_model 1024, H=8, J=256, S=8, B=8, d_v=128)'
 
 
@@ -65,6 +69,30 @@ def c3_bytes_per_token(cfg=C3, batch=C3_BATCH, weight_bytes=0):
     """Decode bytes per token: 3*B*H*S*dv*2 (write tiles in+out, read tiles) + 2*D*2 + weights/batch."""
     B, H, S, V = cfg['selected_banks'], cfg['num_heads'], cfg['bank_size'], cfg['value_width']
     return 3 * B * H * S * (V // H) * 2 + 2 * cfg['dim'] * 2 + weight_bytes / batch
+
+
+def zipf_router_bias(layer, exponent=C4_ZIPF, seed=3):
+    """Add log Zipf(exponent) popularity to each product-key factor's routing bias.
+
+    Each factor's entries get Zipf ranks through a seeded permutation, so bank
+    popularity is p1(row) * p2(col); the bias goes on the shared router base,
+    i.e. on both the read and the write router.
+    """
+    j1, j2 = layer.factors
+    gen = torch.Generator().manual_seed(seed)
+    bias = []
+    for width in (j1, j2):
+        ranks = torch.randperm(width, generator=gen).double() + 1.0
+        pmf = ranks.pow(-exponent)
+        bias.append((pmf / pmf.sum()).log())
+    with torch.no_grad():
+        b = layer.shared_router.base.bias
+        b.add_(torch.cat(bias).to(b.dtype).to(b.device))
+    layer._fused_cache = None
+
+
+def c4_bytes_per_token(cfg=C4, batch=C4_BATCH, time_=C4_TIME):
+    return c2_bytes_per_token(cfg, batch, time_)
 
 
 def load_peaks():

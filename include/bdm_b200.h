@@ -150,15 +150,19 @@ BDM_API int bdm_product_state(const void *row_factor, const void *col_factor, in
  * state_interval-th event of a sequence and rounds the initial state
  * (gdn2_banks.py:33-36); 0 keeps FP32 throughout (prefill).
  * store_final writes the final state into `cache` (cache must be non-NULL).
+ * workspace: device scratch of bdm_bank_scan_workspace_bytes(batch, bank_count)
+ * bytes (the per-launch work list: non-empty sequences by length class, so
+ * long sequences start first and empty ones cost nothing).
  * Supported: bank_size in {4, 8, 16}; head_value_width a multiple of 8.
  */
+BDM_API int64_t bdm_bank_scan_workspace_bytes(int64_t batch, int64_t bank_count);
 BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
-                  const int64_t *write_idx, const void *write_w, const int64_t *read_idx, const void *read_w,
-                  const int64_t *order, const int64_t *cu_seqlens, int64_t batch, int64_t time, int64_t bank_count,
-                  int heads, int bank_size, int head_value_width, int kw, int kr, int dtype, int routed_decay,
-                  float scale, const void *row_factor, const void *col_factor, int64_t factor_cols,
-                  int factor_dtype, void *cache, int cache_dtype, int store_final, int state_interval, void *reads,
-                  void *stream);
+                          const int64_t *write_idx, const void *write_w, const int64_t *read_idx, const void *read_w,
+                          const int64_t *order, const int64_t *cu_seqlens, int64_t batch, int64_t time,
+                          int64_t bank_count, int heads, int bank_size, int head_value_width, int kw, int kr,
+                          int dtype, int routed_decay, float scale, const void *row_factor, const void *col_factor,
+                          int64_t factor_cols, int factor_dtype, void *cache, int cache_dtype, int store_final,
+                          int state_interval, void *reads, void *workspace, int64_t workspace_bytes, void *stream);
 
 /*
  * Read combine + output normalisation + sigmoid gate.  Replaces
