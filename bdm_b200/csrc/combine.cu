@@ -5,6 +5,11 @@
 // _project_bank_output (_parameters.py:222-232).  The KR read rows of a token
 // are summed in ascending bank order -- the packed (bank) order the reference
 // visits -- then LayerNorm (or RMS), then times dtype(sigmoid(gate)).
+//
+// Bank-sharded forward: bdm_combine_partial sums, per token, only the read rows
+// of banks this rank owns (FP32, ascending bank order); the ranks' partials are
+// summed by a reduce-scatter, and bdm_norm_gate_f32 rounds that FP32 sum once to
+// the activation dtype (the forward's round-once combine) before norm and gate.
 #include "common.cuh"
 
 namespace bdm {
@@ -33,6 +38,30 @@ __device__ __forceinline__ void load8(const T *p, float *x, int64_t n_valid, boo
     for (int i = 0; i < kCols; ++i) x[i] = i < n_valid ? Elem<T>::to_float(p[i]) : 0.f;
 }
 
+__device__ __forceinline__ void load8f(const float *p, float *x, int64_t n_valid, bool vec) {
+    if (vec && n_valid >= 8) {
+        const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < kCols; ++i) x[i] = i < n_valid ? p[i] : 0.f;
+}
+
+// slot_at[rank] = the slot of this token's rank-th smallest bank (ties: lower slot).
+__device__ __forceinline__ void bank_order(const int64_t *ri, int64_t t, int kr, int64_t *banks, int *slot_at) {
+    if ((int)threadIdx.x < kr) banks[threadIdx.x] = ri[t * kr + threadIdx.x];
+    __syncthreads();
+    if ((int)threadIdx.x < kr) {
+        const int j = threadIdx.x;
+        const int64_t bj = banks[j];
+        int rank = 0;
+        for (int i = 0; i < kr; ++i) rank += (banks[i] < bj) || (banks[i] == bj && i < j);
+        slot_at[rank] = j;
+    }
+    __syncthreads();
+}
+
 __device__ __forceinline__ float block_sum(float x, float *red) {
     x = warp_sum(x);
     const int warp = threadIdx.x >> 5, lane = (int)lane_id();
@@ -48,24 +77,14 @@ template <typename T>
 __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int64_t *__restrict__ ri, int64_t ntok,
                                          int kr, int64_t width, const T *__restrict__ gate, int64_t ld_gate,
                                          const T *__restrict__ nw, const T *__restrict__ nb, float eps, int norm_mode,
-                                         int round_each, int vec, T *__restrict__ out) {
+                                         int round_each, int vec, T *__restrict__ out,
+                                         const float *__restrict__ combined) {
     __shared__ int64_t banks[kMaxKR];
     __shared__ int slot_at[kMaxKR];
     __shared__ float red[32];
     const int64_t t = blockIdx.x;
     if (t >= ntok) return;
-    if (ri) {
-        if ((int)threadIdx.x < kr) banks[threadIdx.x] = ri[t * kr + threadIdx.x];
-        __syncthreads();
-        if ((int)threadIdx.x < kr) {
-            const int j = threadIdx.x;
-            const int64_t bj = banks[j];
-            int rank = 0;
-            for (int i = 0; i < kr; ++i) rank += (banks[i] < bj) || (banks[i] == bj && i < j);
-            slot_at[rank] = j;
-        }
-        __syncthreads();
-    }
+    if (ri) bank_order(ri, t, kr, banks, slot_at);
     const int64_t c0 = (int64_t)threadIdx.x * kCols;
     float x[kCols];
 #pragma unroll
@@ -96,6 +115,10 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
 #pragma unroll
                 for (int i = 0; i < kCols; ++i) x[i] = rnd<T>(x[i]);
             }
+        } else if (combined) {
+            load8f(combined + t * width + c0, x, nv, vec);
+#pragma unroll
+            for (int i = 0; i < kCols; ++i) x[i] = rnd<T>(x[i]);
         } else {
             load8<T>(reads + t * width + c0, x, nv, vec);
         }
@@ -162,6 +185,48 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
     }
 }
 
+// Per token: FP32 sum, in ascending bank order, of the read rows whose bank this
+// rank owns; zero when it owns none of them.
+template <typename T>
+__global__ void combine_partial_kernel(const T *__restrict__ reads, const int64_t *__restrict__ ri, int64_t ntok,
+                                       int kr, int64_t width, const int32_t *__restrict__ owner, int64_t J, int rank,
+                                       int vec, float *__restrict__ out) {
+    __shared__ int64_t banks[kMaxKR];
+    __shared__ int slot_at[kMaxKR];
+    const int64_t t = blockIdx.x;
+    if (t >= ntok) return;
+    bank_order(ri, t, kr, banks, slot_at);
+    const int64_t c0 = (int64_t)threadIdx.x * kCols;
+    if (c0 >= width) return;
+    const int64_t nv = width - c0;
+    float x[kCols];
+#pragma unroll
+    for (int i = 0; i < kCols; ++i) x[i] = 0.f;
+    for (int r = 0; r < kr; ++r) {
+        const int slot = slot_at[r];
+        int64_t bank = banks[slot];
+        bank = bank < 0 ? 0 : (bank >= J ? J - 1 : bank);
+        if (owner[bank] != rank) continue;
+        float y[kCols];
+        load8<T>(reads + (t * kr + slot) * width + c0, y, nv, vec);
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) x[i] += y[i];
+    }
+    float *orow = out + t * width + c0;
+    if (vec && nv >= 8) {
+        *reinterpret_cast<float4 *>(orow) = make_float4(x[0], x[1], x[2], x[3]);
+        *reinterpret_cast<float4 *>(orow + 4) = make_float4(x[4], x[5], x[6], x[7]);
+    } else {
+        for (int i = 0; i < kCols && i < nv; ++i) orow[i] = x[i];
+    }
+}
+
+int combine_threads(int64_t width, int64_t &threads) {
+    threads = ceil_div(ceil_div(width, kCols), 32) * 32;
+    if (threads < 64) threads = 64;
+    return threads > 1024 ? BDM_ERR_UNSUPPORTED : BDM_OK;
+}
+
 }  // namespace
 }  // namespace bdm
 
@@ -174,9 +239,8 @@ extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx,
     if (ntok == 0) return BDM_OK;
     if (!reads || !gate || !norm_weight || !out) return BDM_ERR_INVALID;
     if (norm_mode != 0 && norm_mode != 1) return BDM_ERR_INVALID;
-    int64_t threads = ceil_div(ceil_div(width, kCols), 32) * 32;
-    if (threads < 64) threads = 64;
-    if (threads > 1024) return BDM_ERR_UNSUPPORTED;
+    int64_t threads = 0;
+    if (combine_threads(width, threads)) return BDM_ERR_UNSUPPORTED;
     if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
     const uintptr_t mis =
         (reinterpret_cast<uintptr_t>(reads) | reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(out)) & 15;
@@ -185,7 +249,50 @@ extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx,
         combine_norm_gate_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
             static_cast<const T *>(reads), read_idx, ntok, read_idx ? kr : 1, width, static_cast<const T *>(gate),
             ld_gate, static_cast<const T *>(norm_weight), static_cast<const T *>(norm_bias), eps, norm_mode,
-            round_each, vec, static_cast<T *>(out));
+            round_each, vec, static_cast<T *>(out), nullptr);
+    });
+    return launch_status();
+}
+
+extern "C" int bdm_combine_partial(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                   const int32_t *owner, int64_t bank_count, int rank, int dtype, float *out,
+                                   void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || width <= 0 || bank_count <= 0 || rank < 0) return BDM_ERR_INVALID;
+    if (kr <= 0 || kr > kMaxKR) return BDM_ERR_UNSUPPORTED;
+    if (ntok == 0) return BDM_OK;
+    if (!reads || !read_idx || !owner || !out) return BDM_ERR_INVALID;
+    int64_t threads = 0;
+    if (combine_threads(width, threads)) return BDM_ERR_UNSUPPORTED;
+    if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    const uintptr_t mis = (reinterpret_cast<uintptr_t>(reads) | reinterpret_cast<uintptr_t>(out)) & 15;
+    const int vec = !mis && width % 8 == 0;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        combine_partial_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
+            static_cast<const T *>(reads), read_idx, ntok, kr, width, owner, bank_count, rank, vec, out);
+    });
+    return launch_status();
+}
+
+extern "C" int bdm_norm_gate_f32(const float *combined, int64_t ntok, int64_t width, const void *gate,
+                                 int64_t ld_gate, const void *norm_weight, const void *norm_bias, float eps,
+                                 int norm_mode, int dtype, void *out, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || width <= 0 || ld_gate < width) return BDM_ERR_INVALID;
+    if (ntok == 0) return BDM_OK;
+    if (!combined || !gate || !norm_weight || !out) return BDM_ERR_INVALID;
+    if (norm_mode != 0 && norm_mode != 1) return BDM_ERR_INVALID;
+    int64_t threads = 0;
+    if (combine_threads(width, threads)) return BDM_ERR_UNSUPPORTED;
+    if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    const uintptr_t mis = (reinterpret_cast<uintptr_t>(combined) | reinterpret_cast<uintptr_t>(gate) |
+                           reinterpret_cast<uintptr_t>(out)) & 15;
+    const int vec = !mis && width % 8 == 0 && ld_gate % 8 == 0;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        combine_norm_gate_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
+            nullptr, nullptr, ntok, 1, width, static_cast<const T *>(gate), ld_gate,
+            static_cast<const T *>(norm_weight), static_cast<const T *>(norm_bias), eps, norm_mode, 0, vec,
+            static_cast<T *>(out), combined);
     });
     return launch_status();
 }

@@ -12,6 +12,11 @@
 //              offsets, then a stable scatter ranked with match_any/popc
 // cu_seqlens comes from a lower-bound search per sequence over the sorted
 // sequence ids (the reference's _bounds, role_bank_dispatch.py:27-38).
+//
+// Bank-sharded ranks sort with an ownership map instead: an event whose bank
+// this rank owns gets the sequence id b*J_local + slot(bank); every other event
+// gets the id one past the last sequence, so it sorts after all owned events
+// and cu_seqlens[B*J_local] is the owned event count.
 #include "common.cuh"
 
 namespace bdm {
@@ -35,6 +40,11 @@ struct EventSource {
     int64_t nt, time, J;
     int kw, kr;
     int32_t *err;
+    // Optional ownership map: owner[bank] == rank selects the event, slot[bank] is
+    // its local bank; unselected events get sequence id `sentinel`.
+    const int32_t *owner, *slot;
+    int rank;
+    int64_t local_banks, sentinel;
     __device__ __forceinline__ void get(int64_t i, uint32_t &seq, uint32_t &id, bool count_errors) const {
         const int per = kw + kr;
         int64_t tok = i / per;
@@ -51,7 +61,16 @@ struct EventSource {
             if (count_errors && err) atomicAdd(err, 1);
             bank = bank < 0 ? 0 : J - 1;  // keep the output a permutation
         }
-        seq = (uint32_t)((tok / time) * J + bank);
+        if (owner) {
+            int64_t l = owner[bank] == rank ? (int64_t)slot[bank] : -1;
+            if (l >= local_banks) {
+                if (count_errors && err) atomicAdd(err, 1);
+                l = -1;
+            }
+            seq = (uint32_t)(l < 0 ? sentinel : (tok / time) * local_banks + l);
+        } else {
+            seq = (uint32_t)((tok / time) * J + bank);
+        }
     }
 };
 
@@ -287,13 +306,14 @@ inline int64_t align256(int64_t x) { return (x + 255) & ~(int64_t)255; }
 
 // Workspace: final sorted sequence ids, two ping-pong (key, id) buffers for
 // intermediate passes, the digit-major tile table and the scan block sums.
-Plan make_plan(int64_t batch, int64_t time, int kw, int kr, int64_t J) {
+// With `sentinel` the sort also carries the id nseq (events of other ranks).
+Plan make_plan(int64_t batch, int64_t time, int kw, int kr, int64_t J, bool sentinel = false) {
     Plan p{};
     p.E = batch * time * (int64_t)(kw + kr);
     p.nseq = batch * J;
     p.tiles = ceil_div(p.E > 0 ? p.E : 1, kTile);
     int bits = 0;
-    while (bits < 32 && ((int64_t)1 << bits) < p.nseq) ++bits;
+    while (bits < 32 && ((int64_t)1 << bits) < p.nseq + (sentinel ? 1 : 0)) ++bits;
     if (bits == 0) bits = 1;
     p.bits = bits;
     p.passes = (bits + kMaxRadixBits - 1) / kMaxRadixBits;
@@ -345,18 +365,21 @@ extern "C" int64_t bdm_dispatch_workspace_bytes(int64_t batch, int64_t time, int
     return bdm::make_plan(batch, time, kw, kr, bank_count).bytes;
 }
 
-extern "C" int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time, int kw,
-                            int kr, int64_t bank_count, int64_t *order, int64_t *cu_seqlens, int64_t *inverse,
-                            int64_t *tokens, int32_t *error_word, void *workspace, int64_t workspace_bytes,
-                            void *stream) {
-    using namespace bdm;
-    if (batch <= 0 || time <= 0 || kw <= 0 || kr <= 0 || bank_count <= 0) return BDM_ERR_INVALID;
-    if (!write_idx || !read_idx || !order || !cu_seqlens) return BDM_ERR_INVALID;
-    Plan p = make_plan(batch, time, kw, kr, bank_count);
-    if (p.E >= ((int64_t)1 << 32) - 1 || p.nseq >= ((int64_t)1 << 32) - 1) return BDM_ERR_UNSUPPORTED;
+namespace bdm {
+namespace {
+
+// owner == nullptr: plain dispatch over bank_count banks; otherwise only the
+// events of banks with owner[bank] == rank, as local_banks sequences per batch row.
+int dispatch_impl(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time, int kw, int kr,
+                  int64_t bank_count, const int32_t *owner, const int32_t *slot, int rank, int64_t local_banks,
+                  int64_t *order, int64_t *cu_seqlens, int64_t *inverse, int64_t *tokens, int32_t *error_word,
+                  void *workspace, int64_t workspace_bytes, cudaStream_t st) {
+    const bool owned = owner != nullptr;
+    const int64_t seq_banks = owned ? local_banks : bank_count;
+    Plan p = make_plan(batch, time, kw, kr, seq_banks, owned);
+    if (p.E >= ((int64_t)1 << 32) - 1 || p.nseq >= ((int64_t)1 << 32) - 2) return BDM_ERR_UNSUPPORTED;
     if (p.table > kScanMax) return BDM_ERR_UNSUPPORTED;
     if (!workspace || workspace_bytes < p.bytes) return BDM_ERR_WORKSPACE;
-    cudaStream_t st = as_stream(stream);
     char *ws = static_cast<char *>(workspace);
     uint32_t *final_keys = reinterpret_cast<uint32_t *>(ws + p.off_final);
     uint32_t *buf_k[2] = {reinterpret_cast<uint32_t *>(ws + p.off_ak), reinterpret_cast<uint32_t *>(ws + p.off_bk)};
@@ -365,7 +388,8 @@ extern "C" int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, i
     uint32_t *sums = reinterpret_cast<uint32_t *>(ws + p.off_sums);
 
     const int64_t nt = batch * time;
-    EventSource src0{write_idx, read_idx, nt, time, bank_count, kw, kr, error_word};
+    EventSource src0{write_idx, read_idx, nt, time, bank_count, kw, kr, error_word,
+                     owner, slot, rank, local_banks, p.nseq};
     FinalSink fin{final_keys, order, inverse, tokens, nt * kw, kw, kr};
     // Pass k (k < passes-1) writes buffer k%2; pass k > 0 reads buffer (k-1)%2;
     // the last pass writes the outputs.
@@ -388,6 +412,39 @@ extern "C" int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, i
     if (blocks > 64 * kNumSMs) blocks = 64 * kNumSMs;
     seq_bounds<<<(unsigned)blocks, 256, 0, st>>>(final_keys, p.E, p.nseq, cu_seqlens);
     return launch_status();
+}
+
+}  // namespace
+}  // namespace bdm
+
+extern "C" int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time, int kw,
+                            int kr, int64_t bank_count, int64_t *order, int64_t *cu_seqlens, int64_t *inverse,
+                            int64_t *tokens, int32_t *error_word, void *workspace, int64_t workspace_bytes,
+                            void *stream) {
+    using namespace bdm;
+    if (batch <= 0 || time <= 0 || kw <= 0 || kr <= 0 || bank_count <= 0) return BDM_ERR_INVALID;
+    if (!write_idx || !read_idx || !order || !cu_seqlens) return BDM_ERR_INVALID;
+    return dispatch_impl(write_idx, read_idx, batch, time, kw, kr, bank_count, nullptr, nullptr, 0, 0, order,
+                         cu_seqlens, inverse, tokens, error_word, workspace, workspace_bytes, as_stream(stream));
+}
+
+extern "C" int64_t bdm_dispatch_owned_workspace_bytes(int64_t batch, int64_t time, int kw, int kr,
+                                                      int64_t local_banks) {
+    if (batch <= 0 || time <= 0 || kw <= 0 || kr <= 0 || local_banks <= 0) return -1;
+    return bdm::make_plan(batch, time, kw, kr, local_banks, true).bytes;
+}
+
+extern "C" int bdm_dispatch_owned(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time,
+                                  int kw, int kr, int64_t bank_count, const int32_t *owner, const int32_t *slot,
+                                  int rank, int64_t local_banks, int64_t *order, int64_t *cu_seqlens,
+                                  int64_t *inverse, int64_t *tokens, int32_t *error_word, void *workspace,
+                                  int64_t workspace_bytes, void *stream) {
+    using namespace bdm;
+    if (batch <= 0 || time <= 0 || kw <= 0 || kr <= 0 || bank_count <= 0 || local_banks <= 0 || rank < 0)
+        return BDM_ERR_INVALID;
+    if (!write_idx || !read_idx || !owner || !slot || !order || !cu_seqlens) return BDM_ERR_INVALID;
+    return dispatch_impl(write_idx, read_idx, batch, time, kw, kr, bank_count, owner, slot, rank, local_banks, order,
+                         cu_seqlens, inverse, tokens, error_word, workspace, workspace_bytes, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------

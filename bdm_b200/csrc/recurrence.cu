@@ -51,6 +51,8 @@ struct ScanParams {
     const void *row_factor, *col_factor;
     int64_t factor_cols;
     int factor_dtype;
+    const int32_t *bank_ids;  // local bank -> bank of the full table (bank-sharded ranks), or null
+    int64_t total_banks;
     void *cache;
     int cache_dtype, store_final, interval;
     void *reads;
@@ -272,9 +274,14 @@ bank_scan_kernel(const ScanParams p) {
                                                         : load_pair<float>(static_cast<const float *>(p.cache) + o);
                 }
         } else if (p.row_factor) {
+            int64_t gbank = bank;
+            if (p.bank_ids) {
+                gbank = p.bank_ids[bank];
+                gbank = gbank < 0 ? 0 : (gbank >= p.total_banks ? p.total_banks - 1 : gbank);
+            }
 #pragma unroll
             for (int s = 0; s < S; ++s) {
-                const int64_t r = (bank * p.H + hh) * S + s;
+                const int64_t r = (gbank * p.H + hh) * S + s;
                 const int64_t ou = (r / p.factor_cols) * p.dv + col0, oz = (r % p.factor_cols) * p.dv + col0;
 #pragma unroll
                 for (int j = 0; j < NP; ++j) {
@@ -642,8 +649,9 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
                              const void *read_w, const int64_t *order, const int64_t *cu_seqlens, int64_t batch,
                              int64_t time, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw,
                              int kr, int dtype, int routed_decay, float scale, const void *row_factor,
-                             const void *col_factor, int64_t factor_cols, int factor_dtype, void *cache,
-                             int cache_dtype, int store_final, int state_interval, void *reads, void *workspace,
+                             const void *col_factor, int64_t factor_cols, int factor_dtype,
+                             const int32_t *bank_ids, int64_t total_banks, void *cache, int cache_dtype,
+                             int store_final, int state_interval, void *reads, void *workspace,
                              int64_t workspace_bytes, void *stream) {
     using namespace bdm;
     if (batch <= 0 || time <= 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0)
@@ -657,9 +665,11 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     if (!valid_dtype(dtype) || (cache && !valid_dtype(cache_dtype))) return BDM_ERR_DTYPE;
     if (batch * time * (int64_t)(kw + kr) >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
     if (batch * bank_count >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
+    if (bank_ids && total_banks < bank_count) return BDM_ERR_INVALID;
+    const int64_t table_banks = bank_ids ? total_banks : bank_count;
     if (!cache && row_factor) {
         if (!col_factor || factor_cols <= 0 || !valid_dtype(factor_dtype)) return BDM_ERR_INVALID;
-        if ((bank_count * heads * bank_size) % factor_cols) return BDM_ERR_INVALID;
+        if ((table_banks * heads * bank_size) % factor_cols) return BDM_ERR_INVALID;
     }
     const int64_t nseq = batch * bank_count;
     if (!workspace || workspace_bytes < scan_workspace_bytes(nseq)) return BDM_ERR_WORKSPACE;
@@ -674,6 +684,7 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.row_factor = cache ? nullptr : row_factor;
     p.col_factor = cache ? nullptr : col_factor;
     p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
+    p.bank_ids = bank_ids; p.total_banks = table_banks;
     p.cache = cache; p.cache_dtype = cache_dtype; p.store_final = store_final; p.interval = state_interval;
     p.reads = reads;
     char *ws = static_cast<char *>(workspace);

@@ -12,6 +12,8 @@ Reference interfaces each op replaces (p0rc314in/bdm, implementation/bdm/):
   bank_scan        routed_update.py:16-32, role_bank_kernel.py:177-202, inference.py:134-158
   combine_norm_gate role_bank_dispatch.py:219-231, _parameters.py:222-232
   decode_step      inference.py:161-194
+Bank-sharded forward (no reference counterpart; the reference runs on one device):
+  bank_histogram, bank_owners, dispatch_owned, combine_partial, norm_gate_f32
 """
 from __future__ import annotations
 
@@ -153,14 +155,20 @@ def product_state(row_factor, col_factor, *, batch: int, bank_count: int, heads:
 
 def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_seqlens, *, batch: int, time: int,
               bank_count: int, heads: int, bank_size: int, head_value_width: int, routed_decay: bool, scale: float,
-              row_factor=None, col_factor=None, cache=None, store_final=False, state_interval=0):
+              row_factor=None, col_factor=None, cache=None, store_final=False, state_interval=0,
+              bank_ids=None, total_banks=0):
     """Per-bank recurrence over dispatched events; returns reads [NT, KR, V] in the activation dtype.
 
     With ``cache`` ([batch, J, H, S, dv]) the state starts from it and, with
     ``store_final``, ends in it; otherwise it starts from the product-key factors
-    (or zero when they are None).
+    (or zero when they are None).  On a bank-sharded rank ``bank_count`` is the
+    local bank count and ``bank_ids`` (int32 [bank_count]) maps local banks into
+    the full table of ``total_banks`` banks.
     """
-    _cuda(q, k, v, g, b, w, write_idx, read_idx, order, cu_seqlens, cache)
+    _cuda(q, k, v, g, b, w, write_idx, read_idx, order, cu_seqlens, cache, bank_ids)
+    if bank_ids is not None and (bank_ids.dtype != torch.int32 or bank_ids.numel() != bank_count
+                                 or total_banks < bank_count):
+        raise ValueError('bank_ids must be int32 [bank_count] into a table of total_banks >= bank_count banks')
     dt = q.dtype
     nt = batch * time
     kw, kr = write_idx.shape[-1], read_idx.shape[-1]
@@ -187,7 +195,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(wi), _ptr(ww), _ptr(ri), _ptr(rw), _ptr(order),
         _ptr(cu_seqlens), batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt),
         int(routed_decay), float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
-        dtype_code(u.dtype) if u is not None else 0, _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
+        dtype_code(u.dtype) if u is not None else 0, _ptr(bank_ids), int(total_banks) if bank_ids is not None else 0,
+        _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
         int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _stream(q.device)), 'bdm_bank_scan')
     return reads
 
@@ -235,3 +244,116 @@ def decode_step(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, state, *
         bank_size, head_value_width, kw, kr, dtype_code(q.dtype), int(routed_decay), float(scale), _ptr(state),
         dtype_code(state.dtype), _ptr(raw), _stream(q.device)), 'bdm_decode_step')
     return raw
+
+
+# ------------------------------------------------------------ bank sharding
+
+def bank_histogram(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int,
+                   counts: torch.Tensor | None = None) -> torch.Tensor:
+    """Events per bank (int32 [bank_count]) of routes [..., KW] / [..., KR]; adds into ``counts`` if given."""
+    _cuda(write_idx, read_idx)
+    wi = write_idx.reshape(-1, write_idx.shape[-1]).contiguous()
+    ri = read_idx.reshape(-1, read_idx.shape[-1]).contiguous()
+    if wi.dtype != torch.long or ri.dtype != torch.long or wi.shape[0] != ri.shape[0]:
+        raise ValueError('routes must be int64 with matching token counts')
+    if counts is None:
+        counts = torch.zeros(bank_count, dtype=torch.int32, device=wi.device)
+    elif counts.dtype != torch.int32 or counts.numel() != bank_count or not counts.is_contiguous():
+        raise ValueError('counts must be contiguous int32 [bank_count]')
+    _lib.check(_lib.load().bdm_bank_histogram(_ptr(wi), _ptr(ri), wi.shape[0], wi.shape[1], ri.shape[1], bank_count,
+                                              _ptr(counts), _stream(wi.device)), 'bdm_bank_histogram')
+    return counts
+
+
+OWNERSHIP_MODES = {'contiguous': 0, 'balanced': 1}
+
+
+def bank_owners(counts: torch.Tensor | None, bank_count: int, world: int, *, mode: str = 'balanced',
+                device=None):
+    """Partition of the bank table over ``world`` ranks -> (owner [J], slot [J], members [world, J/world]) int32."""
+    if mode not in OWNERSHIP_MODES:
+        raise ValueError(f'ownership mode must be one of {sorted(OWNERSHIP_MODES)}')
+    if counts is not None:
+        _cuda(counts)
+        if counts.dtype != torch.int32 or counts.numel() != bank_count or not counts.is_contiguous():
+            raise ValueError('counts must be contiguous int32 [bank_count]')
+        device = counts.device
+    elif mode == 'balanced':
+        raise ValueError('the balanced partition needs the per-bank event counts')
+    if world <= 0 or bank_count % world:
+        raise NotImplementedError('the bank count must divide evenly over the ranks')
+    owner = torch.empty(bank_count, dtype=torch.int32, device=device)
+    slot = torch.empty_like(owner)
+    members = torch.empty((world, bank_count // world), dtype=torch.int32, device=device)
+    _lib.check(_lib.load().bdm_bank_owners(_ptr(counts), bank_count, world, OWNERSHIP_MODES[mode], _ptr(owner),
+                                           _ptr(slot), _ptr(members), _stream(owner.device)), 'bdm_bank_owners')
+    return owner, slot, members
+
+
+def dispatch_owned(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int, owner: torch.Tensor,
+                   slot: torch.Tensor, rank: int, local_banks: int):
+    """``dispatch`` of the events whose bank ``rank`` owns, as (batch, local bank) sequences.
+
+    Returns dict(order [E] (owned events first), cu_seqlens [B*local_banks + 1]).
+    """
+    _cuda(write_idx, read_idx, owner, slot)
+    if write_idx.dtype != torch.long or read_idx.dtype != torch.long:
+        raise ValueError('bank indices must be int64')
+    if write_idx.ndim != 3 or read_idx.ndim != 3 or write_idx.shape[:2] != read_idx.shape[:2]:
+        raise ValueError('routes must be [batch, time, banks] with matching batch and time')
+    for name, t in (('owner', owner), ('slot', slot)):
+        if t.dtype != torch.int32 or t.numel() != bank_count or not t.is_contiguous():
+            raise ValueError(f'{name} must be contiguous int32 [bank_count]')
+    batch, time, kw = write_idx.shape
+    kr = read_idx.shape[-1]
+    dev = write_idx.device
+    wi, ri = write_idx.contiguous(), read_idx.contiguous()
+    order = torch.empty(batch * time * (kw + kr), dtype=torch.int64, device=dev)
+    cu = torch.empty(batch * local_banks + 1, dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    nbytes = lib.bdm_dispatch_owned_workspace_bytes(batch, time, kw, kr, local_banks)
+    if nbytes < 0:
+        raise ValueError('invalid dispatch geometry')
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+    _lib.check(lib.bdm_dispatch_owned(_ptr(wi), _ptr(ri), batch, time, kw, kr, bank_count, _ptr(owner), _ptr(slot),
+                                      int(rank), local_banks, _ptr(order), _ptr(cu), None, None, None, _ptr(ws),
+                                      nbytes, _stream(dev)), 'bdm_dispatch_owned')
+    return dict(order=order, cu_seqlens=cu)
+
+
+def combine_partial(reads: torch.Tensor, read_idx: torch.Tensor, owner: torch.Tensor, rank: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """FP32 [NT, V]: per token, the ascending-bank sum of the read rows of banks ``rank`` owns."""
+    _cuda(reads, read_idx, owner)
+    nt, kr, width = reads.shape
+    ri = read_idx.reshape(nt, kr).contiguous()
+    if owner.dtype != torch.int32 or not owner.is_contiguous():
+        raise ValueError('owner must be contiguous int32 [bank_count]')
+    if out is None:
+        out = torch.empty((nt, width), dtype=torch.float32, device=reads.device)
+    elif out.dtype != torch.float32 or tuple(out.shape) != (nt, width) or not out.is_contiguous():
+        raise ValueError(f'out must be contiguous float32 [{nt}, {width}]')
+    rd = reads.contiguous()
+    _lib.check(_lib.load().bdm_combine_partial(_ptr(rd), _ptr(ri), nt, kr, width, _ptr(owner), owner.numel(),
+                                               int(rank), dtype_code(reads.dtype), _ptr(out), _stream(reads.device)),
+               'bdm_combine_partial')
+    return out
+
+
+def norm_gate_f32(combined: torch.Tensor, gate, norm_weight, norm_bias, *, eps: float, layer_norm: bool,
+                  dtype: torch.dtype) -> torch.Tensor:
+    """``combine_norm_gate`` over an FP32 combined read sum [NT, V], rounded once to ``dtype`` first."""
+    _cuda(combined, gate, norm_weight)
+    if combined.dtype != torch.float32 or combined.ndim != 2 or not combined.is_contiguous():
+        raise ValueError('combined must be contiguous float32 [tokens, width]')
+    if gate.stride(-1) != 1:
+        raise ValueError('gate rows must be contiguous')
+    nt, width = combined.shape
+    out = torch.empty((nt, width), dtype=dtype, device=combined.device)
+    nw = norm_weight.detach().to(dtype).contiguous()
+    nb = norm_bias.detach().to(dtype).contiguous() if norm_bias is not None else None
+    _lib.check(_lib.load().bdm_norm_gate_f32(
+        _ptr(combined), nt, width, _ptr(gate), gate.stride(0) if nt > 1 else gate.shape[-1], _ptr(nw), _ptr(nb),
+        float(eps), 1 if layer_norm else 0, dtype_code(dtype), _ptr(out), _stream(combined.device)),
+        'bdm_norm_gate_f32')
+    return out

@@ -1,0 +1,169 @@
+"""Bank-sharded BDM forward: one bank table partitioned over the GPUs of a node.
+
+The reference runs the whole layer on one device (implementation/bdm/model.py:88-140).
+For large memories -- J >= 16K banks, e.g. 16 x 8192 tokens over J = 16384
+banks of 16 x 128 per head, 16 GiB of bank state -- this module splits the
+bank table over R ranks (one process per GPU, ``torch.distributed``):
+
+* tokens are sharded by batch row: rank r holds global rows [r*B/R, (r+1)*B/R)
+  and runs the fused projection, controllers and router on them;
+* the per-bank event counts are all-reduced and every rank derives the same
+  bank partition (``ops.bank_owners``): balanced by load by default, so a
+  Zipf-skewed router does not pile the hot banks onto one rank; contiguous
+  index ranges on request.  Every rank owns J/R banks;
+* the controller records and routes of all tokens are all-gathered.  Under a
+  balanced partition a token's 2*B routed banks land on nearly every rank, so
+  shipping one record per (token, rank) pair would move the same bytes as the
+  all-gather; the all-gather is the MoE-style exchange in its dense form;
+* each rank sorts the events of its own banks (``ops.dispatch_owned``), runs
+  the recurrence over its banks' sequences (``ops.bank_scan`` with local bank
+  ids mapped into the full table for the product-key initial state), and sums,
+  per token, the reads of its banks in ascending bank order (FP32);
+* a reduce-scatter sums the FP32 partials and returns each token's read sum to
+  the rank that holds the token, which rounds it once to the activation dtype
+  (the forward's round-once combine) and applies norm, gate and o_proj.
+
+Results match the single-device forward up to the FP32 summation order of the
+read combine (the partials are added across ranks, not bank by bank).
+Every rank must call ``forward`` with the same [B/R, T, D] shape.
+
+The stages (``local_stage``, ``histogram``, ``owners``, ``bank_stage``,
+``output_stage``) are methods so that the collective choreography in
+``forward`` can be exercised with other stage implementations (the CPU tests
+run it over gloo with the CPU oracle's stages).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch.nn import functional as F
+
+from . import ops
+from .config import state_interval
+
+
+class ShardComm:
+    """The three collectives of the sharded forward over a ``torch.distributed`` group.
+
+    NCCL moves device tensors directly.  With gloo (CPU tests, or several ranks
+    sharing one GPU) device tensors are staged through host memory, and the
+    gather moves raw bytes (gloo has no 16-bit integer or bfloat16 type).
+    """
+
+    def __init__(self, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.host_staged = dist.get_backend(group) == 'gloo'
+
+    def _host(self, t):
+        return t.cpu() if (self.host_staged and t.is_cuda) else t
+
+    def all_reduce_sum_(self, t: torch.Tensor) -> torch.Tensor:
+        h = self._host(t)
+        dist.all_reduce(h, op=dist.ReduceOp.SUM, group=self.group)
+        if h is not t:
+            t.copy_(h)
+        return t
+
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        """[n, ...] on every rank -> [world*n, ...], rank-major."""
+        t = t.contiguous()
+        out = torch.empty((self.world * t.shape[0], *t.shape[1:]), dtype=t.dtype, device=t.device)
+        src, dst = self._host(t), (out.cpu() if (self.host_staged and out.is_cuda) else out)
+        if self.host_staged and t.numel() > 0:
+            dist.all_gather_into_tensor(dst.reshape(self.world, -1).view(torch.uint8),
+                                        src.reshape(1, -1).view(torch.uint8), group=self.group)
+        else:
+            dist.all_gather_into_tensor(dst, src, group=self.group)
+        if dst is not out:
+            out.copy_(dst)
+        return out
+
+    def reduce_scatter_sum(self, t: torch.Tensor) -> torch.Tensor:
+        """[world*n, ...] on every rank -> the sum over ranks of rows [rank*n, (rank+1)*n)."""
+        if t.shape[0] % self.world:
+            raise ValueError('reduce-scatter rows must divide evenly over the ranks')
+        t = t.contiguous()
+        out = torch.empty((t.shape[0] // self.world, *t.shape[1:]), dtype=t.dtype, device=t.device)
+        src, dst = self._host(t), (out.cpu() if (self.host_staged and out.is_cuda) else out)
+        dist.reduce_scatter_tensor(dst, src, op=dist.ReduceOp.SUM, group=self.group)
+        if dst is not out:
+            out.copy_(dst)
+        return out
+
+
+class BankShardedMemory:
+    """Runs ``layer.forward`` with the bank table partitioned over the ranks of ``group``.
+
+    ``layer`` is a ``BankedDeltaMemory`` with identical parameters on every rank
+    (e.g. the same seed).  ``forward(hidden)`` takes this rank's batch rows and
+    returns this rank's output rows.
+    """
+
+    def __init__(self, layer, group=None, *, ownership: str = 'balanced', comm: ShardComm | None = None):
+        if ownership not in ops.OWNERSHIP_MODES:
+            raise ValueError(f'ownership must be one of {sorted(ops.OWNERSHIP_MODES)}')
+        self.layer = layer
+        self.comm = comm or ShardComm(group)
+        self.ownership = ownership
+        self.rank, self.world = self.comm.rank, self.comm.world
+        if layer.bank_count % self.world:
+            raise NotImplementedError(f'{layer.bank_count} banks do not divide over {self.world} ranks')
+        self.local_banks = layer.bank_count // self.world
+        self.last_partition = None  # (owner, slot, members, counts) of the latest call
+
+    # ------------------------------------------------------------ the exchange
+    @torch.no_grad()
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        lay = self.layer
+        lb, time, dim = hidden.shape
+        controls, routes, gate = self.local_stage(hidden)
+        ww, wi, rw, ri = routes
+        counts = self.histogram(wi, ri)
+        self.comm.all_reduce_sum_(counts)
+        owner, slot, members = self.owners(counts)
+        self.last_partition = (owner, slot, members, counts)
+        all_controls = [self.comm.all_gather(c) for c in controls]
+        all_routes = [self.comm.all_gather(r) for r in routes]
+        partial = self.bank_stage(all_controls, all_routes, owner, slot, members, batch=lb * self.world, time=time)
+        combined = self.comm.reduce_scatter_sum(partial)
+        out = self.output_stage(hidden, combined, gate)
+        return out.reshape(lb, time, lay.hidden_size)
+
+    __call__ = forward
+
+    # --------------------------------------------------------------- stages
+    def local_stage(self, hidden):
+        """Projection, controllers and routes of this rank's tokens."""
+        self.layer._check_hidden(hidden)
+        return self.layer._controls_and_routes(hidden)
+
+    def histogram(self, write_idx, read_idx):
+        return ops.bank_histogram(write_idx, read_idx, self.layer.bank_count)
+
+    def owners(self, counts):
+        mode = self.ownership
+        return ops.bank_owners(counts if mode == 'balanced' else None, self.layer.bank_count, self.world, mode=mode,
+                               device=counts.device)
+
+    def bank_stage(self, controls, routes, owner, slot, members, *, batch, time):
+        """Dispatch, recurrence and partial combine of this rank's banks -> FP32 [batch*time, V]."""
+        lay = self.layer
+        ww, wi, rw, ri = routes
+        meta = ops.dispatch_owned(wi, ri, lay.bank_count, owner, slot, self.rank, self.local_banks)
+        interval = state_interval(lay.bank_size) if lay.config.training_state_dtype == 'bfloat16' else 0
+        reads = ops.bank_scan(*controls, wi, ww, ri, rw, meta['order'], meta['cu_seqlens'], batch=batch, time=time,
+                              bank_count=self.local_banks, heads=lay.num_heads, bank_size=lay.bank_size,
+                              head_value_width=lay.head_value_width, routed_decay=lay.config.routed_decay,
+                              scale=lay.bank_size ** -0.5, row_factor=lay.initial_row_factor,
+                              col_factor=lay.initial_column_factor, state_interval=interval,
+                              bank_ids=members[self.rank], total_banks=lay.bank_count)
+        return ops.combine_partial(reads, ri.reshape(batch * time, -1), owner, self.rank)
+
+    def output_stage(self, hidden, combined, gate):
+        lay = self.layer
+        normed = ops.norm_gate_f32(combined, gate, lay.output_norm_weight, getattr(lay, 'output_norm_bias', None),
+                                   eps=lay.norm_eps, layer_norm=lay.config.output_normalization == 'layer',
+                                   dtype=hidden.dtype)
+        return F.linear(normed, lay.o_proj.weight, lay.o_proj.bias)

@@ -1,10 +1,15 @@
-"""Benchmark: BDM layer prefill tokens/s on B200 (BASELINE config c2), plus c3 decode.
+"""Benchmark: BDM layer prefill tokens/s on B200 (BASELINE config c2), plus c3 decode and c4.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs under torchrun, one process per GPU; every rank runs its own
 replica of the c2 workload (batch shards trivially: weak scaling, no
 data-path collective).  Rank 0 prints ONE JSON line.
+
+The line also carries ``c4``: the large-memory prefill (batch 16 x 8192,
+J = 16384 banks, Zipf(1.1) router skew) on all N GPUs at once -- the plain
+layer at N = 1, the bank-sharded forward (bdm_b200.sharded, NCCL all-gather /
+reduce-scatter) at N > 1.  Its total work is fixed, so it scales strongly.
 
 Timed region (value): K forward steps of the public module call
 ``layer(hidden)`` with the input already in HBM; an L2 flush (256 MiB write)
@@ -350,6 +355,11 @@ def run_ours(args, world, rank, local):
             line['decode'] = run_decode(dev, rank, world, args)
         except Exception as e:  # keep the headline line even if the extra workload fails
             line['decode'] = {'error': repr(e)[:300]}
+    if not args.skip_c4:
+        try:
+            line['c4'] = run_c4(dev, rank, world, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['c4'] = {'error': repr(e)[:300]}
     if rank == 0 and world == 1 and not args.skip_cpu:
         tps, dt, threads = cpu_forward_sample(C2_BATCH, args.cpu_time)
         line['cpu_baseline'] = {'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
@@ -406,6 +416,74 @@ def run_decode(dev, rank, world, args):
                          'peak': hbm_peak, 'unit': 'GB/s', 'frac': bpt * tps / world / 1e9 / hbm_peak}}
 
 
+def c4_hidden(rows, dev):
+    """c4 input rows: row b of the global batch is N(0,1) from seed 3000 + b, for any rank count."""
+    out = torch.empty(len(rows), C4_TIME, C4['dim'], dtype=torch.bfloat16, device=dev)
+    for i, b in enumerate(rows):
+        gen = torch.Generator(device=dev).manual_seed(3000 + b)
+        out[i] = torch.randn(C4_TIME, C4['dim'], generator=gen, device=dev).to(torch.bfloat16)
+    return out
+
+
+def run_c4(dev, rank, world, args):
+    """c4 bank-sharded large-memory prefill forward on all ranks together (strong scaling)."""
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, _lib
+    from bdm_b200.sharded import BankShardedMemory
+    if C4_BATCH % world:
+        return {'skipped': f'batch {C4_BATCH} does not split over {world} ranks'}
+    lib = _lib.load()
+    cfg = BSDMConfig(**C4)
+    layer = BlockSparseDeltaMemory(cfg, seed=3).to(torch.bfloat16).to(dev)
+    zipf_router_bias(layer)
+    rows = C4_BATCH // world
+    x = c4_hidden(range(rank * rows, (rank + 1) * rows), dev)
+    fwd = layer if world == 1 else BankShardedMemory(layer, ownership=args.c4_ownership)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    steps = args.c4_steps
+    clocks = ClockSampler(dev.index).start()
+    with torch.inference_mode():
+        for _ in range(2):
+            fwd(x)
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        barrier(world)
+        torch.cuda.synchronize()
+        launches0 = lib.bdm_kernel_launches()
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record()
+            fwd(x)
+            ends[i].record()
+        torch.cuda.synchronize()
+        clocks.stop()
+        launches = lib.bdm_kernel_launches() - launches0
+        barrier(world)
+    ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)), world) / steps
+    tokens = C4_BATCH * C4_TIME
+    hbm_peak, _, peak_kind = load_peaks()
+    _, layer_bytes = c4_bytes_per_token()
+    roof_ms = layer_bytes * tokens / (hbm_peak * 1e9 * world) * 1000
+    out = {'metric': C4_METRIC, 'value': tokens / (ms / 1000), 'unit': 'tokens/s', 'n_gpus': world,
+           'steps': steps, 'warmup': 2, 'ms_per_step': ms, 'scaling': 'strong',
+           'path': 'BlockSparseDeltaMemory.forward' if world == 1 else
+                   f'BankShardedMemory (bank-sharded, {args.c4_ownership} partition, NCCL all-gather/reduce-scatter)',
+           'config': {'workload': 'c4: BSDMConfig(dim=2048, bank_count=16384, bank_size=16, selected_banks=16, '
+                                  'value_width=2048, num_heads=16), seed 3, Zipf(1.1) bias on both router factors',
+                      'global_batch': C4_BATCH, 'seq_len': C4_TIME, 'rows_per_rank': rows,
+                      'l2': 'inputs larger than L2; 256 MiB flush between steps'},
+           'gpu_launches': int(launches),
+           'roofline': {'bound': 'hbm', 'bytes_per_token': layer_bytes, 'peak': hbm_peak, 'peak_source': peak_kind,
+                        'unit': 'GB/s', 'achieved': layer_bytes * tokens / (ms / 1000) / 1e9 / world,
+                        'frac': roof_ms / ms, 'roofline_ms': roof_ms},
+           'clocks': clocks.summary()}
+    if world > 1 and fwd.last_partition is not None:
+        owner, _, _, counts = fwd.last_partition
+        load = torch.zeros(world, dtype=torch.float64, device=dev).index_add_(0, owner.long(), counts.double())
+        out['partition_load_max_over_mean'] = (load.max() / load.mean()).item()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -417,6 +495,9 @@ def main():
     ap.add_argument('--cpu-time', type=int, default=C2_TIME, help='sequence length of the CPU baseline sample')
     ap.add_argument('--skip-decode', action='store_true')
     ap.add_argument('--skip-cpu', action='store_true')
+    ap.add_argument('--skip-c4', action='store_true')
+    ap.add_argument('--c4-steps', type=int, default=5)
+    ap.add_argument('--c4-ownership', choices=('balanced', 'contiguous'), default='balanced')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3

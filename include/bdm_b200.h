@@ -150,6 +150,10 @@ BDM_API int bdm_product_state(const void *row_factor, const void *col_factor, in
  * state_interval-th event of a sequence and rounds the initial state
  * (gdn2_banks.py:33-36); 0 keeps FP32 throughout (prefill).
  * store_final writes the final state into `cache` (cache must be non-NULL).
+ * bank_ids [bank_count] int32 or NULL: on a bank-sharded rank, the sequences are
+ * (batch, local bank) and bank_ids maps a local bank to its bank in the full
+ * table of total_banks banks (used for the product-key initial state); NULL
+ * means local = global and total_banks is ignored.
  * workspace: device scratch of bdm_bank_scan_workspace_bytes(batch, bank_count)
  * bytes (the per-launch work list: non-empty sequences by length class, so
  * long sequences start first and empty ones cost nothing).
@@ -161,8 +165,9 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
                           const int64_t *order, const int64_t *cu_seqlens, int64_t batch, int64_t time,
                           int64_t bank_count, int heads, int bank_size, int head_value_width, int kw, int kr,
                           int dtype, int routed_decay, float scale, const void *row_factor, const void *col_factor,
-                          int64_t factor_cols, int factor_dtype, void *cache, int cache_dtype, int store_final,
-                          int state_interval, void *reads, void *workspace, int64_t workspace_bytes, void *stream);
+                          int64_t factor_cols, int factor_dtype, const int32_t *bank_ids, int64_t total_banks,
+                          void *cache, int cache_dtype, int store_final, int state_interval, void *reads,
+                          void *workspace, int64_t workspace_bytes, void *stream);
 
 /*
  * Read combine + output normalisation + sigmoid gate.  Replaces
@@ -180,6 +185,52 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
 BDM_API int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
                           const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
                           float eps, int norm_mode, int round_each, int dtype, void *out, void *stream);
+
+/*
+ * Bank-sharded forward (one rank per GPU; no counterpart in the reference,
+ * which runs the layer on one device).  The bank table is partitioned over
+ * `world` ranks; each rank runs the recurrence of its own banks over the events
+ * of all ranks' tokens and returns FP32 read partials.
+ *
+ * bdm_bank_histogram: counts[bank] += number of write and read events routed to
+ *   it by write_idx [ntok, kw] and read_idx [ntok, kr] (int32 counts [bank_count],
+ *   zeroed by the caller; out-of-range banks are clamped).
+ * bdm_bank_owners: the partition.  mode 0 = contiguous index ranges
+ *   (owner = bank / (J/world)); mode 1 = balanced by load: banks sorted by
+ *   (count desc, index asc), then taken in groups of `world`, the heaviest bank
+ *   of a group going to the least loaded rank (ties to the lower rank).  Both
+ *   give every rank exactly J/world banks; J % world == 0 is required and mode 1
+ *   needs J <= 16384 and world <= 32.  Outputs, int32: owner [J], slot [J] (the
+ *   bank's index among its owner's banks, ascending bank order) and members
+ *   [world, J/world] (members[r][slot] = bank).  Deterministic: equal counts give
+ *   equal maps on every rank.
+ * bdm_dispatch_owned: bdm_dispatch restricted to the banks with owner[bank] ==
+ *   rank; sequence ids are batch*local_banks + slot[bank], cu_seqlens has
+ *   batch*local_banks + 1 entries and cu_seqlens[batch*local_banks] is the owned
+ *   event count.  `order` still lists every event: owned ones first (sorted as
+ *   in bdm_dispatch), then the others.
+ * bdm_combine_partial: out[t] = sum, in ascending bank order and FP32, of the
+ *   read rows reads[t, j] (dtype) whose bank read_idx[t, j] this rank owns
+ *   (out [ntok, width] float; zero where it owns none).
+ * bdm_norm_gate_f32: bdm_combine_norm_gate over an FP32 combined read sum
+ *   [ntok, width], rounded once to dtype first (the forward's round-once combine).
+ */
+BDM_API int bdm_bank_histogram(const int64_t *write_idx, const int64_t *read_idx, int64_t ntok, int kw, int kr,
+                               int64_t bank_count, int32_t *counts, void *stream);
+BDM_API int bdm_bank_owners(const int32_t *counts, int64_t bank_count, int world, int mode, int32_t *owner,
+                            int32_t *slot, int32_t *members, void *stream);
+BDM_API int64_t bdm_dispatch_owned_workspace_bytes(int64_t batch, int64_t time, int kw, int kr, int64_t local_banks);
+BDM_API int bdm_dispatch_owned(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time, int kw,
+                               int kr, int64_t bank_count, const int32_t *owner, const int32_t *slot, int rank,
+                               int64_t local_banks, int64_t *order, int64_t *cu_seqlens, int64_t *inverse,
+                               int64_t *tokens, int32_t *error_word, void *workspace, int64_t workspace_bytes,
+                               void *stream);
+BDM_API int bdm_combine_partial(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                const int32_t *owner, int64_t bank_count, int rank, int dtype, float *out,
+                                void *stream);
+BDM_API int bdm_norm_gate_f32(const float *combined, int64_t ntok, int64_t width, const void *gate, int64_t ld_gate,
+                              const void *norm_weight, const void *norm_bias, float eps, int norm_mode, int dtype,
+                              void *out, void *stream);
 
 /*
  * One decode token per batch row.  Replaces inference.step's bank kernels

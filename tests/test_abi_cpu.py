@@ -50,16 +50,34 @@ def test_dispatch_workspace_sizing():
     lambda lib: lib.bdm_route(None, 4, 8, 16, 16, 8, 1, None, None, None),        # ld < j1 + j2
     lambda lib: lib.bdm_dispatch(None, None, 2, 4, 8, 8, 256, None, None, None, None, None, None, 0, None),
     lambda lib: lib.bdm_combine_norm_gate(None, None, 4, 8, 0, None, 0, None, None, 1e-5, 1, 0, 1, None, None),
+    lambda lib: lib.bdm_bank_owners(None, 256, 4, 1, None, None, None, None),          # balanced needs counts
+    lambda lib: lib.bdm_bank_owners(None, 256, 0, 0, None, None, None, None),          # world 0
+    lambda lib: lib.bdm_dispatch_owned(None, None, 2, 4, 8, 8, 256, None, None, 0, 64, None, None, None, None, None,
+                                       None, 0, None),
+    lambda lib: lib.bdm_combine_partial(None, None, 4, 8, 64, None, 256, 0, 1, None, None),
+    lambda lib: lib.bdm_norm_gate_f32(None, 4, 64, None, 64, None, None, 1e-5, 1, 1, None, None),
 ])
 def test_invalid_arguments_are_rejected_on_the_host(call):
     assert call(_lib.load()) == _lib.BDM_ERR_INVALID
 
 
+def test_bank_partition_limits():
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(16)
+    # every rank must get the same number of banks
+    assert lib.bdm_bank_owners(dummy, 250, 4, 0, dummy, dummy, dummy, None) == _lib.BDM_ERR_UNSUPPORTED
+    # the balanced partition sorts the table in one CTA: at most 16384 banks and 32 ranks
+    assert lib.bdm_bank_owners(dummy, 32768, 8, 1, dummy, dummy, dummy, None) == _lib.BDM_ERR_UNSUPPORTED
+    assert lib.bdm_bank_owners(dummy, 16384 * 2, 64, 1, dummy, dummy, dummy, None) == _lib.BDM_ERR_UNSUPPORTED
+    assert lib.bdm_dispatch_owned_workspace_bytes(16, 8192, 16, 16, 2048) > 0
+    assert lib.bdm_dispatch_owned_workspace_bytes(16, 8192, 16, 16, 0) == -1
+
+
 def test_unsupported_geometry_is_reported():
     lib = _lib.load()
     dummy = ctypes.c_void_p(16)
-    rc = lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 32, 64, 8, 8, 1, 1, 0.25, None, None, 0, 0, None, 0, 0,
-                           0, dummy, dummy, 1 << 20, None)
+    rc = lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 32, 64, 8, 8, 1, 1, 0.25, None, None, 0, 0, None, 0, None,
+                           0, 0, 0, dummy, dummy, 1 << 20, None)
     assert rc == _lib.BDM_ERR_UNSUPPORTED  # bank_size 32 is not implemented
     with pytest.raises(NotImplementedError):
         _lib.check(rc, 'bdm_bank_scan')
