@@ -22,6 +22,9 @@
 // batch runs.  N is multiplied back by D (materialised) at every segment end:
 // the end of a batch, a BF16 state-storage point (gdn2_banks.py:35-36), or
 // where the cumulative log-decay would leave the FP32 range (the batch is cut).
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 
 namespace bdm {
@@ -29,6 +32,15 @@ namespace {
 
 #ifndef BDM_SCAN_MIN_BLOCKS
 #define BDM_SCAN_MIN_BLOCKS 4  // resident CTAs per SM the register allocation targets (measured best)
+#endif
+#ifndef BDM_SCAN_LONG
+#define BDM_SCAN_LONG 1  // 1: long sequences run on warp-specialised CTAs; 0: every unit on one warp
+#endif
+#ifndef BDM_SCAN_LONG_CTAS_PER_SM
+#define BDM_SCAN_LONG_CTAS_PER_SM 4  // warp-specialised CTAs per SM (persistent over the long units)
+#endif
+#ifndef BDM_SCAN_DYNAMIC
+#define BDM_SCAN_DYNAMIC 0  // 1: persistent CTAs take work items from an atomic counter; 0: one item per CTA
 #endif
 #ifndef BDM_SCAN_PREFETCH
 #define BDM_SCAN_PREFETCH 4  // value-row prefetch distance (events)
@@ -53,6 +65,7 @@ struct ScanParams {
     int factor_dtype;
     const int32_t *bank_ids;  // local bank -> bank of the full table (bank-sharded ranks), or null
     int64_t total_banks;
+    int head_offset, total_heads;  // this call's heads are [head_offset, head_offset + H) of total_heads
     void *cache;
     int cache_dtype, store_final, interval;
     void *reads;
@@ -61,6 +74,9 @@ struct ScanParams {
     const int *lists;     // kLenClasses lists of capacity nseq
     const int *counts;    // [kLenClasses] list lengths
     unsigned long long *next;  // dynamic work counter (zero at launch)
+    int *status;               // error bits (BDM_SCAN_ERR_*), zero at launch
+    int ws_classes;            // length classes run by warp-specialised CTAs (0: none)
+    int64_t ws_ctas;           // CTAs [0, ws_ctas) run those units
     int64_t nseq;
 };
 
@@ -68,7 +84,11 @@ struct ScanParams {
 // Inside a class sequences keep ascending (batch, bank) order, so warps running
 // at the same time mostly read the same batch row's token rows (L2 locality).
 constexpr int kLenClasses = 4;
-__device__ __constant__ int kLenLower[kLenClasses] = {8192, 2048, 512, 1};
+constexpr int kWsClasses = 1;           // class 0 (the long sequences) runs warp-specialised
+constexpr int64_t kLongEvents = 2048;   // a long sequence has at least this many events
+constexpr int BDM_SCAN_ERR_TIMEOUT = 1;  // a producer/consumer wait gave up
+// Lower bounds of classes 1..3; class 0 starts at the launch's long-sequence bound.
+__device__ __constant__ int kLenLower[kLenClasses] = {0, 2048, 512, 1};
 
 template <int BYTES> struct VecOf;
 template <> struct VecOf<4> { using type = uint32_t; };
@@ -192,8 +212,148 @@ template <int S> struct CtlLayout {
     static constexpr int c = 0, kd = S, p = 2 * S, dprev = 2 * S + 2, size = 3 * S + 2;
 };
 
-template <int S> struct EvBatch { static constexpr int value = S >= 16 ? 16 : 32; };
+#ifndef BDM_SCAN_EB_S16
+#define BDM_SCAN_EB_S16 16  // events per staged batch when S = 16 (32 otherwise)
+#endif
+template <int S> struct EvBatch { static constexpr int value = S >= 16 ? BDM_SCAN_EB_S16 : 32; };
 
+
+// Initial state of a unit's columns: the cache, the product-key factors (bank
+// mapped into the full table on sharded ranks, head offset for head groups),
+// or zero; rounded to BF16 when the training storage policy is on.
+template <int S, int NP>
+__device__ __forceinline__ void load_initial_state(const ScanParams &p, int64_t bank, int hh, int col0, bool active,
+                                                   int64_t state_off, float2 (&N)[S][NP]) {
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int j = 0; j < NP; ++j) N[s][j] = make_float2(0.f, 0.f);
+    if (!active) return;
+    if (p.cache) {
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
+                N[s][j] = p.cache_dtype == BDM_BF16 ? load_pair<bf16>(static_cast<const bf16 *>(p.cache) + o)
+                                                    : load_pair<float>(static_cast<const float *>(p.cache) + o);
+            }
+    } else if (p.row_factor) {
+        int64_t gbank = bank;
+        if (p.bank_ids) {
+            gbank = p.bank_ids[bank];
+            gbank = gbank < 0 ? 0 : (gbank >= p.total_banks ? p.total_banks - 1 : gbank);
+        }
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const int64_t r = (gbank * p.total_heads + p.head_offset + hh) * S + s;
+            const int64_t ou = (r / p.factor_cols) * p.dv + col0, oz = (r % p.factor_cols) * p.dv + col0;
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                if (p.factor_dtype == BDM_BF16) {
+                    const float2 u = load_pair<bf16>(static_cast<const bf16 *>(p.row_factor) + ou + 2 * j);
+                    const float2 z = load_pair<bf16>(static_cast<const bf16 *>(p.col_factor) + oz + 2 * j);
+                    N[s][j] = bf16_round_pair(make_float2(u.x + z.x, u.y + z.y));
+                } else {
+                    const float2 u = load_pair<float>(static_cast<const float *>(p.row_factor) + ou + 2 * j);
+                    const float2 z = load_pair<float>(static_cast<const float *>(p.col_factor) + oz + 2 * j);
+                    N[s][j] = make_float2(u.x + z.x, u.y + z.y);
+                }
+            }
+        }
+    }
+    if (p.interval > 0) {
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+            for (int j = 0; j < NP; ++j) N[s][j] = bf16_round_pair(N[s][j]);
+    }
+}
+
+// One staged event on a lane's columns.  Coefficients come two at a time
+// (128-bit shared loads of duplicated pairs); dot products run in NCH
+// independent chains per column pair.
+template <typename T, int S, int NC>
+__device__ __forceinline__ void event_step(const float2 *row, bool round_point, bool is_write, bool is_read,
+                                           bool active, const Row<T, NC> &vr, const Row<T, NC> &wr, float scale,
+                                           T *out_row, float2 (&N)[S][NC / 2]) {
+    using Ctl = CtlLayout<S>;
+    constexpr int NP = NC / 2;
+    constexpr int NCH = NP >= 2 ? 2 : 4;
+    if (round_point) {  // storage point: materialise, round to BF16
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const float2 d2 = row[Ctl::dprev + s];
+#pragma unroll
+            for (int c = 0; c < NP; ++c) N[s][c] = bf16_round_pair(__fmul2_rn(N[s][c], d2));
+        }
+    }
+    const float4 *crow = reinterpret_cast<const float4 *>(row + Ctl::c);
+    if (is_write) {
+        float2 mer[NP];
+#pragma unroll
+        for (int c = 0; c < NP; ++c) {
+            float2 ch[NCH];
+#pragma unroll
+            for (int i = 0; i < NCH; ++i) ch[i] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int s = 0; s < S; s += 2) {
+                const float4 cc = crow[s / 2];
+                const int i = (s / 2) % NCH;
+                ch[i] = __ffma2_rn(make_float2(cc.x, cc.y), N[s][c], ch[i]);
+                ch[(i + NCH / 2) % NCH] = __ffma2_rn(make_float2(cc.z, cc.w), N[s + 1][c], ch[(i + NCH / 2) % NCH]);
+            }
+#pragma unroll
+            for (int i = 1; i < NCH; ++i) ch[0] = __fadd2_rn(ch[0], ch[i]);
+            mer[c] = make_float2(-ch[0].x, -ch[0].y);
+        }
+        const float2 pw = row[Ctl::p];
+        float2 u[NP];
+#pragma unroll
+        for (int c = 0; c < NP; ++c) u[c] = WriteValue<T>::apply(wr.x + 2 * c, vr.x + 2 * c, pw, mer[c]);
+        const float4 *krow = reinterpret_cast<const float4 *>(row + Ctl::kd);
+#pragma unroll
+        for (int s = 0; s < S; s += 2) {
+            const float4 kk = krow[s / 2];
+#pragma unroll
+            for (int c = 0; c < NP; ++c) {
+                N[s][c] = __ffma2_rn(make_float2(kk.x, kk.y), u[c], N[s][c]);
+                N[s + 1][c] = __ffma2_rn(make_float2(kk.z, kk.w), u[c], N[s + 1][c]);
+            }
+        }
+    } else if (is_read) {
+        float2 acc[NP][NCH];
+#pragma unroll
+        for (int c = 0; c < NP; ++c)
+#pragma unroll
+            for (int i = 0; i < NCH; ++i) acc[c][i] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int s = 0; s < S; s += 2) {
+            const float4 cc = crow[s / 2];
+            const int i = (s / 2) % NCH;
+#pragma unroll
+            for (int c = 0; c < NP; ++c) {
+                acc[c][i] = __ffma2_rn(make_float2(cc.x, cc.y), N[s][c], acc[c][i]);
+                acc[c][(i + NCH / 2) % NCH] =
+                    __ffma2_rn(make_float2(cc.z, cc.w), N[s + 1][c], acc[c][(i + NCH / 2) % NCH]);
+            }
+        }
+        if (active) {
+            Row<T, NC> o;
+#pragma unroll
+            for (int c = 0; c < NP; ++c) {
+#pragma unroll
+                for (int i = 1; i < NCH; ++i) acc[c][0] = __fadd2_rn(acc[c][0], acc[c][i]);
+                store_pair<T>(o.x + 2 * c, __fmul2_rn(acc[c][0], dup(scale)));
+            }
+            store_row<T, NC>(out_row, o);
+        }
+    }
+}
+
+// Short sequences: one warp per (sequence, head, column tile) unit, kScanWarps
+// units per CTA; each warp stages and runs its own batches.  Takes the length
+// classes from p.ws_classes on (all of them when the long kernel does not run).
 template <typename T, int S, int NC>
 __global__ void __launch_bounds__(kScanWarps * 32, BDM_SCAN_MIN_BLOCKS)
 bank_scan_kernel(const ScanParams p) {
@@ -208,6 +368,7 @@ bank_scan_kernel(const ScanParams p) {
     __shared__ __align__(16) unsigned char raw_all[kScanWarps][EB][Raw::size];
     __shared__ int tok_all[kScanWarps][EB];
     __shared__ int rid_all[kScanWarps][EB];
+    __shared__ unsigned long long item_shared;
 
     const int warp = threadIdx.x >> 5;
     const int lane = (int)lane_id();
@@ -217,24 +378,26 @@ bank_scan_kernel(const ScanParams p) {
     int *tok_s = tok_all[warp];
     int *rid_s = rid_all[warp];
     const int64_t per_seq = (int64_t)p.H * p.ctiles;
-    int64_t total = 0;
+    int64_t total = 0;  // units of the classes this kernel runs (the long classes go to the long kernel)
 #pragma unroll
-    for (int c = 0; c < kLenClasses; ++c) total += p.counts[c];
+    for (int c = 0; c < kLenClasses; ++c) total += c >= p.ws_classes ? p.counts[c] : 0;
     total *= per_seq;
 
-    // Persistent CTAs take kScanWarps consecutive (sequence, head, column tile)
-    // units at a time, so the warps of a CTA work on the heads of one sequence
-    // and share its control rows in L1.
-    __shared__ unsigned long long item_s;
+    // CTAs take kScanWarps consecutive (sequence, head, column tile) units at a
+    // time, so the warps of a CTA work on the heads of one sequence and share
+    // its control rows in L1.
+    unsigned long long static_item = blockIdx.x;
     for (;;) {
     __syncthreads();
-    if (threadIdx.x == 0) item_s = atomicAdd(p.next, 1ull);
+    if (threadIdx.x == 0) item_shared = BDM_SCAN_DYNAMIC ? atomicAdd(p.next, 1ull) : static_item;
     __syncthreads();
+    static_item += gridDim.x;
+    const unsigned long long item_s = item_shared;
     const int64_t item = (int64_t)item_s * kScanWarps + warp;
     if ((int64_t)item_s * kScanWarps >= total) break;  // CTA-uniform
     if (item >= total) continue;
     int64_t local = (int64_t)item / per_seq;
-    int cls = 0;
+    int cls = p.ws_classes;
     while (cls < kLenClasses - 1 && local >= p.counts[cls]) local -= p.counts[cls++];
     const int64_t seq = p.lists[(int64_t)cls * p.nseq + local];
     const int64_t rem = (int64_t)item % per_seq;
@@ -259,51 +422,7 @@ bank_scan_kernel(const ScanParams p) {
     // ---------------------------------------------------------- initial state
     float2 N[S][NP];
     const int64_t state_off = ((bidx * p.J + bank) * p.H + hh) * (int64_t)S * p.dv + col0;
-#pragma unroll
-    for (int s = 0; s < S; ++s)
-#pragma unroll
-        for (int j = 0; j < NP; ++j) N[s][j] = make_float2(0.f, 0.f);
-    if (active) {
-        if (p.cache) {
-#pragma unroll
-            for (int s = 0; s < S; ++s)
-#pragma unroll
-                for (int j = 0; j < NP; ++j) {
-                    const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
-                    N[s][j] = p.cache_dtype == BDM_BF16 ? load_pair<bf16>(static_cast<const bf16 *>(p.cache) + o)
-                                                        : load_pair<float>(static_cast<const float *>(p.cache) + o);
-                }
-        } else if (p.row_factor) {
-            int64_t gbank = bank;
-            if (p.bank_ids) {
-                gbank = p.bank_ids[bank];
-                gbank = gbank < 0 ? 0 : (gbank >= p.total_banks ? p.total_banks - 1 : gbank);
-            }
-#pragma unroll
-            for (int s = 0; s < S; ++s) {
-                const int64_t r = (gbank * p.H + hh) * S + s;
-                const int64_t ou = (r / p.factor_cols) * p.dv + col0, oz = (r % p.factor_cols) * p.dv + col0;
-#pragma unroll
-                for (int j = 0; j < NP; ++j) {
-                    if (p.factor_dtype == BDM_BF16) {
-                        const float2 u = load_pair<bf16>(static_cast<const bf16 *>(p.row_factor) + ou + 2 * j);
-                        const float2 z = load_pair<bf16>(static_cast<const bf16 *>(p.col_factor) + oz + 2 * j);
-                        N[s][j] = bf16_round_pair(make_float2(u.x + z.x, u.y + z.y));
-                    } else {
-                        const float2 u = load_pair<float>(static_cast<const float *>(p.row_factor) + ou + 2 * j);
-                        const float2 z = load_pair<float>(static_cast<const float *>(p.col_factor) + oz + 2 * j);
-                        N[s][j] = make_float2(u.x + z.x, u.y + z.y);
-                    }
-                }
-            }
-        }
-        if (p.interval > 0) {
-#pragma unroll
-            for (int s = 0; s < S; ++s)
-#pragma unroll
-                for (int j = 0; j < NP; ++j) N[s][j] = bf16_round_pair(N[s][j]);
-        }
-    }
+    load_initial_state<S, NP>(p, bank, hh, col0, active, state_off, N);
 
     // Clamp caller-provided bounds so a malformed cu_seqlens cannot index past `order`.
     const int64_t start = min(max(p.cu[seq], (int64_t)0), p.E);
@@ -457,53 +576,8 @@ bank_scan_kernel(const ScanParams p) {
             for (int j = 0; j < PD; ++j) {
                 const int ev = e0 + j;
                 if (ev >= n) break;
-                if ((rmask >> ev) & 1u) {  // storage point: materialise, round to BF16
-#pragma unroll
-                    for (int s = 0; s < S; ++s) {
-                        const float2 d2 = ctl[ev][Ctl::dprev + s];
-#pragma unroll
-                        for (int c = 0; c < NP; ++c) N[s][c] = bf16_round_pair(__fmul2_rn(N[s][c], d2));
-                    }
-                }
-                if ((wmask >> ev) & 1u) {
-                    float2 mer[NP];
-#pragma unroll
-                    for (int c = 0; c < NP; ++c) {
-                        float2 lo = __fmul2_rn(ctl[ev][Ctl::c + 0], N[0][c]);
-                        float2 hi = __fmul2_rn(ctl[ev][Ctl::c + 1], N[1][c]);
-#pragma unroll
-                        for (int s = 2; s < S; s += 2) {
-                            lo = __ffma2_rn(ctl[ev][Ctl::c + s], N[s][c], lo);
-                            hi = __ffma2_rn(ctl[ev][Ctl::c + s + 1], N[s + 1][c], hi);
-                        }
-                        mer[c] = make_float2(-(lo.x + hi.x), -(lo.y + hi.y));
-                    }
-                    const float2 pw = ctl[ev][Ctl::p];
-                    float2 u[NP];
-#pragma unroll
-                    for (int c = 0; c < NP; ++c)
-                        u[c] = WriteValue<T>::apply(wr[j].x + 2 * c, vr[j].x + 2 * c, pw, mer[c]);
-#pragma unroll
-                    for (int s = 0; s < S; ++s) {
-                        const float2 k2 = ctl[ev][Ctl::kd + s];
-#pragma unroll
-                        for (int c = 0; c < NP; ++c) N[s][c] = __ffma2_rn(k2, u[c], N[s][c]);
-                    }
-                } else if (tok_s[ev] >= 0) {
-                    float2 acc[NP];
-#pragma unroll
-                    for (int c = 0; c < NP; ++c) acc[c] = __fmul2_rn(ctl[ev][Ctl::c + 0], N[0][c]);
-#pragma unroll
-                    for (int s = 1; s < S; ++s)
-#pragma unroll
-                        for (int c = 0; c < NP; ++c) acc[c] = __ffma2_rn(ctl[ev][Ctl::c + s], N[s][c], acc[c]);
-                    if (active) {
-                        Row<T, NC> out;
-#pragma unroll
-                        for (int c = 0; c < NP; ++c) store_pair<T>(out.x + 2 * c, __fmul2_rn(acc[c], dup(p.scale)));
-                        store_row<T, NC>(outp + (int64_t)rid_s[ev] * V, out);
-                    }
-                }
+                event_step<T, S, NC>(ctl[ev], (rmask >> ev) & 1u, (wmask >> ev) & 1u, tok_s[ev] >= 0, active, vr[j],
+                                     wr[j], p.scale, outp + (int64_t)rid_s[ev] * V, N);
                 prefetch(ev + PD, j);
             }
         }
@@ -536,21 +610,407 @@ bank_scan_kernel(const ScanParams p) {
     }
 }
 
+// ===========================================================================
+// Long sequences: warp-specialised CTAs.
+//
+// A sequence with thousands of events is a serial chain; its latency, not the
+// GPU's throughput, bounds a launch whose router is skewed.  The first
+// p.ws_ctas CTAs of a launch take the units (sequence, head) of the long
+// length classes and split each across warps:
+//   warp 0 (producer) stages a batch of EB events: ids, route weights, async
+//     copies of the k|b|g / q rows and of the lanes' v / w values, the
+//     segmented log-decay scan and the deferred-decay coefficients;
+//   warps 1..T (consumers, one per value-column tile) run the state math from
+//     shared memory only.
+// The producer stages batch i+1 while the consumers run batch i, so a batch
+// costs about max(staging, math) instead of their sum, the tiles of a head
+// share one staging pass, and the consumers never wait on global memory.
+//
+// Handoff through a two-slot ring: mbarriers full[slot] (32 producer
+// arrivals) and empty[slot] (32*T consumer arrivals), waited by phase parity.
+// The value rows of batch i+1 are copied once its slot is free (after the
+// consumers finish batch i-1, while they run batch i).  Every wait is bounded:
+// after kWaitPolls polls or kWaitNs nanoseconds it records
+// BDM_SCAN_ERR_TIMEOUT in the status word, raises the CTA's abort flag and
+// returns; the other warps then fail their own bounded waits and return.
+// ===========================================================================
+constexpr int kWsMaxTiles = kScanWarps - 1;  // consumers per CTA
+constexpr int kWsSlots = 2;
+constexpr long long kWaitPolls = 1ll << 22;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+    return t;
+}
+// Bounded wait for the phase of `parity` to complete; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+    if (mbar_test(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (long long i = 0; i < kWaitPolls; ++i) {
+        if (mbar_test(bar, parity)) return true;
+        if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) break;
+    }
+    return false;
+}
+
+// Shared memory of a warp-specialised CTA: the ring (fixed part), the
+// producer's raw row buffers, then the staged value rows (sized at launch by
+// the number of column tiles).
+constexpr int kWsBatch = 16;  // events per staged batch in long mode (every S)
+template <typename T, int S> struct WsShared {
+    static constexpr int EB = kWsBatch;
+    float2 ctl[kWsSlots][EB][CtlLayout<S>::size];
+    float2 dend[kWsSlots][S];
+    int tok[kWsSlots][EB], rid[kWsSlots][EB];
+    int n[kWsSlots];
+    unsigned wmask[kWsSlots], rmask[kWsSlots];
+    uint64_t full[kWsSlots], empty[kWsSlots];
+    int abort;
+    __align__(16) unsigned char raw[2][EB][RawLayout<T, S>::size];
+};
+template <typename T, int S, int NC>
+__host__ __device__ constexpr int64_t ws_value_bytes(int tiles) {  // v and w rows of a slot's events
+    return (int64_t)kWsSlots * kWsBatch * tiles * 2 * 32 * NC * (int64_t)sizeof(T);
+}
+template <typename T, int S> __host__ __device__ constexpr int64_t ws_fixed_bytes() {
+    return ((int64_t)sizeof(WsShared<T, S>) + 15) / 16 * 16;
+}
+
+struct Staged {
+    int tok, rid;
+    bool write;
+    float wt;
+};
+
+template <typename T, int S, int NC>
+__device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned char *smem) {
+    constexpr int NP = NC / 2;
+    constexpr int EB = kWsBatch;
+    using Raw = RawLayout<T, S>;
+    using Ctl = CtlLayout<S>;
+    constexpr int kRowElems = 32 * NC;  // one tile's columns of a v or w row
+    WsShared<T, S> &sh = *reinterpret_cast<WsShared<T, S> *>(smem);
+    T *vw = reinterpret_cast<T *>(smem + ws_fixed_bytes<T, S>());  // [slot][event][tile][v|w][kRowElems]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = (int)lane_id();
+    const int tiles = p.ctiles;
+    int64_t long_seqs = 0;
+    for (int c = 0; c < p.ws_classes; ++c) long_seqs += p.counts[c];
+    const int64_t total = long_seqs * p.H;
+    if ((int64_t)blockIdx.x >= total) return;  // CTA-uniform
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kWsSlots; ++b) {
+            mbar_init(&sh.full[b], 32);
+            mbar_init(&sh.empty[b], 32 * tiles);
+        }
+        sh.abort = 0;
+    }
+    __syncthreads();
+    if (warp > tiles) return;  // warps beyond the column tiles take no part
+
+    volatile int *abort_flag = &sh.abort;
+    auto fail = [&]() {
+        if (lane == 0) atomicOr(p.status, BDM_SCAN_ERR_TIMEOUT);
+        *abort_flag = 1;
+    };
+    auto slot_values = [&](int slot, int ev, int tile, int which) {
+        return vw + ((((int64_t)slot * EB + ev) * tiles + tile) * 2 + which) * kRowElems;
+    };
+    const int HS = p.H * S;
+    const int64_t V = (int64_t)p.H * p.dv;
+    const int nw = (int)p.nw, kw = p.kw, kr = p.kr, nt = (int)p.nt, E = (int)p.E;
+    unsigned it = 0;  // batches handed through the ring (same count on every warp)
+
+    for (int64_t item = blockIdx.x; item < total && !*abort_flag; item += gridDim.x) {
+        int64_t local = item / p.H;
+        int cls = 0;
+        while (cls < kLenClasses - 1 && local >= p.counts[cls]) local -= p.counts[cls++];
+        const int64_t seq = p.lists[(int64_t)cls * p.nseq + local];
+        const int hh = (int)(item % p.H);
+        const int64_t bidx = seq / p.J, bank = seq % p.J;
+        const int64_t start = min(max(p.cu[seq], (int64_t)0), p.E);
+        const int64_t end = min(max(p.cu[seq + 1], start), p.E);
+
+        if (warp == 0) {
+            // ------------------------------------------------------- producer
+            const T *qp = static_cast<const T *>(p.q);
+            const T *kp = static_cast<const T *>(p.k);
+            const T *bp = static_cast<const T *>(p.b);
+            const T *wwp = static_cast<const T *>(p.ww);
+            const T *rwp = static_cast<const T *>(p.rw);
+            // ids, weights and k|b|g / q rows of events [bbase, bbase + bn): lane = event
+            auto issue_rows = [&](int64_t bbase, int bn, unsigned char (*rawb)[Raw::size], Staged &st) {
+                st.tok = -1;
+                st.rid = -1;
+                st.write = false;
+                st.wt = 0.f;
+                if (lane < bn) {
+                    const int64_t id = p.order[bbase + lane];
+                    if (id >= 0 && id < nw) {
+                        st.tok = (int)id / kw;
+                        st.write = true;
+                        st.wt = Elem<T>::to_float(wwp[id]);
+                    } else if (id >= nw && id < E) {
+                        st.rid = (int)id - nw;
+                        st.tok = st.rid / kr;
+                        st.wt = Elem<T>::to_float(rwp[st.rid]);
+                    }
+                    if (st.tok >= nt) {
+                        st.tok = -1;
+                        st.write = false;
+                        st.rid = -1;
+                    }
+                }
+                if (st.tok >= 0) {
+                    const int64_t o = (int64_t)st.tok * HS + (int64_t)hh * S;
+                    if (st.write) {
+                        cp_async<Raw::kBytes>(rawb[lane] + Raw::kOff, kp + o);
+                        cp_async<Raw::kBytes>(rawb[lane] + Raw::bOff, bp + o);
+                        cp_async<Raw::gBytes>(rawb[lane] + Raw::gOff, p.g + o);
+                    } else {
+                        cp_async<Raw::kBytes>(rawb[lane] + Raw::kOff, qp + o);
+                    }
+                }
+            };
+            // v / w columns of the batch's writes into ring slot `slot` (all lanes per event)
+            auto issue_values = [&](int bn, const Staged &st, int slot) {
+                constexpr int kPiece = 16;
+                const int row_bytes = kRowElems * (int)sizeof(T);
+                const int pieces = tiles * 2 * row_bytes / kPiece;
+                const int64_t dv_bytes = (int64_t)p.dv * sizeof(T);
+                for (int e = 0; e < bn; ++e) {
+                    const int te = __shfl_sync(0xffffffffu, st.tok, e);
+                    const int we = __shfl_sync(0xffffffffu, (int)st.write, e);
+                    if (!we || te < 0) continue;  // warp-uniform
+                    for (int piece = lane; piece < pieces; piece += 32) {
+                        const int r = piece / (row_bytes / kPiece);
+                        const int off = (piece % (row_bytes / kPiece)) * kPiece;
+                        const int tile = r >> 1, which = r & 1;
+                        const int64_t col_bytes = (int64_t)tile * row_bytes + off;
+                        if (col_bytes >= dv_bytes) continue;
+                        const char *src = static_cast<const char *>(which ? p.w : p.v) +
+                                          ((int64_t)te * V + (int64_t)hh * p.dv) * sizeof(T) + col_bytes;
+                        cp_async<kPiece>(reinterpret_cast<char *>(slot_values(slot, e, tile, which)) + off, src);
+                    }
+                }
+            };
+            // coefficients of a staged batch into ring slot b; returns the events to run
+            auto finish = [&](int64_t pos0, int bn, const unsigned char (*rawb)[Raw::size], const Staged &st, int b,
+                              bool newer_pending) -> int {
+                if (newer_pending) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+                else cp_async_wait_all();
+                float2(*ctl)[Ctl::size] = sh.ctl[b];
+                const bool valid = lane < bn;
+                const int64_t pos = pos0 + lane;
+                const bool head = valid && p.interval > 0 && pos > 0 && (pos % p.interval) == 0;
+                const T *rk = reinterpret_cast<const T *>(rawb[lane] + Raw::kOff);
+                const float *rg = reinterpret_cast<const float *>(rawb[lane] + Raw::gOff);
+                float L[S];
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    float ge = 0.f;
+                    if (st.write && st.tok >= 0) ge = fmaxf(p.routed_decay ? rg[s] * st.wt : rg[s], kMinLogDecay);
+                    L[s] = ge;
+                }
+                bool f = head || lane == 0;
+#pragma unroll
+                for (int d = 1; d < EB; d <<= 1) {
+                    const bool fu = __shfl_up_sync(0xffffffffu, f, d);
+                    const bool take = lane >= d && !f;
+#pragma unroll
+                    for (int s = 0; s < S; ++s) {
+                        const float lu = __shfl_up_sync(0xffffffffu, L[s], d);
+                        if (take) L[s] += lu;
+                    }
+                    f = f || (lane >= d && fu);
+                }
+                float lmin = 0.f;
+#pragma unroll
+                for (int s = 0; s < S; ++s) lmin = fminf(lmin, L[s]);
+                const unsigned over = __ballot_sync(0xffffffffu, valid && lmin < kMinLogDecay);
+                const int n = over ? (__ffs(over) - 1) : bn;  // >= 1: one event's decay is floored above
+                const bool use = lane < n;
+                float D[S];
+#pragma unroll
+                for (int s = 0; s < S; ++s) D[s] = expf(L[s]);
+                if (use && st.tok >= 0) {
+                    if (st.write) {
+                        const T *rb = reinterpret_cast<const T *>(rawb[lane] + Raw::bOff);
+#pragma unroll
+                        for (int s = 0; s < S; ++s) {
+                            const float kk = Elem<T>::to_float(rk[s]);
+                            const float a = rnd<T>(Elem<T>::to_float(rb[s]) * st.wt) * kk;
+                            ctl[lane][Ctl::c + s] = dup(a * D[s]);
+                            ctl[lane][Ctl::kd + s] = dup(kk * expf(-L[s]));
+                        }
+                        ctl[lane][Ctl::p] = weight_pair<T>(st.wt);
+                    } else {
+#pragma unroll
+                        for (int s = 0; s < S; ++s)
+                            ctl[lane][Ctl::c + s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * st.wt) * D[s]);
+                    }
+                }
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const float before = __shfl_up_sync(0xffffffffu, D[s], 1);
+                    if (use && head) ctl[lane][Ctl::dprev + s] = dup(lane == 0 ? 1.0f : before);
+                    if (lane == n - 1) sh.dend[b][s] = dup(D[s]);
+                }
+                if (lane < EB) {
+                    sh.tok[b][lane] = use ? st.tok : -1;
+                    sh.rid[b][lane] = use ? st.rid : -1;
+                }
+                const unsigned rm = __ballot_sync(0xffffffffu, use && head);
+                const unsigned wm = __ballot_sync(0xffffffffu, use && st.write && st.tok >= 0);
+                if (lane == 0) {
+                    sh.n[b] = n;
+                    sh.wmask[b] = wm;
+                    sh.rmask[b] = rm;
+                }
+                __syncwarp();
+                return n;
+            };
+
+            Staged cur{-1, -1, false, 0.f}, nxt{-1, -1, false, 0.f};
+            int64_t base = start;
+            int bn = (int)min((int64_t)EB, end - base);
+            bool ok = true;
+            // first batch of the unit: its slot was released by the batch two before it
+            issue_rows(base, bn, sh.raw[it & 1], cur);
+            if (it >= kWsSlots && !mbar_wait(&sh.empty[it & 1], ((it >> 1) - 1) & 1u)) ok = false;
+            if (ok) issue_values(bn, cur, it & 1);
+            cp_async_commit();
+            while (ok && base < end) {
+                const int64_t sbase = base + bn;  // next batch if this one is not cut
+                const int sbn = (int)min((int64_t)EB, end - sbase);
+                if (sbn > 0) {
+                    issue_rows(sbase, sbn, sh.raw[(it + 1) & 1], nxt);
+                    cp_async_commit();
+                }
+                const int b = (int)(it & 1u);
+                const int n = finish(base - start, bn, sh.raw[it & 1], cur, b, sbn > 0);
+                mbar_arrive(&sh.full[b]);
+                if (n < bn) {  // cut: the next batch starts right after the n-th event
+                    cp_async_wait_all();
+                    base += n;
+                    bn = (int)min((int64_t)EB, end - base);
+                    if (bn > 0) issue_rows(base, bn, sh.raw[(it + 1) & 1], nxt);
+                } else {
+                    base = sbase;
+                    bn = sbn;
+                }
+                ++it;
+                if (base < end) {  // the next batch's slot frees when the consumers finish batch it-2
+                    if (it >= kWsSlots && !mbar_wait(&sh.empty[it & 1], ((it >> 1) - 1) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    issue_values(bn, nxt, it & 1);
+                    cp_async_commit();
+                }
+                cur = nxt;
+            }
+            cp_async_wait_all();
+            if (!ok) fail();
+        } else {
+            // ------------------------------------------------------ consumers
+            const int ct = warp - 1;
+            const int col0 = ct * 32 * NC + lane * NC;
+            const bool active = col0 < p.dv;
+            T *outp = static_cast<T *>(p.reads) + (int64_t)hh * p.dv + col0;
+            float2 N[S][NP];
+            const int64_t state_off = ((bidx * p.J + bank) * p.H + hh) * (int64_t)S * p.dv + col0;
+            load_initial_state<S, NP>(p, bank, hh, col0, active, state_off, N);
+            int64_t base = start;
+            bool ok = true;
+            while (base < end) {
+                const int b = (int)(it & 1u);
+                if (!mbar_wait(&sh.full[b], (it >> 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                const int n = sh.n[b];
+                const unsigned wmask = sh.wmask[b], rmask = sh.rmask[b];
+                const float2(*ctl)[Ctl::size] = sh.ctl[b];
+#pragma unroll 4
+                for (int ev = 0; ev < n; ++ev) {
+                    Row<T, NC> vr, wr;
+                    const bool wr_ev = (wmask >> ev) & 1u;
+                    if (wr_ev) {
+                        vr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 0) + lane * NC);
+                        wr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 1) + lane * NC);
+                    }
+                    event_step<T, S, NC>(ctl[ev], (rmask >> ev) & 1u, wr_ev, sh.tok[b][ev] >= 0, active, vr, wr,
+                                         p.scale, outp + (int64_t)sh.rid[b][ev] * V, N);
+                }
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const float2 d2 = sh.dend[b][s];
+#pragma unroll
+                    for (int c = 0; c < NP; ++c) N[s][c] = __fmul2_rn(N[s][c], d2);
+                }
+                __syncwarp();
+                mbar_arrive(&sh.empty[b]);
+                base += n;
+                ++it;
+            }
+            if (!ok) fail();
+            if (ok && p.store_final && p.cache && active) {
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+#pragma unroll
+                    for (int j = 0; j < NP; ++j) {
+                        const int64_t o = state_off + (int64_t)s * p.dv + 2 * j;
+                        if (p.cache_dtype == BDM_BF16) store_pair<bf16>(static_cast<bf16 *>(p.cache) + o, N[s][j]);
+                        else store_pair<float>(static_cast<float *>(p.cache) + o, N[s][j]);
+                    }
+            }
+        }
+    }
+}
+
+template <typename T, int S, int NC>
+__global__ void __launch_bounds__(kScanWarps * 32, BDM_SCAN_MIN_BLOCKS)
+bank_scan_long_kernel(const ScanParams p) {
+    extern __shared__ __align__(16) unsigned char scan_smem[];
+    scan_long_units<T, S, NC>(p, scan_smem);
+}
+
 // Work list: every non-empty sequence goes to the list of its length class, in
 // ascending sequence order (one CTA: per-thread contiguous chunks + block scans).
 constexpr int kListThreads = 1024;
 
-__device__ __forceinline__ int len_class(const int64_t *cu, int64_t s, int64_t E) {
+__device__ __forceinline__ int len_class(const int64_t *cu, int64_t s, int64_t E, int64_t long_min) {
     const int64_t a = min(max(cu[s], (int64_t)0), E), b = min(max(cu[s + 1], a), E);
     const int64_t len = b - a;
     if (len <= 0) return -1;
-    int c = 0;
+    if (len >= long_min) return 0;
+    int c = 1;
     while (c < kLenClasses - 1 && len < kLenLower[c]) ++c;
     return c;
 }
 
 __global__ void __launch_bounds__(kListThreads)
-build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int *__restrict__ lists,
+build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int64_t long_min, int *__restrict__ lists,
                int *__restrict__ counts) {
     __shared__ int warp_tot[kLenClasses][32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -558,7 +1018,7 @@ build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int *__r
     const int64_t lo = min((int64_t)tid * chunk, nseq), hi = min(lo + chunk, nseq);
     int cnt[kLenClasses] = {0, 0, 0, 0};
     for (int64_t s = lo; s < hi; ++s) {
-        const int c = len_class(cu, s, E);
+        const int c = len_class(cu, s, E, long_min);
         if (c >= 0) ++cnt[c];
     }
     int off[kLenClasses];
@@ -592,9 +1052,39 @@ build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int *__r
 #pragma unroll
     for (int c = 0; c < kLenClasses; ++c) off[c] += warp_tot[c][warp];
     for (int64_t s = lo; s < hi; ++s) {
-        const int c = len_class(cu, s, E);
+        const int c = len_class(cu, s, E, long_min);
         if (c >= 0) lists[(int64_t)c * nseq + off[c]++] = (int)s;
     }
+}
+
+// Side stream (and fork / join events) of a caller stream, created on first
+// use and kept for the process.  The long-sequence kernel runs there, forked
+// from and joined back into the caller's stream, so it overlaps the
+// short-sequence kernel; both orderings are expressed with events, which CUDA
+// graph capture records as a fork and a join.
+struct SideStream {
+    int device;
+    cudaStream_t user, side;
+    cudaEvent_t fork, join;
+};
+std::mutex g_side_mutex;
+std::vector<SideStream> g_side;
+
+int side_stream(int dev, cudaStream_t user, SideStream &out) {
+    std::lock_guard<std::mutex> lock(g_side_mutex);
+    for (const SideStream &e : g_side)
+        if (e.device == dev && e.user == user) {
+            out = e;
+            return BDM_OK;
+        }
+    SideStream e{dev, user, nullptr, nullptr, nullptr};
+    int rc = cuda_status(cudaStreamCreateWithFlags(&e.side, cudaStreamNonBlocking));
+    if (!rc) rc = cuda_status(cudaEventCreateWithFlags(&e.fork, cudaEventDisableTiming));
+    if (!rc) rc = cuda_status(cudaEventCreateWithFlags(&e.join, cudaEventDisableTiming));
+    if (rc) return rc;
+    g_side.push_back(e);
+    out = e;
+    return BDM_OK;
 }
 
 template <typename T, int S, int NC>
@@ -603,18 +1093,53 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     q.ctiles = (int)ceil_div(p.dv, 32 * NC);
     q.units = p.batch * p.J * p.H * q.ctiles;
     if (q.units == 0) return BDM_OK;
-    int dev = 0, sms = kNumSMs, per_sm = 1;
+    int dev = 0, sms = kNumSMs;
     int rc = cuda_status(cudaGetDevice(&dev));
     if (rc) return rc;
     rc = cuda_status(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     if (rc) return rc;
+    // A sequence is long when its serial chain would outlast its share of the
+    // launch: more events than the launch's (event, head, tile) work over the
+    // GPU's warp slots (and at least kLongEvents).  Long sequences run on
+    // warp-specialised CTAs in their own kernel, started first; with a long
+    // launch (plenty of work to hide a chain) there are none.
+    const bool long_mode = BDM_SCAN_LONG && q.ctiles <= kWsMaxTiles;
+    const int64_t work = p.E * p.H * (int64_t)q.ctiles;
+    const int64_t long_min = long_mode ? max(kLongEvents, work / ((int64_t)sms * 32)) : (int64_t)8192;
+    build_worklist<<<1, kListThreads, 0, st>>>(p.cu, p.nseq, p.E, long_min, const_cast<int *>(p.lists),
+                                               const_cast<int *>(p.counts));
+    rc = launch_status();
+    if (rc) return rc;
+    q.ws_classes = long_mode ? kWsClasses : 0;
+    SideStream side{};
+    if (long_mode) {
+        q.ws_ctas = min(ceil_div(p.E, long_min) * p.H, (int64_t)sms * BDM_SCAN_LONG_CTAS_PER_SM);
+        const size_t smem = (size_t)(ws_fixed_bytes<T, S>() + ws_value_bytes<T, S, NC>(q.ctiles));
+        auto lk = bank_scan_long_kernel<T, S, NC>;
+        rc = cuda_status(cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (!rc) rc = side_stream(dev, st, side);
+        if (!rc) rc = cuda_status(cudaEventRecord(side.fork, st));
+        if (!rc) rc = cuda_status(cudaStreamWaitEvent(side.side, side.fork, 0));
+        if (rc) return rc;
+        lk<<<(unsigned)q.ws_ctas, kScanWarps * 32, smem, side.side>>>(q);
+        rc = launch_status();
+        if (rc) return rc;
+    }
+    int per_sm = 1;
     rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bank_scan_kernel<T, S, NC>,
                                                                    kScanWarps * 32, 0));
     if (rc) return rc;
     const int64_t want = ceil_div(q.units, kScanWarps);
-    const int64_t blocks = min((int64_t)sms * (per_sm > 0 ? per_sm : 1), want);
+    const int64_t blocks = BDM_SCAN_DYNAMIC ? min((int64_t)sms * (per_sm > 0 ? per_sm : 1), want)
+                                            : min(want, (int64_t)0x7fffffff);
     bank_scan_kernel<T, S, NC><<<(unsigned)blocks, kScanWarps * 32, 0, st>>>(q);
-    return launch_status();
+    rc = launch_status();
+    if (rc) return rc;
+    if (long_mode) {
+        rc = cuda_status(cudaEventRecord(side.join, side.side));
+        if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, side.join, 0));
+    }
+    return rc;
 }
 
 template <typename T>
@@ -633,7 +1158,8 @@ int launch_scan_shape(const ScanParams &p, int S, cudaStream_t st) {
 
 namespace bdm {
 namespace {
-// Workspace: [counts (kLenClasses int32) | dynamic counter (uint64)] then the lists.
+// Workspace: 256-byte header [counts (kLenClasses int32) at 0 | dynamic counter (uint64) at 64 |
+// status word (int32, BDM_SCAN_ERR_* bits) at 128], then the lists.
 constexpr int64_t kWsHeader = 256;
 inline int64_t scan_workspace_bytes(int64_t nseq) { return kWsHeader + (int64_t)kLenClasses * nseq * 4; }
 }  // namespace
@@ -650,7 +1176,8 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
                              int64_t time, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw,
                              int kr, int dtype, int routed_decay, float scale, const void *row_factor,
                              const void *col_factor, int64_t factor_cols, int factor_dtype,
-                             const int32_t *bank_ids, int64_t total_banks, void *cache, int cache_dtype,
+                             const int32_t *bank_ids, int64_t total_banks, int head_offset, int total_heads,
+                             void *cache, int cache_dtype,
                              int store_final, int state_interval, void *reads, void *workspace,
                              int64_t workspace_bytes, void *stream) {
     using namespace bdm;
@@ -666,10 +1193,13 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     if (batch * time * (int64_t)(kw + kr) >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
     if (batch * bank_count >= ((int64_t)1 << 31)) return BDM_ERR_UNSUPPORTED;
     if (bank_ids && total_banks < bank_count) return BDM_ERR_INVALID;
+    if (total_heads == 0) total_heads = heads;
+    if (head_offset < 0 || head_offset + heads > total_heads || (cache && total_heads != heads))
+        return BDM_ERR_INVALID;
     const int64_t table_banks = bank_ids ? total_banks : bank_count;
     if (!cache && row_factor) {
         if (!col_factor || factor_cols <= 0 || !valid_dtype(factor_dtype)) return BDM_ERR_INVALID;
-        if ((table_banks * heads * bank_size) % factor_cols) return BDM_ERR_INVALID;
+        if ((table_banks * total_heads * bank_size) % factor_cols) return BDM_ERR_INVALID;
     }
     const int64_t nseq = batch * bank_count;
     if (!workspace || workspace_bytes < scan_workspace_bytes(nseq)) return BDM_ERR_WORKSPACE;
@@ -685,6 +1215,7 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.col_factor = cache ? nullptr : col_factor;
     p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
     p.bank_ids = bank_ids; p.total_banks = table_banks;
+    p.head_offset = head_offset; p.total_heads = total_heads;
     p.cache = cache; p.cache_dtype = cache_dtype; p.store_final = store_final; p.interval = state_interval;
     p.reads = reads;
     char *ws = static_cast<char *>(workspace);
@@ -692,13 +1223,11 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     int *lists = reinterpret_cast<int *>(ws + kWsHeader);
     p.counts = counts;
     p.next = reinterpret_cast<unsigned long long *>(ws + 64);
+    p.status = reinterpret_cast<int *>(ws + 128);
     p.lists = lists;
     p.nseq = nseq;
     cudaStream_t st = as_stream(stream);
     int rc = cuda_status(cudaMemsetAsync(workspace, 0, kWsHeader, st));
-    if (rc) return rc;
-    build_worklist<<<1, kListThreads, 0, st>>>(cu_seqlens, nseq, p.E, lists, counts);
-    rc = launch_status();
     if (rc) return rc;
     BDM_DISPATCH_DTYPE(dtype, T, { return launch_scan_shape<T>(p, bank_size, st); });
     return BDM_OK;

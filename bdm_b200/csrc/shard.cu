@@ -10,9 +10,12 @@
 // (a Zipf-popular bank can take several percent of all events), so the default
 // partition is balanced by load, computed from the all-reduced per-bank event
 // counts of the current call: banks sorted by (count desc, index asc), then
-// dealt out in groups of `world`, the heaviest bank of each group to the least
-// loaded rank so far.  Every rank gets exactly J/world banks, and the map is a
-// pure function of the counts, so all ranks compute the same one.
+// dealt out in groups of `world`.  The first kGreedyGroups groups -- the heavy
+// head of the distribution -- go greedily, the heaviest bank of a group to the
+// least loaded rank so far; the light tail is dealt in one parallel step, in a
+// serpentine over the ranks ordered by their load after the head.  Every rank
+// gets exactly J/world banks, and the map is a pure function of the counts, so
+// all ranks compute the same one.
 #include "common.cuh"
 
 namespace bdm {
@@ -22,6 +25,7 @@ constexpr int kHistThreads = 256;
 constexpr int kOwnThreads = 1024;
 constexpr int kMaxBalancedBanks = 16384;  // keys of the whole table sorted in shared memory
 constexpr int kMaxBalancedWorld = 32;     // one lane per rank
+constexpr int kGreedyGroups = 128;        // groups dealt greedily (sequential); the rest in one serpentine
 
 __global__ void __launch_bounds__(kHistThreads)
 bank_histogram_kernel(const int64_t *__restrict__ wi, const int64_t *__restrict__ ri, int64_t ntok, int kw, int kr,
@@ -121,24 +125,36 @@ balanced_owners_kernel(const int32_t *__restrict__ counts, int J, int n_pow2, in
             __syncthreads();
         }
     }
-    // Deal out: group g holds sorted positions [g*world, (g+1)*world); the rank
-    // with the p-th smallest load (ties: lower rank) takes position g*world + p.
+    // Deal out: group g holds sorted positions [g*world, (g+1)*world); in the
+    // head, the rank with the p-th smallest load (ties: lower rank) takes
+    // position g*world + p.
+    __shared__ int rank_by_load[kMaxBalancedWorld];
+    const int groups = J / world;
+    const int head = min(groups, kGreedyGroups);
     if (tid < 32) {
         const int lane = tid;
         unsigned long long load = 0ull;
-        const int groups = J / world;
-        for (int g = 0; g < groups; ++g) {
-            int pos = 0;
+        int pos = 0;
+        for (int g = 0; g <= head; ++g) {
+            pos = 0;
             for (int l = 0; l < world; ++l) {
                 const unsigned long long o = __shfl_sync(0xffffffffu, load, l);
                 pos += (o < load) || (o == load && l < lane);
             }
-            if (lane < world) {
+            if (g < head && lane < world) {
                 const unsigned long long key = keys[g * world + pos];
                 own[(int)(key & 0xffffffffu)] = (unsigned char)lane;
                 load += 0xffffffffu - (unsigned)(key >> 32);
             }
         }
+        if (lane < world) rank_by_load[pos] = lane;  // rank order by load after the head
+    }
+    __syncthreads();
+    // Tail: group head + k goes in serpentine order over rank_by_load.
+    for (int i = head * world + tid; i < J; i += kOwnThreads) {
+        const int k = i / world - head, p = i % world;
+        const int r = rank_by_load[(k & 1) ? world - 1 - p : p];
+        own[(int)(keys[i] & 0xffffffffu)] = (unsigned char)r;
     }
     __syncthreads();
     // Slots: each thread owns a contiguous run of bank indices.

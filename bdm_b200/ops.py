@@ -23,6 +23,7 @@ from . import _lib
 from .config import near_square_factors
 
 _DT = {torch.float32: _lib.BDM_F32, torch.bfloat16: _lib.BDM_BF16}
+SCAN_STATUS_OFFSET = 128  # int32 error bits in the bank-scan workspace header
 
 
 def dtype_code(dtype: torch.dtype) -> int:
@@ -156,14 +157,15 @@ def product_state(row_factor, col_factor, *, batch: int, bank_count: int, heads:
 def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_seqlens, *, batch: int, time: int,
               bank_count: int, heads: int, bank_size: int, head_value_width: int, routed_decay: bool, scale: float,
               row_factor=None, col_factor=None, cache=None, store_final=False, state_interval=0,
-              bank_ids=None, total_banks=0):
+              bank_ids=None, total_banks=0, head_offset=0, total_heads=0, check_status=False):
     """Per-bank recurrence over dispatched events; returns reads [NT, KR, V] in the activation dtype.
 
     With ``cache`` ([batch, J, H, S, dv]) the state starts from it and, with
     ``store_final``, ends in it; otherwise it starts from the product-key factors
     (or zero when they are None).  On a bank-sharded rank ``bank_count`` is the
     local bank count and ``bank_ids`` (int32 [bank_count]) maps local banks into
-    the full table of ``total_banks`` banks.
+    the full table of ``total_banks`` banks.  ``heads`` may be a head group
+    [head_offset, head_offset + heads) of a layer with ``total_heads`` heads.
     """
     _cuda(q, k, v, g, b, w, write_idx, read_idx, order, cu_seqlens, cache, bank_ids)
     if bank_ids is not None and (bank_ids.dtype != torch.int32 or bank_ids.numel() != bank_count
@@ -196,8 +198,13 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         _ptr(cu_seqlens), batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt),
         int(routed_decay), float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
         dtype_code(u.dtype) if u is not None else 0, _ptr(bank_ids), int(total_banks) if bank_ids is not None else 0,
+        int(head_offset), int(total_heads),
         _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
         int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _stream(q.device)), 'bdm_bank_scan')
+    if check_status:  # synchronises: the kernel's error bits (a bounded producer/consumer wait that gave up)
+        status = int(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32).item())
+        if status:
+            raise _lib.BDMError(f'bdm_bank_scan: device status {status:#x} (a staging wait timed out)')
     return reads
 
 

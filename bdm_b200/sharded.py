@@ -23,14 +23,21 @@ bank table over R ranks (one process per GPU, ``torch.distributed``):
   the rank that holds the token, which rounds it once to the activation dtype
   (the forward's round-once combine) and applies norm, gate and o_proj.
 
+The bank stage runs in head groups (heads are independent in the recurrence),
+each group on its own CUDA stream: a group's recurrence starts as soon as its
+all-gather lands and its reduce-scatter starts as soon as its partial combine
+ends, so the exchange of one group overlaps the recurrence of the others, and
+the groups' longest bank sequences (the critical path of a skewed router) run
+side by side instead of once per group.
+
 Results match the single-device forward up to the FP32 summation order of the
 read combine (the partials are added across ranks, not bank by bank).
 Every rank must call ``forward`` with the same [B/R, T, D] shape.
 
-The stages (``local_stage``, ``histogram``, ``owners``, ``bank_stage``,
-``output_stage``) are methods so that the collective choreography in
-``forward`` can be exercised with other stage implementations (the CPU tests
-run it over gloo with the CPU oracle's stages).
+The stages (``local_stage``, ``histogram``, ``owners``, ``dispatch_stage``,
+``bank_stage``, ``output_stage``) are methods so that the collective
+choreography in ``forward`` can be exercised with other stage implementations
+(the CPU tests run it over gloo with the CPU oracle's stages).
 """
 from __future__ import annotations
 
@@ -42,12 +49,44 @@ from . import ops
 from .config import state_interval
 
 
-class ShardComm:
-    """The three collectives of the sharded forward over a ``torch.distributed`` group.
+class _Ready:
+    """A collective result that is already complete."""
 
-    NCCL moves device tensors directly.  With gloo (CPU tests, or several ranks
-    sharing one GPU) device tensors are staged through host memory, and the
+    def __init__(self, value):
+        self.value = value
+
+    def wait(self):
+        return self.value
+
+
+class _InFlight:
+    """An asynchronous NCCL collective; ``wait`` orders the current stream after it."""
+
+    def __init__(self, value, work):
+        self.value, self.work = value, work
+
+    def wait(self):
+        self.work.wait()
+        return self.value
+
+
+class _NoStream:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+class ShardComm:
+    """The collectives of the sharded forward over a ``torch.distributed`` group.
+
+    NCCL moves device tensors directly and asynchronously (on its own stream).
+    With gloo (CPU tests, or several ranks sharing one GPU) device tensors are
+    staged through host memory, every call completes before it returns, and the
     gather moves raw bytes (gloo has no 16-bit integer or bfloat16 type).
+    ``all_gather`` and ``reduce_scatter_sum`` return a handle whose ``wait()``
+    gives the result.
     """
 
     def __init__(self, group=None):
@@ -66,31 +105,34 @@ class ShardComm:
             t.copy_(h)
         return t
 
-    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
-        """[n, ...] on every rank -> [world*n, ...], rank-major."""
+    def all_gather(self, t: torch.Tensor):
+        """[n, ...] on every rank -> handle of [world*n, ...], rank-major."""
         t = t.contiguous()
         out = torch.empty((self.world * t.shape[0], *t.shape[1:]), dtype=t.dtype, device=t.device)
-        src, dst = self._host(t), (out.cpu() if (self.host_staged and out.is_cuda) else out)
-        if self.host_staged and t.numel() > 0:
+        if not self.host_staged:
+            return _InFlight(out, dist.all_gather_into_tensor(out, t, group=self.group, async_op=True))
+        src, dst = self._host(t), (out.cpu() if out.is_cuda else out)
+        if t.numel() > 0:
             dist.all_gather_into_tensor(dst.reshape(self.world, -1).view(torch.uint8),
                                         src.reshape(1, -1).view(torch.uint8), group=self.group)
-        else:
-            dist.all_gather_into_tensor(dst, src, group=self.group)
         if dst is not out:
             out.copy_(dst)
-        return out
+        return _Ready(out)
 
-    def reduce_scatter_sum(self, t: torch.Tensor) -> torch.Tensor:
-        """[world*n, ...] on every rank -> the sum over ranks of rows [rank*n, (rank+1)*n)."""
+    def reduce_scatter_sum(self, t: torch.Tensor):
+        """[world*n, ...] on every rank -> handle of the sum over ranks of rows [rank*n, (rank+1)*n)."""
         if t.shape[0] % self.world:
             raise ValueError('reduce-scatter rows must divide evenly over the ranks')
         t = t.contiguous()
         out = torch.empty((t.shape[0] // self.world, *t.shape[1:]), dtype=t.dtype, device=t.device)
-        src, dst = self._host(t), (out.cpu() if (self.host_staged and out.is_cuda) else out)
+        if not self.host_staged:
+            return _InFlight(out, dist.reduce_scatter_tensor(out, t, op=dist.ReduceOp.SUM, group=self.group,
+                                                             async_op=True))
+        src, dst = self._host(t), (out.cpu() if out.is_cuda else out)
         dist.reduce_scatter_tensor(dst, src, op=dist.ReduceOp.SUM, group=self.group)
         if dst is not out:
             out.copy_(dst)
-        return out
+        return _Ready(out)
 
 
 class BankShardedMemory:
@@ -101,7 +143,8 @@ class BankShardedMemory:
     returns this rank's output rows.
     """
 
-    def __init__(self, layer, group=None, *, ownership: str = 'balanced', comm: ShardComm | None = None):
+    def __init__(self, layer, group=None, *, ownership: str = 'balanced', head_groups: int | None = None,
+                 comm: ShardComm | None = None):
         if ownership not in ops.OWNERSHIP_MODES:
             raise ValueError(f'ownership must be one of {sorted(ops.OWNERSHIP_MODES)}')
         self.layer = layer
@@ -111,27 +154,76 @@ class BankShardedMemory:
         if layer.bank_count % self.world:
             raise NotImplementedError(f'{layer.bank_count} banks do not divide over {self.world} ranks')
         self.local_banks = layer.bank_count // self.world
+        heads = layer.num_heads
+        if head_groups is None:
+            head_groups = max(g for g in (1, 2, 4) if heads % g == 0)
+        if head_groups <= 0 or heads % head_groups:
+            raise ValueError(f'{heads} heads do not split into {head_groups} groups')
+        step = heads // head_groups
+        self.groups = [(h, h + step) for h in range(0, heads, step)]
         self.last_partition = None  # (owner, slot, members, counts) of the latest call
 
     # ------------------------------------------------------------ the exchange
     @torch.no_grad()
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
         lay = self.layer
-        lb, time, dim = hidden.shape
+        comm = self.comm
+        lb, time, _ = hidden.shape
+        batch = lb * self.world
         controls, routes, gate = self.local_stage(hidden)
         ww, wi, rw, ri = routes
         counts = self.histogram(wi, ri)
-        self.comm.all_reduce_sum_(counts)
+        comm.all_reduce_sum_(counts)
         owner, slot, members = self.owners(counts)
         self.last_partition = (owner, slot, members, counts)
-        all_controls = [self.comm.all_gather(c) for c in controls]
-        all_routes = [self.comm.all_gather(r) for r in routes]
-        partial = self.bank_stage(all_controls, all_routes, owner, slot, members, batch=lb * self.world, time=time)
-        combined = self.comm.reduce_scatter_sum(partial)
+        # every gather is queued now; NCCL runs them in order while this stream computes
+        route_h = [comm.all_gather(r) for r in routes]
+        control_h = [[comm.all_gather(self.head_slice(c, h0, h1)) for c in controls] for h0, h1 in self.groups]
+        all_routes = [h.wait() for h in route_h]
+        meta = self.dispatch_stage(all_routes, owner, slot)
+        partial_h = []
+        streams = self._streams(hidden)
+        main = torch.cuda.current_stream(hidden.device) if streams else None
+        for gi, ((h0, h1), handles) in enumerate(zip(self.groups, control_h)):
+            if streams:
+                streams[gi].wait_stream(main)
+                ctx = torch.cuda.stream(streams[gi])
+            else:
+                ctx = _NoStream()
+            with ctx:
+                group_controls = [h.wait() for h in handles]
+                partial = self.bank_stage(group_controls, all_routes, meta, owner, members, batch=batch,
+                                          time=time, head0=h0, heads=h1 - h0)
+                partial_h.append(comm.reduce_scatter_sum(partial))
+        for st in streams:
+            main.wait_stream(st)  # before any tensor used on a group stream is released
+        dv = lay.head_value_width
+        if len(self.groups) == 1:
+            combined = partial_h[0].wait()
+        else:
+            combined = torch.empty((lb * time, lay.value_width), dtype=torch.float32, device=hidden.device)
+            for (h0, h1), h in zip(self.groups, partial_h):
+                combined[:, h0 * dv:h1 * dv] = h.wait()
         out = self.output_stage(hidden, combined, gate)
         return out.reshape(lb, time, lay.hidden_size)
 
-    __call__ = forward
+    def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
+        return self.forward(hidden)
+
+    def _streams(self, hidden):
+        """One side stream per head group (device tensors with more than one group), created once."""
+        if not hidden.is_cuda or len(self.groups) == 1:
+            return []
+        if getattr(self, '_group_streams', None) is None or self._group_streams[0].device != hidden.device:
+            self._group_streams = [torch.cuda.Stream(device=hidden.device) for _ in self.groups]
+        return self._group_streams
+
+    def head_slice(self, control, h0, h1):
+        """Columns of heads [h0, h1) of a [tokens, H * width] controller tensor."""
+        if (h0, h1) == (0, self.layer.num_heads):
+            return control
+        width = control.shape[1] // self.layer.num_heads
+        return control[:, h0 * width:h1 * width]
 
     # --------------------------------------------------------------- stages
     def local_stage(self, hidden):
@@ -147,18 +239,23 @@ class BankShardedMemory:
         return ops.bank_owners(counts if mode == 'balanced' else None, self.layer.bank_count, self.world, mode=mode,
                                device=counts.device)
 
-    def bank_stage(self, controls, routes, owner, slot, members, *, batch, time):
-        """Dispatch, recurrence and partial combine of this rank's banks -> FP32 [batch*time, V]."""
+    def dispatch_stage(self, routes, owner, slot):
+        ww, wi, rw, ri = routes
+        return ops.dispatch_owned(wi, ri, self.layer.bank_count, owner, slot, self.rank, self.local_banks)
+
+    def bank_stage(self, controls, routes, meta, owner, members, *, batch, time, head0, heads):
+        """Recurrence and partial combine of this rank's banks for heads [head0, head0 + heads)
+        -> FP32 [batch*time, heads*dv]."""
         lay = self.layer
         ww, wi, rw, ri = routes
-        meta = ops.dispatch_owned(wi, ri, lay.bank_count, owner, slot, self.rank, self.local_banks)
         interval = state_interval(lay.bank_size) if lay.config.training_state_dtype == 'bfloat16' else 0
         reads = ops.bank_scan(*controls, wi, ww, ri, rw, meta['order'], meta['cu_seqlens'], batch=batch, time=time,
-                              bank_count=self.local_banks, heads=lay.num_heads, bank_size=lay.bank_size,
+                              bank_count=self.local_banks, heads=heads, bank_size=lay.bank_size,
                               head_value_width=lay.head_value_width, routed_decay=lay.config.routed_decay,
                               scale=lay.bank_size ** -0.5, row_factor=lay.initial_row_factor,
                               col_factor=lay.initial_column_factor, state_interval=interval,
-                              bank_ids=members[self.rank], total_banks=lay.bank_count)
+                              bank_ids=members[self.rank], total_banks=lay.bank_count, head_offset=head0,
+                              total_heads=lay.num_heads)
         return ops.combine_partial(reads, ri.reshape(batch * time, -1), owner, self.rank)
 
     def output_stage(self, hidden, combined, gate):

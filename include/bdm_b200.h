@@ -154,9 +154,16 @@ BDM_API int bdm_product_state(const void *row_factor, const void *col_factor, in
  * (batch, local bank) and bank_ids maps a local bank to its bank in the full
  * table of total_banks banks (used for the product-key initial state); NULL
  * means local = global and total_banks is ignored.
+ * head_offset, total_heads: the call's `heads` heads are heads
+ * [head_offset, head_offset + heads) of a layer with total_heads heads (a head
+ * group; only the product-key initial state depends on it).  total_heads = 0
+ * means heads (and head_offset 0); a cache needs the whole layer.
  * workspace: device scratch of bdm_bank_scan_workspace_bytes(batch, bank_count)
  * bytes (the per-launch work list: non-empty sequences by length class, so
- * long sequences start first and empty ones cost nothing).
+ * long sequences start first and empty ones cost nothing).  The int32 at byte
+ * 128 of the workspace holds error bits after the kernel: 1 = a wait between
+ * the staging warp and the state warps of a CTA gave up (bounded at ~2 s; the
+ * CTA's outputs are then incomplete).
  * Supported: bank_size in {4, 8, 16}; head_value_width a multiple of 8.
  */
 BDM_API int64_t bdm_bank_scan_workspace_bytes(int64_t batch, int64_t bank_count);
@@ -166,7 +173,8 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
                           int64_t bank_count, int heads, int bank_size, int head_value_width, int kw, int kr,
                           int dtype, int routed_decay, float scale, const void *row_factor, const void *col_factor,
                           int64_t factor_cols, int factor_dtype, const int32_t *bank_ids, int64_t total_banks,
-                          void *cache, int cache_dtype, int store_final, int state_interval, void *reads,
+                          int head_offset, int total_heads, void *cache, int cache_dtype, int store_final,
+                          int state_interval, void *reads,
                           void *workspace, int64_t workspace_bytes, void *stream);
 
 /*
@@ -197,8 +205,10 @@ BDM_API int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, in
  *   zeroed by the caller; out-of-range banks are clamped).
  * bdm_bank_owners: the partition.  mode 0 = contiguous index ranges
  *   (owner = bank / (J/world)); mode 1 = balanced by load: banks sorted by
- *   (count desc, index asc), then taken in groups of `world`, the heaviest bank
- *   of a group going to the least loaded rank (ties to the lower rank).  Both
+ *   (count desc, index asc), then taken in groups of `world`; in the first 128
+ *   groups the p-th heaviest bank of a group goes to the rank with the p-th
+ *   smallest load (ties to the lower rank), later groups go in a serpentine
+ *   over the ranks ordered by their load after group 128.  Both
  *   give every rank exactly J/world banks; J % world == 0 is required and mode 1
  *   needs J <= 16384 and world <= 32.  Outputs, int32: owner [J], slot [J] (the
  *   bank's index among its owner's banks, ascending bank order) and members

@@ -19,6 +19,9 @@ from __future__ import annotations
 import numpy as np
 
 
+GREEDY_GROUPS = 128  # groups of the balanced partition dealt greedily
+
+
 def oracle_bank_histogram(wi, ri, bank_count: int) -> np.ndarray:
     banks = np.concatenate([np.asarray(wi, np.int64).ravel(), np.asarray(ri, np.int64).ravel()])
     banks = np.clip(banks, 0, bank_count - 1)
@@ -29,9 +32,12 @@ def oracle_bank_owners(counts, bank_count: int, world: int, mode: str = 'balance
     """-> (owner [J], slot [J], members [world, J/world]) int32.
 
     contiguous: owner = bank // (J/world).  balanced: banks in (count desc, index
-    asc) order are dealt out in groups of ``world``; within a group the p-th
-    heaviest bank goes to the rank with the p-th smallest load so far (ties to
-    the lower rank).  Slots number each rank's banks in ascending bank order.
+    asc) order are dealt out in groups of ``world``.  In the first GREEDY_GROUPS
+    groups the p-th heaviest bank of a group goes to the rank with the p-th
+    smallest load so far (ties to the lower rank); the remaining groups go in a
+    serpentine (forward on even groups, backward on odd ones, counted from the
+    first tail group) over the ranks ordered by their load after those groups.
+    Slots number each rank's banks in ascending bank order.
     """
     if bank_count % world:
         raise ValueError('bank count must divide over the ranks')
@@ -43,12 +49,18 @@ def oracle_bank_owners(counts, bank_count: int, world: int, mode: str = 'balance
         order = sorted(range(bank_count), key=lambda j: (-c[j], j))
         load = [0] * world
         owner = np.empty(bank_count, np.int64)
-        for g in range(per):
+        head = min(per, GREEDY_GROUPS)
+        for g in range(head):
             ranks = sorted(range(world), key=lambda r: (load[r], r))
             for p, r in enumerate(ranks):
                 j = order[g * world + p]
                 owner[j] = r
                 load[r] += int(c[j])
+        ranks = sorted(range(world), key=lambda r: (load[r], r))
+        for g in range(head, per):
+            k = g - head
+            for p in range(world):
+                owner[order[g * world + p]] = ranks[world - 1 - p] if k % 2 else ranks[p]
     else:
         raise ValueError(mode)
     slot = np.empty(bank_count, np.int64)

@@ -76,8 +76,8 @@ def test_bank_partition_limits():
 def test_unsupported_geometry_is_reported():
     lib = _lib.load()
     dummy = ctypes.c_void_p(16)
-    rc = lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 32, 64, 8, 8, 1, 1, 0.25, None, None, 0, 0, None, 0, None,
-                           0, 0, 0, dummy, dummy, 1 << 20, None)
+    rc = lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 32, 64, 8, 8, 1, 1, 0.25, None, None, 0, 0, None, 0, 0, 0,
+                           None, 0, 0, 0, dummy, dummy, 1 << 20, None)
     assert rc == _lib.BDM_ERR_UNSUPPORTED  # bank_size 32 is not implemented
     with pytest.raises(NotImplementedError):
         _lib.check(rc, 'bdm_bank_scan')

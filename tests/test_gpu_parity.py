@@ -123,21 +123,21 @@ def test_dispatch_edge_cases_and_golden(golden_dir):
 
 
 # -------------------------------------------------------------- recurrence
-def _controls(gen, nt, heads, s, dv, dtype):
+def _controls(gen, nt, heads, s, dv, dtype, decay=0.3):
     q = torch.nn.functional.normalize(torch.randn(nt, heads, s, generator=gen), dim=-1).to(dtype)
     k = torch.nn.functional.normalize(torch.randn(nt, heads, s, generator=gen), dim=-1).to(dtype)
     v = torch.randn(nt, heads * dv, generator=gen).to(dtype)
-    g = -torch.rand(nt, heads, s, generator=gen) * 0.3
+    g = -torch.rand(nt, heads, s, generator=gen) * decay
     b = torch.rand(nt, heads, s, generator=gen).to(dtype)
     w = torch.rand(nt, heads * dv, generator=gen).to(dtype)
     return q.reshape(nt, -1), k.reshape(nt, -1), v, g.reshape(nt, -1), b.reshape(nt, -1), w
 
 
 def _run_scan(batch, time, bank_count, selected, heads, s, dv, dtype, *, interval, routed, cache_dtype=None,
-              seed=0):
+              seed=0, decay=0.3):
     gen = torch.Generator().manual_seed(seed)
     nt = batch * time
-    ctl = _controls(gen, nt, heads, s, dv, dtype)
+    ctl = _controls(gen, nt, heads, s, dv, dtype, decay)
     ww, wi, rw, ri = _random_routes(gen, batch, time, bank_count, selected)
     ww, rw = ww.to(dtype), rw.to(dtype)
     rows, cols = near_square_factors(bank_count * heads * s)
@@ -151,13 +151,15 @@ def _run_scan(batch, time, bank_count, selected, heads, s, dv, dtype, *, interva
     kw = dict(batch=batch, time=time, bank_count=bank_count, heads=heads, bank_size=s, head_value_width=dv,
               routed_decay=routed, scale=s ** -0.5)
     if cache_dtype is None:
-        reads = ops.bank_scan(*args, **kw, row_factor=u.to(DEV), col_factor=z.to(DEV), state_interval=interval)
+        reads = ops.bank_scan(*args, **kw, row_factor=u.to(DEV), col_factor=z.to(DEV), state_interval=interval,
+                              check_status=True)
         final = None
         init_b = init[None]
     else:
         cache = torch.from_numpy(np.broadcast_to(init, (batch,) + init.shape).copy()).to(cache_dtype).to(DEV)
         init_b = npf(cache)
-        reads = ops.bank_scan(*args, **kw, cache=cache, store_final=True, state_interval=interval)
+        reads = ops.bank_scan(*args, **kw, cache=cache, store_final=True, state_interval=interval,
+                              check_status=True)
         final = cache
     q, k, v, g, b, w = (npf(t) for t in ctl)
     sh = lambda x, last: x.reshape(batch, time, heads, last)
@@ -175,6 +177,30 @@ def test_bank_scan_forward(s, dv, heads, dtype):
     ours, ref, _, _ = _run_scan(2, 200, 64, 4, heads, s, dv, dtype, interval=interval, routed=True, seed=s + dv)
     tol = BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
     assert max_rel(ours, ref) <= tol, max_rel(ours, ref)
+
+
+@pytest.mark.parametrize('s,dv,heads', [(16, 128, 2), (8, 128, 1), (8, 192, 1), (16, 192, 1), (4, 64, 2)])
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_bank_scan_long_sequences(s, dv, heads, dtype):
+    # 4 banks, 2 per role: every (batch, bank) sequence has ~2600 events, so the
+    # sequences run on the warp-specialised (producer / consumer warps) path
+    interval = state_interval(s) if dtype == torch.bfloat16 else 0
+    ours, ref, _, _ = _run_scan(2, 2600, 4, 2, heads, s, dv, dtype, interval=interval, routed=True, seed=11 + s)
+    tol = BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
+    assert max_rel(ours, ref) <= tol, max_rel(ours, ref)
+
+
+@pytest.mark.parametrize('cache_dtype', [torch.float32, torch.bfloat16])
+def test_bank_scan_long_sequences_prefill_and_decay_cuts(cache_dtype):
+    # strong decays: the cumulative log-decay crosses the -60 floor inside batches,
+    # so batches are cut short and the staging restarts mid-batch
+    for dtype in (torch.float32, torch.bfloat16):
+        ours, ref, final, ofinal = _run_scan(1, 2400, 4, 2, 2, 16, 128, dtype, interval=0, routed=True,
+                                             cache_dtype=cache_dtype, seed=5, decay=12.0)
+        tol = BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
+        assert max_rel(ours, ref) <= tol, max_rel(ours, ref)
+        ofinal_c = oracle.bf16_round(ofinal) if cache_dtype == torch.bfloat16 else ofinal
+        assert max_rel(final.reshape(ofinal_c.shape), ofinal_c) <= (tol if cache_dtype == torch.float32 else BF16_TOL)
 
 
 @pytest.mark.parametrize('cache_dtype', [torch.float32, torch.bfloat16])

@@ -81,12 +81,16 @@ class OracleStages(BankShardedMemory):
         return tuple(torch.from_numpy(a) for a in oracle.oracle_bank_owners(
             counts.numpy(), self.layer.bank_count, self.world, self.ownership))
 
-    def bank_stage(self, controls, routes, owner, slot, members, *, batch, time):
+    def dispatch_stage(self, routes, owner, slot):
+        return None  # the oracle recurrence orders events itself
+
+    def bank_stage(self, controls, routes, meta, owner, members, *, batch, time, head0, heads):
         o = self.o
-        q, k, v, g, b, w = (c.numpy().reshape(batch, time, o.H, -1) for c in controls)
+        q, k, v, g, b, w = (c.numpy().reshape(batch, time, heads, -1) for c in controls)
         ww, wi, rw, ri = (r.numpy() for r in routes)
         interval = oracle.state_interval(o.S) if o.c['training_state_dtype'] == 'bfloat16' else 0
-        reads, _ = oracle.oracle_recurrence(q, k, v, g, b, w, wi, ww, ri, rw, o.initial_state()[None],
+        init = np.ascontiguousarray(o.initial_state()[None][:, :, head0:head0 + heads])
+        reads, _ = oracle.oracle_recurrence(q, k, v, g, b, w, wi, ww, ri, rw, init,
                                             bank_count=o.J, bf16=o.bf16, routed_decay=o.c['routed_decay'],
                                             interval=interval, scale=o.S ** -0.5, want_state=False)
         kr = ri.shape[-1]
@@ -113,29 +117,29 @@ def _hidden():
     return torch.randn(BATCH, TIME, CFG['dim'], generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, mode, out_dir):
+def _worker(rank, world, port, mode, groups, out_dir):
     os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
     dist.init_process_group('gloo', rank=rank, world_size=world)
     try:
         m, olayer = _model()
         x = _hidden()
         rows = BATCH // world
-        sharded = OracleStages(m, olayer, ownership=mode)
+        sharded = OracleStages(m, olayer, ownership=mode, head_groups=groups)
         y = sharded(x[rank * rows:(rank + 1) * rows])
         owner = sharded.last_partition[0]
         # the gather carries any element type bit for bit (bf16 controllers, int64 routes)
         comm = sharded.comm
         probe = [torch.full((3, 5), rank + 0.5, dtype=torch.bfloat16), torch.full((2, 4, 3), 7 * rank + 1)]
-        gathered = [comm.all_gather(t) for t in probe]
+        gathered = [comm.all_gather(t).wait() for t in probe]
         torch.save({'y': y, 'owner': owner, 'gathered': gathered}, os.path.join(out_dir, f'rank{rank}.pt'))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize('mode', ['balanced', 'contiguous'])
-def test_sharded_forward_gloo_world2(tmp_path, mode):
+@pytest.mark.parametrize('mode,groups', [('balanced', 2), ('contiguous', 1)])
+def test_sharded_forward_gloo_world2(tmp_path, mode, groups):
     world = 2
-    mp.spawn(_worker, args=(world, _free_port(), mode, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), mode, groups, str(tmp_path)), nprocs=world, join=True)
     m, olayer = _model()
     want = olayer.forward(olayer.r(_hidden().float().numpy()))
     parts = [torch.load(tmp_path / f'rank{r}.pt') for r in range(world)]

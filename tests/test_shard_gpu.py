@@ -126,6 +126,32 @@ def test_owned_recurrence_reproduces_single_device_reads(dtype, world):
 
 
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_head_group_recurrence_reproduces_all_head_reads(dtype):
+    cfg = dict(dim=128, bank_count=256, bank_size=4, selected_banks=8, value_width=512, num_heads=4)
+    m = _layer(cfg, 12, dtype)
+    batch, time = 2, 150
+    x = torch.randn(batch, time, cfg['dim'], generator=torch.Generator().manual_seed(5)).to(dtype).to(DEV)
+    J, H, S, dv = m.bank_count, m.num_heads, m.bank_size, m.head_value_width
+    common = dict(batch=batch, time=time, bank_size=S, head_value_width=dv, routed_decay=True, scale=S ** -0.5,
+                  row_factor=m.initial_row_factor, col_factor=m.initial_column_factor, state_interval=state_interval(S))
+    with torch.no_grad():
+        controls, routes, _ = m._controls_and_routes(x)
+        ww, wi, rw, ri = routes
+        counts = ops.bank_histogram(wi, ri, J)
+        owner, slot, members = ops.bank_owners(counts, J, 2, mode='balanced')
+        mo = ops.dispatch_owned(wi, ri, J, owner, slot, 1, J // 2)
+        full = ops.bank_scan(*controls, wi, ww, ri, rw, mo['order'], mo['cu_seqlens'], bank_count=J // 2, heads=H,
+                             bank_ids=members[1], total_banks=J, **common)
+        mine = (owner[ri.reshape(-1)] == 1).reshape(batch * time, -1)
+        for h0, h1 in ((0, 2), (2, 3), (3, 4)):
+            part = [c.reshape(batch * time, H, -1)[:, h0:h1].reshape(batch * time, -1).contiguous() for c in controls]
+            got = ops.bank_scan(*part, wi, ww, ri, rw, mo['order'], mo['cu_seqlens'], bank_count=J // 2,
+                                heads=h1 - h0, bank_ids=members[1], total_banks=J, head_offset=h0, total_heads=H,
+                                **common)
+            assert torch.equal(got[mine], full[mine][:, h0 * dv:h1 * dv])
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize('layer_norm', [True, False])
 def test_norm_gate_f32_equals_round_once_combine(dtype, layer_norm):
     gen = torch.Generator().manual_seed(4)
@@ -158,7 +184,7 @@ def _shard_inputs():
                        generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
 
 
-def _shard_worker(rank, world, port, backend, mode, out_dir):
+def _shard_worker(rank, world, port, backend, mode, groups, out_dir):
     os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
     dev = torch.device('cuda', rank if backend == 'nccl' else 0)
     torch.cuda.set_device(dev)
@@ -172,7 +198,7 @@ def _shard_worker(rank, world, port, backend, mode, out_dir):
         m._fused_cache = None
         rows = SHARD_BATCH // world
         x = _shard_inputs()[rank * rows:(rank + 1) * rows].to(dev)
-        y = BankShardedMemory(m, ownership=mode)(x)
+        y = BankShardedMemory(m, ownership=mode, head_groups=groups)(x)
         torch.cuda.synchronize()
         torch.save(y.cpu(), os.path.join(out_dir, f'rank{rank}.pt'))
     finally:
@@ -188,10 +214,11 @@ def _single_device_reference():
         return m(_shard_inputs().to(DEV)).float().cpu()
 
 
-@pytest.mark.parametrize('mode', ['balanced', 'contiguous'])
-def test_sharded_forward_two_ranks_one_gpu(tmp_path, mode):
+@pytest.mark.parametrize('mode,groups', [('balanced', 4), ('contiguous', 1)])
+def test_sharded_forward_two_ranks_one_gpu(tmp_path, mode, groups):
     world = 2
-    mp.spawn(_shard_worker, args=(world, _free_port(), 'gloo', mode, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_shard_worker, args=(world, _free_port(), 'gloo', mode, groups, str(tmp_path)), nprocs=world,
+             join=True)
     got = torch.cat([torch.load(tmp_path / f'rank{r}.pt') for r in range(world)]).float()
     want = _single_device_reference()
     err = ((got - want).abs().max() / want.abs().max()).item()
@@ -204,7 +231,7 @@ def test_sharded_forward_nccl():
     world = 4 if torch.cuda.device_count() >= 4 else 2
     import tempfile
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_shard_worker, args=(world, _free_port(), 'nccl', 'balanced', d), nprocs=world, join=True)
+        mp.spawn(_shard_worker, args=(world, _free_port(), 'nccl', 'balanced', 2, d), nprocs=world, join=True)
         got = torch.cat([torch.load(os.path.join(d, f'rank{r}.pt')) for r in range(world)]).float()
     want = _single_device_reference()
     err = ((got - want).abs().max() / want.abs().max()).item()
