@@ -74,6 +74,7 @@ struct ScanParams {
     const int *lists;     // kLenClasses lists of capacity nseq
     const int *counts;    // [kLenClasses] list lengths
     unsigned long long *next;  // dynamic work counter (zero at launch)
+    unsigned long long *long_next;  // the long kernel's work counter (zero at launch)
     int *status;               // error bits (BDM_SCAN_ERR_*), zero at launch
     int ws_classes;            // length classes run by warp-specialised CTAs (0: none)
     int64_t ws_ctas;           // CTAs [0, ws_ctas) run those units
@@ -635,7 +636,7 @@ bank_scan_kernel(const ScanParams p) {
 // returns; the other warps then fail their own bounded waits and return.
 // ===========================================================================
 constexpr int kWsMaxTiles = kScanWarps - 1;  // consumers per CTA
-constexpr int kWsSlots = 2;
+constexpr int kWsSlots = 3;
 constexpr long long kWaitPolls = 1ll << 22;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
@@ -674,7 +675,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
 // Shared memory of a warp-specialised CTA: the ring (fixed part), the
 // producer's raw row buffers, then the staged value rows (sized at launch by
 // the number of column tiles).
-constexpr int kWsBatch = 16;  // events per staged batch in long mode (every S)
+constexpr int kWsBatch = 32;  // events per staged batch in long mode (every S): one per producer lane
 template <typename T, int S> struct WsShared {
     static constexpr int EB = kWsBatch;
     float2 ctl[kWsSlots][EB][CtlLayout<S>::size];
@@ -683,6 +684,7 @@ template <typename T, int S> struct WsShared {
     int n[kWsSlots];
     unsigned wmask[kWsSlots], rmask[kWsSlots];
     uint64_t full[kWsSlots], empty[kWsSlots];
+    long long item;
     int abort;
     __align__(16) unsigned char raw[2][EB][RawLayout<T, S>::size];
 };
@@ -699,6 +701,10 @@ struct Staged {
     bool write;
     float wt;
 };
+
+// Ring slot of the it-th batch and the phase parity of its n-th use.
+__device__ __forceinline__ int ring_slot(unsigned it) { return (int)(it % kWsSlots); }
+__device__ __forceinline__ unsigned use_parity(unsigned it) { return (it / kWsSlots) & 1u; }
 
 template <typename T, int S, int NC>
 __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned char *smem) {
@@ -725,7 +731,6 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
         sh.abort = 0;
     }
     __syncthreads();
-    if (warp > tiles) return;  // warps beyond the column tiles take no part
 
     volatile int *abort_flag = &sh.abort;
     auto fail = [&]() {
@@ -740,7 +745,13 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
     const int nw = (int)p.nw, kw = p.kw, kr = p.kr, nt = (int)p.nt, E = (int)p.E;
     unsigned it = 0;  // batches handed through the ring (same count on every warp)
 
-    for (int64_t item = blockIdx.x; item < total && !*abort_flag; item += gridDim.x) {
+    for (;;) {
+        // units in LPT order: the next longest unit goes to the next free CTA
+        __syncthreads();
+        if (threadIdx.x == 0) sh.item = (long long)atomicAdd(p.long_next, 1ull);
+        __syncthreads();
+        const int64_t item = sh.item;
+        if (item >= total || *abort_flag) break;
         int64_t local = item / p.H;
         int cls = 0;
         while (cls < kLenClasses - 1 && local >= p.counts[cls]) local -= p.counts[cls++];
@@ -758,13 +769,18 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
             const T *wwp = static_cast<const T *>(p.ww);
             const T *rwp = static_cast<const T *>(p.rw);
             // ids, weights and k|b|g / q rows of events [bbase, bbase + bn): lane = event
+            // ids of the batch after the one being issued, loaded one batch ahead
+            int64_t pre_base = -1, pre_id = -1;
             auto issue_rows = [&](int64_t bbase, int bn, unsigned char (*rawb)[Raw::size], Staged &st) {
                 st.tok = -1;
                 st.rid = -1;
                 st.write = false;
                 st.wt = 0.f;
+                const int64_t my_id = bbase == pre_base ? pre_id : (lane < bn ? p.order[bbase + lane] : -1);
+                pre_base = bbase + bn;
+                pre_id = (lane < EB && pre_base + lane < end) ? p.order[pre_base + lane] : -1;
                 if (lane < bn) {
-                    const int64_t id = p.order[bbase + lane];
+                    const int64_t id = my_id;
                     if (id >= 0 && id < nw) {
                         st.tok = (int)id / kw;
                         st.write = true;
@@ -865,9 +881,19 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
                         ctl[lane][Ctl::p] = weight_pair<T>(st.wt);
                     } else {
 #pragma unroll
-                        for (int s = 0; s < S; ++s)
+                        for (int s = 0; s < S; ++s) {
                             ctl[lane][Ctl::c + s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * st.wt) * D[s]);
+                            ctl[lane][Ctl::kd + s] = make_float2(0.f, 0.f);
+                        }
+                        ctl[lane][Ctl::p] = make_float2(0.f, 0.f);
                     }
+                } else if (use) {
+#pragma unroll
+                    for (int s = 0; s < S; ++s) {
+                        ctl[lane][Ctl::c + s] = make_float2(0.f, 0.f);
+                        ctl[lane][Ctl::kd + s] = make_float2(0.f, 0.f);
+                    }
+                    ctl[lane][Ctl::p] = make_float2(0.f, 0.f);
                 }
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
@@ -894,10 +920,13 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
             int64_t base = start;
             int bn = (int)min((int64_t)EB, end - base);
             bool ok = true;
-            // first batch of the unit: its slot was released by the batch two before it
+            // A batch's slot frees when the consumers finish the batch kWsSlots before it.
+            auto acquire = [&](unsigned j) {
+                return j < kWsSlots || mbar_wait(&sh.empty[ring_slot(j)], use_parity(j - kWsSlots));
+            };
             issue_rows(base, bn, sh.raw[it & 1], cur);
-            if (it >= kWsSlots && !mbar_wait(&sh.empty[it & 1], ((it >> 1) - 1) & 1u)) ok = false;
-            if (ok) issue_values(bn, cur, it & 1);
+            if (!acquire(it)) ok = false;
+            if (ok) issue_values(bn, cur, ring_slot(it));
             cp_async_commit();
             while (ok && base < end) {
                 const int64_t sbase = base + bn;  // next batch if this one is not cut
@@ -906,7 +935,7 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
                     issue_rows(sbase, sbn, sh.raw[(it + 1) & 1], nxt);
                     cp_async_commit();
                 }
-                const int b = (int)(it & 1u);
+                const int b = ring_slot(it);
                 const int n = finish(base - start, bn, sh.raw[it & 1], cur, b, sbn > 0);
                 mbar_arrive(&sh.full[b]);
                 if (n < bn) {  // cut: the next batch starts right after the n-th event
@@ -919,12 +948,12 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
                     bn = sbn;
                 }
                 ++it;
-                if (base < end) {  // the next batch's slot frees when the consumers finish batch it-2
-                    if (it >= kWsSlots && !mbar_wait(&sh.empty[it & 1], ((it >> 1) - 1) & 1u)) {
+                if (base < end) {
+                    if (!acquire(it)) {
                         ok = false;
                         break;
                     }
-                    issue_values(bn, nxt, it & 1);
+                    issue_values(bn, nxt, ring_slot(it));
                     cp_async_commit();
                 }
                 cur = nxt;
@@ -943,24 +972,69 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
             int64_t base = start;
             bool ok = true;
             while (base < end) {
-                const int b = (int)(it & 1u);
-                if (!mbar_wait(&sh.full[b], (it >> 1) & 1u)) {
+                const int b = ring_slot(it);
+                if (!mbar_wait(&sh.full[b], use_parity(it))) {
                     ok = false;
                     break;
                 }
                 const int n = sh.n[b];
                 const unsigned wmask = sh.wmask[b], rmask = sh.rmask[b];
                 const float2(*ctl)[Ctl::size] = sh.ctl[b];
-#pragma unroll 4
+                // Every event runs the same straight-line code (reads have zero k/D rows
+                // and a zeroed update), so consecutive events pipeline.
                 for (int ev = 0; ev < n; ++ev) {
-                    Row<T, NC> vr, wr;
-                    const bool wr_ev = (wmask >> ev) & 1u;
-                    if (wr_ev) {
-                        vr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 0) + lane * NC);
-                        wr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 1) + lane * NC);
+                    if ((rmask >> ev) & 1u) {  // storage point: materialise, round to BF16
+#pragma unroll
+                        for (int s = 0; s < S; ++s) {
+                            const float2 d2 = ctl[ev][Ctl::dprev + s];
+#pragma unroll
+                            for (int c = 0; c < NP; ++c) N[s][c] = bf16_round_pair(__fmul2_rn(N[s][c], d2));
+                        }
                     }
-                    event_step<T, S, NC>(ctl[ev], (rmask >> ev) & 1u, wr_ev, sh.tok[b][ev] >= 0, active, vr, wr,
-                                         p.scale, outp + (int64_t)sh.rid[b][ev] * V, N);
+                    const bool wr_ev = (wmask >> ev) & 1u;
+                    const float4 *crow = reinterpret_cast<const float4 *>(ctl[ev] + Ctl::c);
+                    const float4 *krow = reinterpret_cast<const float4 *>(ctl[ev] + Ctl::kd);
+                    const Row<T, NC> vr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 0) + lane * NC);
+                    const Row<T, NC> wr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 1) + lane * NC);
+                    float2 dot[NP][4];
+#pragma unroll
+                    for (int c = 0; c < NP; ++c)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) dot[c][i] = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int s = 0; s < S; s += 2) {
+                        const float4 cc = crow[s / 2];
+                        const int i = (s / 2) & 3;
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) {
+                            dot[c][i] = __ffma2_rn(make_float2(cc.x, cc.y), N[s][c], dot[c][i]);
+                            dot[c][(i + 2) & 3] = __ffma2_rn(make_float2(cc.z, cc.w), N[s + 1][c], dot[c][(i + 2) & 3]);
+                        }
+                    }
+                    const float2 pw = ctl[ev][Ctl::p];
+                    float2 u[NP];
+#pragma unroll
+                    for (int c = 0; c < NP; ++c) {
+                        const float2 d = __fadd2_rn(__fadd2_rn(dot[c][0], dot[c][1]), __fadd2_rn(dot[c][2], dot[c][3]));
+                        dot[c][0] = d;
+                        const float2 uw = WriteValue<T>::apply(wr.x + 2 * c, vr.x + 2 * c, pw, make_float2(-d.x, -d.y));
+                        u[c] = wr_ev ? uw : make_float2(0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int s = 0; s < S; s += 2) {
+                        const float4 kk = krow[s / 2];
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) {
+                            N[s][c] = __ffma2_rn(make_float2(kk.x, kk.y), u[c], N[s][c]);
+                            N[s + 1][c] = __ffma2_rn(make_float2(kk.z, kk.w), u[c], N[s + 1][c]);
+                        }
+                    }
+                    if (!wr_ev && sh.tok[b][ev] >= 0 && active) {
+                        Row<T, NC> o;
+#pragma unroll
+                        for (int c = 0; c < NP; ++c) store_pair<T>(o.x + 2 * c, __fmul2_rn(dot[c][0], dup(p.scale)));
+                        store_row<T, NC>(outp + (int64_t)sh.rid[b][ev] * V, o);
+                    }
                 }
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
@@ -998,6 +1072,7 @@ bank_scan_long_kernel(const ScanParams p) {
 // Work list: every non-empty sequence goes to the list of its length class, in
 // ascending sequence order (one CTA: per-thread contiguous chunks + block scans).
 constexpr int kListThreads = 1024;
+constexpr int kMaxSortedLong = 4096;  // long sequences sorted by length (more stay in sequence order)
 
 __device__ __forceinline__ int len_class(const int64_t *cu, int64_t s, int64_t E, int64_t long_min) {
     const int64_t a = min(max(cu[s], (int64_t)0), E), b = min(max(cu[s + 1], a), E);
@@ -1010,8 +1085,14 @@ __device__ __forceinline__ int len_class(const int64_t *cu, int64_t s, int64_t E
 }
 
 __global__ void __launch_bounds__(kListThreads)
-build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int64_t long_min, int *__restrict__ lists,
+build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int64_t unit_factor, int64_t slots,
+               int *__restrict__ lists,
                int *__restrict__ counts) {
+    // long-sequence bound of this launch: the (event, head, tile) work of the
+    // events it runs (cu[nseq]; fewer than E on a bank-sharded rank) over the
+    // GPU's warp slots, and at least kLongEvents; unit_factor 0 disables it
+    const int64_t ran = min(max(cu[nseq], (int64_t)0), E);
+    const int64_t long_min = unit_factor > 0 ? max(kLongEvents, ran * unit_factor / slots) : ((int64_t)1 << 62);
     __shared__ int warp_tot[kLenClasses][32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t chunk = (nseq + kListThreads - 1) / kListThreads;
@@ -1055,6 +1136,42 @@ build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int64_t 
         const int c = len_class(cu, s, E, long_min);
         if (c >= 0) lists[(int64_t)c * nseq + off[c]++] = (int)s;
     }
+    // Long sequences longest first (bitonic sort of (length desc, sequence asc)),
+    // so the long kernel's CTAs take them in LPT order.
+    __shared__ unsigned long long keys[kMaxSortedLong];
+    __syncthreads();
+    const int nlong = counts[0];
+    if (nlong > 1 && nlong <= kMaxSortedLong) {
+        int n2 = 1;
+        while (n2 < nlong) n2 <<= 1;
+        for (int i = tid; i < n2; i += kListThreads) {
+            unsigned long long key = ~0ull;
+            if (i < nlong) {
+                const int sq = lists[i];
+                const int64_t a = min(max(cu[sq], (int64_t)0), E), b = min(max(cu[sq + 1], a), E);
+                key = ((unsigned long long)(0xffffffffu - (unsigned)min(b - a, (int64_t)0xffffffff)) << 32) |
+                      (unsigned)sq;
+            }
+            keys[i] = key;
+        }
+        __syncthreads();
+        for (int k = 2; k <= n2; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int i = tid; i < n2; i += kListThreads) {
+                    const int ixj = i ^ j;
+                    if (ixj > i) {
+                        const unsigned long long x = keys[i], y = keys[ixj];
+                        if ((x > y) == ((i & k) == 0)) {
+                            keys[i] = y;
+                            keys[ixj] = x;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        for (int i = tid; i < nlong; i += kListThreads) lists[i] = (int)(keys[i] & 0xffffffffu);
+    }
 }
 
 // Side stream (and fork / join events) of a caller stream, created on first
@@ -1078,7 +1195,9 @@ int side_stream(int dev, cudaStream_t user, SideStream &out) {
             return BDM_OK;
         }
     SideStream e{dev, user, nullptr, nullptr, nullptr};
-    int rc = cuda_status(cudaStreamCreateWithFlags(&e.side, cudaStreamNonBlocking));
+    int lo_prio = 0, hi_prio = 0;  // greatest priority: the long chains' CTAs are scheduled first
+    int rc = cuda_status(cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio));
+    if (!rc) rc = cuda_status(cudaStreamCreateWithPriority(&e.side, cudaStreamNonBlocking, hi_prio));
     if (!rc) rc = cuda_status(cudaEventCreateWithFlags(&e.fork, cudaEventDisableTiming));
     if (!rc) rc = cuda_status(cudaEventCreateWithFlags(&e.join, cudaEventDisableTiming));
     if (rc) return rc;
@@ -1100,20 +1219,20 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     if (rc) return rc;
     // A sequence is long when its serial chain would outlast its share of the
     // launch: more events than the launch's (event, head, tile) work over the
-    // GPU's warp slots (and at least kLongEvents).  Long sequences run on
+    // GPU's warp slots (and at least kLongEvents; decided on the device, which
+    // knows how many events the launch runs).  Long sequences run on
     // warp-specialised CTAs in their own kernel, started first; with a long
     // launch (plenty of work to hide a chain) there are none.
     const bool long_mode = BDM_SCAN_LONG && q.ctiles <= kWsMaxTiles;
-    const int64_t work = p.E * p.H * (int64_t)q.ctiles;
-    const int64_t long_min = long_mode ? max(kLongEvents, work / ((int64_t)sms * 32)) : (int64_t)8192;
-    build_worklist<<<1, kListThreads, 0, st>>>(p.cu, p.nseq, p.E, long_min, const_cast<int *>(p.lists),
+    build_worklist<<<1, kListThreads, 0, st>>>(p.cu, p.nseq, p.E, long_mode ? (int64_t)p.H * q.ctiles : 0,
+                                               (int64_t)sms * 32, const_cast<int *>(p.lists),
                                                const_cast<int *>(p.counts));
     rc = launch_status();
     if (rc) return rc;
     q.ws_classes = long_mode ? kWsClasses : 0;
     SideStream side{};
     if (long_mode) {
-        q.ws_ctas = min(ceil_div(p.E, long_min) * p.H, (int64_t)sms * BDM_SCAN_LONG_CTAS_PER_SM);
+        q.ws_ctas = min(ceil_div(p.E, kLongEvents) * p.H, (int64_t)sms * BDM_SCAN_LONG_CTAS_PER_SM);
         const size_t smem = (size_t)(ws_fixed_bytes<T, S>() + ws_value_bytes<T, S, NC>(q.ctiles));
         auto lk = bank_scan_long_kernel<T, S, NC>;
         rc = cuda_status(cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -1121,7 +1240,7 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
         if (!rc) rc = cuda_status(cudaEventRecord(side.fork, st));
         if (!rc) rc = cuda_status(cudaStreamWaitEvent(side.side, side.fork, 0));
         if (rc) return rc;
-        lk<<<(unsigned)q.ws_ctas, kScanWarps * 32, smem, side.side>>>(q);
+        lk<<<(unsigned)q.ws_ctas, 32 * (1 + q.ctiles), smem, side.side>>>(q);
         rc = launch_status();
         if (rc) return rc;
     }
@@ -1158,8 +1277,8 @@ int launch_scan_shape(const ScanParams &p, int S, cudaStream_t st) {
 
 namespace bdm {
 namespace {
-// Workspace: 256-byte header [counts (kLenClasses int32) at 0 | dynamic counter (uint64) at 64 |
-// status word (int32, BDM_SCAN_ERR_* bits) at 128], then the lists.
+// Workspace: 256-byte header [counts (kLenClasses int32) at 0 | dynamic counters (uint64) at 64
+// (short kernel) and 72 (long kernel) | status word (int32, BDM_SCAN_ERR_* bits) at 128], then the lists.
 constexpr int64_t kWsHeader = 256;
 inline int64_t scan_workspace_bytes(int64_t nseq) { return kWsHeader + (int64_t)kLenClasses * nseq * 4; }
 }  // namespace
@@ -1224,6 +1343,7 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.counts = counts;
     p.next = reinterpret_cast<unsigned long long *>(ws + 64);
     p.status = reinterpret_cast<int *>(ws + 128);
+    p.long_next = reinterpret_cast<unsigned long long *>(ws + 72);
     p.lists = lists;
     p.nseq = nseq;
     cudaStream_t st = as_stream(stream);
