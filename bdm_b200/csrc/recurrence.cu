@@ -769,26 +769,42 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
             const T *wwp = static_cast<const T *>(p.ww);
             const T *rwp = static_cast<const T *>(p.rw);
             // ids, weights and k|b|g / q rows of events [bbase, bbase + bn): lane = event
-            // ids of the batch after the one being issued, loaded one batch ahead
+            // id and route weight of each lane's event in the batch after the one
+            // being issued, loaded one batch ahead (nothing waits on them until then)
             int64_t pre_base = -1, pre_id = -1;
+            T pre_wt = Elem<T>::from_float(0.f);
+            auto weight_of = [&](int64_t id) -> T {
+                if (id >= 0 && id < nw) return wwp[id];
+                if (id >= nw && id < E) return rwp[id - nw];
+                return Elem<T>::from_float(0.f);
+            };
             auto issue_rows = [&](int64_t bbase, int bn, unsigned char (*rawb)[Raw::size], Staged &st) {
                 st.tok = -1;
                 st.rid = -1;
                 st.write = false;
                 st.wt = 0.f;
-                const int64_t my_id = bbase == pre_base ? pre_id : (lane < bn ? p.order[bbase + lane] : -1);
+                int64_t my_id = -1;
+                T my_wt = Elem<T>::from_float(0.f);
+                if (bbase == pre_base) {
+                    my_id = pre_id;
+                    my_wt = pre_wt;
+                } else if (lane < bn) {
+                    my_id = p.order[bbase + lane];
+                    my_wt = weight_of(my_id);
+                }
                 pre_base = bbase + bn;
                 pre_id = (lane < EB && pre_base + lane < end) ? p.order[pre_base + lane] : -1;
+                pre_wt = weight_of(pre_id);
                 if (lane < bn) {
                     const int64_t id = my_id;
                     if (id >= 0 && id < nw) {
                         st.tok = (int)id / kw;
                         st.write = true;
-                        st.wt = Elem<T>::to_float(wwp[id]);
+                        st.wt = Elem<T>::to_float(my_wt);
                     } else if (id >= nw && id < E) {
                         st.rid = (int)id - nw;
                         st.tok = st.rid / kr;
-                        st.wt = Elem<T>::to_float(rwp[st.rid]);
+                        st.wt = Elem<T>::to_float(my_wt);
                     }
                     if (st.tok >= nt) {
                         st.tok = -1;
@@ -808,24 +824,21 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
                 }
             };
             // v / w columns of the batch's writes into ring slot `slot` (all lanes per event)
+            // each lane copies its own write event's v and w columns (every tile)
             auto issue_values = [&](int bn, const Staged &st, int slot) {
                 constexpr int kPiece = 16;
                 const int row_bytes = kRowElems * (int)sizeof(T);
-                const int pieces = tiles * 2 * row_bytes / kPiece;
                 const int64_t dv_bytes = (int64_t)p.dv * sizeof(T);
-                for (int e = 0; e < bn; ++e) {
-                    const int te = __shfl_sync(0xffffffffu, st.tok, e);
-                    const int we = __shfl_sync(0xffffffffu, (int)st.write, e);
-                    if (!we || te < 0) continue;  // warp-uniform
-                    for (int piece = lane; piece < pieces; piece += 32) {
-                        const int r = piece / (row_bytes / kPiece);
-                        const int off = (piece % (row_bytes / kPiece)) * kPiece;
-                        const int tile = r >> 1, which = r & 1;
-                        const int64_t col_bytes = (int64_t)tile * row_bytes + off;
-                        if (col_bytes >= dv_bytes) continue;
-                        const char *src = static_cast<const char *>(which ? p.w : p.v) +
-                                          ((int64_t)te * V + (int64_t)hh * p.dv) * sizeof(T) + col_bytes;
-                        cp_async<kPiece>(reinterpret_cast<char *>(slot_values(slot, e, tile, which)) + off, src);
+                if (lane >= bn || !st.write || st.tok < 0) return;
+                const int64_t head_off = ((int64_t)st.tok * V + (int64_t)hh * p.dv) * sizeof(T);
+                for (int which = 0; which < 2; ++which) {
+                    const char *src = static_cast<const char *>(which ? p.w : p.v) + head_off;
+                    for (int tile = 0; tile < tiles; ++tile) {
+                        char *dst = reinterpret_cast<char *>(slot_values(slot, lane, tile, which));
+                        for (int off = 0; off < row_bytes; off += kPiece) {
+                            const int64_t col_bytes = (int64_t)tile * row_bytes + off;
+                            if (col_bytes < dv_bytes) cp_async<kPiece>(dst + off, src + col_bytes);
+                        }
                     }
                 }
             };
@@ -996,27 +1009,32 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
                     const float4 *krow = reinterpret_cast<const float4 *>(ctl[ev] + Ctl::kd);
                     const Row<T, NC> vr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 0) + lane * NC);
                     const Row<T, NC> wr = *reinterpret_cast<const Row<T, NC> *>(slot_values(b, ev, ct, 1) + lane * NC);
-                    float2 dot[NP][4];
+                    // same chains and summation order as event_step (a sequence gives the
+                    // same bits whichever kernel runs it)
+                    constexpr int NCH = NP >= 2 ? 2 : 4;
+                    float2 dot[NP][NCH];
 #pragma unroll
                     for (int c = 0; c < NP; ++c)
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) dot[c][i] = make_float2(0.f, 0.f);
+                        for (int i = 0; i < NCH; ++i) dot[c][i] = make_float2(0.f, 0.f);
 #pragma unroll
                     for (int s = 0; s < S; s += 2) {
                         const float4 cc = crow[s / 2];
-                        const int i = (s / 2) & 3;
+                        const int i = (s / 2) % NCH;
 #pragma unroll
                         for (int c = 0; c < NP; ++c) {
                             dot[c][i] = __ffma2_rn(make_float2(cc.x, cc.y), N[s][c], dot[c][i]);
-                            dot[c][(i + 2) & 3] = __ffma2_rn(make_float2(cc.z, cc.w), N[s + 1][c], dot[c][(i + 2) & 3]);
+                            dot[c][(i + NCH / 2) % NCH] =
+                                __ffma2_rn(make_float2(cc.z, cc.w), N[s + 1][c], dot[c][(i + NCH / 2) % NCH]);
                         }
                     }
                     const float2 pw = ctl[ev][Ctl::p];
                     float2 u[NP];
 #pragma unroll
                     for (int c = 0; c < NP; ++c) {
-                        const float2 d = __fadd2_rn(__fadd2_rn(dot[c][0], dot[c][1]), __fadd2_rn(dot[c][2], dot[c][3]));
-                        dot[c][0] = d;
+#pragma unroll
+                        for (int i = 1; i < NCH; ++i) dot[c][0] = __fadd2_rn(dot[c][0], dot[c][i]);
+                        const float2 d = dot[c][0];
                         const float2 uw = WriteValue<T>::apply(wr.x + 2 * c, vr.x + 2 * c, pw, make_float2(-d.x, -d.y));
                         u[c] = wr_ev ? uw : make_float2(0.f, 0.f);
                     }
