@@ -22,9 +22,6 @@
 // batch runs.  N is multiplied back by D (materialised) at every segment end:
 // the end of a batch, a BF16 state-storage point (gdn2_banks.py:35-36), or
 // where the cumulative log-decay would leave the FP32 range (the batch is cut).
-#include <mutex>
-#include <vector>
-
 #include "common.cuh"
 
 namespace bdm {
@@ -37,7 +34,7 @@ namespace {
 #define BDM_SCAN_LONG 1  // 1: long sequences run on warp-specialised CTAs; 0: every unit on one warp
 #endif
 #ifndef BDM_SCAN_LONG_CTAS_PER_SM
-#define BDM_SCAN_LONG_CTAS_PER_SM 4  // warp-specialised CTAs per SM (persistent over the long units)
+#define BDM_SCAN_LONG_CTAS_PER_SM 2  // warp-specialised CTAs per SM (persistent over the long units)
 #endif
 #ifndef BDM_SCAN_DYNAMIC
 #define BDM_SCAN_DYNAMIC 0  // 1: persistent CTAs take work items from an atomic counter; 0: one item per CTA
@@ -636,7 +633,15 @@ bank_scan_kernel(const ScanParams p) {
 // returns; the other warps then fail their own bounded waits and return.
 // ===========================================================================
 constexpr int kWsMaxTiles = kScanWarps - 1;  // consumers per CTA
-constexpr int kWsSlots = 3;
+// Ring depth and batch size: two slots of 32 events (~67 KB at S = 16, two
+// column tiles), so two long CTAs and two short CTAs share an SM.
+#ifndef BDM_SCAN_LONG_SLOTS
+#define BDM_SCAN_LONG_SLOTS 2
+#endif
+#ifndef BDM_SCAN_LONG_BATCH
+#define BDM_SCAN_LONG_BATCH 32
+#endif
+constexpr int kWsSlots = BDM_SCAN_LONG_SLOTS;
 constexpr long long kWaitPolls = 1ll << 22;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
@@ -675,7 +680,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
 // Shared memory of a warp-specialised CTA: the ring (fixed part), the
 // producer's raw row buffers, then the staged value rows (sized at launch by
 // the number of column tiles).
-constexpr int kWsBatch = 32;  // events per staged batch in long mode (every S): one per producer lane
+constexpr int kWsBatch = BDM_SCAN_LONG_BATCH;  // events per staged batch in long mode (every S)
 template <typename T, int S> struct WsShared {
     static constexpr int EB = kWsBatch;
     float2 ctl[kWsSlots][EB][CtlLayout<S>::size];
@@ -1083,6 +1088,10 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
 template <typename T, int S, int NC>
 __global__ void __launch_bounds__(kScanWarps * 32, BDM_SCAN_MIN_BLOCKS)
 bank_scan_long_kernel(const ScanParams p) {
+    // The short-sequence kernel is this kernel's programmatic dependent: it may
+    // start once every CTA here has started, i.e. after the long chains hold
+    // their SM slots.  It reads nothing this kernel writes.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     extern __shared__ __align__(16) unsigned char scan_smem[];
     scan_long_units<T, S, NC>(p, scan_smem);
 }
@@ -1192,38 +1201,6 @@ build_worklist(const int64_t *__restrict__ cu, int64_t nseq, int64_t E, int64_t 
     }
 }
 
-// Side stream (and fork / join events) of a caller stream, created on first
-// use and kept for the process.  The long-sequence kernel runs there, forked
-// from and joined back into the caller's stream, so it overlaps the
-// short-sequence kernel; both orderings are expressed with events, which CUDA
-// graph capture records as a fork and a join.
-struct SideStream {
-    int device;
-    cudaStream_t user, side;
-    cudaEvent_t fork, join;
-};
-std::mutex g_side_mutex;
-std::vector<SideStream> g_side;
-
-int side_stream(int dev, cudaStream_t user, SideStream &out) {
-    std::lock_guard<std::mutex> lock(g_side_mutex);
-    for (const SideStream &e : g_side)
-        if (e.device == dev && e.user == user) {
-            out = e;
-            return BDM_OK;
-        }
-    SideStream e{dev, user, nullptr, nullptr, nullptr};
-    int lo_prio = 0, hi_prio = 0;  // greatest priority: the long chains' CTAs are scheduled first
-    int rc = cuda_status(cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio));
-    if (!rc) rc = cuda_status(cudaStreamCreateWithPriority(&e.side, cudaStreamNonBlocking, hi_prio));
-    if (!rc) rc = cuda_status(cudaEventCreateWithFlags(&e.fork, cudaEventDisableTiming));
-    if (!rc) rc = cuda_status(cudaEventCreateWithFlags(&e.join, cudaEventDisableTiming));
-    if (rc) return rc;
-    g_side.push_back(e);
-    out = e;
-    return BDM_OK;
-}
-
 template <typename T, int S, int NC>
 int launch_scan(const ScanParams &p, cudaStream_t st) {
     ScanParams q = p;
@@ -1248,17 +1225,15 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     rc = launch_status();
     if (rc) return rc;
     q.ws_classes = long_mode ? kWsClasses : 0;
-    SideStream side{};
     if (long_mode) {
+        // Long units first: at most BDM_SCAN_LONG_CTAS_PER_SM persistent CTAs per SM
+        // (the rest of each SM stays free for short CTAs from the start).
         q.ws_ctas = min(ceil_div(p.E, kLongEvents) * p.H, (int64_t)sms * BDM_SCAN_LONG_CTAS_PER_SM);
         const size_t smem = (size_t)(ws_fixed_bytes<T, S>() + ws_value_bytes<T, S, NC>(q.ctiles));
         auto lk = bank_scan_long_kernel<T, S, NC>;
         rc = cuda_status(cudaFuncSetAttribute(lk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        if (!rc) rc = side_stream(dev, st, side);
-        if (!rc) rc = cuda_status(cudaEventRecord(side.fork, st));
-        if (!rc) rc = cuda_status(cudaStreamWaitEvent(side.side, side.fork, 0));
         if (rc) return rc;
-        lk<<<(unsigned)q.ws_ctas, 32 * (1 + q.ctiles), smem, side.side>>>(q);
+        lk<<<(unsigned)q.ws_ctas, 32 * (1 + q.ctiles), smem, st>>>(q);
         rc = launch_status();
         if (rc) return rc;
     }
@@ -1269,13 +1244,21 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     const int64_t want = ceil_div(q.units, kScanWarps);
     const int64_t blocks = BDM_SCAN_DYNAMIC ? min((int64_t)sms * (per_sm > 0 ? per_sm : 1), want)
                                             : min(want, (int64_t)0x7fffffff);
-    bank_scan_kernel<T, S, NC><<<(unsigned)blocks, kScanWarps * 32, 0, st>>>(q);
-    rc = launch_status();
-    if (rc) return rc;
-    if (long_mode) {
-        rc = cuda_status(cudaEventRecord(side.join, side.side));
-        if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, side.join, 0));
-    }
+    // With long units the short kernel is a programmatic dependent launch of the
+    // long kernel (starts once the long CTAs are resident; work after it in the
+    // stream still waits for both).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(kScanWarps * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = long_mode ? 1 : 0;
+    rc = cuda_status(cudaLaunchKernelEx(&cfg, bank_scan_kernel<T, S, NC>, q));
+    count_launch();
     return rc;
 }
 

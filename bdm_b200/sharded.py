@@ -23,12 +23,12 @@ bank table over R ranks (one process per GPU, ``torch.distributed``):
   the rank that holds the token, which rounds it once to the activation dtype
   (the forward's round-once combine) and applies norm, gate and o_proj.
 
-The bank stage runs in head groups (heads are independent in the recurrence),
-each group on its own CUDA stream: a group's recurrence starts as soon as its
-all-gather lands and its reduce-scatter starts as soon as its partial combine
-ends, so the exchange of one group overlaps the recurrence of the others, and
-the groups' longest bank sequences (the critical path of a skewed router) run
-side by side instead of once per group.
+The exchange runs in row chunks: chunk c holds local batch row(s) c of every
+rank, whose bank sequences are independent of the other chunks'.  Each chunk
+runs on its own CUDA stream: its recurrence starts as soon as its all-gather
+lands, so the gather of chunk c+1 overlaps the recurrence of chunk c, its
+reduce-scatter starts as soon as its partial combine ends, and the chunks'
+longest bank sequences (the critical path of a skewed router) run side by side.
 
 Results match the single-device forward up to the FP32 summation order of the
 read combine (the partials are added across ranks, not bank by bank).
@@ -143,25 +143,22 @@ class BankShardedMemory:
     returns this rank's output rows.
     """
 
-    def __init__(self, layer, group=None, *, ownership: str = 'balanced', head_groups: int | None = None,
+    def __init__(self, layer, group=None, *, ownership: str = 'balanced', row_chunks: int = 1,
                  comm: ShardComm | None = None):
         if ownership not in ops.OWNERSHIP_MODES:
             raise ValueError(f'ownership must be one of {sorted(ops.OWNERSHIP_MODES)}')
+        if row_chunks <= 0:
+            raise ValueError('row_chunks must be positive')
         self.layer = layer
         self.comm = comm or ShardComm(group)
         self.ownership = ownership
+        self.row_chunks = row_chunks
         self.rank, self.world = self.comm.rank, self.comm.world
         if layer.bank_count % self.world:
             raise NotImplementedError(f'{layer.bank_count} banks do not divide over {self.world} ranks')
         self.local_banks = layer.bank_count // self.world
-        heads = layer.num_heads
-        if head_groups is None:
-            head_groups = max(g for g in (1, 2, 4) if heads % g == 0)
-        if head_groups <= 0 or heads % head_groups:
-            raise ValueError(f'{heads} heads do not split into {head_groups} groups')
-        step = heads // head_groups
-        self.groups = [(h, h + step) for h in range(0, heads, step)]
         self.last_partition = None  # (owner, slot, members, counts) of the latest call
+        self._chunk_streams = None
 
     # ------------------------------------------------------------ the exchange
     @torch.no_grad()
@@ -169,61 +166,63 @@ class BankShardedMemory:
         lay = self.layer
         comm = self.comm
         lb, time, _ = hidden.shape
-        batch = lb * self.world
         controls, routes, gate = self.local_stage(hidden)
         ww, wi, rw, ri = routes
         counts = self.histogram(wi, ri)
         comm.all_reduce_sum_(counts)
         owner, slot, members = self.owners(counts)
         self.last_partition = (owner, slot, members, counts)
-        # every gather is queued now; NCCL runs them in order while this stream computes
-        route_h = [comm.all_gather(r) for r in routes]
-        control_h = [[comm.all_gather(self.head_slice(c, h0, h1)) for c in controls] for h0, h1 in self.groups]
-        all_routes = [h.wait() for h in route_h]
-        meta = self.dispatch_stage(all_routes, owner, slot)
-        partial_h = []
-        streams = self._streams(hidden)
+        chunks = self.chunks(lb)
+        # every gather is queued now, chunk by chunk; NCCL runs them in order while the streams compute
+        gathers = []
+        for r0, r1 in chunks:
+            t0, t1 = r0 * time, r1 * time
+            gathers.append(([comm.all_gather(r[r0:r1]) for r in routes],
+                            [comm.all_gather(c[t0:t1]) for c in controls]))
+        streams = self._streams(hidden, len(chunks))
         main = torch.cuda.current_stream(hidden.device) if streams else None
-        for gi, ((h0, h1), handles) in enumerate(zip(self.groups, control_h)):
+        partial_h = []
+        for ci, ((r0, r1), (route_h, control_h)) in enumerate(zip(chunks, gathers)):
             if streams:
-                streams[gi].wait_stream(main)
-                ctx = torch.cuda.stream(streams[gi])
+                streams[ci].wait_stream(main)
+                ctx = torch.cuda.stream(streams[ci])
             else:
                 ctx = _NoStream()
             with ctx:
-                group_controls = [h.wait() for h in handles]
-                partial = self.bank_stage(group_controls, all_routes, meta, owner, members, batch=batch,
-                                          time=time, head0=h0, heads=h1 - h0)
+                all_routes = [h.wait() for h in route_h]
+                meta = self.dispatch_stage(all_routes, owner, slot)
+                all_controls = [h.wait() for h in control_h]
+                partial = self.bank_stage(all_controls, all_routes, meta, owner, members,
+                                          batch=(r1 - r0) * self.world, time=time)
                 partial_h.append(comm.reduce_scatter_sum(partial))
         for st in streams:
-            main.wait_stream(st)  # before any tensor used on a group stream is released
-        dv = lay.head_value_width
-        if len(self.groups) == 1:
+            main.wait_stream(st)  # before any tensor used on a chunk stream is released
+        if len(chunks) == 1:
             combined = partial_h[0].wait()
         else:
             combined = torch.empty((lb * time, lay.value_width), dtype=torch.float32, device=hidden.device)
-            for (h0, h1), h in zip(self.groups, partial_h):
-                combined[:, h0 * dv:h1 * dv] = h.wait()
+            for (r0, r1), h in zip(chunks, partial_h):
+                combined[r0 * time:r1 * time] = h.wait()
         out = self.output_stage(hidden, combined, gate)
         return out.reshape(lb, time, lay.hidden_size)
 
     def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
         return self.forward(hidden)
 
-    def _streams(self, hidden):
-        """One side stream per head group (device tensors with more than one group), created once."""
-        if not hidden.is_cuda or len(self.groups) == 1:
-            return []
-        if getattr(self, '_group_streams', None) is None or self._group_streams[0].device != hidden.device:
-            self._group_streams = [torch.cuda.Stream(device=hidden.device) for _ in self.groups]
-        return self._group_streams
+    def chunks(self, rows):
+        """Local row ranges of the exchange's chunks (at most ``row_chunks``, near-equal)."""
+        n = max(1, min(self.row_chunks, rows))
+        bounds = [rows * i // n for i in range(n + 1)]
+        return [(bounds[i], bounds[i + 1]) for i in range(n) if bounds[i + 1] > bounds[i]]
 
-    def head_slice(self, control, h0, h1):
-        """Columns of heads [h0, h1) of a [tokens, H * width] controller tensor."""
-        if (h0, h1) == (0, self.layer.num_heads):
-            return control
-        width = control.shape[1] // self.layer.num_heads
-        return control[:, h0 * width:h1 * width]
+    def _streams(self, hidden, n):
+        """One side stream per chunk (device tensors, more than one chunk), created once."""
+        if not hidden.is_cuda or n == 1:
+            return []
+        cached = self._chunk_streams
+        if cached is None or len(cached) < n or cached[0].device != hidden.device:
+            self._chunk_streams = cached = [torch.cuda.Stream(device=hidden.device) for _ in range(n)]
+        return cached[:n]
 
     # --------------------------------------------------------------- stages
     def local_stage(self, hidden):
@@ -243,19 +242,17 @@ class BankShardedMemory:
         ww, wi, rw, ri = routes
         return ops.dispatch_owned(wi, ri, self.layer.bank_count, owner, slot, self.rank, self.local_banks)
 
-    def bank_stage(self, controls, routes, meta, owner, members, *, batch, time, head0, heads):
-        """Recurrence and partial combine of this rank's banks for heads [head0, head0 + heads)
-        -> FP32 [batch*time, heads*dv]."""
+    def bank_stage(self, controls, routes, meta, owner, members, *, batch, time):
+        """Recurrence and partial combine of this rank's banks -> FP32 [batch*time, V]."""
         lay = self.layer
         ww, wi, rw, ri = routes
         interval = state_interval(lay.bank_size) if lay.config.training_state_dtype == 'bfloat16' else 0
         reads = ops.bank_scan(*controls, wi, ww, ri, rw, meta['order'], meta['cu_seqlens'], batch=batch, time=time,
-                              bank_count=self.local_banks, heads=heads, bank_size=lay.bank_size,
+                              bank_count=self.local_banks, heads=lay.num_heads, bank_size=lay.bank_size,
                               head_value_width=lay.head_value_width, routed_decay=lay.config.routed_decay,
                               scale=lay.bank_size ** -0.5, row_factor=lay.initial_row_factor,
                               col_factor=lay.initial_column_factor, state_interval=interval,
-                              bank_ids=members[self.rank], total_banks=lay.bank_count, head_offset=head0,
-                              total_heads=lay.num_heads)
+                              bank_ids=members[self.rank], total_banks=lay.bank_count)
         return ops.combine_partial(reads, ri.reshape(batch * time, -1), owner, self.rank)
 
     def output_stage(self, hidden, combined, gate):

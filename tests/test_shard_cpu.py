@@ -84,12 +84,12 @@ class OracleStages(BankShardedMemory):
     def dispatch_stage(self, routes, owner, slot):
         return None  # the oracle recurrence orders events itself
 
-    def bank_stage(self, controls, routes, meta, owner, members, *, batch, time, head0, heads):
+    def bank_stage(self, controls, routes, meta, owner, members, *, batch, time):
         o = self.o
-        q, k, v, g, b, w = (c.numpy().reshape(batch, time, heads, -1) for c in controls)
+        q, k, v, g, b, w = (c.numpy().reshape(batch, time, o.H, -1) for c in controls)
         ww, wi, rw, ri = (r.numpy() for r in routes)
         interval = oracle.state_interval(o.S) if o.c['training_state_dtype'] == 'bfloat16' else 0
-        init = np.ascontiguousarray(o.initial_state()[None][:, :, head0:head0 + heads])
+        init = o.initial_state()[None]
         reads, _ = oracle.oracle_recurrence(q, k, v, g, b, w, wi, ww, ri, rw, init,
                                             bank_count=o.J, bf16=o.bf16, routed_decay=o.c['routed_decay'],
                                             interval=interval, scale=o.S ** -0.5, want_state=False)
@@ -124,7 +124,7 @@ def _worker(rank, world, port, mode, groups, out_dir):
         m, olayer = _model()
         x = _hidden()
         rows = BATCH // world
-        sharded = OracleStages(m, olayer, ownership=mode, head_groups=groups)
+        sharded = OracleStages(m, olayer, ownership=mode, row_chunks=groups)
         y = sharded(x[rank * rows:(rank + 1) * rows])
         owner = sharded.last_partition[0]
         # the gather carries any element type bit for bit (bf16 controllers, int64 routes)
@@ -136,7 +136,7 @@ def _worker(rank, world, port, mode, groups, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize('mode,groups', [('balanced', 2), ('contiguous', 1)])
+@pytest.mark.parametrize('mode,groups', [('balanced', 2), ('contiguous', 1), ('balanced', 3)])
 def test_sharded_forward_gloo_world2(tmp_path, mode, groups):
     world = 2
     mp.spawn(_worker, args=(world, _free_port(), mode, groups, str(tmp_path)), nprocs=world, join=True)
