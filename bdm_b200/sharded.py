@@ -159,6 +159,9 @@ class BankShardedMemory:
         self.local_banks = layer.bank_count // self.world
         self.last_partition = None  # (owner, slot, members, counts) of the latest call
         self._chunk_streams = None
+        # Optional list; when set (device tensors, one row chunk), forward appends
+        # (phase name, CUDA event) pairs recorded on the current stream at each phase end.
+        self.phase_events = None
 
     # ------------------------------------------------------------ the exchange
     @torch.no_grad()
@@ -166,12 +169,15 @@ class BankShardedMemory:
         lay = self.layer
         comm = self.comm
         lb, time, _ = hidden.shape
+        self._mark('start', hidden)
         controls, routes, gate = self.local_stage(hidden)
         ww, wi, rw, ri = routes
+        self._mark('local', hidden)
         counts = self.histogram(wi, ri)
         comm.all_reduce_sum_(counts)
         owner, slot, members = self.owners(counts)
         self.last_partition = (owner, slot, members, counts)
+        self._mark('partition', hidden)
         chunks = self.chunks(lb)
         # every gather is queued now, chunk by chunk; NCCL runs them in order while the streams compute
         gathers = []
@@ -190,8 +196,10 @@ class BankShardedMemory:
                 ctx = _NoStream()
             with ctx:
                 all_routes = [h.wait() for h in route_h]
-                meta = self.dispatch_stage(all_routes, owner, slot)
                 all_controls = [h.wait() for h in control_h]
+                self._mark('gather', hidden)
+                meta = self.dispatch_stage(all_routes, owner, slot)
+                self._mark('dispatch', hidden)
                 partial = self.bank_stage(all_controls, all_routes, meta, owner, members,
                                           batch=(r1 - r0) * self.world, time=time)
                 partial_h.append(comm.reduce_scatter_sum(partial))
@@ -199,12 +207,25 @@ class BankShardedMemory:
             main.wait_stream(st)  # before any tensor used on a chunk stream is released
         if len(chunks) == 1:
             combined = partial_h[0].wait()
+            self._mark('reduce_scatter', hidden)
         else:
             combined = torch.empty((lb * time, lay.value_width), dtype=torch.float32, device=hidden.device)
             for (r0, r1), h in zip(chunks, partial_h):
                 combined[r0 * time:r1 * time] = h.wait()
         out = self.output_stage(hidden, combined, gate)
+        self._mark('output', hidden)
         return out.reshape(lb, time, lay.hidden_size)
+
+    def _mark(self, name, hidden):
+        if self.phase_events is not None and hidden.is_cuda:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.phase_events.append((name, ev))
+
+    def phase_times(self):
+        """Milliseconds of each recorded phase (after a synchronize), from ``phase_events``."""
+        ev = self.phase_events or []
+        return {name: ev[i - 1][1].elapsed_time(e) for i, (name, e) in enumerate(ev) if i > 0}
 
     def __call__(self, hidden: torch.Tensor) -> torch.Tensor:
         return self.forward(hidden)
@@ -253,7 +274,10 @@ class BankShardedMemory:
                               scale=lay.bank_size ** -0.5, row_factor=lay.initial_row_factor,
                               col_factor=lay.initial_column_factor, state_interval=interval,
                               bank_ids=members[self.rank], total_banks=lay.bank_count)
-        return ops.combine_partial(reads, ri.reshape(batch * time, -1), owner, self.rank)
+        self._mark('recurrence', reads)
+        part = ops.combine_partial(reads, ri.reshape(batch * time, -1), owner, self.rank)
+        self._mark('partial_combine', part)
+        return part
 
     def output_stage(self, hidden, combined, gate):
         lay = self.layer

@@ -481,6 +481,15 @@ def run_c4(dev, rank, world, args):
         owner, _, _, counts = fwd.last_partition
         load = torch.zeros(world, dtype=torch.float64, device=dev).index_add_(0, owner.long(), counts.double())
         out['partition_load_max_over_mean'] = (load.max() / load.mean()).item()
+        # one more (untimed) step with per-phase CUDA events; every rank reports, rank 0 prints the max
+        with torch.inference_mode():
+            fwd.phase_events = []
+            barrier(world)
+            fwd(x)
+            torch.cuda.synchronize()
+            phases = fwd.phase_times()
+            fwd.phase_events = None
+        out['phases_ms_max_over_ranks'] = {k: max_over_ranks(v, world) for k, v in phases.items()}
     return out
 
 
