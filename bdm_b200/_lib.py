@@ -49,7 +49,7 @@ SIGNATURES = {
     'bdm_combine_partial': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _int, _int, _vp, _vp]),
     'bdm_norm_gate_f32': (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _vp, _vp]),
     'bdm_decode_step': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _int, _int,
-                               _int, _int, _int, _flt, _vp, _int, _vp, _vp]),
+                               _int, _int, _int, _flt, _vp, _int, _vp, _vp, _i64, _vp, _vp, _flt, _int, _vp, _vp]),
 }
 
 _lib = None

@@ -365,10 +365,15 @@ class BankedDeltaMemory(nn.Module):
         batch = hidden.shape[0]
         controls, routes, gate = self._controls_and_routes(hidden)
         ww, wi, rw, ri = (r.reshape(batch, -1) for r in routes)
-        raw = ops.decode_step(*controls, wi, ww, ri, rw, state, bank_count=self.bank_count, heads=self.num_heads,
-                              bank_size=self.bank_size, head_value_width=self.head_value_width,
-                              routed_decay=self.config.routed_decay, scale=self.bank_size ** -0.5)
-        return self._output(hidden, raw, None, gate, round_each=True), state
+        # the step kernel also applies the output norm and gate (one launch instead of two)
+        normed = ops.decode_step(*controls, wi, ww, ri, rw, state, bank_count=self.bank_count, heads=self.num_heads,
+                                 bank_size=self.bank_size, head_value_width=self.head_value_width,
+                                 routed_decay=self.config.routed_decay, scale=self.bank_size ** -0.5, gate=gate,
+                                 norm_weight=self.output_norm_weight,
+                                 norm_bias=getattr(self, 'output_norm_bias', None), eps=self.norm_eps,
+                                 layer_norm=self.config.output_normalization == 'layer')
+        out = F.linear(normed, self.o_proj.weight, self.o_proj.bias)
+        return out.reshape(batch, 1, self.hidden_size), state
 
     def capture_step(self, state, *, warmup=2):
         """CUDA-graph one decode step bound to ``state`` (a cache from ``prefill``/``create_state``).

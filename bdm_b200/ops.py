@@ -235,22 +235,37 @@ def combine_norm_gate(reads, read_idx, gate, norm_weight, norm_bias, *, eps: flo
 
 
 def decode_step(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, state, *, bank_count: int, heads: int,
-                bank_size: int, head_value_width: int, routed_decay: bool, scale: float):
-    """One decode token per batch row; ``state`` [B, J, H, S, dv] updated in place. Returns raw [B, V]."""
-    _cuda(q, state)
+                bank_size: int, head_value_width: int, routed_decay: bool, scale: float, gate=None,
+                norm_weight=None, norm_bias=None, eps: float = 1e-5, layer_norm: bool = True):
+    """One decode token per batch row; ``state`` [B, J, H, S, dv] updated in place.
+
+    Returns raw [B, V] (the ascending-bank read sum), or, with ``gate`` ([B, >=V], row stride
+    honoured), the normalised and gated [B, V] of the output interface, computed in the same kernel.
+    """
+    _cuda(q, state, gate)
     if not state.is_contiguous():
         raise ValueError('state must be contiguous')
     batch = q.shape[0]
     kw, kr = write_idx.shape[-1], read_idx.shape[-1]
-    raw = torch.empty((batch, heads * head_value_width), dtype=q.dtype, device=q.device)
+    v_width = heads * head_value_width
+    raw = out = nw = nb = None
+    if gate is None:
+        raw = torch.empty((batch, v_width), dtype=q.dtype, device=q.device)
+    else:
+        if gate.stride(-1) != 1:
+            raise ValueError('gate rows must be contiguous')
+        out = torch.empty((batch, v_width), dtype=q.dtype, device=q.device)
+        nw = norm_weight.detach().to(q.dtype).contiguous()
+        nb = norm_bias.detach().to(q.dtype).contiguous() if norm_bias is not None else None
     wi, ww, ri, rw = (t.contiguous() for t in (write_idx, write_w, read_idx, read_w))
     q, k, v, g, b, w = (t.contiguous() for t in (q, k, v, g, b, w))
+    ld_gate = (gate.stride(0) if batch > 1 else gate.shape[-1]) if gate is not None else 0
     _lib.check(_lib.load().bdm_decode_step(
         _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(wi), _ptr(ww), _ptr(ri), _ptr(rw), batch,
-        bank_count, heads,
-        bank_size, head_value_width, kw, kr, dtype_code(q.dtype), int(routed_decay), float(scale), _ptr(state),
-        dtype_code(state.dtype), _ptr(raw), _stream(q.device)), 'bdm_decode_step')
-    return raw
+        bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(q.dtype), int(routed_decay), float(scale),
+        _ptr(state), dtype_code(state.dtype), _ptr(raw), _ptr(gate), ld_gate, _ptr(nw), _ptr(nb), float(eps),
+        1 if layer_norm else 0, _ptr(out), _stream(q.device)), 'bdm_decode_step')
+    return raw if gate is None else out
 
 
 # ------------------------------------------------------------ bank sharding

@@ -249,12 +249,20 @@ BDM_API int bdm_norm_gate_f32(const float *combined, int64_t ntok, int64_t width
  *   state [batch, J, H, S, dv] (state_dtype) updated in place: every write
  *   bank of a row is rewritten in state_dtype, then reads (scale * M^T dtype(q*r),
  *   rounded to dtype) see the updated banks and are summed in ascending bank
- *   order with a rounding after each add into raw [batch, V] (dtype).
+ *   order with a rounding after each add into raw [batch, V] (dtype; may be NULL when
+ *   gate is given).
+ * With gate != NULL the step also applies the output interface's norm and gate to
+ * the summed row, exactly as bdm_combine_norm_gate does for an already combined
+ * input: out [batch, V] (dtype) = dtype(norm(raw) * dtype(sigmoid(gate))), gate
+ * [batch, ld_gate] (dtype), norm_mode 1 = LayerNorm(norm_weight, norm_bias, eps),
+ * 0 = RMS(norm_weight, eps).
  */
 BDM_API int bdm_decode_step(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
                     const int64_t *write_idx, const void *write_w, const int64_t *read_idx, const void *read_w,
                     int64_t batch, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw, int kr,
-                    int dtype, int routed_decay, float scale, void *state, int state_dtype, void *raw, void *stream);
+                    int dtype, int routed_decay, float scale, void *state, int state_dtype, void *raw,
+                    const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias, float eps,
+                    int norm_mode, void *out, void *stream);
 
 #ifdef __cplusplus
 }

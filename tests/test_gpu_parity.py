@@ -358,6 +358,37 @@ def test_forward_is_deterministic():
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize('layer_norm', [True, False])
+def test_decode_step_fused_norm_gate(dtype, layer_norm):
+    # the step kernel's fused output norm + gate equals the separate combine_norm_gate over its raw sum
+    gen = torch.Generator().manual_seed(21)
+    batch, heads, s, dv, J, k = 16, 2, 8, 64, 64, 4
+    ctl = [t.to(DEV) for t in _controls(gen, batch, heads, s, dv, dtype)]
+    wi = torch.stack([torch.randperm(J, generator=gen)[:k] for _ in range(batch)]).to(DEV)
+    ri = torch.stack([torch.randperm(J, generator=gen)[:k] for _ in range(batch)]).to(DEV)
+    ww = torch.softmax(torch.randn(batch, k, generator=gen), -1).to(dtype).to(DEV)
+    rw = torch.softmax(torch.randn(batch, k, generator=gen), -1).to(dtype).to(DEV)
+    state = (0.1 * torch.randn(batch, J, heads, s, dv, generator=gen)).to(dtype).to(DEV)
+    gate = torch.randn(batch, heads * dv + 8, generator=gen).to(dtype).to(DEV)[:, :heads * dv]
+    nw = (1 + 0.1 * torch.randn(heads * dv, generator=gen)).to(DEV)
+    nb = 0.1 * torch.randn(heads * dv, generator=gen).to(DEV) if layer_norm else None
+    kw = dict(bank_count=J, heads=heads, bank_size=s, head_value_width=dv, routed_decay=True, scale=s ** -0.5)
+    st1, st2 = state.clone(), state.clone()
+    raw = ops.decode_step(*ctl, wi, ww, ri, rw, st1, **kw)
+    want = ops.combine_norm_gate(raw, None, gate, nw, nb, eps=1e-5, layer_norm=layer_norm, round_each=True)
+    got = ops.decode_step(*ctl, wi, ww, ri, rw, st2, **kw, gate=gate, norm_weight=nw, norm_bias=nb, eps=1e-5,
+                          layer_norm=layer_norm)
+    assert torch.equal(st1, st2)
+    # the norm's FP32 sums associate differently (one column per thread): BF16 outputs at most one
+    # ulp apart, FP32 outputs within 1e-6 max-relative
+    diff = (got.float() - want.float()).abs()
+    if dtype == torch.bfloat16:
+        assert (diff <= 2 ** -7 * want.float().abs().clamp_min(1e-3)).all()
+    else:
+        assert diff.max() <= 1e-6 * want.float().abs().max()
+
+
 def test_captured_decode_step_matches_eager_step():
     cfg = BSDMConfig(dim=256, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
     m = BlockSparseDeltaMemory(cfg, seed=2).to(torch.bfloat16).to(DEV)
