@@ -29,11 +29,12 @@ SIGNATURES = {
     'bdm_abi_version': (_int, []),
     'bdm_kernel_launches': (ctypes.c_longlong, []),
     'bdm_route': (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _vp, _vp, _vp]),
+    'bdm_route_pair': (_int, [_vp, _i64, _i64, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp]),
     'bdm_dispatch_workspace_bytes': (_i64, [_i64, _i64, _int, _int, _i64]),
     'bdm_dispatch': (_int, [_vp, _vp, _i64, _i64, _int, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     'bdm_dispatch_noalloc': (_int, [_vp, _vp, _i64, _i64, _int, _int, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
-    'bdm_controllers': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _int, _int, _int,
-                               _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    'bdm_controllers': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _int, _vp, _vp,
+                               _int, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'bdm_product_state': (_int, [_vp, _vp, _i64, _i64, _int, _i64, _i64, _int, _int, _int, _vp, _int, _vp]),
     'bdm_bank_scan_workspace_bytes': (_i64, [_i64, _i64]),
     'bdm_bank_scan': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int,

@@ -30,6 +30,9 @@ from . import ops
 from .config import BDMConfig, near_square_factors, state_interval
 
 
+FUSED_F_MAX_TOKENS = 4096  # at most this many tokens: the controllers kernel computes f_proj.1 itself
+
+
 class SharedResidualRouter(nn.Module):
     """Routing base plus learned read / write residuals (routing.py:12-35).
 
@@ -254,17 +257,18 @@ class BankedDeltaMemory(nn.Module):
     def _controls_and_routes(self, hidden):
         batch, time, _ = hidden.shape
         proj, cols = self._project(hidden.reshape(batch * time, self.hidden_size))
-        f1 = proj[:, cols['f']:cols['f'] + self.head_value_width]
-        f = torch.mm(f1, self.f_proj[1].weight.t())  # f_proj.1, rounded to the activation dtype
+        f = None
+        if batch * time > FUSED_F_MAX_TOKENS:  # many tokens: f_proj.1 as a GEMM; few (decode): in the kernel
+            f1 = proj[:, cols['f']:cols['f'] + self.head_value_width]
+            f = torch.mm(f1, self.f_proj[1].weight.t())  # f_proj.1, rounded to the activation dtype
         q, k, v, g, b, w = ops.controllers(proj, cols, f, self.A_log, self.dt_bias,
                                            heads=self.num_heads, bank_size=self.bank_size,
                                            head_value_width=self.head_value_width,
-                                           qk_norm=self.config.qk_normalization)
-        width = sum(self.factors)
-        ww, wi = ops.route(proj[:, cols['write']:cols['write'] + width], bank_count=self.bank_count,
-                           selected_banks=self.num_writes, factors=self.factors)
-        rw, ri = ops.route(proj[:, cols['read']:cols['read'] + width], bank_count=self.bank_count,
-                           selected_banks=self.num_reads, factors=self.factors)
+                                           qk_norm=self.config.qk_normalization,
+                                           f_weight=self.f_proj[1].weight, f1_width=self.head_value_width)
+        # both routers (read block, then write block of the fused projection) in one launch
+        (rw, ri), (ww, wi) = ops.route_pair(proj, cols['read'], cols['write'], bank_count=self.bank_count,
+                                            selected_banks=self.num_reads, factors=self.factors)
         shape = (batch, time, -1)
         routes = (ww.reshape(shape), wi.reshape(shape), rw.reshape(shape), ri.reshape(shape))
         gate = proj[:, cols['gate']:cols['gate'] + self.value_width]

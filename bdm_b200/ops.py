@@ -74,6 +74,34 @@ def route(logits: torch.Tensor, *, bank_count: int, selected_banks: int, factors
     return w.reshape(*lead, count), idx.reshape(*lead, count)
 
 
+def route_pair(proj: torch.Tensor, first: int, second: int, *, bank_count: int, selected_banks: int, factors=None):
+    """Two product-key routers over the rows of ``proj`` [NT, ld] in one launch: the logits at
+    columns [first, first+J1+J2) and [second, second+J1+J2).  Returns ((weights, indices) of the
+    first block, (weights, indices) of the second), each [NT, count], as two ``route`` calls.
+    """
+    _cuda(proj)
+    j1, j2 = factors or near_square_factors(bank_count)
+    if proj.ndim != 2 or proj.stride(1) != 1:
+        raise ValueError('proj must be a row-major [tokens, width] matrix')
+    if not 1 <= selected_banks <= bank_count:
+        raise ValueError('selected bank count is outside the bank table')
+    if second < first:
+        raise ValueError('the second block must follow the first')
+    ntok = proj.shape[0]
+    sub = min(selected_banks, j1, j2)
+    count = min(selected_banks, sub * sub)
+    dev, dt = proj.device, proj.dtype
+    idx1 = torch.empty((ntok, count), dtype=torch.int64, device=dev)
+    w1 = torch.empty((ntok, count), dtype=dt, device=dev)
+    idx2, w2 = torch.empty_like(idx1), torch.empty_like(w1)
+    ld = proj.stride(0) if ntok > 1 else proj.shape[1]
+    base = proj[:, first:] if ntok else proj
+    _lib.check(_lib.load().bdm_route_pair(_ptr(base), ntok, ld, second - first, j1, j2, selected_banks,
+                                          dtype_code(dt), _ptr(idx1), _ptr(w1), _ptr(idx2), _ptr(w2),
+                                          _stream(dev)), 'bdm_route_pair')
+    return (w1, idx1), (w2, idx2)
+
+
 def dispatch(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int, *, want_inverse=False,
              want_tokens=False, error_word: torch.Tensor | None = None):
     """Stable (batch, bank) counting sort of all routed events.
@@ -110,21 +138,29 @@ def dispatch(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int, *
     return out
 
 
-def controllers(proj: torch.Tensor, cols: dict, f: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
-                *, heads: int, bank_size: int, head_value_width: int, qk_norm: str):
+def controllers(proj: torch.Tensor, cols: dict, f: torch.Tensor | None, a_log: torch.Tensor, dt_bias: torch.Tensor,
+                *, heads: int, bank_size: int, head_value_width: int, qk_norm: str, f_weight=None,
+                f1_width: int = 0):
     """Controller epilogue over the fused projection ``proj [NT, ld]`` (column offsets in ``cols``)
-    and the f_proj output ``f [NT, H*S]``.
+    and the f_proj output ``f [NT, H*S]``, or, with ``f=None``, ``f_weight`` (f_proj.1's
+    [H*S, f1_width]) applied in the kernel to the f1 columns of ``proj``.
 
     Returns q, k, v, g, b, w as [NT, H*S] / [NT, V] tensors (g float32).
     """
-    _cuda(proj, f)
-    if proj.ndim != 2 or proj.stride(1) != 1 or f.ndim != 2 or f.stride(1) != 1:
+    _cuda(proj, f, f_weight)
+    if proj.ndim != 2 or proj.stride(1) != 1 or (f is not None and (f.ndim != 2 or f.stride(1) != 1)):
         raise ValueError('proj and f must be row-major [tokens, width] matrices')
     nt = proj.shape[0]
     hs, v_width = heads * bank_size, heads * head_value_width
     dev, dt = proj.device, proj.dtype
-    if f.dtype != dt or f.shape != (nt, hs):
-        raise ValueError(f'f must be [{nt}, {hs}] in {dt}')
+    wf2 = None
+    if f is not None:
+        if f.dtype != dt or f.shape != (nt, hs):
+            raise ValueError(f'f must be [{nt}, {hs}] in {dt}')
+    else:
+        if f_weight is None or tuple(f_weight.shape) != (hs, f1_width) or f_weight.dtype != dt:
+            raise ValueError(f'f_weight must be [{hs}, {f1_width}] in {dt}')
+        wf2 = f_weight.detach().contiguous()
     q = torch.empty((nt, hs), dtype=dt, device=dev)
     k = torch.empty_like(q)
     b = torch.empty_like(q)
@@ -135,7 +171,8 @@ def controllers(proj: torch.Tensor, cols: dict, f: torch.Tensor, a_log: torch.Te
     dtb = dt_bias.detach().float().contiguous()
     _lib.check(_lib.load().bdm_controllers(
         _ptr(proj), nt, proj.stride(0) if nt > 1 else proj.shape[1], cols['q'], cols['k'], cols['v'], cols['b'],
-        cols['w'], _ptr(f), f.stride(0) if nt > 1 else f.shape[1], _ptr(al), _ptr(dtb), heads, bank_size,
+        cols['w'], _ptr(f), (f.stride(0) if nt > 1 else f.shape[1]) if f is not None else 0, _ptr(wf2),
+        cols['f'], int(f1_width), _ptr(al), _ptr(dtb), heads, bank_size,
         head_value_width, 1 if qk_norm == 'nvidia' else 0, dtype_code(dt), _ptr(q), _ptr(k), _ptr(v), _ptr(g),
         _ptr(b), _ptr(w), _stream(dev)), 'bdm_controllers')
     return q, k, v, g, b, w

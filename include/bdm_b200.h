@@ -72,6 +72,16 @@ BDM_API int bdm_route(const void *logits, int64_t ntok, int64_t ld, int j1, int 
               int64_t *indices, void *weights, void *stream);
 
 /*
+ * Two product-key routers over the same rows in one launch (the layer's write
+ * router at columns [0, j1+j2) and read router at [second, second+j1+j2) of the
+ * fused projection): results as two bdm_route calls.  No reference counterpart
+ * (the reference calls product_key_route once per role, gdn2_banks.py:74-114).
+ */
+BDM_API int bdm_route_pair(const void *logits, int64_t ntok, int64_t ld, int64_t second, int j1, int j2, int selected,
+                           int dtype, int64_t *indices, void *weights, int64_t *indices2, void *weights2,
+                           void *stream);
+
+/*
  * Causal bank dispatch: a stable counting sort of all events by (batch, bank).
  * Replaces role_bank_dispatch.metadata (role_bank_dispatch.py:143-153: _keys,
  * torch.sort, _bounds) and the ordering of pack_bank_events
@@ -112,12 +122,16 @@ BDM_API int bdm_dispatch_noalloc(const int64_t *write_idx, const int64_t *read_i
  * done by the caller: proj = hidden @ [Wq;Wk;Wv;Wf1;Wb;Ww;...]^T and
  * f = f1 @ Wf2^T (the second f_proj layer, rounded to dtype like the reference's Linear).
  *   proj [ntok, ld] (dtype) with the q, k, v, b, w blocks at the given column offsets
- *   f [ntok, ldf] (dtype, H*S columns); a_log [H], dt_bias [H*S] float
+ *   f [ntok, ldf] (dtype, H*S columns); or f = NULL and wf2 [H*S, f1_width] (dtype, the
+ *   second f_proj layer's weight): the kernel computes f = dtype(f1 @ wf2^T) itself from
+ *   proj columns [col_f1, col_f1 + f1_width) (FP32 accumulation; meant for few tokens)
+ *   a_log [H], dt_bias [H*S] float
  *   qk_norm: 0 = F.normalize (original), 1 = x*rsqrt(sum x^2 + 1e-6) (nvidia)
  *   out: q, k, b [ntok, H, S] (dtype), g [ntok, H, S] float, v, w [ntok, V] (dtype)
  */
 BDM_API int bdm_controllers(const void *proj, int64_t ntok, int64_t ld, int64_t col_q, int64_t col_k, int64_t col_v,
-                            int64_t col_b, int64_t col_w, const void *f, int64_t ldf, const float *a_log,
+                            int64_t col_b, int64_t col_w, const void *f, int64_t ldf, const void *wf2,
+                            int64_t col_f1, int f1_width, const float *a_log,
                             const float *dt_bias, int heads, int bank_size, int head_value_width, int qk_norm,
                             int dtype, void *q, void *k, void *v, float *g, void *b, void *w, void *stream);
 

@@ -54,6 +54,41 @@ def test_router_bit_exact(bank_count, selected, dtype, ties):
         np.testing.assert_allclose(npf(w), ow, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_route_pair_equals_two_routes(dtype):
+    gen = torch.Generator().manual_seed(17)
+    bank_count, selected = 2048, 8
+    j1, j2 = near_square_factors(bank_count)
+    proj = torch.randn(700, 40 + 2 * (j1 + j2) + 13, generator=gen).to(dtype).to(DEV)
+    first, second = 40, 40 + j1 + j2
+    (w1, i1), (w2, i2) = ops.route_pair(proj, first, second, bank_count=bank_count, selected_banks=selected)
+    rw1, ri1 = ops.route(proj[:, first:first + j1 + j2], bank_count=bank_count, selected_banks=selected)
+    rw2, ri2 = ops.route(proj[:, second:second + j1 + j2], bank_count=bank_count, selected_banks=selected)
+    for a, b in ((w1, rw1), (i1, ri1), (w2, rw2), (i2, ri2)):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_controllers_in_kernel_f_proj(dtype):
+    # f_proj.1 computed in the controllers kernel (few tokens) vs the GEMM path
+    cfg = dict(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=512, num_heads=4)
+    m = BlockSparseDeltaMemory(BSDMConfig(**cfg), seed=9).to(dtype).to(DEV)
+    x = torch.randn(64, 256, generator=torch.Generator().manual_seed(2)).to(dtype).to(DEV)
+    with torch.no_grad():
+        proj, cols = m._project(x)
+        f = torch.mm(proj[:, cols['f']:cols['f'] + m.head_value_width], m.f_proj[1].weight.t())
+        kw = dict(heads=m.num_heads, bank_size=m.bank_size, head_value_width=m.head_value_width,
+                  qk_norm=m.config.qk_normalization)
+        a = ops.controllers(proj, cols, f, m.A_log, m.dt_bias, **kw)
+        b = ops.controllers(proj, cols, None, m.A_log, m.dt_bias, **kw, f_weight=m.f_proj[1].weight,
+                            f1_width=m.head_value_width)
+    for i in (0, 1, 2, 4, 5):  # q, k, v, b, w do not depend on f
+        assert torch.equal(a[i], b[i])
+    # f's FP32 accumulation order differs from the GEMM's: at most one ulp of f apart
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    assert max_rel(npf(b[3]), npf(a[3])) <= tol
+
+
 def test_router_strided_logits_and_golden(golden_dir):
     data = torch.load(os.path.join(golden_dir, 'router.pt'), weights_only=False)
     for case in data['cases']:
