@@ -42,6 +42,24 @@ SIGNATURES = {
                              _int, _int, _int, _vp, _vp, _i64, _vp]),
     'bdm_combine_norm_gate': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _int, _vp,
                                      _vp]),
+    'bdm_combine_norm_gate_save': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _int,
+                                          _vp, _vp, _vp]),
+    'bdm_norm_gate_backward_partial_floats': (_i64, [_i64, _i64]),
+    'bdm_norm_gate_backward': (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _vp, _vp, _i64,
+                                      _vp, _vp, _vp, _vp]),
+    'bdm_scan_backward_checkpoint_bytes': (_i64, [_i64, _i64, _int, _int, _i64, _int, _int, _int]),
+    'bdm_scan_backward': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _int,
+                                 _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp,
+                                 _i64, _vp]),
+    'bdm_event_vjp': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int,
+                             _int, _int, _flt, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    'bdm_product_state_backward': (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp]),
+    'bdm_route_backward': (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _int, _vp, _i64,
+                                  _vp]),
+    'bdm_controllers_backward_partial_floats': (_i64, [_i64, _int, _int]),
+    'bdm_controllers_backward': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp,
+                                        _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _vp, _i64,
+                                        _vp, _vp, _vp, _vp, _vp]),
     'bdm_bank_histogram': (_int, [_vp, _vp, _i64, _int, _int, _i64, _vp, _vp]),
     'bdm_bank_owners': (_int, [_vp, _i64, _int, _int, _vp, _vp, _vp, _vp]),
     'bdm_dispatch_owned_workspace_bytes': (_i64, [_i64, _i64, _int, _int, _i64]),

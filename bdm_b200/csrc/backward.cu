@@ -1,0 +1,1108 @@
+// Training backward of the BDM bank path.
+//
+// Restates the reference's training derivatives:
+//   recurrence      role_bank_kernel.py:76-150 (_role_backward: checkpoint replay, then the
+//                   reverse per-event chain), routed_update.py:31-49 (decay_transform's dp term)
+//   event VJP       role_bank_dispatch.py:76-132 (_vjp: per-token gather of the event
+//                   gradients, rounded to the parameter dtype where the reference stores them)
+//   initial state   product_routed_update.py:51-76 (factor gradients = sums of the state gradient)
+//   router          autograd of product_key_route (gdn2_banks.py:74-114)
+//   controllers     autograd of _controllers (_parameters.py:189-220, heads.py:11-22)
+//   output          autograd of _project_bank_output (_parameters.py:222-232)
+//
+// Recurrence backward, per event of one (sequence, head) on one state column x
+// (h0 = state before the event, dh = adjoint of the state after it):
+//   write:  hd = h0*e (e = exp(g_e)), u = w_e*v - sum_s a_s hd_s (a = b_e*k),
+//           du = sum_s dh_s k_s,  c_s = hd_s du,  A_s = dh_s u,  dh'_s = dh_s - a_s du,
+//           G_s = dh'_s hd_s,  dh <- dh' * e
+//   read:   o_s = h0_s do (do = output gradient of the read's token), dh += scale * q_e do
+// The per-event S-vectors A, c, G (write) and o (read) are sums over the columns;
+// dk_e = A - b_e c, db_e = -k c, dg_e = G, dq_e = scale * o follow in the VJP.
+//
+// One warp per (sequence, head, tile of 32 columns), one column per lane, so a
+// column's S rows stay in registers.  States come back by replay at three levels:
+// HBM checkpoints every kBlock events (written by a first forward sweep), shared-
+// memory sub-checkpoints every kSub events inside a block, and a register history
+// of the kSub states inside a sub-block, walked in reverse.
+#include "common.cuh"
+
+namespace bdm {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// ------------------------------------------------------------ warp reductions
+
+template <int N> struct Pow2Ceil {
+    static constexpr int value = N <= 1 ? 1 : 2 * Pow2Ceil<(N + 1) / 2>::value;
+};
+template <> struct Pow2Ceil<1> { static constexpr int value = 1; };
+
+constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
+
+// Sums N (a power of two) per-lane values across the warp by recursive halving:
+// at each of the five butterfly levels a lane keeps one half of its live values
+// and adds the partner's copy of that half.  Afterwards, for N >= 32, live value i
+// of lane l is the warp total of value l*(N/32) + i; for N < 32, value 0 of lane l
+// is the total of value l >> (5 - log2 N), held by 32/N lanes.
+template <int LIVE, int OFF, int N> struct HalvingReduce {
+    static __device__ __forceinline__ void run(float (&v)[N], unsigned lane) {
+        if constexpr (LIVE >= 2) {
+            constexpr int H = LIVE / 2;
+            const bool up = (lane & OFF) != 0;
+#pragma unroll
+            for (int i = 0; i < H; ++i) {
+                const float send = up ? v[i] : v[i + H];
+                const float keep = up ? v[i + H] : v[i];
+                v[i] = keep + __shfl_xor_sync(kFull, send, OFF);
+            }
+            if constexpr (OFF > 1) HalvingReduce<H, OFF / 2, N>::run(v, lane);
+        } else {
+            v[0] += __shfl_xor_sync(kFull, v[0], OFF);
+            if constexpr (OFF > 1) HalvingReduce<1, OFF / 2, N>::run(v, lane);
+        }
+    }
+};
+
+// Store the first `used` of N reduced values to out[0..used).
+template <int N>
+__device__ __forceinline__ void reduce_store(float (&v)[N], int used, float *out) {
+    const unsigned lane = lane_id();
+    HalvingReduce<N, 16, N>::run(v, lane);
+    if constexpr (N >= 32) {
+#pragma unroll
+        for (int i = 0; i < N / 32; ++i) {
+            const int idx = (int)lane * (N / 32) + i;
+            if (idx < used) out[idx] = v[i];
+        }
+    } else {
+        constexpr int shift = 5 - ilog2(N);
+        const int idx = (int)(lane >> shift);
+        if ((lane & ((1u << shift) - 1u)) == 0 && idx < used) out[idx] = v[0];
+    }
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(kFull, x, o));
+    return x;
+}
+
+// ------------------------------------------------------- recurrence backward
+
+struct ScanBwdParams {
+    const void *q, *k, *v;
+    const float *g;
+    const void *b, *w, *ww, *rw;
+    const int64_t *order, *cu;
+    int64_t nseq, J, nt, nw, E, units;
+    int H, dv, kw, kr, routed_decay, interval, tiles;
+    float scale;
+    const void *row_factor, *col_factor;
+    int64_t factor_cols;
+    int factor_dtype;
+    const void *dread;  // [nt, H*dv] gradient of the combined read output (activation dtype)
+    float *ckpt;        // [slots, H, S, dv] states at block starts
+    float *evg;         // [tiles, E, 3S] per-event column sums (A | c | G; o for reads)
+    float *du;          // [nt*kw, H*dv] write-event du per column
+    float *dinit;       // [nseq, H, S, dv] gradient of each sequence's initial state
+};
+
+template <int S> struct BwdGeom {
+    static constexpr int kSub = 64 / S;          // register history depth (64 floats per lane)
+    static constexpr int kNSub = 8;              // shared-memory sub-checkpoints per block
+    static constexpr int kBlock = kSub * kNSub;  // events between HBM checkpoints
+    static constexpr int kWarps = S >= 16 ? 2 : 4;
+    static constexpr int kRec = 3 * S;           // floats per event record
+    static constexpr int kRedW = Pow2Ceil<3 * S>::value;
+};
+
+// Controls of one event, as this lane uses them (lane-uniform rows, per-lane column).
+template <int S> struct EventCtl {
+    float k[S];   // write: key; read: q_e = dtype(q*r)
+    float a[S];   // write: dtype(b*p) * k
+    float e[S];   // write: exp(g_e)
+    float wv;     // write: dtype(w*p) * v on this lane's column
+    float dout;   // read: output gradient on this lane's column
+    int64_t id;
+    bool write;
+};
+
+template <typename T, int S>
+__device__ __forceinline__ void load_event(const ScanBwdParams &p, int64_t pos, int h, int col, bool active,
+                                           bool want_dout, EventCtl<S> &c) {
+    const int64_t id = __ldg(p.order + pos);
+    const int64_t V = (int64_t)p.H * p.dv;
+    c.id = id;
+    c.write = id < p.nw;
+    c.wv = 0.f;
+    c.dout = 0.f;
+    if (c.write) {
+        const int64_t tok = id / p.kw;
+        const float pw = ld_f(static_cast<const T *>(p.ww), id);
+        const int64_t base = (tok * p.H + h) * S;
+        const T *kp = static_cast<const T *>(p.k) + base;
+        const T *bp = static_cast<const T *>(p.b) + base;
+        const float *gp = p.g + base;
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const float kk = ld_f(kp, s);
+            c.k[s] = kk;
+            c.a[s] = rnd<T>(ld_f(bp, s) * pw) * kk;
+            c.e[s] = expf(p.routed_decay ? gp[s] * pw : gp[s]);
+        }
+        if (active) {
+            const int64_t o = tok * V + (int64_t)h * p.dv + col;
+            c.wv = rnd<T>(ld_f(static_cast<const T *>(p.w), o) * pw) * ld_f(static_cast<const T *>(p.v), o);
+        }
+    } else {
+        const int64_t rid = id - p.nw;
+        const int64_t tok = rid / p.kr;
+        const float r = ld_f(static_cast<const T *>(p.rw), rid);
+        const T *qp = static_cast<const T *>(p.q) + (tok * p.H + h) * S;
+#pragma unroll
+        for (int s = 0; s < S; ++s) c.k[s] = rnd<T>(ld_f(qp, s) * r);
+        if (want_dout && active)
+            c.dout = ld_f(static_cast<const T *>(p.dread), tok * V + (int64_t)h * p.dv + col);
+    }
+}
+
+template <int S>
+__device__ __forceinline__ void replay(const EventCtl<S> &c, float (&hs)[S]) {
+    if (!c.write) return;
+    float er = 0.f;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        hs[s] *= c.e[s];
+        er = fmaf(c.a[s], hs[s], er);
+    }
+    const float u = c.wv - er;
+#pragma unroll
+    for (int s = 0; s < S; ++s) hs[s] = fmaf(c.k[s], u, hs[s]);
+}
+
+template <int S>
+__device__ __forceinline__ void storage_round(const ScanBwdParams &p, int64_t e, float (&hs)[S]) {
+    if (p.interval > 0 && (int)e % p.interval == 0) {  // e < 2^31: events of one sequence
+#pragma unroll
+        for (int s = 0; s < S; ++s) hs[s] = bf16_round(hs[s]);
+    }
+}
+
+// Initial state of one column: product-key factors (rounded to their dtype), or zero;
+// rounded to BF16 under the training storage policy.
+template <int S>
+__device__ __forceinline__ void initial_column(const ScanBwdParams &p, int64_t seq, int h, int col, bool active,
+                                               float (&hs)[S]) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) hs[s] = 0.f;
+    if (!active || !p.row_factor) return;
+    const int64_t bank = seq % p.J;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int64_t r = (bank * p.H + h) * S + s;
+        const int64_t ou = (r / p.factor_cols) * p.dv + col, oz = (r % p.factor_cols) * p.dv + col;
+        if (p.factor_dtype == BDM_BF16) {
+            hs[s] = bf16_round(ld_f(static_cast<const bf16 *>(p.row_factor), ou) +
+                               ld_f(static_cast<const bf16 *>(p.col_factor), oz));
+        } else {
+            hs[s] = static_cast<const float *>(p.row_factor)[ou] + static_cast<const float *>(p.col_factor)[oz];
+        }
+        if (p.interval > 0) hs[s] = bf16_round(hs[s]);
+    }
+}
+
+template <int S>
+__device__ __forceinline__ void reverse_event(const ScanBwdParams &p, const EventCtl<S> &c, const float (&h0)[S],
+                                              int tile, int h, int col, bool active, float (&dh)[S]) {
+    using G = BwdGeom<S>;
+    float *rec = p.evg + ((int64_t)tile * p.E + c.id) * G::kRec;
+    if (c.write) {
+        float hd[S], er = 0.f, du = 0.f;
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            hd[s] = h0[s] * c.e[s];
+            er = fmaf(c.a[s], hd[s], er);
+            du = fmaf(dh[s], c.k[s], du);
+        }
+        const float u = c.wv - er;
+        float red[G::kRedW];
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            red[s] = dh[s] * u;
+            red[S + s] = hd[s] * du;
+            const float dp = fmaf(-c.a[s], du, dh[s]);
+            red[2 * S + s] = dp * hd[s];
+            dh[s] = dp * c.e[s];
+        }
+#pragma unroll
+        for (int i = 3 * S; i < G::kRedW; ++i) red[i] = 0.f;
+        if (active) p.du[c.id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + col] = du;
+        reduce_store<G::kRedW>(red, 3 * S, rec);
+    } else {
+        float red[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            red[s] = h0[s] * c.dout;
+            dh[s] = fmaf(c.k[s] * c.dout, p.scale, dh[s]);
+        }
+        reduce_store<S>(red, S, rec);
+    }
+}
+
+template <typename T, int S>
+__global__ void __launch_bounds__(32 * BwdGeom<S>::kWarps) scan_backward_kernel(const ScanBwdParams p) {
+    using G = BwdGeom<S>;
+    __shared__ float sub_sm[G::kWarps][G::kNSub][S][32];
+    const int warp = (int)(threadIdx.x >> 5);
+    const unsigned lane = lane_id();
+    const int64_t unit = (int64_t)blockIdx.x * G::kWarps + warp;
+    if (unit >= p.units) return;  // uniform per warp
+    const int tile = (int)(unit % p.tiles);
+    const int h = (int)((unit / p.tiles) % p.H);
+    const int64_t seq = unit / ((int64_t)p.tiles * p.H);
+    const int col = tile * 32 + (int)lane;
+    const bool active = col < p.dv;
+    const int64_t start = p.cu[seq], L = p.cu[seq + 1] - start;
+    float(*sub)[S][32] = sub_sm[warp];
+    float dh[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) dh[s] = 0.f;
+    const int64_t stride_state = (int64_t)S * p.dv;
+    if (L > 0) {
+        const int64_t nblk = (L + G::kBlock - 1) / G::kBlock;
+        const int64_t slot0 = start / G::kBlock + seq;  // disjoint slot ranges across sequences
+        float hs[S];
+        EventCtl<S> c;
+        if (nblk > 1) {  // sweep 1: checkpoints at the starts of blocks 1 .. nblk-1
+            initial_column<S>(p, seq, h, col, active, hs);
+            for (int64_t m = 1; m < nblk; ++m) {
+                for (int64_t e = (m - 1) * G::kBlock; e < m * G::kBlock; ++e) {
+                    storage_round<S>(p, e, hs);
+                    load_event<T, S>(p, start + e, h, col, active, false, c);
+                    replay<S>(c, hs);
+                }
+                if (active) {
+                    float *ck = p.ckpt + ((slot0 + m) * p.H + h) * stride_state + col;
+#pragma unroll
+                    for (int s = 0; s < S; ++s) ck[(int64_t)s * p.dv] = hs[s];
+                }
+            }
+        }
+        for (int64_t m = nblk - 1; m >= 0; --m) {  // sweep 2: blocks in reverse
+            if (m == 0) {
+                initial_column<S>(p, seq, h, col, active, hs);
+            } else {
+                const float *ck = p.ckpt + ((slot0 + m) * p.H + h) * stride_state + col;
+#pragma unroll
+                for (int s = 0; s < S; ++s) hs[s] = active ? ck[(int64_t)s * p.dv] : 0.f;
+            }
+            const int64_t e0 = m * G::kBlock;
+            const int blen = (int)min((int64_t)G::kBlock, L - e0);
+            const int nsub = (blen + G::kSub - 1) / G::kSub;
+            for (int n = 0; n < nsub; ++n) {  // sub-checkpoints (lane-private shared memory)
+#pragma unroll
+                for (int s = 0; s < S; ++s) sub[n][s][lane] = hs[s];
+                if (n == nsub - 1) break;
+                for (int j = 0; j < G::kSub; ++j) {
+                    const int64_t e = e0 + n * G::kSub + j;
+                    storage_round<S>(p, e, hs);
+                    load_event<T, S>(p, start + e, h, col, active, false, c);
+                    replay<S>(c, hs);
+                }
+            }
+            for (int n = nsub - 1; n >= 0; --n) {
+#pragma unroll
+                for (int s = 0; s < S; ++s) hs[s] = sub[n][s][lane];
+                const int slen = min(G::kSub, blen - n * G::kSub);
+                const int64_t eb = e0 + n * G::kSub;
+                float hist[G::kSub][S];
+#pragma unroll
+                for (int j = 0; j < G::kSub; ++j) {
+                    if (j < slen) {
+                        storage_round<S>(p, eb + j, hs);
+#pragma unroll
+                        for (int s = 0; s < S; ++s) hist[j][s] = hs[s];
+                        if (j + 1 < slen) {
+                            load_event<T, S>(p, start + eb + j, h, col, active, false, c);
+                            replay<S>(c, hs);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = G::kSub - 1; j >= 0; --j) {
+                    if (j < slen) {
+                        load_event<T, S>(p, start + eb + j, h, col, active, true, c);
+                        reverse_event<S>(p, c, hist[j], tile, h, col, active, dh);
+                    }
+                }
+            }
+        }
+    }
+    if (active) {
+        float *di = p.dinit + (seq * p.H + h) * stride_state + col;
+#pragma unroll
+        for (int s = 0; s < S; ++s) di[(int64_t)s * p.dv] = dh[s];
+    }
+}
+
+template <typename T, int S>
+int launch_scan_backward(const ScanBwdParams &p, cudaStream_t st) {
+    using G = BwdGeom<S>;
+    const int64_t blocks = ceil_div(p.units, G::kWarps);
+    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    scan_backward_kernel<T, S><<<(unsigned)blocks, 32 * G::kWarps, 0, st>>>(p);
+    return launch_status();
+}
+
+int64_t block_events(int S) { return S == 4 ? BwdGeom<4>::kBlock : S == 8 ? BwdGeom<8>::kBlock : BwdGeom<16>::kBlock; }
+
+// ------------------------------------------------------------------ event VJP
+
+struct VjpParams {
+    const void *q, *k, *v;
+    const float *g;
+    const void *b, *w, *ww, *rw;
+    const float *evg, *du;
+    int64_t nt, nw, E;
+    int H, dv, kw, kr, routed_decay, tiles;
+    float scale;
+    void *dq, *dk, *dv_out, *db, *dw_out, *dww, *drw;
+    float *dg;
+};
+
+constexpr int kVjpMaxCols = 8;   // value columns per lane: head width <= 256
+constexpr int kVjpMaxSlots = 64;
+
+// One CTA per token, one warp per head.  Mirrors _vjp's per-token loop over the
+// write slots, then the read slots, with its rounding points; route-weight
+// gradients are per head (the reference runs one routed update per head) and
+// summed over heads in ascending order.
+template <typename T, int S>
+__global__ void event_vjp_kernel(const VjpParams p) {
+    __shared__ float part_w[32][kVjpMaxSlots];
+    __shared__ float part_r[32][kVjpMaxSlots];
+    const int64_t t = blockIdx.x;
+    const int h = (int)(threadIdx.x >> 5);
+    const int lane = (int)lane_id();
+    const int dv = p.dv;
+    const int64_t V = (int64_t)p.H * dv;
+    const int64_t hs0 = (t * p.H + h) * S;
+    const bool nl = lane < S;
+    constexpr int R = 3 * S;
+    float k0 = 0.f, b0 = 0.f, g0 = 0.f, q0 = 0.f;
+    if (nl) {
+        k0 = ld_f(static_cast<const T *>(p.k), hs0 + lane);
+        b0 = ld_f(static_cast<const T *>(p.b), hs0 + lane);
+        g0 = p.g[hs0 + lane];
+        q0 = ld_f(static_cast<const T *>(p.q), hs0 + lane);
+    }
+    float v0[kVjpMaxCols], w0[kVjpMaxCols], accv[kVjpMaxCols], accw[kVjpMaxCols];
+#pragma unroll
+    for (int i = 0; i < kVjpMaxCols; ++i) {
+        const int c = lane + 32 * i;
+        const bool on = c < dv;
+        v0[i] = on ? ld_f(static_cast<const T *>(p.v), t * V + (int64_t)h * dv + c) : 0.f;
+        w0[i] = on ? ld_f(static_cast<const T *>(p.w), t * V + (int64_t)h * dv + c) : 0.f;
+        accv[i] = accw[i] = 0.f;
+    }
+    float dk_acc = 0.f, db_acc = 0.f, dg_acc = 0.f, dq_acc = 0.f;
+    for (int j = 0; j < p.kw; ++j) {
+        const int64_t id = t * p.kw + j;
+        const float pw = ld_f(static_cast<const T *>(p.ww), id);
+        float wvp = 0.f;
+        const float *durow = p.du + id * V + (int64_t)h * dv;
+#pragma unroll
+        for (int i = 0; i < kVjpMaxCols; ++i) {
+            const int c = lane + 32 * i;
+            if (c < dv) {
+                const float du = durow[c];
+                const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
+                const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
+                accv[i] = rnd<T>(accv[i] + dve);
+                accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
+                wvp += rnd<T>(dwe * w0[i]);
+            }
+        }
+        const float wv = rnd<T>(warp_sum(wvp));
+        float wbp = 0.f, dec = 0.f;
+        if (nl) {
+            float A = 0.f, C = 0.f, Gs = 0.f;
+            for (int tile = 0; tile < p.tiles; ++tile) {
+                const float *rec = p.evg + ((int64_t)tile * p.E + id) * R;
+                A += rec[lane];
+                C += rec[S + lane];
+                Gs += rec[2 * S + lane];
+            }
+            const float be = rnd<T>(b0 * pw);
+            const float dke = rnd<T>(A - be * C);
+            const float dbe = rnd<T>(-k0 * C);
+            dk_acc += dke;
+            db_acc += rnd<T>(dbe * pw);
+            if (p.routed_decay) {
+                dg_acc += Gs * pw;
+                dec = Gs * g0;
+            } else {
+                dg_acc += Gs;
+            }
+            wbp = rnd<T>(dbe * b0);
+        }
+        const float wb = rnd<T>(warp_sum(wbp));
+        const float decs = warp_sum(dec);
+        if (lane == 0) part_w[h][j] = rnd<T>(rnd<T>(wb + wv) + decs);
+    }
+    for (int j = 0; j < p.kr; ++j) {
+        const int64_t rid = t * p.kr + j;
+        const int64_t id = p.nw + rid;
+        const float r = ld_f(static_cast<const T *>(p.rw), rid);
+        float wrp = 0.f;
+        if (nl) {
+            float o = 0.f;
+            for (int tile = 0; tile < p.tiles; ++tile) o += p.evg[((int64_t)tile * p.E + id) * R + lane] * p.scale;
+            const float dqe = rnd<T>(o);
+            dq_acc += rnd<T>(dqe * r);
+            wrp = rnd<T>(dqe * q0);
+        }
+        const float wr = rnd<T>(warp_sum(wrp));
+        if (lane == 0) part_r[h][j] = wr;
+    }
+    if (nl) {
+        st_f(static_cast<T *>(p.dq), hs0 + lane, dq_acc);
+        st_f(static_cast<T *>(p.dk), hs0 + lane, dk_acc);
+        st_f(static_cast<T *>(p.db), hs0 + lane, db_acc);
+        p.dg[hs0 + lane] = dg_acc;
+    }
+#pragma unroll
+    for (int i = 0; i < kVjpMaxCols; ++i) {
+        const int c = lane + 32 * i;
+        if (c < dv) {
+            st_f(static_cast<T *>(p.dv_out), t * V + (int64_t)h * dv + c, accv[i]);
+            st_f(static_cast<T *>(p.dw_out), t * V + (int64_t)h * dv + c, accw[i]);
+        }
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < p.kw + p.kr; j += blockDim.x) {
+        const bool wr = j < p.kw;
+        const int jj = wr ? j : j - p.kw;
+        float s = wr ? part_w[0][jj] : part_r[0][jj];
+        for (int hh = 1; hh < p.H; ++hh) s = rnd<T>(s + (wr ? part_w[hh][jj] : part_r[hh][jj]));
+        if (wr)
+            st_f(static_cast<T *>(p.dww), t * p.kw + jj, s);
+        else
+            st_f(static_cast<T *>(p.drw), t * p.kr + jj, s);
+    }
+}
+
+// ------------------------------------------------------- initial-state factors
+
+// ds[r][x] = dtype(sum_b dtype(dinit[b][r][x])): the state gradient of one logical row,
+// rounded per sequence as the reference rounds each routed update's state gradient.
+template <typename T>
+__global__ void state_rows_kernel(const float *__restrict__ dinit, int64_t batch, int64_t rows, int dv,
+                                  float *__restrict__ ds) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * dv) return;
+    float acc = 0.f;
+    for (int64_t b = 0; b < batch; ++b) acc += rnd<T>(dinit[b * rows * dv + i]);
+    ds[i] = rnd<T>(acc);
+}
+
+// dU[p][x] = sum_q ds[p*Q+q][x] and dZ[q][x] = sum_p ds[p*Q+q][x], each rounded once.
+template <typename T>
+__global__ void factor_sums_kernel(const float *__restrict__ ds, int64_t P, int64_t Q, int dv,
+                                   float *__restrict__ du, float *__restrict__ dz) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < P * dv) {
+        const int64_t pp = i / dv, x = i % dv;
+        float acc = 0.f;
+        for (int64_t q = 0; q < Q; ++q) acc += ds[(pp * Q + q) * dv + x];
+        du[i] = rnd<T>(acc);
+    } else if (i < (P + Q) * dv) {
+        const int64_t j = i - P * dv;
+        const int64_t qq = j / dv, x = j % dv;
+        float acc = 0.f;
+        for (int64_t pp = 0; pp < P; ++pp) acc += ds[(pp * Q + qq) * dv + x];
+        dz[j] = rnd<T>(acc);
+    }
+}
+
+// ---------------------------------------------------------------- router
+
+struct RouteBwdParams {
+    const void *logits;  // [ntok, ld] holding both blocks
+    void *dlogits;       // [ntok, ldd]
+    int64_t ntok, ld, ldd, first, second;
+    int j1, j2, count;
+    const int64_t *idx1, *idx2;
+    const void *dw1, *dw2;
+};
+
+// One warp per (token, block).  Weights = softmax over the selected pair scores
+// dtype(L1[row] + L2[col]); their gradient is softmax's backward, rounded to the
+// logits dtype, then summed onto each selected row of the first factor and each
+// selected column of the second (in selection order); all other logits get 0.
+template <typename T>
+__global__ void route_backward_kernel(const RouteBwdParams p) {
+    const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= 2 * p.ntok) return;
+    const int lane = (int)lane_id();
+    const int64_t t = item >> 1;
+    const int blk = (int)(item & 1);
+    const int64_t off = blk ? p.second : p.first;
+    const T *lg = static_cast<const T *>(p.logits) + t * p.ld + off;
+    T *out = static_cast<T *>(p.dlogits) + t * p.ldd + off;
+    const int64_t *idx = (blk ? p.idx2 : p.idx1) + t * p.count;
+    const T *dw = static_cast<const T *>(blk ? p.dw2 : p.dw1) + t * p.count;
+    for (int i = lane; i < p.j1 + p.j2; i += 32) out[i] = Elem<T>::from_float(0.f);
+    __syncwarp();
+    const bool on = lane < p.count;
+    int row = -1, colj = -1;
+    float val = -INFINITY, dwc = 0.f;
+    if (on) {
+        const int64_t id = idx[lane];
+        row = (int)(id / p.j2);
+        colj = (int)(id % p.j2);
+        val = rnd<T>(ld_f(lg, row) + ld_f(lg, p.j1 + colj));
+        dwc = ld_f(dw, lane);
+    }
+    const float m = warp_max(val);
+    const float ex = on ? expf(val - m) : 0.f;
+    const float tot = warp_sum(ex);
+    const float wgt = on ? ex / tot : 0.f;
+    const float dot = warp_sum(wgt * dwc);
+    const float dval = on ? rnd<T>(wgt * (dwc - dot)) : 0.f;
+    float trow = 0.f, tcol = 0.f;
+    bool frow = on, fcol = on;
+    for (int c = 0; c < p.count; ++c) {
+        const int rc = __shfl_sync(kFull, row, c), cc = __shfl_sync(kFull, colj, c);
+        const float dc = __shfl_sync(kFull, dval, c);
+        if (rc == row) {
+            trow += dc;
+            if (c < lane) frow = false;
+        }
+        if (cc == colj) {
+            tcol += dc;
+            if (c < lane) fcol = false;
+        }
+    }
+    if (frow) out[row] = Elem<T>::from_float(trow);
+    if (fcol) out[p.j1 + colj] = Elem<T>::from_float(tcol);
+}
+
+// ------------------------------------------------------------- controllers
+
+constexpr int kCtlThreads = 256;
+constexpr int kMaxS = 16;
+constexpr int kGateTokens = 64;  // tokens per thread in the b / g range (parameter partial sums)
+
+__device__ __forceinline__ float sigmoid_ieee(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_grad(float z) {
+    const float s = sigmoid_ieee(z);
+    return s * (1.0f + z * (1.0f - s));
+}
+
+struct CtlBwdArgs {
+    const void *proj;
+    int64_t ntok, ld, col_q, col_k, col_v, col_b, col_w;
+    const void *f;
+    int64_t ldf;
+    const float *a_log, *dt_bias, *g;
+    const void *b, *w;                 // forward outputs (sigmoid results)
+    const void *dq, *dk, *dvv, *db, *dw;
+    const float *dg;
+    void *dproj;
+    int64_t ldd;
+    void *df;                          // [ntok, H*S]
+    float *part_dt, *part_a;           // [chunks, H*S]
+    int H, S, dv, qk_norm;
+    int64_t narrow_blocks, gate_blocks, chunks;
+};
+
+// q and k of one (token, head): normalize(silu(z)) backward, then silu's.
+template <typename T>
+__device__ __forceinline__ void ctl_narrow(const CtlBwdArgs &a, int64_t t, int h) {
+    const T *row = static_cast<const T *>(a.proj) + t * a.ld;
+    T *drow = static_cast<T *>(a.dproj) + t * a.ldd;
+    const int S = a.S;
+    const int64_t o = (t * a.H + h) * S;
+#pragma unroll
+    for (int role = 0; role < 2; ++role) {
+        const int64_t col = (role ? a.col_k : a.col_q) + (int64_t)h * S;
+        const T *dy = static_cast<const T *>(role ? a.dk : a.dq) + o;
+        float z[kMaxS], x[kMaxS];
+        float ss = 0.f, xdy = 0.f;
+        for (int s = 0; s < S; ++s) {
+            z[s] = Elem<T>::to_float(row[col + s]);
+            x[s] = rnd<T>(z[s] / (1.0f + expf(-z[s])));
+            ss += x[s] * x[s];
+            xdy += x[s] * ld_f(dy, s);
+        }
+        float scale, cube;
+        if (a.qk_norm) {  // x * rsqrt(sum x^2 + 1e-6)
+            scale = 1.0f / sqrtf(ss + 1e-6f);
+            cube = scale * scale * scale;
+        } else {          // x / max(|x|, 1e-12)
+            const float n = sqrtf(ss);
+            scale = 1.0f / fmaxf(n, 1e-12f);
+            cube = n > 1e-12f ? scale * scale * scale : 0.f;
+        }
+        for (int s = 0; s < S; ++s) {
+            const float dx = rnd<T>(scale * ld_f(dy, s) - x[s] * cube * xdy);
+            drow[col + s] = Elem<T>::from_float(dx * silu_grad(z[s]));
+        }
+    }
+}
+
+// b and the decay gate of one head*S + s over a chunk of tokens; FP32 partial sums of
+// the dt_bias gradient and of dg * g (the A_log gradient) per chunk.
+template <typename T>
+__device__ __forceinline__ void ctl_gate(const CtlBwdArgs &a, int64_t chunk, int hs) {
+    const int HS = a.H * a.S;
+    const int h = hs / a.S;
+    const float na = -expf(a.a_log[h]);
+    const float dtb = a.dt_bias[hs];
+    float pdt = 0.f, pa = 0.f;
+    const int64_t t1 = min(a.ntok, (chunk + 1) * kGateTokens);
+    for (int64_t t = chunk * kGateTokens; t < t1; ++t) {
+        const int64_t o = t * HS + hs;
+        const float bo = ld_f(static_cast<const T *>(a.b), o);
+        const float dbv = ld_f(static_cast<const T *>(a.db), o);
+        st_f(static_cast<T *>(a.dproj), t * a.ldd + a.col_b + hs, dbv * (1.0f - bo) * bo);
+        const float z = ld_f(static_cast<const T *>(a.f), t * a.ldf + hs) + dtb;
+        const float dgv = a.dg[o];
+        const float dz = dgv * na * (z > 20.0f ? 1.0f : sigmoid_ieee(z));
+        st_f(static_cast<T *>(a.df), o, dz);
+        pdt += dz;
+        pa += dgv * a.g[o];
+    }
+    a.part_dt[chunk * HS + hs] = pdt;
+    a.part_a[chunk * HS + hs] = pa;
+}
+
+template <typename T>
+__device__ __forceinline__ void ctl_wide(const CtlBwdArgs &a, int64_t i) {
+    const int64_t V = (int64_t)a.H * a.dv;
+    const int64_t t = i / V, c = i % V;
+    const T *row = static_cast<const T *>(a.proj) + t * a.ld;
+    T *drow = static_cast<T *>(a.dproj) + t * a.ldd;
+    const float zv = Elem<T>::to_float(row[a.col_v + c]);
+    drow[a.col_v + c] = Elem<T>::from_float(ld_f(static_cast<const T *>(a.dvv), i) * silu_grad(zv));
+    const float wo = ld_f(static_cast<const T *>(a.w), i);
+    drow[a.col_w + c] = Elem<T>::from_float(ld_f(static_cast<const T *>(a.dw), i) * (1.0f - wo) * wo);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kCtlThreads) controllers_backward_kernel(const CtlBwdArgs a) {
+    const int64_t blk = blockIdx.x;
+    if (blk < a.narrow_blocks) {
+        const int64_t item = blk * kCtlThreads + threadIdx.x;
+        if (item < a.ntok * a.H) ctl_narrow<T>(a, item / a.H, (int)(item % a.H));
+    } else if (blk < a.narrow_blocks + a.gate_blocks) {
+        const int64_t item = (blk - a.narrow_blocks) * kCtlThreads + threadIdx.x;
+        const int HS = a.H * a.S;
+        if (item < a.chunks * HS) ctl_gate<T>(a, item / HS, (int)(item % HS));
+    } else {
+        const int64_t item = (blk - a.narrow_blocks - a.gate_blocks) * kCtlThreads + threadIdx.x;
+        if (item < a.ntok * a.H * a.dv) ctl_wide<T>(a, item);
+    }
+}
+
+// ----------------------------------------------------------- output interface
+
+constexpr int kNgCols = 8;
+constexpr int kNgTokens = 16;  // tokens per CTA (norm-parameter partial sums)
+
+template <typename T> __device__ __forceinline__ float gate_sigmoid(float x);
+template <> __device__ __forceinline__ float gate_sigmoid<bf16>(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+template <> __device__ __forceinline__ float gate_sigmoid<float>(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float ng_block_sum(float x, float *red) {
+    x = warp_sum(x);
+    const int warp = threadIdx.x >> 5, lane = (int)lane_id();
+    const int nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = x;
+    __syncthreads();
+    float s = lane < nw ? red[lane] : 0.f;
+    return warp_sum(s);
+}
+
+struct NgBwdArgs {
+    const void *dout, *raw, *gate, *nw, *nb;
+    int64_t ntok, width, ld_gate, ldd;
+    float eps;
+    int norm_mode;
+    void *draw, *dgate;
+    float *part_w, *part_b;  // [blocks, width]
+};
+
+// Backward of  out = norm(raw) * dtype(sigmoid(gate_logit))  for kNgTokens tokens per
+// CTA, each thread on 8 columns; norm = LayerNorm (mode 1) or the reference's RMS
+// form dtype(dtype(raw * dtype(rsqrt(mean raw^2 + eps))) * weight) (mode 0).
+template <typename T>
+__global__ void norm_gate_backward_kernel(const NgBwdArgs a) {
+    __shared__ float red[32];
+    const int64_t c0 = (int64_t)threadIdx.x * kNgCols;
+    const bool act = c0 < a.width;
+    const float inv_w = 1.0f / (float)a.width;
+    float gw[kNgCols], gb[kNgCols], wv[kNgCols], bv[kNgCols];
+#pragma unroll
+    for (int i = 0; i < kNgCols; ++i) {
+        const bool on = act && c0 + i < a.width;
+        gw[i] = gb[i] = 0.f;
+        wv[i] = on ? ld_f(static_cast<const T *>(a.nw), c0 + i) : 0.f;
+        bv[i] = on && a.nb ? ld_f(static_cast<const T *>(a.nb), c0 + i) : 0.f;
+    }
+    const int64_t t0 = (int64_t)blockIdx.x * kNgTokens;
+    const int64_t t1 = min(a.ntok, t0 + kNgTokens);
+    for (int64_t t = t0; t < t1; ++t) {
+        float x[kNgCols], dy[kNgCols], gt[kNgCols];
+#pragma unroll
+        for (int i = 0; i < kNgCols; ++i) {
+            const bool on = act && c0 + i < a.width;
+            x[i] = on ? ld_f(static_cast<const T *>(a.raw), t * a.width + c0 + i) : 0.f;
+            dy[i] = on ? ld_f(static_cast<const T *>(a.dout), t * a.width + c0 + i) : 0.f;
+            gt[i] = on ? rnd<T>(gate_sigmoid<T>(ld_f(static_cast<const T *>(a.gate), t * a.ld_gate + c0 + i))) : 0.f;
+        }
+        float n[kNgCols], dn[kNgCols], dx[kNgCols];
+        if (a.norm_mode == 1) {
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i) s += x[i];
+            const float mean = ng_block_sum(s, red) * inv_w;
+            float sq = 0.f;
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i)
+                if (act && c0 + i < a.width) sq += (x[i] - mean) * (x[i] - mean);
+            const float rstd = 1.0f / sqrtf(ng_block_sum(sq, red) * inv_w + a.eps);
+            float xh[kNgCols], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i) {
+                const bool on = act && c0 + i < a.width;
+                xh[i] = on ? (x[i] - mean) * rstd : 0.f;
+                n[i] = on ? rnd<T>(xh[i] * wv[i] + bv[i]) : 0.f;
+                dn[i] = rnd<T>(dy[i] * gt[i]);
+                const float dxh = dn[i] * wv[i];
+                s1 += dxh;
+                s2 += dxh * xh[i];
+                gw[i] += dn[i] * xh[i];
+                gb[i] += dn[i];
+            }
+            s1 = ng_block_sum(s1, red);
+            s2 = ng_block_sum(s2, red);
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i)
+                dx[i] = rnd<T>(rstd * inv_w * ((float)a.width * dn[i] * wv[i] - s1 - xh[i] * s2));
+        } else {
+            float sq = 0.f;
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i) sq += x[i] * x[i];
+            const float rs32 = 1.0f / sqrtf(ng_block_sum(sq, red) * inv_w + a.eps);
+            const float rs = rnd<T>(rs32);
+            float n1[kNgCols], dn1[kNgCols], drs = 0.f;
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i) {
+                n1[i] = rnd<T>(x[i] * rs);
+                n[i] = rnd<T>(n1[i] * wv[i]);
+                dn[i] = rnd<T>(dy[i] * gt[i]);
+                gw[i] += rnd<T>(dn[i] * n1[i]);
+                dn1[i] = rnd<T>(dn[i] * wv[i]);
+                drs += rnd<T>(dn1[i] * x[i]);
+            }
+            drs = rnd<T>(ng_block_sum(drs, red));
+            const float dvar = drs * -0.5f * rs32 * rs32 * rs32;
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i)
+                dx[i] = rnd<T>(rnd<T>(dn1[i] * rs) + rnd<T>(dvar * 2.0f * x[i] * inv_w));
+        }
+        if (act) {
+#pragma unroll
+            for (int i = 0; i < kNgCols; ++i) {
+                if (c0 + i < a.width) {
+                    st_f(static_cast<T *>(a.draw), t * a.width + c0 + i, dx[i]);
+                    const float dgt = rnd<T>(dy[i] * n[i]);
+                    st_f(static_cast<T *>(a.dgate), t * a.ldd + c0 + i, dgt * gt[i] * (1.0f - gt[i]));
+                }
+            }
+        }
+    }
+    if (act) {
+#pragma unroll
+        for (int i = 0; i < kNgCols; ++i) {
+            if (c0 + i < a.width) {
+                a.part_w[(int64_t)blockIdx.x * a.width + c0 + i] = gw[i];
+                if (a.part_b) a.part_b[(int64_t)blockIdx.x * a.width + c0 + i] = gb[i];
+            }
+        }
+    }
+}
+
+// out[c] = sum over rows r of in[r*ld + c] (ascending r inside 8 interleaved groups, then
+// the groups in order): deterministic column sums of partial-sum tables.
+__global__ void column_sums_kernel(const float *__restrict__ in, int64_t rows, int64_t cols, int64_t ld,
+                                   float *__restrict__ out) {
+    __shared__ float part[8][32];
+    const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+    const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+    float acc = 0.f;
+    if (c < cols)
+        for (int64_t r = grp; r < rows; r += 8) acc += in[r * ld + c];
+    part[grp][lane] = acc;
+    __syncthreads();
+    if (grp == 0 && c < cols) {
+        float s = 0.f;
+        for (int i = 0; i < 8; ++i) s += part[i][lane];
+        out[c] = s;
+    }
+}
+
+int column_sums(const float *in, int64_t rows, int64_t cols, int64_t ld, float *out, cudaStream_t st) {
+    if (cols <= 0) return BDM_OK;
+    column_sums_kernel<<<(unsigned)ceil_div(cols, 32), 256, 0, st>>>(in, rows, cols, ld, out);
+    return launch_status();
+}
+
+// out[i] = sum_{j < len} in[i*len + j] (ascending j): per-head sums of per-row totals.
+__global__ void segment_sums_kernel(const float *__restrict__ in, int nseg, int len, float *__restrict__ out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nseg) return;
+    float s = 0.f;
+    for (int j = 0; j < len; ++j) s += in[(int64_t)i * len + j];
+    out[i] = s;
+}
+
+}  // namespace
+}  // namespace bdm
+
+// ------------------------------------------------------------------ C ABI
+
+extern "C" int64_t bdm_scan_backward_checkpoint_bytes(int64_t batch, int64_t time, int kw, int kr, int64_t bank_count,
+                                                      int heads, int bank_size, int head_value_width) {
+    using namespace bdm;
+    if (batch < 0 || time < 0 || kw <= 0 || kr <= 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0)
+        return -1;
+    if (bank_size != 4 && bank_size != 8 && bank_size != 16) return -1;
+    const int64_t E = batch * time * (kw + kr);
+    const int64_t slots = E / block_events(bank_size) + batch * bank_count + 1;
+    return slots * heads * bank_size * head_value_width * (int64_t)sizeof(float);
+}
+
+extern "C" int bdm_scan_backward(const void *q, const void *k, const void *v, const float *g, const void *b,
+                                 const void *w, const void *write_w, const void *read_w, const int64_t *order,
+                                 const int64_t *cu_seqlens, int64_t batch, int64_t time, int64_t bank_count, int heads,
+                                 int bank_size, int head_value_width, int kw, int kr, int dtype, int routed_decay,
+                                 float scale, const void *row_factor, const void *col_factor, int64_t factor_cols,
+                                 int factor_dtype, int state_interval, const void *d_read, float *event_grads,
+                                 float *d_write_value, float *d_initial, float *checkpoints, int64_t checkpoint_bytes,
+                                 void *stream) {
+    using namespace bdm;
+    if (batch < 0 || time < 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0 ||
+        state_interval < 0)
+        return BDM_ERR_INVALID;
+    if (bank_size != 4 && bank_size != 8 && bank_size != 16) return BDM_ERR_UNSUPPORTED;
+    if (!valid_dtype(dtype)) return BDM_ERR_DTYPE;
+    if (row_factor && (!col_factor || factor_cols <= 0 || !valid_dtype(factor_dtype))) return BDM_ERR_INVALID;
+    const int64_t need = bdm_scan_backward_checkpoint_bytes(batch, time, kw, kr, bank_count, heads, bank_size,
+                                                            head_value_width);
+    if (batch * time == 0) return BDM_OK;
+    if (!q || !k || !v || !g || !b || !w || !write_w || !read_w || !order || !cu_seqlens || !d_read ||
+        !event_grads || !d_write_value || !d_initial)
+        return BDM_ERR_INVALID;
+    if (!checkpoints || checkpoint_bytes < need) return BDM_ERR_WORKSPACE;
+    ScanBwdParams p{};
+    p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w; p.ww = write_w; p.rw = read_w;
+    p.order = order; p.cu = cu_seqlens;
+    p.nseq = batch * bank_count; p.J = bank_count; p.nt = batch * time; p.nw = p.nt * kw;
+    p.E = p.nt * (kw + kr);
+    p.H = heads; p.dv = head_value_width; p.kw = kw; p.kr = kr; p.routed_decay = routed_decay;
+    p.interval = state_interval; p.tiles = (int)ceil_div(head_value_width, 32); p.scale = scale;
+    p.row_factor = row_factor; p.col_factor = col_factor; p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
+    p.dread = d_read; p.ckpt = checkpoints; p.evg = event_grads; p.du = d_write_value; p.dinit = d_initial;
+    p.units = p.nseq * heads * p.tiles;
+    const cudaStream_t st = as_stream(stream);
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        if (bank_size == 4) return launch_scan_backward<T, 4>(p, st);
+        if (bank_size == 8) return launch_scan_backward<T, 8>(p, st);
+        return launch_scan_backward<T, 16>(p, st);
+    });
+    return BDM_ERR_UNSUPPORTED;
+}
+
+extern "C" int bdm_event_vjp(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
+                             const void *write_w, const void *read_w, const float *event_grads,
+                             const float *d_write_value, int64_t ntok, int heads, int bank_size, int head_value_width,
+                             int kw, int kr, int dtype, int routed_decay, float scale, void *dq, void *dk, void *dv,
+                             float *dg, void *db, void *dw, void *d_write_w, void *d_read_w, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0) return BDM_ERR_INVALID;
+    if (bank_size != 4 && bank_size != 8 && bank_size != 16) return BDM_ERR_UNSUPPORTED;
+    if (heads > 32 || head_value_width > 32 * kVjpMaxCols || kw > kVjpMaxSlots || kr > kVjpMaxSlots)
+        return BDM_ERR_UNSUPPORTED;
+    if (!valid_dtype(dtype)) return BDM_ERR_DTYPE;
+    if (ntok == 0) return BDM_OK;
+    if (!q || !k || !v || !g || !b || !w || !write_w || !read_w || !event_grads || !d_write_value || !dq || !dk ||
+        !dv || !dg || !db || !dw || !d_write_w || !d_read_w)
+        return BDM_ERR_INVALID;
+    if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    VjpParams p{};
+    p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w; p.ww = write_w; p.rw = read_w;
+    p.evg = event_grads; p.du = d_write_value;
+    p.nt = ntok; p.nw = ntok * kw; p.E = ntok * (kw + kr);
+    p.H = heads; p.dv = head_value_width; p.kw = kw; p.kr = kr; p.routed_decay = routed_decay;
+    p.tiles = (int)ceil_div(head_value_width, 32); p.scale = scale;
+    p.dq = dq; p.dk = dk; p.dv_out = dv; p.db = db; p.dw_out = dw; p.dww = d_write_w; p.drw = d_read_w; p.dg = dg;
+    const cudaStream_t st = as_stream(stream);
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        if (bank_size == 4) event_vjp_kernel<T, 4><<<(unsigned)ntok, 32 * heads, 0, st>>>(p);
+        else if (bank_size == 8) event_vjp_kernel<T, 8><<<(unsigned)ntok, 32 * heads, 0, st>>>(p);
+        else event_vjp_kernel<T, 16><<<(unsigned)ntok, 32 * heads, 0, st>>>(p);
+    });
+    return launch_status();
+}
+
+extern "C" int bdm_product_state_backward(const float *d_initial, int64_t batch, int64_t rows_p, int64_t cols_q,
+                                          int head_value_width, int factor_dtype, float *d_rows, float *d_row_factor,
+                                          float *d_col_factor, void *stream) {
+    using namespace bdm;
+    if (batch < 0 || rows_p <= 0 || cols_q <= 0 || head_value_width <= 0) return BDM_ERR_INVALID;
+    if (!valid_dtype(factor_dtype)) return BDM_ERR_DTYPE;
+    if (!d_initial || !d_rows || !d_row_factor || !d_col_factor) return BDM_ERR_INVALID;
+    const int64_t rows = rows_p * cols_q;
+    const cudaStream_t st = as_stream(stream);
+    const int64_t n1 = rows * head_value_width, n2 = (rows_p + cols_q) * head_value_width;
+    if (ceil_div(n1, 256) > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    BDM_DISPATCH_DTYPE(factor_dtype, T, {
+        state_rows_kernel<T><<<(unsigned)ceil_div(n1, 256), 256, 0, st>>>(d_initial, batch, rows, head_value_width,
+                                                                          d_rows);
+        int rc = launch_status();
+        if (rc != BDM_OK) return rc;
+        factor_sums_kernel<T><<<(unsigned)ceil_div(n2, 256), 256, 0, st>>>(d_rows, rows_p, cols_q, head_value_width,
+                                                                          d_row_factor, d_col_factor);
+    });
+    return launch_status();
+}
+
+extern "C" int bdm_route_backward(const void *logits, int64_t ntok, int64_t ld, int64_t first, int64_t second, int j1,
+                                  int j2, int count, const int64_t *idx_first, const void *dw_first,
+                                  const int64_t *idx_second, const void *dw_second, int dtype, void *d_logits,
+                                  int64_t ldd, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || j1 <= 0 || j2 <= 0 || count <= 0 || first < 0 || second < first + j1 + j2 ||
+        ld < second + j1 + j2 || ldd < second + j1 + j2)
+        return BDM_ERR_INVALID;
+    if (count > 32) return BDM_ERR_UNSUPPORTED;
+    if (!valid_dtype(dtype)) return BDM_ERR_DTYPE;
+    if (ntok == 0) return BDM_OK;
+    if (!logits || !idx_first || !dw_first || !idx_second || !dw_second || !d_logits) return BDM_ERR_INVALID;
+    RouteBwdParams p{};
+    p.logits = logits; p.dlogits = d_logits; p.ntok = ntok; p.ld = ld; p.ldd = ldd; p.first = first;
+    p.second = second; p.j1 = j1; p.j2 = j2; p.count = count; p.idx1 = idx_first; p.idx2 = idx_second;
+    p.dw1 = dw_first; p.dw2 = dw_second;
+    const int64_t blocks = ceil_div(2 * ntok, 8);
+    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        route_backward_kernel<T><<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(p);
+    });
+    return launch_status();
+}
+
+extern "C" int64_t bdm_controllers_backward_partial_floats(int64_t ntok, int heads, int bank_size) {
+    if (ntok < 0 || heads <= 0 || bank_size <= 0) return -1;
+    return (2 * bdm::ceil_div(ntok, bdm::kGateTokens) + 1) * heads * bank_size;
+}
+
+extern "C" int bdm_controllers_backward(const void *proj, int64_t ntok, int64_t ld, int64_t col_q, int64_t col_k,
+                                        int64_t col_v, int64_t col_b, int64_t col_w, const void *f, int64_t ldf,
+                                        const float *a_log, const float *dt_bias, const float *g, const void *b,
+                                        const void *w, const void *dq, const void *dk, const void *dv, const float *dg,
+                                        const void *db, const void *dw, int heads, int bank_size,
+                                        int head_value_width, int qk_norm, int dtype, void *d_proj, int64_t ldd,
+                                        void *df, float *partials, float *d_dt_bias, float *d_a_log, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || heads <= 0 || bank_size <= 0 || head_value_width <= 0) return BDM_ERR_INVALID;
+    if (bank_size > kMaxS) return BDM_ERR_UNSUPPORTED;
+    if (!valid_dtype(dtype)) return BDM_ERR_DTYPE;
+    const int64_t HS = (int64_t)heads * bank_size, V = (int64_t)heads * head_value_width;
+    if (col_q < 0 || col_k < 0 || col_v < 0 || col_b < 0 || col_w < 0 || col_q + HS > ld || col_k + HS > ld ||
+        col_v + V > ld || col_b + HS > ld || col_w + V > ld || ldf < HS || ldd < ld)
+        return BDM_ERR_INVALID;
+    if (!d_dt_bias || !d_a_log) return BDM_ERR_INVALID;
+    const cudaStream_t st = as_stream(stream);
+    if (ntok == 0) {
+        int rc = cuda_status(cudaMemsetAsync(d_dt_bias, 0, sizeof(float) * HS, st));
+        if (rc != BDM_OK) return rc;
+        return cuda_status(cudaMemsetAsync(d_a_log, 0, sizeof(float) * heads, st));
+    }
+    if (!proj || !f || !a_log || !dt_bias || !g || !b || !w || !dq || !dk || !dv || !dg || !db || !dw || !d_proj ||
+        !df || !partials)
+        return BDM_ERR_INVALID;
+    CtlBwdArgs a{};
+    a.proj = proj; a.ntok = ntok; a.ld = ld; a.col_q = col_q; a.col_k = col_k; a.col_v = col_v; a.col_b = col_b;
+    a.col_w = col_w; a.f = f; a.ldf = ldf; a.a_log = a_log; a.dt_bias = dt_bias; a.g = g; a.b = b; a.w = w;
+    a.dq = dq; a.dk = dk; a.dvv = dv; a.db = db; a.dw = dw; a.dg = dg; a.dproj = d_proj; a.ldd = ldd; a.df = df;
+    a.H = heads; a.S = bank_size; a.dv = head_value_width; a.qk_norm = qk_norm;
+    a.chunks = ceil_div(ntok, kGateTokens);
+    a.part_dt = partials;
+    a.part_a = partials + a.chunks * HS;
+    a.narrow_blocks = ceil_div(ntok * heads, kCtlThreads);
+    a.gate_blocks = ceil_div(a.chunks * HS, kCtlThreads);
+    const int64_t wide_blocks = ceil_div(ntok * V, kCtlThreads);
+    if (a.narrow_blocks + a.gate_blocks + wide_blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        controllers_backward_kernel<T><<<(unsigned)(a.narrow_blocks + a.gate_blocks + wide_blocks), kCtlThreads, 0,
+                                         st>>>(a);
+    });
+    int rc = launch_status();
+    if (rc != BDM_OK) return rc;
+    // dt_bias: column sums over the chunks; A_log[h]: the same, then summed over the head's S columns
+    rc = column_sums(a.part_dt, a.chunks, HS, HS, d_dt_bias, st);
+    if (rc != BDM_OK) return rc;
+    float *a_rows = a.part_a + a.chunks * HS;  // [HS] scratch after the two partial tables
+    rc = column_sums(a.part_a, a.chunks, HS, HS, a_rows, st);
+    if (rc != BDM_OK) return rc;
+    segment_sums_kernel<<<(unsigned)ceil_div(heads, 128), 128, 0, st>>>(a_rows, heads, bank_size, d_a_log);
+    return launch_status();
+}
+
+extern "C" int64_t bdm_norm_gate_backward_partial_floats(int64_t ntok, int64_t width) {
+    if (ntok < 0 || width <= 0) return -1;
+    return 2 * bdm::ceil_div(ntok, bdm::kNgTokens) * width;
+}
+
+extern "C" int bdm_norm_gate_backward(const void *d_out, const void *raw, int64_t ntok, int64_t width,
+                                      const void *gate, int64_t ld_gate, const void *norm_weight,
+                                      const void *norm_bias, float eps, int norm_mode, int dtype, void *d_raw,
+                                      void *d_gate, int64_t ld_d_gate, float *partials, float *d_norm_weight,
+                                      float *d_norm_bias, void *stream) {
+    using namespace bdm;
+    if (ntok < 0 || width <= 0 || ld_gate < width || ld_d_gate < width) return BDM_ERR_INVALID;
+    if (norm_mode != 0 && norm_mode != 1) return BDM_ERR_INVALID;
+    if (!valid_dtype(dtype)) return BDM_ERR_DTYPE;
+    if (width > 1024 * kNgCols) return BDM_ERR_UNSUPPORTED;
+    if (!d_norm_weight || (norm_mode == 1 && norm_bias && !d_norm_bias)) return BDM_ERR_INVALID;
+    const cudaStream_t st = as_stream(stream);
+    const bool want_b = norm_bias != nullptr && d_norm_bias != nullptr;
+    if (ntok == 0) {
+        int rc = cuda_status(cudaMemsetAsync(d_norm_weight, 0, sizeof(float) * width, st));
+        if (rc != BDM_OK || !want_b) return rc;
+        return cuda_status(cudaMemsetAsync(d_norm_bias, 0, sizeof(float) * width, st));
+    }
+    if (!d_out || !raw || !gate || !norm_weight || !d_raw || !d_gate || !partials) return BDM_ERR_INVALID;
+    NgBwdArgs a{};
+    a.dout = d_out; a.raw = raw; a.gate = gate; a.nw = norm_weight; a.nb = norm_bias; a.ntok = ntok;
+    a.width = width; a.ld_gate = ld_gate; a.ldd = ld_d_gate; a.eps = eps; a.norm_mode = norm_mode;
+    a.draw = d_raw; a.dgate = d_gate;
+    const int64_t blocks = ceil_div(ntok, kNgTokens);
+    a.part_w = partials;
+    a.part_b = want_b ? partials + blocks * width : nullptr;
+    const int threads = (int)(ceil_div(ceil_div(width, kNgCols), 32) * 32);
+    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    BDM_DISPATCH_DTYPE(dtype, T, {
+        norm_gate_backward_kernel<T><<<(unsigned)blocks, threads, 0, st>>>(a);
+    });
+    int rc = launch_status();
+    if (rc != BDM_OK) return rc;
+    rc = column_sums(a.part_w, blocks, width, width, d_norm_weight, st);
+    if (rc != BDM_OK || !want_b) return rc;
+    return column_sums(a.part_b, blocks, width, width, d_norm_bias, st);
+}

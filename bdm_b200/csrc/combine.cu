@@ -78,7 +78,7 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
                                          int kr, int64_t width, const T *__restrict__ gate, int64_t ld_gate,
                                          const T *__restrict__ nw, const T *__restrict__ nb, float eps, int norm_mode,
                                          int round_each, int vec, T *__restrict__ out,
-                                         const float *__restrict__ combined) {
+                                         const float *__restrict__ combined, T *__restrict__ raw_out) {
     __shared__ int64_t banks[kMaxKR];
     __shared__ int slot_at[kMaxKR];
     __shared__ float red[32];
@@ -121,6 +121,11 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
             for (int i = 0; i < kCols; ++i) x[i] = rnd<T>(x[i]);
         } else {
             load8<T>(reads + t * width + c0, x, nv, vec);
+        }
+        if (raw_out) {  // the combined read sum in the activation dtype (kept for the backward)
+#pragma unroll
+            for (int i = 0; i < kCols; ++i)
+                if (c0 + i < width) raw_out[t * width + c0 + i] = Elem<T>::from_float(x[i]);
         }
     }
     const float inv_w = 1.0f / (float)width;
@@ -230,9 +235,10 @@ int combine_threads(int64_t width, int64_t &threads) {
 }  // namespace
 }  // namespace bdm
 
-extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
-                                     const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
-                                     float eps, int norm_mode, int round_each, int dtype, void *out, void *stream) {
+static int combine_norm_gate_impl(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                  const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
+                                  float eps, int norm_mode, int round_each, int dtype, void *out, void *raw_out,
+                                  void *stream) {
     using namespace bdm;
     if (ntok < 0 || width <= 0 || ld_gate < width) return BDM_ERR_INVALID;
     if (read_idx && (kr <= 0 || kr > kMaxKR)) return BDM_ERR_UNSUPPORTED;
@@ -249,9 +255,25 @@ extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx,
         combine_norm_gate_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
             static_cast<const T *>(reads), read_idx, ntok, read_idx ? kr : 1, width, static_cast<const T *>(gate),
             ld_gate, static_cast<const T *>(norm_weight), static_cast<const T *>(norm_bias), eps, norm_mode,
-            round_each, vec, static_cast<T *>(out), nullptr);
+            round_each, vec, static_cast<T *>(out), nullptr, static_cast<T *>(raw_out));
     });
     return launch_status();
+}
+
+extern "C" int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                     const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
+                                     float eps, int norm_mode, int round_each, int dtype, void *out, void *stream) {
+    return combine_norm_gate_impl(reads, read_idx, ntok, kr, width, gate, ld_gate, norm_weight, norm_bias, eps,
+                                  norm_mode, round_each, dtype, out, nullptr, stream);
+}
+
+extern "C" int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_idx, int64_t ntok, int kr,
+                                          int64_t width, const void *gate, int64_t ld_gate, const void *norm_weight,
+                                          const void *norm_bias, float eps, int norm_mode, int round_each, int dtype,
+                                          void *out, void *raw_out, void *stream) {
+    if (ntok > 0 && !raw_out) return BDM_ERR_INVALID;
+    return combine_norm_gate_impl(reads, read_idx, ntok, kr, width, gate, ld_gate, norm_weight, norm_bias, eps,
+                                  norm_mode, round_each, dtype, out, raw_out, stream);
 }
 
 extern "C" int bdm_combine_partial(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
@@ -292,7 +314,7 @@ extern "C" int bdm_norm_gate_f32(const float *combined, int64_t ntok, int64_t wi
         combine_norm_gate_kernel<T><<<(unsigned)ntok, (unsigned)threads, 0, as_stream(stream)>>>(
             nullptr, nullptr, ntok, 1, width, static_cast<const T *>(gate), ld_gate,
             static_cast<const T *>(norm_weight), static_cast<const T *>(norm_bias), eps, norm_mode, 0, vec,
-            static_cast<T *>(out), combined);
+            static_cast<T *>(out), combined, nullptr);
     });
     return launch_status();
 }

@@ -14,8 +14,13 @@ Per forward: ONE projection GEMM (all controllers, both routers and the output
 gate, biases in its epilogue) and the small f_proj.1 GEMM, then the CUDA kernels
 of ``ops`` -- controller epilogue, router, dispatch, bank recurrence, combine +
 norm + gate -- and the o_proj GEMM.  There is no backend switch and no CPU path; CPU inputs raise.
-The backward pass is not implemented: forward / prefill / step run without
-autograd, and a forward that would need gradients raises.
+
+Training: when autograd needs gradients, ``forward`` runs the same kernels inside
+``_BankTraining`` (a torch.autograd.Function from the fused projection's output to
+the o_proj input) whose backward runs the CUDA backward kernels of ``ops``
+(role_bank_kernel.py:76-150, routed_update.py:31-49, role_bank_dispatch.py:76-132,
+product_routed_update.py:51-76); the GEMMs around it (fused projection, f_proj.1,
+o_proj) differentiate through cuBLAS via autograd.
 """
 from __future__ import annotations
 
@@ -128,8 +133,10 @@ class BankedDeltaMemory(nn.Module):
             self.output_norm_bias = nn.Parameter(torch.zeros(config.value_width))
         self.o_proj = nn.Linear(config.value_width, config.dim, bias=config.output_bias)
         self._fused_cache = None
-        # Optional list; when set, (start, end) CUDA events bracket every bank-recurrence launch.
+        # Optional lists; when set, (start, end) CUDA events bracket every bank-recurrence launch
+        # (forward) and every recurrence-backward launch.
         self.scan_events = None
+        self.backward_events = None
         self.init_weights(initialization_seed=self.initialization_seed)
 
     # ---------------------------------------------------------- initialisation
@@ -244,6 +251,20 @@ class BankedDeltaMemory(nn.Module):
         weight, bias, cols = self._fused_projection()
         return torch.addmm(bias, hidden2d, weight.t()), cols
 
+    def _fused_projection_autograd(self):
+        """``_fused_projection`` built from the live parameters (autograd records the concatenation)."""
+        _, _, cols = self._fused_projection()
+        router = self.shared_router
+        rw = router.base.weight + router.read_residual.weight
+        rb = router.base.bias + router.read_residual.bias
+        ww = router.base.weight + router.write_residual.weight
+        wb = router.base.bias + router.write_residual.bias
+        weight = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.f_proj[0].weight,
+                            self.b_proj.weight, self.w_proj.weight, rw, ww, self.output_gate.weight], 0)
+        zeros = torch.zeros(cols['read'], dtype=weight.dtype, device=weight.device)
+        bias = torch.cat([zeros, rb, wb, self.output_gate.bias], 0)
+        return weight, bias, cols
+
     # ------------------------------------------------------------------ steps
     def _check_hidden(self, hidden):
         if hidden.ndim != 3 or hidden.shape[-1] != self.hidden_size or hidden.shape[1] == 0:
@@ -298,11 +319,13 @@ class BankedDeltaMemory(nn.Module):
         return reads
 
     def forward(self, hidden):
-        """Full-sequence forward (model.py:88-140): training-state BF16 storage policy, FP32 combine."""
+        """Full-sequence forward (model.py:88-140): training-state BF16 storage policy, FP32 combine.
+
+        Differentiable when autograd is on and the input or a parameter requires a gradient.
+        """
         self._check_hidden(hidden)
         if torch.is_grad_enabled() and (hidden.requires_grad or any(p.requires_grad for p in self.parameters())):
-            raise NotImplementedError('bdm_b200 implements the forward pass only; call it under torch.no_grad() '
-                                      'or torch.inference_mode()')
+            return self._forward_train(hidden)
         batch, time, _ = hidden.shape
         controls, routes, gate = self._controls_and_routes(hidden)
         interval = state_interval(self.bank_size) if self.config.training_state_dtype == 'bfloat16' else 0
@@ -310,6 +333,17 @@ class BankedDeltaMemory(nn.Module):
                                 col_factor=self.initial_column_factor, state_interval=interval)
         ri = routes[3].reshape(batch * time, -1)
         return self._output(hidden, reads, ri, gate, round_each=False)
+
+    def _forward_train(self, hidden):
+        batch, time, _ = hidden.shape
+        if self.bank_size not in (4, 8, 16):
+            raise NotImplementedError('the training backward supports bank_size 4, 8 or 16')
+        weight, bias, cols = self._fused_projection_autograd()
+        proj = torch.addmm(bias, hidden.reshape(batch * time, self.hidden_size), weight.t())
+        normed = _BankTraining.apply(proj, self.f_proj[1].weight, self.A_log, self.dt_bias, self.initial_row_factor,
+                                     self.initial_column_factor, self.output_norm_weight,
+                                     getattr(self, 'output_norm_bias', None), self, cols, batch, time)
+        return F.linear(normed, self.o_proj.weight, self.o_proj.bias).reshape(batch, time, self.hidden_size)
 
     # ---------------------------------------------------- stateful inference
     def _state_shape(self, batch):
@@ -413,6 +447,91 @@ class BankedDeltaMemory(nn.Module):
 
         run.graph = graph  # keep the graph (and its memory pool) alive with the callable
         return run
+
+
+class _BankTraining(torch.autograd.Function):
+    """Differentiable bank path: fused projection output ``proj`` [NT, ld] -> o_proj input [NT, V].
+
+    Forward: f_proj.1 (cuBLAS), controller epilogue, both routers, dispatch, the
+    factor-initialised recurrence under the training storage policy, and the combine
+    with norm and gate (which also keeps the combined read sum for the backward).
+    Backward (the reference's RoutedUpdate / ProductRoutedUpdate backward plus the
+    autograd of the ops around it): norm and gate, recurrence, event VJP, router,
+    controllers, f_proj.1 and the product-key factors; every column block of
+    d proj is written by exactly one of them.
+    """
+
+    @staticmethod
+    def forward(ctx, proj, wf2, a_log, dt_bias, row_factor, col_factor, norm_w, norm_b, layer, cols, batch, time):
+        m = layer
+        H, S, dv, V, J = m.num_heads, m.bank_size, m.head_value_width, m.value_width, m.bank_count
+        f1 = proj[:, cols['f']:cols['f'] + dv]
+        f = torch.mm(f1, wf2.t())
+        q, k, v, g, b, w = ops.controllers(proj, cols, f, a_log, dt_bias, heads=H, bank_size=S, head_value_width=dv,
+                                           qk_norm=m.config.qk_normalization)
+        (rw, ri), (ww, wi) = ops.route_pair(proj, cols['read'], cols['write'], bank_count=J,
+                                            selected_banks=m.num_reads, factors=m.factors)
+        shape = (batch, time, -1)
+        meta = ops.dispatch(wi.reshape(shape), ri.reshape(shape), J)
+        interval = state_interval(S) if m.config.training_state_dtype == 'bfloat16' else 0
+        reads = ops.bank_scan(q, k, v, g, b, w, wi.reshape(shape), ww.reshape(shape), ri.reshape(shape),
+                              rw.reshape(shape), meta['order'], meta['cu_seqlens'], batch=batch, time=time,
+                              bank_count=J, heads=H, bank_size=S, head_value_width=dv,
+                              routed_decay=m.config.routed_decay, scale=S ** -0.5, row_factor=row_factor,
+                              col_factor=col_factor, state_interval=interval)
+        gate = proj[:, cols['gate']:cols['gate'] + V]
+        layer_norm = m.config.output_normalization == 'layer'
+        normed, raw = ops.combine_norm_gate(reads, ri, gate, norm_w, norm_b if layer_norm else None, eps=m.norm_eps,
+                                            layer_norm=layer_norm, round_each=False, save_raw=True)
+        del reads
+        ctx.save_for_backward(proj, f, wf2, a_log, dt_bias, row_factor, col_factor, norm_w, norm_b, q, k, v, g, b, w,
+                              ww, wi, rw, ri, meta['order'], meta['cu_seqlens'], raw)
+        ctx.layer, ctx.cols, ctx.batch, ctx.time, ctx.interval = m, cols, batch, time, interval
+        return normed
+
+    @staticmethod
+    def backward(ctx, d_normed):
+        (proj, f, wf2, a_log, dt_bias, row_factor, col_factor, norm_w, norm_b, q, k, v, g, b, w, ww, wi, rw, ri,
+         order, cu, raw) = ctx.saved_tensors
+        m, cols, batch, time = ctx.layer, ctx.cols, ctx.batch, ctx.time
+        H, S, dv, V, J = m.num_heads, m.bank_size, m.head_value_width, m.value_width, m.bank_count
+        layer_norm = m.config.output_normalization == 'layer'
+        d_proj = torch.empty_like(proj)
+        d_raw, d_nw, d_nb = ops.norm_gate_backward(d_normed, raw, proj[:, cols['gate']:cols['gate'] + V], norm_w,
+                                                   norm_b if layer_norm else None, eps=m.norm_eps,
+                                                   layer_norm=layer_norm,
+                                                   d_gate=d_proj[:, cols['gate']:cols['gate'] + V])
+        kw, kr = ww.shape[-1], rw.shape[-1]
+        timing = m.backward_events is not None
+        if timing:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+        evg, du, dinit = ops.scan_backward(q, k, v, g, b, w, ww, rw, order, cu, d_raw, batch=batch, time=time,
+                                           bank_count=J, heads=H, bank_size=S, head_value_width=dv, kw=kw, kr=kr,
+                                           routed_decay=m.config.routed_decay, scale=S ** -0.5,
+                                           row_factor=row_factor, col_factor=col_factor,
+                                           state_interval=ctx.interval)
+        if timing:
+            end.record()
+            m.backward_events.append((start, end))
+        dq, dk, dvv, dg, db, dw, dww, drw = ops.event_vjp(q, k, v, g, b, w, ww, rw, evg, du, heads=H, bank_size=S,
+                                                          head_value_width=dv, routed_decay=m.config.routed_decay,
+                                                          scale=S ** -0.5)
+        del evg, du
+        ops.route_backward(proj, cols['read'], cols['write'], ri, drw, wi, dww, d_proj, bank_count=J,
+                           factors=m.factors)
+        df, d_a, d_dt = ops.controllers_backward(proj, cols, f, a_log, dt_bias, g, b, w, dq, dk, dvv, dg, db, dw,
+                                                 d_proj, heads=H, bank_size=S, head_value_width=dv,
+                                                 qk_norm=m.config.qk_normalization)
+        f1 = proj[:, cols['f']:cols['f'] + dv]
+        d_proj[:, cols['f']:cols['f'] + dv] = torch.mm(df, wf2)
+        d_wf2 = torch.mm(df.t(), f1)
+        d_u, d_z = ops.product_state_backward(dinit, batch=batch, rows_p=row_factor.shape[0],
+                                              cols_q=col_factor.shape[0], factor_dtype=row_factor.dtype)
+        d_nb_out = d_nb.to(norm_b.dtype) if (norm_b is not None and d_nb is not None) else (
+            torch.zeros_like(norm_b) if norm_b is not None else None)
+        return (d_proj, d_wf2, d_a.to(a_log.dtype), d_dt.to(dt_bias.dtype), d_u.to(row_factor.dtype),
+                d_z.to(col_factor.dtype), d_nw.to(norm_w.dtype), d_nb_out, None, None, None, None)
 
 
 BlockSparseDeltaMemory = BankedDeltaMemory

@@ -14,6 +14,13 @@ Reference interfaces each op replaces (p0rc314in/bdm, implementation/bdm/):
   decode_step      inference.py:161-194
 Bank-sharded forward (no reference counterpart; the reference runs on one device):
   bank_histogram, bank_owners, dispatch_owned, combine_partial, norm_gate_f32
+Training backward:
+  norm_gate_backward     autograd of _project_bank_output (_parameters.py:222-232)
+  scan_backward          role_bank_kernel.py:76-150 (checkpoint replay + reverse chain)
+  event_vjp              role_bank_dispatch.py:76-132 + routed_update.py:43-47
+  product_state_backward product_routed_update.py:72-75
+  route_backward         autograd of product_key_route (gdn2_banks.py:74-114)
+  controllers_backward   autograd of _controllers (_parameters.py:189-220, heads.py:11-22)
 """
 from __future__ import annotations
 
@@ -246,11 +253,13 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
 
 
 def combine_norm_gate(reads, read_idx, gate, norm_weight, norm_bias, *, eps: float, layer_norm: bool,
-                      round_each: bool):
+                      round_each: bool, save_raw: bool = False):
     """Ascending-bank read combine, LayerNorm/RMS and sigmoid gate -> [NT, V].
 
     ``reads`` [NT, KR, V] with ``read_idx`` [NT, KR], or an already combined
     [NT, V] with ``read_idx=None``; ``gate`` [NT, >=V] (row stride honoured).
+    With ``save_raw`` returns (out, raw): raw is the combined read sum [NT, V]
+    in the activation dtype (what the output backward consumes).
     """
     _cuda(reads, gate, norm_weight)
     dt = reads.dtype
@@ -263,9 +272,17 @@ def combine_norm_gate(reads, read_idx, gate, norm_weight, norm_bias, *, eps: flo
     nb = norm_bias.detach().to(dt).contiguous() if norm_bias is not None else None
     rd = reads.contiguous()
     ri = read_idx.contiguous() if read_idx is not None else None
+    ld_gate = gate.stride(0) if nt > 1 else gate.shape[-1]
+    if save_raw:
+        raw = torch.empty((nt, width), dtype=dt, device=reads.device)
+        _lib.check(_lib.load().bdm_combine_norm_gate_save(
+            _ptr(rd), _ptr(ri), nt, kr, width, _ptr(gate), ld_gate, _ptr(nw), _ptr(nb), float(eps),
+            1 if layer_norm else 0, int(round_each), dtype_code(dt), _ptr(out), _ptr(raw), _stream(reads.device)),
+            'bdm_combine_norm_gate_save')
+        return out, raw
     _lib.check(_lib.load().bdm_combine_norm_gate(
         _ptr(rd), _ptr(ri), nt, kr, width,
-        _ptr(gate), gate.stride(0) if nt > 1 else gate.shape[-1], _ptr(nw), _ptr(nb), float(eps),
+        _ptr(gate), ld_gate, _ptr(nw), _ptr(nb), float(eps),
         1 if layer_norm else 0, int(round_each), dtype_code(dt), _ptr(out), _stream(reads.device)),
         'bdm_combine_norm_gate')
     return out
@@ -416,3 +433,151 @@ def norm_gate_f32(combined: torch.Tensor, gate, norm_weight, norm_bias, *, eps: 
         float(eps), 1 if layer_norm else 0, dtype_code(dtype), _ptr(out), _stream(combined.device)),
         'bdm_norm_gate_f32')
     return out
+
+
+# -------------------------------------------------------- training backward
+
+def norm_gate_backward(d_out, raw, gate, norm_weight, norm_bias, *, eps: float, layer_norm: bool,
+                       d_gate: torch.Tensor):
+    """Backward of ``combine_norm_gate``'s norm and gate over the saved combined sum ``raw`` [NT, V].
+
+    Writes the gate pre-activation gradient into ``d_gate`` ([NT, >=V] view, row stride
+    honoured) and returns (d_raw [NT, V] in the activation dtype, d_norm_weight,
+    d_norm_bias or None) with the parameter gradients in FP32.
+    """
+    _cuda(d_out, raw, gate, norm_weight, d_gate)
+    nt, width = raw.shape
+    dt = raw.dtype
+    if gate.stride(-1) != 1 or d_gate.stride(-1) != 1:
+        raise ValueError('gate rows must be contiguous')
+    dout = d_out.reshape(nt, width).to(dt).contiguous()
+    nw = norm_weight.detach().to(dt).contiguous()
+    nb = norm_bias.detach().to(dt).contiguous() if (norm_bias is not None and layer_norm) else None
+    dev = raw.device
+    d_raw = torch.empty((nt, width), dtype=dt, device=dev)
+    lib = _lib.load()
+    part = torch.empty(max(lib.bdm_norm_gate_backward_partial_floats(nt, width), 1), dtype=torch.float32, device=dev)
+    dw = torch.empty(width, dtype=torch.float32, device=dev)
+    db = torch.empty(width, dtype=torch.float32, device=dev) if nb is not None else None
+    ld_gate = gate.stride(0) if nt > 1 else gate.shape[-1]
+    ldd = d_gate.stride(0) if nt > 1 else d_gate.shape[-1]
+    lib_check = _lib.check
+    lib_check(lib.bdm_norm_gate_backward(_ptr(dout), _ptr(raw), nt, width, _ptr(gate), ld_gate, _ptr(nw), _ptr(nb),
+                                         float(eps), 1 if layer_norm else 0, dtype_code(dt), _ptr(d_raw),
+                                         _ptr(d_gate), ldd, _ptr(part), _ptr(dw), _ptr(db), _stream(dev)),
+              'bdm_norm_gate_backward')
+    return d_raw, dw, db
+
+
+def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, *, batch: int, time: int,
+                  bank_count: int, heads: int, bank_size: int, head_value_width: int, kw: int, kr: int,
+                  routed_decay: bool, scale: float, row_factor=None, col_factor=None, state_interval=0):
+    """Recurrence backward over the dispatched events of a factor-initialised training forward.
+
+    ``d_read`` [NT, H*dv] is the gradient of the combined read sum.  Returns
+    (event_grads [ceil(dv/32), E, 3S], d_write_value [NT*KW, H*dv], d_initial [B*J, H, S, dv]), FP32.
+    """
+    _cuda(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read)
+    dt, dev = q.dtype, q.device
+    nt = batch * time
+    e = nt * (kw + kr)
+    tiles = -(-head_value_width // 32)
+    v_width = heads * head_value_width
+    lib = _lib.load()
+    ck_bytes = lib.bdm_scan_backward_checkpoint_bytes(batch, time, kw, kr, bank_count, heads, bank_size,
+                                                      head_value_width)
+    if ck_bytes < 0:
+        raise NotImplementedError('scan backward supports bank_size 4, 8 or 16')
+    ck = torch.empty(max(ck_bytes // 4, 1), dtype=torch.float32, device=dev)
+    evg = torch.empty((tiles, e, 3 * bank_size), dtype=torch.float32, device=dev)
+    du = torch.empty((nt * kw, v_width), dtype=torch.float32, device=dev)
+    dinit = torch.empty((batch * bank_count, heads, bank_size, head_value_width), dtype=torch.float32, device=dev)
+    u = z = None
+    if row_factor is not None:
+        u, z = row_factor.detach().contiguous(), col_factor.detach().contiguous()
+    dr = d_read.reshape(nt, v_width).to(dt).contiguous()
+    ww, rw = write_w.contiguous(), read_w.contiguous()
+    _lib.check(lib.bdm_scan_backward(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(ww), _ptr(rw), _ptr(order), _ptr(cu_seqlens),
+        batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt), int(routed_decay),
+        float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
+        dtype_code(u.dtype) if u is not None else 0, int(state_interval), _ptr(dr), _ptr(evg), _ptr(du),
+        _ptr(dinit), _ptr(ck), ck_bytes, _stream(dev)), 'bdm_scan_backward')
+    return evg, du, dinit
+
+
+def event_vjp(q, k, v, g, b, w, write_w, read_w, event_grads, d_write_value, *, heads: int, bank_size: int,
+              head_value_width: int, routed_decay: bool, scale: float):
+    """Token gradients from the event gradients: (dq, dk, dv, dg, db, dw, d_write_w, d_read_w)."""
+    _cuda(q, event_grads, d_write_value)
+    dt, dev = q.dtype, q.device
+    nt = q.shape[0]
+    kw, kr = write_w.shape[-1], read_w.shape[-1]
+    ww, rw = write_w.reshape(nt, kw).contiguous(), read_w.reshape(nt, kr).contiguous()
+    dq, dk, db = (torch.empty_like(q) for _ in range(3))
+    dg = torch.empty_like(g)
+    dv, dw = torch.empty_like(v), torch.empty_like(w)
+    dww, drw = torch.empty_like(ww), torch.empty_like(rw)
+    _lib.check(_lib.load().bdm_event_vjp(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(ww), _ptr(rw), _ptr(event_grads),
+        _ptr(d_write_value), nt, heads, bank_size, head_value_width, kw, kr, dtype_code(dt), int(routed_decay),
+        float(scale), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dg), _ptr(db), _ptr(dw), _ptr(dww), _ptr(drw),
+        _stream(dev)), 'bdm_event_vjp')
+    return dq, dk, dv, dg, db, dw, dww, drw
+
+
+def product_state_backward(d_initial, *, batch: int, rows_p: int, cols_q: int, factor_dtype: torch.dtype):
+    """Factor gradients (FP32 holding factor-dtype values) from d_initial [B*J, H, S, dv]."""
+    _cuda(d_initial)
+    dv = d_initial.shape[-1]
+    dev = d_initial.device
+    rows = torch.empty((rows_p * cols_q, dv), dtype=torch.float32, device=dev)
+    du = torch.empty((rows_p, dv), dtype=torch.float32, device=dev)
+    dz = torch.empty((cols_q, dv), dtype=torch.float32, device=dev)
+    _lib.check(_lib.load().bdm_product_state_backward(_ptr(d_initial.contiguous()), batch, rows_p, cols_q, dv,
+                                                      dtype_code(factor_dtype), _ptr(rows), _ptr(du), _ptr(dz),
+                                                      _stream(dev)), 'bdm_product_state_backward')
+    return du, dz
+
+
+def route_backward(proj, first: int, second: int, idx_first, dw_first, idx_second, dw_second, d_proj, *,
+                   bank_count: int, factors=None):
+    """Both routers' logit gradients into ``d_proj`` (blocks at columns ``first`` and ``second``)."""
+    _cuda(proj, idx_first, dw_first, idx_second, dw_second, d_proj)
+    j1, j2 = factors or near_square_factors(bank_count)
+    nt = proj.shape[0]
+    count = idx_first.shape[-1]
+    i1, i2 = idx_first.reshape(nt, count).contiguous(), idx_second.reshape(nt, count).contiguous()
+    w1, w2 = (t.reshape(nt, count).to(proj.dtype).contiguous() for t in (dw_first, dw_second))
+    ld = proj.stride(0) if nt > 1 else proj.shape[1]
+    ldd = d_proj.stride(0) if nt > 1 else d_proj.shape[1]
+    _lib.check(_lib.load().bdm_route_backward(_ptr(proj), nt, ld, first, second, j1, j2, count, _ptr(i1), _ptr(w1),
+                                              _ptr(i2), _ptr(w2), dtype_code(proj.dtype), _ptr(d_proj), ldd,
+                                              _stream(proj.device)), 'bdm_route_backward')
+
+
+def controllers_backward(proj, cols: dict, f, a_log, dt_bias, g, b, w, dq, dk, dv, dg, db, dw, d_proj, *,
+                         heads: int, bank_size: int, head_value_width: int, qk_norm: str):
+    """Controller-epilogue backward: writes the q, k, v, b, w blocks of ``d_proj``; returns
+    (df [NT, H*S] in the activation dtype, d_a_log [H] FP32, d_dt_bias [H*S] FP32)."""
+    _cuda(proj, f, d_proj)
+    nt = proj.shape[0]
+    dt, dev = proj.dtype, proj.device
+    hs = heads * bank_size
+    df = torch.empty((nt, hs), dtype=dt, device=dev)
+    lib = _lib.load()
+    part = torch.empty(max(lib.bdm_controllers_backward_partial_floats(nt, heads, bank_size), 1),
+                       dtype=torch.float32, device=dev)
+    d_dt = torch.empty(hs, dtype=torch.float32, device=dev)
+    d_a = torch.empty(heads, dtype=torch.float32, device=dev)
+    al = a_log.detach().float().contiguous()
+    dtb = dt_bias.detach().float().contiguous()
+    ld = proj.stride(0) if nt > 1 else proj.shape[1]
+    ldd = d_proj.stride(0) if nt > 1 else d_proj.shape[1]
+    ldf = f.stride(0) if nt > 1 else f.shape[1]
+    _lib.check(lib.bdm_controllers_backward(
+        _ptr(proj), nt, ld, cols['q'], cols['k'], cols['v'], cols['b'], cols['w'], _ptr(f), ldf, _ptr(al), _ptr(dtb),
+        _ptr(g), _ptr(b), _ptr(w), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dg), _ptr(db), _ptr(dw), heads, bank_size,
+        head_value_width, 1 if qk_norm == 'nvidia' else 0, dtype_code(dt), _ptr(d_proj), ldd, _ptr(df), _ptr(part),
+        _ptr(d_dt), _ptr(d_a), _stream(dev)), 'bdm_controllers_backward')
+    return df, d_a, d_dt

@@ -1,4 +1,4 @@
-"""Benchmark: BDM layer prefill tokens/s on B200 (BASELINE config c2), plus c3 decode and c4.
+"""Benchmark: BDM layer prefill tokens/s on B200 (BASELINE config c2), plus c3 decode, c4 and training.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -10,6 +10,8 @@ The line also carries ``c4``: the large-memory prefill (batch 16 x 8192,
 J = 16384 banks, Zipf(1.1) router skew) on all N GPUs at once -- the plain
 layer at N = 1, the bank-sharded forward (bdm_b200.sharded, NCCL all-gather /
 reduce-scatter) at N > 1.  Its total work is fixed, so it scales strongly.
+``train``: one layer's forward + backward at the c5 layer geometry (batch 32 x
+2048 split over the ranks, gradients all-reduced over NCCL at N > 1).
 
 Timed region (value): K forward steps of the public module call
 ``layer(hidden)`` with the input already in HBM; an L2 flush (256 MiB write)
@@ -46,6 +48,10 @@ C3 = dict(dim=1024, bank_count=2048, bank_size=8, selected_banks=8, value_width=
 C3_BATCH, C3_PREFIX, C3_STEPS = 64, 2048, 1024
 C4 = dict(dim=2048, bank_count=16384, bank_size=16, selected_banks=16, value_width=2048, num_heads=16)
 C4_BATCH, C4_TIME, C4_ZIPF = 16, 8192, 1.1
+C5 = dict(dim=768, bank_count=512, bank_size=8, selected_banks=8, value_width=768, num_heads=12)
+C5_BATCH, C5_TIME = 32, 2048
+C5_METRIC = ('BDM layer training step (forward + backward) tokens/sec, c5 layer geometry (batch 32 x seq 2048, '
+             'd_model 768, H=12, J=512, S=8, B=8, d_v=64)')
 C4_METRIC = ('BDM layer prefill tokens/sec, bank-sharded large memory (c4: batch 16 x seq 8192, d_model 2048, '
              'H=16, J=16384, S=16, B=16, d_v=128, Zipf(1.1) bank popularity)')
 METRIC = 'BDM layer prefill tokens/sec (c2: batch 8 x seq 4096, d_model 1024, H=8, J=256, S=8, B=8, d_v=128)'
@@ -360,6 +366,11 @@ def run_ours(args, world, rank, local):
             line['c4'] = run_c4(dev, rank, world, args)
         except Exception as e:  # keep the headline line even if the extra workload fails
             line['c4'] = {'error': repr(e)[:300]}
+    if not args.skip_train:
+        try:
+            line['train'] = run_train(dev, rank, world, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['train'] = {'error': repr(e)[:300]}
     if rank == 0 and world == 1 and not args.skip_cpu:
         tps, dt, threads = cpu_forward_sample(C2_BATCH, args.cpu_time)
         line['cpu_baseline'] = {'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
@@ -414,6 +425,92 @@ def run_decode(dev, rank, world, args):
             'eager_step_ms': eager_ms, 'state_bytes': state.numel() * state.element_size(),
             'roofline': {'bound': 'hbm', 'bytes_per_token': bpt, 'achieved': bpt * tps / world / 1e9,
                          'peak': hbm_peak, 'unit': 'GB/s', 'frac': bpt * tps / world / 1e9 / hbm_peak}}
+
+
+def c5_gemm_flops(tokens, cfg=C5):
+    """Dense GEMM FLOPs of one layer training step: fused input projection, f_proj.1 and o_proj,
+    forward (1x) plus backward (2x: input and weight gradients)."""
+    H, S, V, D = cfg['num_heads'], cfg['bank_size'], cfg['value_width'], cfg['dim']
+    dv = V // H
+    j = cfg['bank_count']
+    first = 1
+    while first * first <= j:
+        first += 1
+    first -= 1
+    while j % first:
+        first -= 1
+    route = first + j // first
+    width = 3 * H * S + 2 * V + dv + 2 * route + V  # q k b | v w | f1 | read write | gate
+    per_token = 2 * D * width + 2 * dv * H * S + 2 * V * D
+    return 3 * per_token * tokens
+
+
+def run_train(dev, rank, world, args):
+    """c5 layer geometry: forward + backward of one BDM layer (BF16), the global batch split over the
+    ranks; at N > 1 the layer's parameter gradients are all-reduced over NCCL (data parallel)."""
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, _lib
+    if C5_BATCH % world:
+        return {'skipped': f'batch {C5_BATCH} does not split over {world} ranks'}
+    lib = _lib.load()
+    cfg = BSDMConfig(**C5)
+    layer = BlockSparseDeltaMemory(cfg, seed=4).to(torch.bfloat16).to(dev)
+    rows = C5_BATCH // world
+    gen = torch.Generator(device=dev).manual_seed(4000 + rank)
+    x = torch.randn(rows, C5_TIME, cfg.dim, generator=gen, device=dev).to(torch.bfloat16)
+    dy = torch.randn(rows, C5_TIME, cfg.dim, generator=gen, device=dev).to(torch.bfloat16)
+    params = [p for p in layer.parameters()]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    steps = args.train_steps
+
+    def step():
+        for p in params:
+            p.grad = None
+        y = layer(x)
+        y.backward(dy)
+        if world > 1:
+            flat = torch.cat([p.grad.reshape(-1).float() for p in params])
+            torch.distributed.all_reduce(flat)
+
+    clocks = ClockSampler(dev.index).start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    layer.backward_events = []
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = lib.bdm_kernel_launches()
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    clocks.stop()
+    launches = lib.bdm_kernel_launches() - launches0
+    barrier(world)
+    scan_bwd_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in layer.backward_events), world)
+    layer.backward_events = None
+    ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)), world) / steps
+    tokens = C5_BATCH * C5_TIME
+    _, bf16_peak, peak_kind = load_peaks()
+    gemm_ms = c5_gemm_flops(tokens // world) / (bf16_peak * 1e12) * 1000
+    return {'metric': C5_METRIC, 'value': tokens / (ms / 1000), 'unit': 'tokens/s', 'n_gpus': world,
+            'steps': steps, 'warmup': args.warmup, 'ms_per_step': ms, 'scaling': 'strong',
+            'dtype': 'bf16', 'path': 'BlockSparseDeltaMemory.forward + autograd backward (bdm_b200 CUDA kernels)'
+                                     + (', NCCL all-reduce of the parameter gradients' if world > 1 else ''),
+            'config': {'workload': 'c5 layer: BSDMConfig(dim=768, bank_count=512, bank_size=8, selected_banks=8, '
+                                   'value_width=768, num_heads=12), seed 4, random-init; one layer, no LM shell',
+                       'global_batch': C5_BATCH, 'seq_len': C5_TIME, 'rows_per_rank': rows,
+                       'l2': 'inputs larger than L2; 256 MiB flush between steps'},
+            'gpu_launches': int(launches),
+            'scan_backward_ms': scan_bwd_ms,
+            'roofline': {'bound': 'tensor', 'what': 'the step\'s dense GEMMs (projection, f_proj.1, o_proj; fwd+bwd) '
+                                                   'at the measured bf16 peak: a lower bound on the step',
+                         'gemm_floor_ms': gemm_ms, 'peak': bf16_peak, 'unit': 'TFLOP/s', 'peak_source': peak_kind,
+                         'frac': gemm_ms / ms},
+            'clocks': clocks.summary()}
 
 
 def c4_hidden(rows, dev):
@@ -507,6 +604,8 @@ def main():
     ap.add_argument('--skip-c4', action='store_true')
     ap.add_argument('--c4-steps', type=int, default=5)
     ap.add_argument('--c4-ownership', choices=('balanced', 'contiguous'), default='balanced')
+    ap.add_argument('--skip-train', action='store_true')
+    ap.add_argument('--train-steps', type=int, default=3)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3

@@ -207,6 +207,90 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
 BDM_API int bdm_combine_norm_gate(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
                           const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
                           float eps, int norm_mode, int round_each, int dtype, void *out, void *stream);
+/* bdm_combine_norm_gate that also stores the combined read sum raw_out [ntok, width]
+ * (dtype): the tensor the reference's readout returns (routed_update.py:28-29) and
+ * its output backward consumes. */
+BDM_API int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                       const void *gate, int64_t ld_gate, const void *norm_weight,
+                                       const void *norm_bias, float eps, int norm_mode, int round_each, int dtype,
+                                       void *out, void *raw_out, void *stream);
+
+/*
+ * Training backward.  Replaces the backward passes of RoutedUpdate /
+ * RoleBankTraining / ProductRoutedUpdate (routed_update.py:31-49,
+ * role_bank_kernel.py:76-150,204-215, product_routed_update.py:44-76) and, for the
+ * ops around them, the autograd of product_key_route (gdn2_banks.py:74-114),
+ * _controllers (_parameters.py:189-220, heads.py:11-22) and _project_bank_output
+ * (_parameters.py:222-232).  All gradients accumulate in FP32; tensors the
+ * reference keeps in the parameter dtype are rounded to it at the same points.
+ *
+ * bdm_norm_gate_backward: d_out [ntok, width] (gradient of the o_proj input),
+ *   raw [ntok, width] (from bdm_combine_norm_gate_save), gate [ntok, ld_gate]
+ *   pre-activations -> d_raw [ntok, width], d_gate [ntok, ld_d_gate] (dtype) and
+ *   the FP32 parameter gradients d_norm_weight [width], d_norm_bias [width]
+ *   (LayerNorm with a bias only; may be NULL otherwise).  `partials` holds
+ *   bdm_norm_gate_backward_partial_floats(ntok, width) floats.
+ * bdm_scan_backward: the recurrence backward over the dispatched events (same
+ *   inputs as bdm_bank_scan's factor-initialised training call, plus d_read
+ *   [ntok, H*dv] = gradient of the combined read sum).  Outputs, FP32:
+ *   event_grads [ceil(dv/32), E, 3*S] per-event column sums (per write event id:
+ *   sum_x dh*u | sum_x hd*du | sum_x dh'*hd; per read event id: sum_x h*do),
+ *   d_write_value [ntok*kw, H*dv] (du per write event id) and d_initial
+ *   [batch*J, H, S, dv].  checkpoints: bdm_scan_backward_checkpoint_bytes() bytes
+ *   of scratch (states replayed at block starts).  S in {4, 8, 16}.
+ * bdm_event_vjp: per-token gather of the event gradients (role_bank_dispatch.py:
+ *   76-132 plus the routed-decay dp term of routed_update.py:43-47): dq, dk, db
+ *   [ntok, H*S], dv, dw [ntok, H*dv] (dtype), dg [ntok, H*S] (float), and the route
+ *   weight gradients d_write_w [ntok, kw], d_read_w [ntok, kr] (dtype; per head,
+ *   summed over heads).  H <= 32, dv <= 256, kw, kr <= 64.
+ * bdm_product_state_backward: d_initial [batch, P*Q, dv] -> d_rows [P*Q, dv]
+ *   (per logical row, batch-summed) and the factor gradients d_row_factor [P, dv],
+ *   d_col_factor [Q, dv] (FP32 holding factor-dtype values).
+ * bdm_route_backward: both routers' backward over one projection [ntok, ld]:
+ *   blocks at columns first and second (J1+J2 logits each), selections idx_* [ntok,
+ *   count] and weight gradients dw_* [ntok, count] (dtype) -> d_logits blocks of
+ *   [ntok, ldd] (every logit of both blocks written).  count <= 32.
+ * bdm_controllers_backward: q, k, v, b, w column blocks of d_proj [ntok, ldd]
+ *   (dtype), df [ntok, H*S] (dtype; gradient of f_proj's output) and the FP32
+ *   d_dt_bias [H*S], d_a_log [H], from the forward's proj, f, g, b, w and the
+ *   control gradients.  `partials` holds
+ *   bdm_controllers_backward_partial_floats(ntok, H, S) floats.
+ */
+BDM_API int64_t bdm_norm_gate_backward_partial_floats(int64_t ntok, int64_t width);
+BDM_API int bdm_norm_gate_backward(const void *d_out, const void *raw, int64_t ntok, int64_t width, const void *gate,
+                                   int64_t ld_gate, const void *norm_weight, const void *norm_bias, float eps,
+                                   int norm_mode, int dtype, void *d_raw, void *d_gate, int64_t ld_d_gate,
+                                   float *partials, float *d_norm_weight, float *d_norm_bias, void *stream);
+BDM_API int64_t bdm_scan_backward_checkpoint_bytes(int64_t batch, int64_t time, int kw, int kr, int64_t bank_count,
+                                                   int heads, int bank_size, int head_value_width);
+BDM_API int bdm_scan_backward(const void *q, const void *k, const void *v, const float *g, const void *b,
+                              const void *w, const void *write_w, const void *read_w, const int64_t *order,
+                              const int64_t *cu_seqlens, int64_t batch, int64_t time, int64_t bank_count, int heads,
+                              int bank_size, int head_value_width, int kw, int kr, int dtype, int routed_decay,
+                              float scale, const void *row_factor, const void *col_factor, int64_t factor_cols,
+                              int factor_dtype, int state_interval, const void *d_read, float *event_grads,
+                              float *d_write_value, float *d_initial, float *checkpoints, int64_t checkpoint_bytes,
+                              void *stream);
+BDM_API int bdm_event_vjp(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
+                          const void *write_w, const void *read_w, const float *event_grads,
+                          const float *d_write_value, int64_t ntok, int heads, int bank_size, int head_value_width,
+                          int kw, int kr, int dtype, int routed_decay, float scale, void *dq, void *dk, void *dv,
+                          float *dg, void *db, void *dw, void *d_write_w, void *d_read_w, void *stream);
+BDM_API int bdm_product_state_backward(const float *d_initial, int64_t batch, int64_t rows_p, int64_t cols_q,
+                                       int head_value_width, int factor_dtype, float *d_rows, float *d_row_factor,
+                                       float *d_col_factor, void *stream);
+BDM_API int bdm_route_backward(const void *logits, int64_t ntok, int64_t ld, int64_t first, int64_t second, int j1,
+                               int j2, int count, const int64_t *idx_first, const void *dw_first,
+                               const int64_t *idx_second, const void *dw_second, int dtype, void *d_logits,
+                               int64_t ldd, void *stream);
+BDM_API int64_t bdm_controllers_backward_partial_floats(int64_t ntok, int heads, int bank_size);
+BDM_API int bdm_controllers_backward(const void *proj, int64_t ntok, int64_t ld, int64_t col_q, int64_t col_k,
+                                     int64_t col_v, int64_t col_b, int64_t col_w, const void *f, int64_t ldf,
+                                     const float *a_log, const float *dt_bias, const float *g, const void *b,
+                                     const void *w, const void *dq, const void *dk, const void *dv, const float *dg,
+                                     const void *db, const void *dw, int heads, int bank_size, int head_value_width,
+                                     int qk_norm, int dtype, void *d_proj, int64_t ldd, void *df, float *partials,
+                                     float *d_dt_bias, float *d_a_log, void *stream);
 
 /*
  * Bank-sharded forward (one rank per GPU; no counterpart in the reference,

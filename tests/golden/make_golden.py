@@ -19,6 +19,10 @@ Fixtures:
   layer_*.pt    BlockSparseDeltaMemory(backend='reference').forward on small
                 configs (FP32 and BF16, H=1 and H=2) with their state_dicts,
                 controller tensors and router logits; plus c1 at T=64.
+  grad_*.pt     torch autograd through the same reference forward (backend='reference'):
+                the gradients of every parameter and of the input for a seeded
+                output cotangent, on BSDMConfig (routed decay, 'nvidia' q/k norm,
+                LayerNorm) and BDMConfig (plain decay, 'original' norm, RMS) layers.
 """
 from __future__ import annotations
 
@@ -33,6 +37,7 @@ sys.path.insert(0, REF)
 
 from bdm.gdn2_banks import (pack_bank_events, product_key_route, reference_packed_gdn2,  # noqa: E402
                             scatter_bank_outputs, serial_banked_gdn2)
+from bdm import BankedDeltaMemory, BDMConfig  # noqa: E402
 from bsdm import BlockSparseDeltaMemory, BSDMConfig  # noqa: E402
 
 
@@ -154,6 +159,27 @@ def make_layer(name, cfg, batch, time, dtype, seed=0, x_seed=0, factor_std=None)
                os.path.join(HERE, f'layer_{name}.pt'))
 
 
+def make_grad(name, cls, cfg, batch, time, dtype, seed=0, x_seed=0):
+    """Gradients of <dy, layer(x)> for every parameter and for x (reference autograd)."""
+    m = cls(cfg, seed=seed, backend='reference').to(dtype)
+    gen = torch.Generator().manual_seed(1000 + x_seed)
+    x = torch.randn(batch, time, cfg.dim, generator=gen).to(dtype).requires_grad_(True)
+    y = m(x)
+    dy = torch.randn(y.shape, generator=gen).to(dtype)
+    y.backward(dy)
+    grads = {n: p.grad.detach().clone() for n, p in m.named_parameters() if p.grad is not None}
+    with torch.no_grad():  # the reference's own selections: torch.topk orders BF16 ties its own way
+        rl, wl = m._route_projections(x)
+        wi = m._route(wl, m.num_writes)[1]
+        ri = m._route(rl, m.num_reads)[1]
+    cfg_dict = {k: getattr(cfg, k) for k in cfg.__dataclass_fields__}
+    torch.save(dict(config=cfg_dict, config_class='BSDM' if isinstance(cfg, BSDMConfig) else 'BDM',
+                    dtype=str(dtype), seed=seed, state_dict={k: v.detach() for k, v in m.state_dict().items()},
+                    x=x.detach(), out=y.detach(), dy=dy, x_grad=x.grad.detach(), grads=grads, write_idx=wi, read_idx=ri,
+                    source=f'{cls.__module__}.{cls.__name__}(backend="reference"): torch autograd of <dy, forward(x)>'),
+               os.path.join(HERE, f'grad_{name}.pt'))
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     torch.save(dict(cases=_route_cases(), source='bdm.gdn2_banks.product_key_route'), os.path.join(HERE, 'router.pt'))
@@ -172,6 +198,14 @@ def main():
                torch.float32, seed=3)
     c1 = BSDMConfig(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=64, num_heads=1)
     make_layer('c1_t64', c1, 2, 64, torch.float32, seed=0, x_seed=0, factor_std=0.02 / 2 ** 0.5)
+    make_grad('h1_fp32_state32', BlockSparseDeltaMemory,
+              BSDMConfig(**small, num_heads=1, training_state_dtype='float32'), 2, 40, torch.float32, seed=1)
+    make_grad('h2_fp32_state32', BlockSparseDeltaMemory,
+              BSDMConfig(**small, num_heads=2, training_state_dtype='float32'), 2, 40, torch.float32, seed=2)
+    make_grad('h2_bf16', BlockSparseDeltaMemory, BSDMConfig(**small, num_heads=2), 2, 40, torch.bfloat16, seed=3)
+    make_grad('bdm_h1_fp32_state32', BankedDeltaMemory,
+              BDMConfig(**small, num_heads=1, training_state_dtype='float32'), 2, 40, torch.float32, seed=4)
+    make_grad('bdm_h2_bf16', BankedDeltaMemory, BDMConfig(**small, num_heads=2), 2, 40, torch.bfloat16, seed=5)
     print('golden fixtures written to', HERE)
 
 

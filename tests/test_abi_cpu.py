@@ -56,6 +56,17 @@ def test_dispatch_workspace_sizing():
                                        None, 0, None),
     lambda lib: lib.bdm_combine_partial(None, None, 4, 8, 64, None, 256, 0, 1, None, None),
     lambda lib: lib.bdm_norm_gate_f32(None, 4, 64, None, 64, None, None, 1e-5, 1, 1, None, None),
+    lambda lib: lib.bdm_combine_norm_gate_save(None, None, 4, 8, 64, None, 64, None, None, 1e-5, 1, 0, 1, None, None,
+                                               None),
+    lambda lib: lib.bdm_norm_gate_backward(None, None, 4, 64, None, 32, None, None, 1e-5, 1, 1, None, None, 64, None,
+                                           None, None, None),                          # ld_gate < width
+    lambda lib: lib.bdm_scan_backward(*([None] * 10), 2, 4, 16, 1, 8, 32, 4, 4, 1, 1, 0.35, None, None, 0, 0, 0,
+                                      *([None] * 5), 0, None),                         # null inputs
+    lambda lib: lib.bdm_event_vjp(*([None] * 10), 4, 1, 8, 32, 4, 4, 1, 1, 0.35, *([None] * 8), None),
+    lambda lib: lib.bdm_product_state_backward(None, 2, 0, 4, 32, 1, None, None, None, None),
+    lambda lib: lib.bdm_route_backward(None, 4, 32, 0, 4, 4, 4, 4, None, None, None, None, 1, None, 32, None),
+    lambda lib: lib.bdm_controllers_backward(None, 4, 64, 0, 8, 16, 48, 56, None, 8, *([None] * 11), 1, 8, 32, 0,
+                                             1, None, 64, None, None, None, None, None),  # col_w + V > ld
 ])
 def test_invalid_arguments_are_rejected_on_the_host(call):
     assert call(_lib.load()) == _lib.BDM_ERR_INVALID
@@ -81,3 +92,21 @@ def test_unsupported_geometry_is_reported():
     assert rc == _lib.BDM_ERR_UNSUPPORTED  # bank_size 32 is not implemented
     with pytest.raises(NotImplementedError):
         _lib.check(rc, 'bdm_bank_scan')
+
+
+def test_backward_sizing_and_limits():
+    lib = _lib.load()
+    dummy = ctypes.c_void_p(16)
+    small = lib.bdm_scan_backward_checkpoint_bytes(2, 64, 8, 8, 64, 1, 8, 32)
+    assert 0 < small < lib.bdm_scan_backward_checkpoint_bytes(32, 2048, 8, 8, 512, 12, 8, 64)
+    assert lib.bdm_scan_backward_checkpoint_bytes(2, 64, 8, 8, 64, 1, 6, 32) == -1   # bank_size 4, 8 or 16
+    assert lib.bdm_norm_gate_backward_partial_floats(33, 64) == 2 * 3 * 64
+    assert lib.bdm_controllers_backward_partial_floats(65, 2, 8) == (2 * 2 + 1) * 16
+    # more heads than a VJP CTA's warps, more selected banks than a route warp's lanes
+    assert lib.bdm_event_vjp(*([dummy] * 10), 4, 33, 8, 32, 4, 4, 1, 1, 0.35, *([dummy] * 8), None) \
+        == _lib.BDM_ERR_UNSUPPORTED
+    assert lib.bdm_route_backward(dummy, 4, 200, 0, 100, 10, 10, 40, dummy, dummy, dummy, dummy, 1, dummy, 200,
+                                  None) == _lib.BDM_ERR_UNSUPPORTED
+    # checkpoint scratch below the required size
+    assert lib.bdm_scan_backward(*([dummy] * 10), 2, 4, 16, 1, 8, 32, 4, 4, 1, 1, 0.35, None, None, 0, 0, 0, dummy,
+                                 dummy, dummy, dummy, dummy, 16, None) == _lib.BDM_ERR_WORKSPACE

@@ -199,3 +199,27 @@ def test_layer_forward_matches_reference(golden_dir, name, tol):
     if not bf16:
         # FP32 logits rarely tie: the oracle's own end-to-end forward agrees as well
         assert max_rel(layer.forward(x), _np(data['out'])) <= tol
+
+
+GRADS = ['h1_fp32_state32', 'h2_fp32_state32', 'bdm_h1_fp32_state32', 'h2_bf16', 'bdm_h2_bf16']
+
+
+@pytest.mark.parametrize('name', GRADS)
+def test_gradient_oracle_matches_reference(golden_dir, name):
+    """oracle/grad.py autograd against the reference's own autograd (tests/golden/grad_*.pt).
+
+    FP32: 1e-5 max-relative per tensor.  BF16: 2e-2 (both sides round intermediate
+    gradients to BF16 at slightly different points); the reference's bank selections
+    are used, since torch.topk orders exact BF16 score ties its own way.
+    """
+    from oracle.grad import layer_grads
+    data = _load(golden_dir, f'grad_{name}.pt')
+    bf16 = data['dtype'] == 'torch.bfloat16'
+    grads, xg, y = layer_grads(data['state_dict'], data['x'], data['dy'], data['config'], data['write_idx'],
+                               data['read_idx'])
+    tol = 2e-2 if bf16 else 1e-5
+    assert max_rel(y.float().numpy(), _np(data['out'])) <= (0.0 if bf16 else 1e-6)
+    assert set(grads) == set(data['grads'])
+    for n, ref in data['grads'].items():
+        assert max_rel(grads[n].float().numpy(), _np(ref)) <= tol, n
+    assert max_rel(xg.float().numpy(), _np(data['x_grad'])) <= tol
