@@ -23,7 +23,9 @@
 // column's S rows stay in registers.  States come back by replay at three levels:
 // HBM checkpoints every kBlock events (written by a first forward sweep), shared-
 // memory sub-checkpoints every kSub events inside a block, and a register history
-// of the kSub states inside a sub-block, walked in reverse.
+// of the kSub states inside a sub-block, walked in reverse.  Each pass over a block
+// first stages the block's event controls in shared memory (all loads of the block
+// in flight at once), so the replay and reverse steps read only shared memory.
 #include "common.cuh"
 
 namespace bdm {
@@ -103,7 +105,7 @@ struct ScanBwdParams {
     int factor_dtype;
     const void *dread;  // [nt, H*dv] gradient of the combined read output (activation dtype)
     float *ckpt;        // [slots, H, S, dv] states at block starts
-    float *evg;         // [tiles, E, 3S] per-event column sums (A | c | G; o for reads)
+    float *evg;         // [tiles, E, H, 3S] per-(event, head) column sums (A | c | G; o for reads)
     float *du;          // [nt*kw, H*dv] write-event du per column
     float *dinit;       // [nseq, H, S, dv] gradient of each sequence's initial state
 };
@@ -111,74 +113,85 @@ struct ScanBwdParams {
 template <int S> struct BwdGeom {
     static constexpr int kSub = 64 / S;          // register history depth (64 floats per lane)
     static constexpr int kNSub = 8;              // shared-memory sub-checkpoints per block
-    static constexpr int kBlock = kSub * kNSub;  // events between HBM checkpoints
-    static constexpr int kWarps = S >= 16 ? 2 : 4;
-    static constexpr int kRec = 3 * S;           // floats per event record
+    static constexpr int kBlock = kSub * kNSub;  // events between HBM checkpoints (staged together)
+    static constexpr int kRec = 3 * S;           // floats per (event, head) record
     static constexpr int kRedW = Pow2Ceil<3 * S>::value;
 };
 
-// Controls of one event, as this lane uses them (lane-uniform rows, per-lane column).
-template <int S> struct EventCtl {
-    float k[S];   // write: key; read: q_e = dtype(q*r)
-    float a[S];   // write: dtype(b*p) * k
-    float e[S];   // write: exp(g_e)
-    float wv;     // write: dtype(w*p) * v on this lane's column
-    float dout;   // read: output gradient on this lane's column
-    int64_t id;
-    bool write;
+// One block of events staged in shared memory by the warp that owns the unit:
+// lane-uniform rows [k | a | e] per event (a = dtype(b*p)*k, e = exp(g_e); a read
+// keeps q_e = dtype(q*r) in the k slot), the lane's column value per event
+// (write: dtype(w*p)*v; read: the output gradient) and the event ids.
+template <int S> struct BlockStage {
+    float sub[BwdGeom<S>::kNSub][S][32];
+    alignas(16) float uni[BwdGeom<S>::kBlock][3 * S];
+    float col[BwdGeom<S>::kBlock][32];
+    int64_t id[BwdGeom<S>::kBlock];
 };
 
 template <typename T, int S>
-__device__ __forceinline__ void load_event(const ScanBwdParams &p, int64_t pos, int h, int col, bool active,
-                                           bool want_dout, EventCtl<S> &c) {
-    const int64_t id = __ldg(p.order + pos);
+__device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S> &st, int64_t pos0, int n, int h,
+                                            int col, bool active, bool want_dout) {
+    const unsigned lane = lane_id();
     const int64_t V = (int64_t)p.H * p.dv;
-    c.id = id;
-    c.write = id < p.nw;
-    c.wv = 0.f;
-    c.dout = 0.f;
-    if (c.write) {
-        const int64_t tok = id / p.kw;
-        const float pw = ld_f(static_cast<const T *>(p.ww), id);
-        const int64_t base = (tok * p.H + h) * S;
-        const T *kp = static_cast<const T *>(p.k) + base;
-        const T *bp = static_cast<const T *>(p.b) + base;
-        const float *gp = p.g + base;
+    __syncwarp();
+    for (int i = (int)lane; i < n; i += 32) {  // lanes over events: ids and the lane-uniform rows
+        const int64_t id = __ldg(p.order + pos0 + i);
+        st.id[i] = id;
+        float *u = st.uni[i];
+        if (id < p.nw) {
+            const int64_t tok = id / p.kw;
+            const float pw = ld_f(static_cast<const T *>(p.ww), id);
+            const int64_t base = (tok * p.H + h) * S;
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
-            const float kk = ld_f(kp, s);
-            c.k[s] = kk;
-            c.a[s] = rnd<T>(ld_f(bp, s) * pw) * kk;
-            c.e[s] = expf(p.routed_decay ? gp[s] * pw : gp[s]);
-        }
-        if (active) {
-            const int64_t o = tok * V + (int64_t)h * p.dv + col;
-            c.wv = rnd<T>(ld_f(static_cast<const T *>(p.w), o) * pw) * ld_f(static_cast<const T *>(p.v), o);
-        }
-    } else {
-        const int64_t rid = id - p.nw;
-        const int64_t tok = rid / p.kr;
-        const float r = ld_f(static_cast<const T *>(p.rw), rid);
-        const T *qp = static_cast<const T *>(p.q) + (tok * p.H + h) * S;
+            for (int s = 0; s < S; ++s) {
+                const float kk = ld_f(static_cast<const T *>(p.k), base + s);
+                const float gg = p.g[base + s];
+                u[s] = kk;
+                u[S + s] = rnd<T>(ld_f(static_cast<const T *>(p.b), base + s) * pw) * kk;
+                u[2 * S + s] = expf(p.routed_decay ? gg * pw : gg);
+            }
+        } else {
+            const int64_t rid = id - p.nw;
+            const int64_t base = (rid / p.kr * p.H + h) * S;
+            const float r = ld_f(static_cast<const T *>(p.rw), rid);
 #pragma unroll
-        for (int s = 0; s < S; ++s) c.k[s] = rnd<T>(ld_f(qp, s) * r);
-        if (want_dout && active)
-            c.dout = ld_f(static_cast<const T *>(p.dread), tok * V + (int64_t)h * p.dv + col);
+            for (int s = 0; s < S; ++s) u[s] = rnd<T>(ld_f(static_cast<const T *>(p.q), base + s) * r);
+        }
     }
+    __syncwarp();
+#pragma unroll 8
+    for (int i = 0; i < n; ++i) {  // every lane over the events: its own column
+        const int64_t id = st.id[i];
+        float val = 0.f;
+        if (id < p.nw) {
+            if (active) {
+                const int64_t o = id / p.kw * V + (int64_t)h * p.dv + col;
+                const float pw = ld_f(static_cast<const T *>(p.ww), id);
+                val = rnd<T>(ld_f(static_cast<const T *>(p.w), o) * pw) * ld_f(static_cast<const T *>(p.v), o);
+            }
+        } else if (want_dout && active) {
+            val = ld_f(static_cast<const T *>(p.dread), (id - p.nw) / p.kr * V + (int64_t)h * p.dv + col);
+        }
+        st.col[i][lane] = val;
+    }
+    __syncwarp();
 }
 
 template <int S>
-__device__ __forceinline__ void replay(const EventCtl<S> &c, float (&hs)[S]) {
-    if (!c.write) return;
+__device__ __forceinline__ void replay(const BlockStage<S> &st, int i, float (&hs)[S]) {
+    const unsigned lane = lane_id();
+    // (the caller skips reads: they leave the state unchanged)
+    const float *u = st.uni[i];
     float er = 0.f;
 #pragma unroll
     for (int s = 0; s < S; ++s) {
-        hs[s] *= c.e[s];
-        er = fmaf(c.a[s], hs[s], er);
+        hs[s] *= u[2 * S + s];
+        er = fmaf(u[S + s], hs[s], er);
     }
-    const float u = c.wv - er;
+    const float uu = st.col[i][lane] - er;
 #pragma unroll
-    for (int s = 0; s < S; ++s) hs[s] = fmaf(c.k[s], u, hs[s]);
+    for (int s = 0; s < S; ++s) hs[s] = fmaf(u[s], uu, hs[s]);
 }
 
 template <int S>
@@ -213,58 +226,62 @@ __device__ __forceinline__ void initial_column(const ScanBwdParams &p, int64_t s
 }
 
 template <int S>
-__device__ __forceinline__ void reverse_event(const ScanBwdParams &p, const EventCtl<S> &c, const float (&h0)[S],
-                                              int tile, int h, int col, bool active, float (&dh)[S]) {
+__device__ __forceinline__ void reverse_event(const ScanBwdParams &p, const BlockStage<S> &st, int i,
+                                              const float (&h0)[S], int tile, int h, int col, bool active,
+                                              float (&dh)[S]) {
     using G = BwdGeom<S>;
-    float *rec = p.evg + ((int64_t)tile * p.E + c.id) * G::kRec;
-    if (c.write) {
+    const unsigned lane = lane_id();
+    const int64_t id = st.id[i];
+    const float *u = st.uni[i];
+    const float cv = st.col[i][lane];
+    float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
+    if (id < p.nw) {
         float hd[S], er = 0.f, du = 0.f;
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            hd[s] = h0[s] * c.e[s];
-            er = fmaf(c.a[s], hd[s], er);
-            du = fmaf(dh[s], c.k[s], du);
+            hd[s] = h0[s] * u[2 * S + s];
+            er = fmaf(u[S + s], hd[s], er);
+            du = fmaf(dh[s], u[s], du);
         }
-        const float u = c.wv - er;
+        const float uu = cv - er;
         float red[G::kRedW];
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            red[s] = dh[s] * u;
+            red[s] = dh[s] * uu;
             red[S + s] = hd[s] * du;
-            const float dp = fmaf(-c.a[s], du, dh[s]);
+            const float dp = fmaf(-u[S + s], du, dh[s]);
             red[2 * S + s] = dp * hd[s];
-            dh[s] = dp * c.e[s];
+            dh[s] = dp * u[2 * S + s];
         }
 #pragma unroll
-        for (int i = 3 * S; i < G::kRedW; ++i) red[i] = 0.f;
-        if (active) p.du[c.id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + col] = du;
+        for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
+        if (active) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + col] = du;
         reduce_store<G::kRedW>(red, 3 * S, rec);
     } else {
         float red[S];
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            red[s] = h0[s] * c.dout;
-            dh[s] = fmaf(c.k[s] * c.dout, p.scale, dh[s]);
+            red[s] = h0[s] * cv;
+            dh[s] = fmaf(u[s] * cv, p.scale, dh[s]);
         }
         reduce_store<S>(red, S, rec);
     }
 }
 
+// One warp (one CTA) per (sequence, head, column tile).
 template <typename T, int S>
-__global__ void __launch_bounds__(32 * BwdGeom<S>::kWarps) scan_backward_kernel(const ScanBwdParams p) {
+__global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p) {
     using G = BwdGeom<S>;
-    __shared__ float sub_sm[G::kWarps][G::kNSub][S][32];
-    const int warp = (int)(threadIdx.x >> 5);
+    __shared__ BlockStage<S> st;
     const unsigned lane = lane_id();
-    const int64_t unit = (int64_t)blockIdx.x * G::kWarps + warp;
-    if (unit >= p.units) return;  // uniform per warp
+    const int64_t unit = blockIdx.x;
+    if (unit >= p.units) return;
     const int tile = (int)(unit % p.tiles);
     const int h = (int)((unit / p.tiles) % p.H);
     const int64_t seq = unit / ((int64_t)p.tiles * p.H);
     const int col = tile * 32 + (int)lane;
     const bool active = col < p.dv;
     const int64_t start = p.cu[seq], L = p.cu[seq + 1] - start;
-    float(*sub)[S][32] = sub_sm[warp];
     float dh[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) dh[s] = 0.f;
@@ -273,17 +290,17 @@ __global__ void __launch_bounds__(32 * BwdGeom<S>::kWarps) scan_backward_kernel(
         const int64_t nblk = (L + G::kBlock - 1) / G::kBlock;
         const int64_t slot0 = start / G::kBlock + seq;  // disjoint slot ranges across sequences
         float hs[S];
-        EventCtl<S> c;
         if (nblk > 1) {  // sweep 1: checkpoints at the starts of blocks 1 .. nblk-1
             initial_column<S>(p, seq, h, col, active, hs);
-            for (int64_t m = 1; m < nblk; ++m) {
-                for (int64_t e = (m - 1) * G::kBlock; e < m * G::kBlock; ++e) {
-                    storage_round<S>(p, e, hs);
-                    load_event<T, S>(p, start + e, h, col, active, false, c);
-                    replay<S>(c, hs);
+            for (int64_t m = 0; m + 1 < nblk; ++m) {
+                const int64_t e0 = m * G::kBlock;
+                stage_block<T, S>(p, st, start + e0, G::kBlock, h, col, active, false);
+                for (int i = 0; i < G::kBlock; ++i) {
+                    storage_round<S>(p, e0 + i, hs);
+                    if (st.id[i] < p.nw) replay<S>(st, i, hs);
                 }
                 if (active) {
-                    float *ck = p.ckpt + ((slot0 + m) * p.H + h) * stride_state + col;
+                    float *ck = p.ckpt + ((slot0 + m + 1) * p.H + h) * stride_state + col;
 #pragma unroll
                     for (int s = 0; s < S; ++s) ck[(int64_t)s * p.dv] = hs[s];
                 }
@@ -300,42 +317,35 @@ __global__ void __launch_bounds__(32 * BwdGeom<S>::kWarps) scan_backward_kernel(
             const int64_t e0 = m * G::kBlock;
             const int blen = (int)min((int64_t)G::kBlock, L - e0);
             const int nsub = (blen + G::kSub - 1) / G::kSub;
+            stage_block<T, S>(p, st, start + e0, blen, h, col, active, true);
             for (int n = 0; n < nsub; ++n) {  // sub-checkpoints (lane-private shared memory)
 #pragma unroll
-                for (int s = 0; s < S; ++s) sub[n][s][lane] = hs[s];
+                for (int s = 0; s < S; ++s) st.sub[n][s][lane] = hs[s];
                 if (n == nsub - 1) break;
                 for (int j = 0; j < G::kSub; ++j) {
-                    const int64_t e = e0 + n * G::kSub + j;
-                    storage_round<S>(p, e, hs);
-                    load_event<T, S>(p, start + e, h, col, active, false, c);
-                    replay<S>(c, hs);
+                    const int i = n * G::kSub + j;
+                    storage_round<S>(p, e0 + i, hs);
+                    if (st.id[i] < p.nw) replay<S>(st, i, hs);
                 }
             }
             for (int n = nsub - 1; n >= 0; --n) {
 #pragma unroll
-                for (int s = 0; s < S; ++s) hs[s] = sub[n][s][lane];
+                for (int s = 0; s < S; ++s) hs[s] = st.sub[n][s][lane];
                 const int slen = min(G::kSub, blen - n * G::kSub);
-                const int64_t eb = e0 + n * G::kSub;
+                const int i0 = n * G::kSub;
                 float hist[G::kSub][S];
 #pragma unroll
                 for (int j = 0; j < G::kSub; ++j) {
                     if (j < slen) {
-                        storage_round<S>(p, eb + j, hs);
+                        storage_round<S>(p, e0 + i0 + j, hs);
 #pragma unroll
                         for (int s = 0; s < S; ++s) hist[j][s] = hs[s];
-                        if (j + 1 < slen) {
-                            load_event<T, S>(p, start + eb + j, h, col, active, false, c);
-                            replay<S>(c, hs);
-                        }
+                        if (j + 1 < slen && st.id[i0 + j] < p.nw) replay<S>(st, i0 + j, hs);
                     }
                 }
 #pragma unroll
-                for (int j = G::kSub - 1; j >= 0; --j) {
-                    if (j < slen) {
-                        load_event<T, S>(p, start + eb + j, h, col, active, true, c);
-                        reverse_event<S>(p, c, hist[j], tile, h, col, active, dh);
-                    }
-                }
+                for (int j = G::kSub - 1; j >= 0; --j)
+                    if (j < slen) reverse_event<S>(p, st, i0 + j, hist[j], tile, h, col, active, dh);
             }
         }
     }
@@ -348,10 +358,8 @@ __global__ void __launch_bounds__(32 * BwdGeom<S>::kWarps) scan_backward_kernel(
 
 template <typename T, int S>
 int launch_scan_backward(const ScanBwdParams &p, cudaStream_t st) {
-    using G = BwdGeom<S>;
-    const int64_t blocks = ceil_div(p.units, G::kWarps);
-    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
-    scan_backward_kernel<T, S><<<(unsigned)blocks, 32 * G::kWarps, 0, st>>>(p);
+    if (p.units > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    scan_backward_kernel<T, S><<<(unsigned)p.units, 32, 0, st>>>(p);
     return launch_status();
 }
 
@@ -429,7 +437,7 @@ __global__ void event_vjp_kernel(const VjpParams p) {
         if (nl) {
             float A = 0.f, C = 0.f, Gs = 0.f;
             for (int tile = 0; tile < p.tiles; ++tile) {
-                const float *rec = p.evg + ((int64_t)tile * p.E + id) * R;
+                const float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * R;
                 A += rec[lane];
                 C += rec[S + lane];
                 Gs += rec[2 * S + lane];
@@ -458,7 +466,8 @@ __global__ void event_vjp_kernel(const VjpParams p) {
         float wrp = 0.f;
         if (nl) {
             float o = 0.f;
-            for (int tile = 0; tile < p.tiles; ++tile) o += p.evg[((int64_t)tile * p.E + id) * R + lane] * p.scale;
+            for (int tile = 0; tile < p.tiles; ++tile)
+                o += p.evg[(((int64_t)tile * p.E + id) * p.H + h) * R + lane] * p.scale;
             const float dqe = rnd<T>(o);
             dq_acc += rnd<T>(dqe * r);
             wrp = rnd<T>(dqe * q0);

@@ -475,7 +475,7 @@ def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, 
     """Recurrence backward over the dispatched events of a factor-initialised training forward.
 
     ``d_read`` [NT, H*dv] is the gradient of the combined read sum.  Returns
-    (event_grads [ceil(dv/32), E, 3S], d_write_value [NT*KW, H*dv], d_initial [B*J, H, S, dv]), FP32.
+    (event_grads [ceil(dv/32), E, H, 3S], d_write_value [NT*KW, H*dv], d_initial [B*J, H, S, dv]), FP32.
     """
     _cuda(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read)
     dt, dev = q.dtype, q.device
@@ -489,7 +489,7 @@ def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, 
     if ck_bytes < 0:
         raise NotImplementedError('scan backward supports bank_size 4, 8 or 16')
     ck = torch.empty(max(ck_bytes // 4, 1), dtype=torch.float32, device=dev)
-    evg = torch.empty((tiles, e, 3 * bank_size), dtype=torch.float32, device=dev)
+    evg = torch.empty((tiles, e, heads, 3 * bank_size), dtype=torch.float32, device=dev)
     du = torch.empty((nt * kw, v_width), dtype=torch.float32, device=dev)
     dinit = torch.empty((batch * bank_count, heads, bank_size, head_value_width), dtype=torch.float32, device=dev)
     u = z = None

@@ -449,12 +449,13 @@ def run_train(dev, rank, world, args):
     """c5 layer geometry: forward + backward of one BDM layer (BF16), the global batch split over the
     ranks; at N > 1 the layer's parameter gradients are all-reduced over NCCL (data parallel)."""
     from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, _lib
-    if C5_BATCH % world:
-        return {'skipped': f'batch {C5_BATCH} does not split over {world} ranks'}
+    batch = args.train_batch
+    if batch % world:
+        return {'skipped': f'batch {batch} does not split over {world} ranks'}
     lib = _lib.load()
     cfg = BSDMConfig(**C5)
     layer = BlockSparseDeltaMemory(cfg, seed=4).to(torch.bfloat16).to(dev)
-    rows = C5_BATCH // world
+    rows = batch // world
     gen = torch.Generator(device=dev).manual_seed(4000 + rank)
     x = torch.randn(rows, C5_TIME, cfg.dim, generator=gen, device=dev).to(torch.bfloat16)
     dy = torch.randn(rows, C5_TIME, cfg.dim, generator=gen, device=dev).to(torch.bfloat16)
@@ -493,7 +494,7 @@ def run_train(dev, rank, world, args):
     scan_bwd_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in layer.backward_events), world)
     layer.backward_events = None
     ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)), world) / steps
-    tokens = C5_BATCH * C5_TIME
+    tokens = batch * C5_TIME
     _, bf16_peak, peak_kind = load_peaks()
     gemm_ms = c5_gemm_flops(tokens // world) / (bf16_peak * 1e12) * 1000
     return {'metric': C5_METRIC, 'value': tokens / (ms / 1000), 'unit': 'tokens/s', 'n_gpus': world,
@@ -502,7 +503,7 @@ def run_train(dev, rank, world, args):
                                      + (', NCCL all-reduce of the parameter gradients' if world > 1 else ''),
             'config': {'workload': 'c5 layer: BSDMConfig(dim=768, bank_count=512, bank_size=8, selected_banks=8, '
                                    'value_width=768, num_heads=12), seed 4, random-init; one layer, no LM shell',
-                       'global_batch': C5_BATCH, 'seq_len': C5_TIME, 'rows_per_rank': rows,
+                       'global_batch': batch, 'seq_len': C5_TIME, 'rows_per_rank': rows,
                        'l2': 'inputs larger than L2; 256 MiB flush between steps'},
             'gpu_launches': int(launches),
             'scan_backward_ms': scan_bwd_ms,
@@ -606,6 +607,7 @@ def main():
     ap.add_argument('--c4-ownership', choices=('balanced', 'contiguous'), default='balanced')
     ap.add_argument('--skip-train', action='store_true')
     ap.add_argument('--train-steps', type=int, default=3)
+    ap.add_argument('--train-batch', type=int, default=C5_BATCH, help='c5 batch (32 is the benchmark)')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3

@@ -233,7 +233,7 @@ BDM_API int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_id
  * bdm_scan_backward: the recurrence backward over the dispatched events (same
  *   inputs as bdm_bank_scan's factor-initialised training call, plus d_read
  *   [ntok, H*dv] = gradient of the combined read sum).  Outputs, FP32:
- *   event_grads [ceil(dv/32), E, 3*S] per-event column sums (per write event id:
+ *   event_grads [ceil(dv/32), E, H, 3*S] per-(event, head) column sums (per write event id:
  *   sum_x dh*u | sum_x hd*du | sum_x dh'*hd; per read event id: sum_x h*do),
  *   d_write_value [ntok*kw, H*dv] (du per write event id) and d_initial
  *   [batch*J, H, S, dv].  checkpoints: bdm_scan_backward_checkpoint_bytes() bytes
