@@ -47,6 +47,7 @@ SIGNATURES = {
     'bdm_norm_gate_backward_partial_floats': (_i64, [_i64, _i64]),
     'bdm_norm_gate_backward': (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _vp, _vp, _i64,
                                       _vp, _vp, _vp, _vp]),
+    'bdm_scan_backward_tiles': (_int, [_int, _int]),
     'bdm_scan_backward_checkpoint_bytes': (_i64, [_i64, _i64, _int, _int, _i64, _int, _int, _int]),
     'bdm_scan_backward': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _int,
                                  _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp,

@@ -19,8 +19,8 @@
 // The per-event S-vectors A, c, G (write) and o (read) are sums over the columns;
 // dk_e = A - b_e c, db_e = -k c, dg_e = G, dq_e = scale * o follow in the VJP.
 //
-// One warp per (sequence, head, tile of 32 columns), one column per lane, so a
-// column's S rows stay in registers.  States come back by replay at three levels:
+// One warp per (sequence, head, tile of 32 or 64 columns), one or two columns per
+// lane, so a column's S rows stay in registers.  States come back by replay at three levels:
 // HBM checkpoints every kBlock events (written by a first forward sweep), shared-
 // memory sub-checkpoints every kSub events inside a block, and a register history
 // of the kSub states inside a sub-block, walked in reverse.  Each pass over a block
@@ -110,28 +110,31 @@ struct ScanBwdParams {
     float *dinit;       // [nseq, H, S, dv] gradient of each sequence's initial state
 };
 
-template <int S> struct BwdGeom {
-    static constexpr int kSub = 64 / S;          // register history depth (64 floats per lane)
-    static constexpr int kNSub = 8;              // shared-memory sub-checkpoints per block
-    static constexpr int kBlock = kSub * kNSub;  // events between HBM checkpoints (staged together)
-    static constexpr int kRec = 3 * S;           // floats per (event, head) record
+template <int S, int COLS> struct BwdGeom {
+    static constexpr int kSub = 64 / (S * COLS);  // register history depth (64 floats per lane)
+    static constexpr int kNSub = 4;               // shared-memory sub-checkpoints per block
+    static constexpr int kBlock = kSub * kNSub;   // events between HBM checkpoints (staged together)
+    static constexpr int kRec = 3 * S;            // floats per (event, head) record
     static constexpr int kRedW = Pow2Ceil<3 * S>::value;
+    static constexpr int kTileCols = 32 * COLS;   // value columns per warp (lane l: l, l+32, ...)
 };
 
 // One block of events staged in shared memory by the warp that owns the unit:
 // lane-uniform rows [k | a | e] per event (a = dtype(b*p)*k, e = exp(g_e); a read
-// keeps q_e = dtype(q*r) in the k slot), the lane's column value per event
-// (write: dtype(w*p)*v; read: the output gradient) and the event ids.
-template <int S> struct BlockStage {
-    float sub[BwdGeom<S>::kNSub][S][32];
-    alignas(16) float uni[BwdGeom<S>::kBlock][3 * S];
-    float col[BwdGeom<S>::kBlock][32];
-    int64_t id[BwdGeom<S>::kBlock];
+// keeps q_e = dtype(q*r) in the k slot), the lane's column values per event
+// (write: dtype(w*p)*v; read: the output gradient), the event ids, and the
+// sub-block checkpoints (lane-private).
+template <int S, int COLS> struct BlockStage {
+    using G = BwdGeom<S, COLS>;
+    float sub[G::kNSub][S][COLS][32];
+    alignas(16) float uni[G::kBlock][3 * S];
+    float col[G::kBlock][COLS][32];
+    int64_t id[G::kBlock];
 };
 
-template <typename T, int S>
-__device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S> &st, int64_t pos0, int n, int h,
-                                            int col, bool active, bool want_dout) {
+template <typename T, int S, int COLS>
+__device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S, COLS> &st, int64_t pos0, int n,
+                                            int h, int col0, bool want_dout) {
     const unsigned lane = lane_id();
     const int64_t V = (int64_t)p.H * p.dv;
     __syncwarp();
@@ -160,210 +163,277 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
         }
     }
     __syncwarp();
-#pragma unroll 8
-    for (int i = 0; i < n; ++i) {  // every lane over the events: its own column
+#pragma unroll 4
+    for (int i = 0; i < n; ++i) {  // every lane over the events: its own columns
         const int64_t id = st.id[i];
-        float val = 0.f;
-        if (id < p.nw) {
-            if (active) {
-                const int64_t o = id / p.kw * V + (int64_t)h * p.dv + col;
-                const float pw = ld_f(static_cast<const T *>(p.ww), id);
-                val = rnd<T>(ld_f(static_cast<const T *>(p.w), o) * pw) * ld_f(static_cast<const T *>(p.v), o);
+        const bool wr = id < p.nw;
+        const int64_t row = wr ? id / p.kw * V : (id - p.nw) / p.kr * V;
+        const float pw = wr ? ld_f(static_cast<const T *>(p.ww), id) : 0.f;
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) {
+            const int cc = col0 + 32 * c;
+            float val = 0.f;
+            if (cc < p.dv) {
+                const int64_t o = row + (int64_t)h * p.dv + cc;
+                if (wr)
+                    val = rnd<T>(ld_f(static_cast<const T *>(p.w), o) * pw) * ld_f(static_cast<const T *>(p.v), o);
+                else if (want_dout)
+                    val = ld_f(static_cast<const T *>(p.dread), o);
             }
-        } else if (want_dout && active) {
-            val = ld_f(static_cast<const T *>(p.dread), (id - p.nw) / p.kr * V + (int64_t)h * p.dv + col);
+            st.col[i][c][lane] = val;
         }
-        st.col[i][lane] = val;
     }
     __syncwarp();
 }
 
-template <int S>
-__device__ __forceinline__ void replay(const BlockStage<S> &st, int i, float (&hs)[S]) {
-    const unsigned lane = lane_id();
+template <int S, int COLS>
+__device__ __forceinline__ void replay(const BlockStage<S, COLS> &st, int i, float (&hs)[S][COLS]) {
     // (the caller skips reads: they leave the state unchanged)
+    const unsigned lane = lane_id();
     const float *u = st.uni[i];
-    float er = 0.f;
+    float er[COLS][2];
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = 0.f;
 #pragma unroll
     for (int s = 0; s < S; ++s) {
-        hs[s] *= u[2 * S + s];
-        er = fmaf(u[S + s], hs[s], er);
-    }
-    const float uu = st.col[i][lane] - er;
+        const float e = u[2 * S + s], a = u[S + s];
 #pragma unroll
-    for (int s = 0; s < S; ++s) hs[s] = fmaf(u[s], uu, hs[s]);
+        for (int c = 0; c < COLS; ++c) {
+            hs[s][c] *= e;
+            er[c][s & 1] = fmaf(a, hs[s][c], er[c][s & 1]);
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
+        const float uu = st.col[i][c][lane] - (er[c][0] + er[c][1]);
+#pragma unroll
+        for (int s = 0; s < S; ++s) hs[s][c] = fmaf(u[s], uu, hs[s][c]);
+    }
 }
 
-template <int S>
-__device__ __forceinline__ void storage_round(const ScanBwdParams &p, int64_t e, float (&hs)[S]) {
+template <int S, int COLS>
+__device__ __forceinline__ void storage_round(const ScanBwdParams &p, int64_t e, float (&hs)[S][COLS]) {
     if (p.interval > 0 && (int)e % p.interval == 0) {  // e < 2^31: events of one sequence
 #pragma unroll
-        for (int s = 0; s < S; ++s) hs[s] = bf16_round(hs[s]);
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) hs[s][c] = bf16_round(hs[s][c]);
     }
 }
 
-// Initial state of one column: product-key factors (rounded to their dtype), or zero;
-// rounded to BF16 under the training storage policy.
-template <int S>
-__device__ __forceinline__ void initial_column(const ScanBwdParams &p, int64_t seq, int h, int col, bool active,
-                                               float (&hs)[S]) {
-#pragma unroll
-    for (int s = 0; s < S; ++s) hs[s] = 0.f;
-    if (!active || !p.row_factor) return;
+// Initial state of the lane's columns: product-key factors (rounded to their dtype), or
+// zero; rounded to BF16 under the training storage policy.
+template <int S, int COLS>
+__device__ __forceinline__ void initial_columns(const ScanBwdParams &p, int64_t seq, int h, int col0,
+                                                float (&hs)[S][COLS]) {
     const int64_t bank = seq % p.J;
 #pragma unroll
     for (int s = 0; s < S; ++s) {
         const int64_t r = (bank * p.H + h) * S + s;
-        const int64_t ou = (r / p.factor_cols) * p.dv + col, oz = (r % p.factor_cols) * p.dv + col;
-        if (p.factor_dtype == BDM_BF16) {
-            hs[s] = bf16_round(ld_f(static_cast<const bf16 *>(p.row_factor), ou) +
-                               ld_f(static_cast<const bf16 *>(p.col_factor), oz));
-        } else {
-            hs[s] = static_cast<const float *>(p.row_factor)[ou] + static_cast<const float *>(p.col_factor)[oz];
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) {
+            const int cc = col0 + 32 * c;
+            float x = 0.f;
+            if (cc < p.dv && p.row_factor) {
+                const int64_t ou = (r / p.factor_cols) * p.dv + cc, oz = (r % p.factor_cols) * p.dv + cc;
+                if (p.factor_dtype == BDM_BF16)
+                    x = bf16_round(ld_f(static_cast<const bf16 *>(p.row_factor), ou) +
+                                   ld_f(static_cast<const bf16 *>(p.col_factor), oz));
+                else
+                    x = static_cast<const float *>(p.row_factor)[ou] + static_cast<const float *>(p.col_factor)[oz];
+                if (p.interval > 0) x = bf16_round(x);
+            }
+            hs[s][c] = x;
         }
-        if (p.interval > 0) hs[s] = bf16_round(hs[s]);
     }
 }
 
-template <int S>
-__device__ __forceinline__ void reverse_event(const ScanBwdParams &p, const BlockStage<S> &st, int i,
-                                              const float (&h0)[S], int tile, int h, int col, bool active,
-                                              float (&dh)[S]) {
-    using G = BwdGeom<S>;
+template <int S, int COLS>
+__device__ __forceinline__ void reverse_event(const ScanBwdParams &p, const BlockStage<S, COLS> &st, int i,
+                                              const float (&h0)[S][COLS], int tile, int h, int col0,
+                                              float (&dh)[S][COLS]) {
+    using G = BwdGeom<S, COLS>;
     const unsigned lane = lane_id();
     const int64_t id = st.id[i];
     const float *u = st.uni[i];
-    const float cv = st.col[i][lane];
     float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
     if (id < p.nw) {
-        float hd[S], er = 0.f, du = 0.f;
+        float hd[S][COLS], er[COLS][2], du[COLS][2], uu[COLS], dus[COLS];
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = du[c][0] = du[c][1] = 0.f;
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            hd[s] = h0[s] * u[2 * S + s];
-            er = fmaf(u[S + s], hd[s], er);
-            du = fmaf(dh[s], u[s], du);
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) {
+                hd[s][c] = h0[s][c] * u[2 * S + s];
+                er[c][s & 1] = fmaf(u[S + s], hd[s][c], er[c][s & 1]);
+                du[c][s & 1] = fmaf(dh[s][c], u[s], du[c][s & 1]);
+            }
         }
-        const float uu = cv - er;
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) {
+            uu[c] = st.col[i][c][lane] - (er[c][0] + er[c][1]);
+            dus[c] = du[c][0] + du[c][1];
+        }
         float red[G::kRedW];
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            red[s] = dh[s] * uu;
-            red[S + s] = hd[s] * du;
-            const float dp = fmaf(-u[S + s], du, dh[s]);
-            red[2 * S + s] = dp * hd[s];
-            dh[s] = dp * u[2 * S + s];
+            float A = 0.f, C = 0.f, Gs = 0.f;
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) {
+                A = fmaf(dh[s][c], uu[c], A);
+                C = fmaf(hd[s][c], dus[c], C);
+                const float dp = fmaf(-u[S + s], dus[c], dh[s][c]);
+                Gs = fmaf(dp, hd[s][c], Gs);
+                dh[s][c] = dp * u[2 * S + s];
+            }
+            red[s] = A;
+            red[S + s] = C;
+            red[2 * S + s] = Gs;
         }
 #pragma unroll
         for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
-        if (active) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + col] = du;
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) {
+            const int cc = col0 + 32 * c;
+            if (cc < p.dv) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + cc] = dus[c];
+        }
         reduce_store<G::kRedW>(red, 3 * S, rec);
     } else {
         float red[S];
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            red[s] = h0[s] * cv;
-            dh[s] = fmaf(u[s] * cv, p.scale, dh[s]);
+            float o = 0.f;
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) {
+                const float cv = st.col[i][c][lane];
+                o = fmaf(h0[s][c], cv, o);
+                dh[s][c] = fmaf(u[s] * cv, p.scale, dh[s][c]);
+            }
+            red[s] = o;
         }
         reduce_store<S>(red, S, rec);
     }
 }
 
-// One warp (one CTA) per (sequence, head, column tile).
-template <typename T, int S>
+// One warp (one CTA) per (sequence, head, tile of 32*COLS columns).
+template <typename T, int S, int COLS>
 __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p) {
-    using G = BwdGeom<S>;
-    __shared__ BlockStage<S> st;
+    using G = BwdGeom<S, COLS>;
+    __shared__ BlockStage<S, COLS> st;
     const unsigned lane = lane_id();
     const int64_t unit = blockIdx.x;
     if (unit >= p.units) return;
     const int tile = (int)(unit % p.tiles);
     const int h = (int)((unit / p.tiles) % p.H);
     const int64_t seq = unit / ((int64_t)p.tiles * p.H);
-    const int col = tile * 32 + (int)lane;
-    const bool active = col < p.dv;
+    const int col0 = tile * G::kTileCols + (int)lane;
     const int64_t start = p.cu[seq], L = p.cu[seq + 1] - start;
-    float dh[S];
+    float dh[S][COLS];
 #pragma unroll
-    for (int s = 0; s < S; ++s) dh[s] = 0.f;
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) dh[s][c] = 0.f;
     const int64_t stride_state = (int64_t)S * p.dv;
     if (L > 0) {
         const int64_t nblk = (L + G::kBlock - 1) / G::kBlock;
         const int64_t slot0 = start / G::kBlock + seq;  // disjoint slot ranges across sequences
-        float hs[S];
+        float hs[S][COLS];
         if (nblk > 1) {  // sweep 1: checkpoints at the starts of blocks 1 .. nblk-1
-            initial_column<S>(p, seq, h, col, active, hs);
+            initial_columns<S, COLS>(p, seq, h, col0, hs);
             for (int64_t m = 0; m + 1 < nblk; ++m) {
                 const int64_t e0 = m * G::kBlock;
-                stage_block<T, S>(p, st, start + e0, G::kBlock, h, col, active, false);
+                stage_block<T, S, COLS>(p, st, start + e0, G::kBlock, h, col0, false);
                 for (int i = 0; i < G::kBlock; ++i) {
-                    storage_round<S>(p, e0 + i, hs);
-                    if (st.id[i] < p.nw) replay<S>(st, i, hs);
+                    storage_round<S, COLS>(p, e0 + i, hs);
+                    if (st.id[i] < p.nw) replay<S, COLS>(st, i, hs);
                 }
-                if (active) {
-                    float *ck = p.ckpt + ((slot0 + m + 1) * p.H + h) * stride_state + col;
+                float *ck = p.ckpt + ((slot0 + m + 1) * p.H + h) * stride_state;
 #pragma unroll
-                    for (int s = 0; s < S; ++s) ck[(int64_t)s * p.dv] = hs[s];
-                }
+                for (int s = 0; s < S; ++s)
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c)
+                        if (col0 + 32 * c < p.dv) ck[(int64_t)s * p.dv + col0 + 32 * c] = hs[s][c];
             }
         }
         for (int64_t m = nblk - 1; m >= 0; --m) {  // sweep 2: blocks in reverse
             if (m == 0) {
-                initial_column<S>(p, seq, h, col, active, hs);
+                initial_columns<S, COLS>(p, seq, h, col0, hs);
             } else {
-                const float *ck = p.ckpt + ((slot0 + m) * p.H + h) * stride_state + col;
+                const float *ck = p.ckpt + ((slot0 + m) * p.H + h) * stride_state;
 #pragma unroll
-                for (int s = 0; s < S; ++s) hs[s] = active ? ck[(int64_t)s * p.dv] : 0.f;
+                for (int s = 0; s < S; ++s)
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c)
+                        hs[s][c] = col0 + 32 * c < p.dv ? ck[(int64_t)s * p.dv + col0 + 32 * c] : 0.f;
             }
             const int64_t e0 = m * G::kBlock;
             const int blen = (int)min((int64_t)G::kBlock, L - e0);
             const int nsub = (blen + G::kSub - 1) / G::kSub;
-            stage_block<T, S>(p, st, start + e0, blen, h, col, active, true);
+            stage_block<T, S, COLS>(p, st, start + e0, blen, h, col0, true);
             for (int n = 0; n < nsub; ++n) {  // sub-checkpoints (lane-private shared memory)
 #pragma unroll
-                for (int s = 0; s < S; ++s) st.sub[n][s][lane] = hs[s];
+                for (int s = 0; s < S; ++s)
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c) st.sub[n][s][c][lane] = hs[s][c];
                 if (n == nsub - 1) break;
                 for (int j = 0; j < G::kSub; ++j) {
                     const int i = n * G::kSub + j;
-                    storage_round<S>(p, e0 + i, hs);
-                    if (st.id[i] < p.nw) replay<S>(st, i, hs);
+                    storage_round<S, COLS>(p, e0 + i, hs);
+                    if (st.id[i] < p.nw) replay<S, COLS>(st, i, hs);
                 }
             }
             for (int n = nsub - 1; n >= 0; --n) {
 #pragma unroll
-                for (int s = 0; s < S; ++s) hs[s] = st.sub[n][s][lane];
+                for (int s = 0; s < S; ++s)
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c) hs[s][c] = st.sub[n][s][c][lane];
                 const int slen = min(G::kSub, blen - n * G::kSub);
                 const int i0 = n * G::kSub;
-                float hist[G::kSub][S];
+                float hist[G::kSub][S][COLS];
 #pragma unroll
                 for (int j = 0; j < G::kSub; ++j) {
                     if (j < slen) {
-                        storage_round<S>(p, e0 + i0 + j, hs);
+                        storage_round<S, COLS>(p, e0 + i0 + j, hs);
 #pragma unroll
-                        for (int s = 0; s < S; ++s) hist[j][s] = hs[s];
-                        if (j + 1 < slen && st.id[i0 + j] < p.nw) replay<S>(st, i0 + j, hs);
+                        for (int s = 0; s < S; ++s)
+#pragma unroll
+                            for (int c = 0; c < COLS; ++c) hist[j][s][c] = hs[s][c];
+                        if (j + 1 < slen && st.id[i0 + j] < p.nw) replay<S, COLS>(st, i0 + j, hs);
                     }
                 }
 #pragma unroll
                 for (int j = G::kSub - 1; j >= 0; --j)
-                    if (j < slen) reverse_event<S>(p, st, i0 + j, hist[j], tile, h, col, active, dh);
+                    if (j < slen) reverse_event<S, COLS>(p, st, i0 + j, hist[j], tile, h, col0, dh);
             }
         }
     }
-    if (active) {
-        float *di = p.dinit + (seq * p.H + h) * stride_state + col;
+    float *di = p.dinit + (seq * p.H + h) * stride_state;
 #pragma unroll
-        for (int s = 0; s < S; ++s) di[(int64_t)s * p.dv] = dh[s];
-    }
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int c = 0; c < COLS; ++c)
+            if (col0 + 32 * c < p.dv) di[(int64_t)s * p.dv + col0 + 32 * c] = dh[s][c];
 }
 
-template <typename T, int S>
+template <typename T, int S, int COLS>
 int launch_scan_backward(const ScanBwdParams &p, cudaStream_t st) {
     if (p.units > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
-    scan_backward_kernel<T, S><<<(unsigned)p.units, 32, 0, st>>>(p);
+    scan_backward_kernel<T, S, COLS><<<(unsigned)p.units, 32, 0, st>>>(p);
     return launch_status();
 }
 
-int64_t block_events(int S) { return S == 4 ? BwdGeom<4>::kBlock : S == 8 ? BwdGeom<8>::kBlock : BwdGeom<16>::kBlock; }
+// Columns per lane: two for heads of 64 or more value columns with S <= 8 (one warp per
+// 64-column tile), else one.
+int scan_cols(int S, int dv) { return (S <= 8 && dv >= 64) ? 2 : 1; }
+
+int64_t block_events(int S, int dv) {
+    if (scan_cols(S, dv) == 2) return S == 4 ? BwdGeom<4, 2>::kBlock : BwdGeom<8, 2>::kBlock;
+    return S == 4 ? BwdGeom<4, 1>::kBlock : S == 8 ? BwdGeom<8, 1>::kBlock : BwdGeom<16, 1>::kBlock;
+}
+
+int scan_tiles(int S, int dv) { return (int)ceil_div(dv, 32 * scan_cols(S, dv)); }
+
 
 // ------------------------------------------------------------------ event VJP
 
@@ -415,6 +485,7 @@ __global__ void event_vjp_kernel(const VjpParams p) {
         accv[i] = accw[i] = 0.f;
     }
     float dk_acc = 0.f, db_acc = 0.f, dg_acc = 0.f, dq_acc = 0.f;
+#pragma unroll 4
     for (int j = 0; j < p.kw; ++j) {
         const int64_t id = t * p.kw + j;
         const float pw = ld_f(static_cast<const T *>(p.ww), id);
@@ -459,6 +530,7 @@ __global__ void event_vjp_kernel(const VjpParams p) {
         const float decs = warp_sum(dec);
         if (lane == 0) part_w[h][j] = rnd<T>(rnd<T>(wb + wv) + decs);
     }
+#pragma unroll 4
     for (int j = 0; j < p.kr; ++j) {
         const int64_t rid = t * p.kr + j;
         const int64_t id = p.nw + rid;
@@ -892,8 +964,13 @@ extern "C" int64_t bdm_scan_backward_checkpoint_bytes(int64_t batch, int64_t tim
         return -1;
     if (bank_size != 4 && bank_size != 8 && bank_size != 16) return -1;
     const int64_t E = batch * time * (kw + kr);
-    const int64_t slots = E / block_events(bank_size) + batch * bank_count + 1;
+    const int64_t slots = E / block_events(bank_size, head_value_width) + batch * bank_count + 1;
     return slots * heads * bank_size * head_value_width * (int64_t)sizeof(float);
+}
+
+extern "C" int bdm_scan_backward_tiles(int bank_size, int head_value_width) {
+    if ((bank_size != 4 && bank_size != 8 && bank_size != 16) || head_value_width <= 0) return -1;
+    return bdm::scan_tiles(bank_size, head_value_width);
 }
 
 extern "C" int bdm_scan_backward(const void *q, const void *k, const void *v, const float *g, const void *b,
@@ -924,15 +1001,16 @@ extern "C" int bdm_scan_backward(const void *q, const void *k, const void *v, co
     p.nseq = batch * bank_count; p.J = bank_count; p.nt = batch * time; p.nw = p.nt * kw;
     p.E = p.nt * (kw + kr);
     p.H = heads; p.dv = head_value_width; p.kw = kw; p.kr = kr; p.routed_decay = routed_decay;
-    p.interval = state_interval; p.tiles = (int)ceil_div(head_value_width, 32); p.scale = scale;
+    p.interval = state_interval; p.tiles = scan_tiles(bank_size, head_value_width); p.scale = scale;
     p.row_factor = row_factor; p.col_factor = col_factor; p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
     p.dread = d_read; p.ckpt = checkpoints; p.evg = event_grads; p.du = d_write_value; p.dinit = d_initial;
     p.units = p.nseq * heads * p.tiles;
     const cudaStream_t st = as_stream(stream);
+    const bool two = scan_cols(bank_size, head_value_width) == 2;
     BDM_DISPATCH_DTYPE(dtype, T, {
-        if (bank_size == 4) return launch_scan_backward<T, 4>(p, st);
-        if (bank_size == 8) return launch_scan_backward<T, 8>(p, st);
-        return launch_scan_backward<T, 16>(p, st);
+        if (bank_size == 4) return two ? launch_scan_backward<T, 4, 2>(p, st) : launch_scan_backward<T, 4, 1>(p, st);
+        if (bank_size == 8) return two ? launch_scan_backward<T, 8, 2>(p, st) : launch_scan_backward<T, 8, 1>(p, st);
+        return launch_scan_backward<T, 16, 1>(p, st);
     });
     return BDM_ERR_UNSUPPORTED;
 }
@@ -958,7 +1036,7 @@ extern "C" int bdm_event_vjp(const void *q, const void *k, const void *v, const 
     p.evg = event_grads; p.du = d_write_value;
     p.nt = ntok; p.nw = ntok * kw; p.E = ntok * (kw + kr);
     p.H = heads; p.dv = head_value_width; p.kw = kw; p.kr = kr; p.routed_decay = routed_decay;
-    p.tiles = (int)ceil_div(head_value_width, 32); p.scale = scale;
+    p.tiles = scan_tiles(bank_size, head_value_width); p.scale = scale;
     p.dq = dq; p.dk = dk; p.dv_out = dv; p.db = db; p.dw_out = dw; p.dww = d_write_w; p.drw = d_read_w; p.dg = dg;
     const cudaStream_t st = as_stream(stream);
     BDM_DISPATCH_DTYPE(dtype, T, {

@@ -475,15 +475,15 @@ def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, 
     """Recurrence backward over the dispatched events of a factor-initialised training forward.
 
     ``d_read`` [NT, H*dv] is the gradient of the combined read sum.  Returns
-    (event_grads [ceil(dv/32), E, H, 3S], d_write_value [NT*KW, H*dv], d_initial [B*J, H, S, dv]), FP32.
+    (event_grads [tiles, E, H, 3S], d_write_value [NT*KW, H*dv], d_initial [B*J, H, S, dv]), FP32.
     """
     _cuda(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read)
     dt, dev = q.dtype, q.device
     nt = batch * time
     e = nt * (kw + kr)
-    tiles = -(-head_value_width // 32)
     v_width = heads * head_value_width
     lib = _lib.load()
+    tiles = lib.bdm_scan_backward_tiles(bank_size, head_value_width)
     ck_bytes = lib.bdm_scan_backward_checkpoint_bytes(batch, time, kw, kr, bank_count, heads, bank_size,
                                                       head_value_width)
     if ck_bytes < 0:

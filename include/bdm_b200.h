@@ -233,7 +233,8 @@ BDM_API int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_id
  * bdm_scan_backward: the recurrence backward over the dispatched events (same
  *   inputs as bdm_bank_scan's factor-initialised training call, plus d_read
  *   [ntok, H*dv] = gradient of the combined read sum).  Outputs, FP32:
- *   event_grads [ceil(dv/32), E, H, 3*S] per-(event, head) column sums (per write event id:
+ *   event_grads [tiles, E, H, 3*S] per-(event, head) column sums (tiles =
+ *   bdm_scan_backward_tiles(S, dv)) (per write event id:
  *   sum_x dh*u | sum_x hd*du | sum_x dh'*hd; per read event id: sum_x h*do),
  *   d_write_value [ntok*kw, H*dv] (du per write event id) and d_initial
  *   [batch*J, H, S, dv].  checkpoints: bdm_scan_backward_checkpoint_bytes() bytes
@@ -261,6 +262,8 @@ BDM_API int bdm_norm_gate_backward(const void *d_out, const void *raw, int64_t n
                                    int64_t ld_gate, const void *norm_weight, const void *norm_bias, float eps,
                                    int norm_mode, int dtype, void *d_raw, void *d_gate, int64_t ld_d_gate,
                                    float *partials, float *d_norm_weight, float *d_norm_bias, void *stream);
+/* Column tiles of bdm_scan_backward's event_grads (its leading dimension); -1 if unsupported. */
+BDM_API int bdm_scan_backward_tiles(int bank_size, int head_value_width);
 BDM_API int64_t bdm_scan_backward_checkpoint_bytes(int64_t batch, int64_t time, int kw, int kr, int64_t bank_count,
                                                    int heads, int bank_size, int head_value_width);
 BDM_API int bdm_scan_backward(const void *q, const void *k, const void *v, const float *g, const void *b,

@@ -100,6 +100,10 @@ def test_backward_sizing_and_limits():
     small = lib.bdm_scan_backward_checkpoint_bytes(2, 64, 8, 8, 64, 1, 8, 32)
     assert 0 < small < lib.bdm_scan_backward_checkpoint_bytes(32, 2048, 8, 8, 512, 12, 8, 64)
     assert lib.bdm_scan_backward_checkpoint_bytes(2, 64, 8, 8, 64, 1, 6, 32) == -1   # bank_size 4, 8 or 16
+    # one warp per 64 value columns for S <= 8 and dv >= 64, else per 32
+    assert [lib.bdm_scan_backward_tiles(8, d) for d in (16, 32, 64, 128)] == [1, 1, 1, 2]
+    assert [lib.bdm_scan_backward_tiles(16, d) for d in (32, 64, 128)] == [1, 2, 4]
+    assert lib.bdm_scan_backward_tiles(6, 64) == -1
     assert lib.bdm_norm_gate_backward_partial_floats(33, 64) == 2 * 3 * 64
     assert lib.bdm_controllers_backward_partial_floats(65, 2, 8) == (2 * 2 + 1) * 16
     # more heads than a VJP CTA's warps, more selected banks than a route warp's lanes
