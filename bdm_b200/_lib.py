@@ -55,8 +55,8 @@ SIGNATURES = {
     'bdm_event_vjp': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int,
                              _int, _int, _flt, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'bdm_product_state_backward': (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp]),
-    'bdm_route_backward': (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _vp, _vp, _vp, _vp, _int, _vp, _i64,
-                                  _vp]),
+    'bdm_route_backward': (_int, [_vp, _i64, _i64, _i64, _i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _int, _vp,
+                                  _i64, _vp]),
     'bdm_controllers_backward_partial_floats': (_i64, [_i64, _int, _int]),
     'bdm_controllers_backward': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp,
                                         _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _vp, _i64,

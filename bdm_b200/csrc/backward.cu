@@ -143,7 +143,7 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
         st.id[i] = id;
         float *u = st.uni[i];
         if (id < p.nw) {
-            const int64_t tok = id / p.kw;
+            const int64_t tok = (uint32_t)id / (uint32_t)p.kw;  // event ids < 2^31 (checked on the host)
             const float pw = ld_f(static_cast<const T *>(p.ww), id);
             const int64_t base = (tok * p.H + h) * S;
 #pragma unroll
@@ -156,7 +156,7 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
             }
         } else {
             const int64_t rid = id - p.nw;
-            const int64_t base = (rid / p.kr * p.H + h) * S;
+            const int64_t base = ((int64_t)((uint32_t)rid / (uint32_t)p.kr) * p.H + h) * S;
             const float r = ld_f(static_cast<const T *>(p.rw), rid);
 #pragma unroll
             for (int s = 0; s < S; ++s) u[s] = rnd<T>(ld_f(static_cast<const T *>(p.q), base + s) * r);
@@ -167,7 +167,7 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
     for (int i = 0; i < n; ++i) {  // every lane over the events: its own columns
         const int64_t id = st.id[i];
         const bool wr = id < p.nw;
-        const int64_t row = wr ? id / p.kw * V : (id - p.nw) / p.kr * V;
+        const int64_t row = (int64_t)(wr ? (uint32_t)id / (uint32_t)p.kw : (uint32_t)(id - p.nw) / (uint32_t)p.kr) * V;
         const float pw = wr ? ld_f(static_cast<const T *>(p.ww), id) : 0.f;
 #pragma unroll
         for (int c = 0; c < COLS; ++c) {
@@ -442,26 +442,26 @@ struct VjpParams {
     const float *g;
     const void *b, *w, *ww, *rw;
     const float *evg, *du;
-    int64_t nt, nw, E;
+    int64_t nt, nw, E, items;
     int H, dv, kw, kr, routed_decay, tiles;
     float scale;
-    void *dq, *dk, *dv_out, *db, *dw_out, *dww, *drw;
+    void *dq, *dk, *dv_out, *db, *dw_out;
+    void *dww_h, *drw_h;  // [nt, H, kw] / [nt, H, kr] per-head route-weight gradients
     float *dg;
 };
 
-constexpr int kVjpMaxCols = 8;   // value columns per lane: head width <= 256
-constexpr int kVjpMaxSlots = 64;
+constexpr int kVjpWarps = 4;
 
-// One CTA per token, one warp per head.  Mirrors _vjp's per-token loop over the
-// write slots, then the read slots, with its rounding points; route-weight
-// gradients are per head (the reference runs one routed update per head) and
-// summed over heads in ascending order.
-template <typename T, int S>
-__global__ void event_vjp_kernel(const VjpParams p) {
-    __shared__ float part_w[32][kVjpMaxSlots];
-    __shared__ float part_r[32][kVjpMaxSlots];
-    const int64_t t = blockIdx.x;
-    const int h = (int)(threadIdx.x >> 5);
+// One warp per (token, head).  Mirrors _vjp's per-token loop over the write slots,
+// then the read slots, with its rounding points.  The route-weight gradients stay
+// per head (the reference runs one routed update per head); the router backward
+// sums them over heads.  CPL = value columns per lane (lane l: l, l+32, ...).
+template <typename T, int S, int CPL>
+__global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpParams p) {
+    const int64_t item = (int64_t)blockIdx.x * kVjpWarps + (threadIdx.x >> 5);
+    if (item >= p.items) return;
+    const int64_t t = item / p.H;
+    const int h = (int)(item % p.H);
     const int lane = (int)lane_id();
     const int dv = p.dv;
     const int64_t V = (int64_t)p.H * dv;
@@ -475,24 +475,27 @@ __global__ void event_vjp_kernel(const VjpParams p) {
         g0 = p.g[hs0 + lane];
         q0 = ld_f(static_cast<const T *>(p.q), hs0 + lane);
     }
-    float v0[kVjpMaxCols], w0[kVjpMaxCols], accv[kVjpMaxCols], accw[kVjpMaxCols];
+    const int64_t vrow = t * V + (int64_t)h * dv;
+    float v0[CPL], w0[CPL], accv[CPL], accw[CPL];
 #pragma unroll
-    for (int i = 0; i < kVjpMaxCols; ++i) {
+    for (int i = 0; i < CPL; ++i) {
         const int c = lane + 32 * i;
         const bool on = c < dv;
-        v0[i] = on ? ld_f(static_cast<const T *>(p.v), t * V + (int64_t)h * dv + c) : 0.f;
-        w0[i] = on ? ld_f(static_cast<const T *>(p.w), t * V + (int64_t)h * dv + c) : 0.f;
+        v0[i] = on ? ld_f(static_cast<const T *>(p.v), vrow + c) : 0.f;
+        w0[i] = on ? ld_f(static_cast<const T *>(p.w), vrow + c) : 0.f;
         accv[i] = accw[i] = 0.f;
     }
     float dk_acc = 0.f, db_acc = 0.f, dg_acc = 0.f, dq_acc = 0.f;
-#pragma unroll 4
+    T *dwwh = static_cast<T *>(p.dww_h) + (t * p.H + h) * p.kw;
+    T *drwh = static_cast<T *>(p.drw_h) + (t * p.H + h) * p.kr;
+#pragma unroll 2
     for (int j = 0; j < p.kw; ++j) {
         const int64_t id = t * p.kw + j;
         const float pw = ld_f(static_cast<const T *>(p.ww), id);
         float wvp = 0.f;
         const float *durow = p.du + id * V + (int64_t)h * dv;
 #pragma unroll
-        for (int i = 0; i < kVjpMaxCols; ++i) {
+        for (int i = 0; i < CPL; ++i) {
             const int c = lane + 32 * i;
             if (c < dv) {
                 const float du = durow[c];
@@ -503,7 +506,6 @@ __global__ void event_vjp_kernel(const VjpParams p) {
                 wvp += rnd<T>(dwe * w0[i]);
             }
         }
-        const float wv = rnd<T>(warp_sum(wvp));
         float wbp = 0.f, dec = 0.f;
         if (nl) {
             float A = 0.f, C = 0.f, Gs = 0.f;
@@ -526,11 +528,12 @@ __global__ void event_vjp_kernel(const VjpParams p) {
             }
             wbp = rnd<T>(dbe * b0);
         }
+        const float wv = rnd<T>(warp_sum(wvp));
         const float wb = rnd<T>(warp_sum(wbp));
         const float decs = warp_sum(dec);
-        if (lane == 0) part_w[h][j] = rnd<T>(rnd<T>(wb + wv) + decs);
+        if (lane == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
     }
-#pragma unroll 4
+#pragma unroll 2
     for (int j = 0; j < p.kr; ++j) {
         const int64_t rid = t * p.kr + j;
         const int64_t id = p.nw + rid;
@@ -544,8 +547,8 @@ __global__ void event_vjp_kernel(const VjpParams p) {
             dq_acc += rnd<T>(dqe * r);
             wrp = rnd<T>(dqe * q0);
         }
-        const float wr = rnd<T>(warp_sum(wrp));
-        if (lane == 0) part_r[h][j] = wr;
+        const float wr = warp_sum(wrp);
+        if (lane == 0) drwh[j] = Elem<T>::from_float(wr);
     }
     if (nl) {
         st_f(static_cast<T *>(p.dq), hs0 + lane, dq_acc);
@@ -554,24 +557,21 @@ __global__ void event_vjp_kernel(const VjpParams p) {
         p.dg[hs0 + lane] = dg_acc;
     }
 #pragma unroll
-    for (int i = 0; i < kVjpMaxCols; ++i) {
+    for (int i = 0; i < CPL; ++i) {
         const int c = lane + 32 * i;
         if (c < dv) {
-            st_f(static_cast<T *>(p.dv_out), t * V + (int64_t)h * dv + c, accv[i]);
-            st_f(static_cast<T *>(p.dw_out), t * V + (int64_t)h * dv + c, accw[i]);
+            st_f(static_cast<T *>(p.dv_out), vrow + c, accv[i]);
+            st_f(static_cast<T *>(p.dw_out), vrow + c, accw[i]);
         }
     }
-    __syncthreads();
-    for (int j = threadIdx.x; j < p.kw + p.kr; j += blockDim.x) {
-        const bool wr = j < p.kw;
-        const int jj = wr ? j : j - p.kw;
-        float s = wr ? part_w[0][jj] : part_r[0][jj];
-        for (int hh = 1; hh < p.H; ++hh) s = rnd<T>(s + (wr ? part_w[hh][jj] : part_r[hh][jj]));
-        if (wr)
-            st_f(static_cast<T *>(p.dww), t * p.kw + jj, s);
-        else
-            st_f(static_cast<T *>(p.drw), t * p.kr + jj, s);
-    }
+}
+
+template <typename T, int S>
+void launch_vjp(const VjpParams &p, int cpl, unsigned blocks, cudaStream_t st) {
+    if (cpl <= 1) event_vjp_kernel<T, S, 1><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+    else if (cpl == 2) event_vjp_kernel<T, S, 2><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+    else if (cpl <= 4) event_vjp_kernel<T, S, 4><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+    else event_vjp_kernel<T, S, 8><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
 }
 
 // ------------------------------------------------------- initial-state factors
@@ -613,9 +613,9 @@ struct RouteBwdParams {
     const void *logits;  // [ntok, ld] holding both blocks
     void *dlogits;       // [ntok, ldd]
     int64_t ntok, ld, ldd, first, second;
-    int j1, j2, count;
+    int j1, j2, count, heads;
     const int64_t *idx1, *idx2;
-    const void *dw1, *dw2;
+    const void *dw1, *dw2;  // [ntok, heads, count] per-head weight gradients
 };
 
 // One warp per (token, block).  Weights = softmax over the selected pair scores
@@ -633,7 +633,7 @@ __global__ void route_backward_kernel(const RouteBwdParams p) {
     const T *lg = static_cast<const T *>(p.logits) + t * p.ld + off;
     T *out = static_cast<T *>(p.dlogits) + t * p.ldd + off;
     const int64_t *idx = (blk ? p.idx2 : p.idx1) + t * p.count;
-    const T *dw = static_cast<const T *>(blk ? p.dw2 : p.dw1) + t * p.count;
+    const T *dw = static_cast<const T *>(blk ? p.dw2 : p.dw1) + t * p.heads * p.count;
     for (int i = lane; i < p.j1 + p.j2; i += 32) out[i] = Elem<T>::from_float(0.f);
     __syncwarp();
     const bool on = lane < p.count;
@@ -644,7 +644,8 @@ __global__ void route_backward_kernel(const RouteBwdParams p) {
         row = (int)(id / p.j2);
         colj = (int)(id % p.j2);
         val = rnd<T>(ld_f(lg, row) + ld_f(lg, p.j1 + colj));
-        dwc = ld_f(dw, lane);
+        dwc = ld_f(dw, lane);  // the heads' weight gradients, summed in ascending head order
+        for (int hh = 1; hh < p.heads; ++hh) dwc = rnd<T>(dwc + ld_f(dw, (int64_t)hh * p.count + lane));
     }
     const float m = warp_max(val);
     const float ex = on ? expf(val - m) : 0.f;
@@ -995,6 +996,7 @@ extern "C" int bdm_scan_backward(const void *q, const void *k, const void *v, co
         !event_grads || !d_write_value || !d_initial)
         return BDM_ERR_INVALID;
     if (!checkpoints || checkpoint_bytes < need) return BDM_ERR_WORKSPACE;
+    if (batch * time * (kw + kr) > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;  // 32-bit event ids in the kernel
     ScanBwdParams p{};
     p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w; p.ww = write_w; p.rw = read_w;
     p.order = order; p.cu = cu_seqlens;
@@ -1019,30 +1021,33 @@ extern "C" int bdm_event_vjp(const void *q, const void *k, const void *v, const 
                              const void *write_w, const void *read_w, const float *event_grads,
                              const float *d_write_value, int64_t ntok, int heads, int bank_size, int head_value_width,
                              int kw, int kr, int dtype, int routed_decay, float scale, void *dq, void *dk, void *dv,
-                             float *dg, void *db, void *dw, void *d_write_w, void *d_read_w, void *stream) {
+                             float *dg, void *db, void *dw, void *d_write_w_heads, void *d_read_w_heads,
+                             void *stream) {
     using namespace bdm;
     if (ntok < 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0) return BDM_ERR_INVALID;
     if (bank_size != 4 && bank_size != 8 && bank_size != 16) return BDM_ERR_UNSUPPORTED;
-    if (heads > 32 || head_value_width > 32 * kVjpMaxCols || kw > kVjpMaxSlots || kr > kVjpMaxSlots)
-        return BDM_ERR_UNSUPPORTED;
+    if (head_value_width > 256) return BDM_ERR_UNSUPPORTED;
     if (!valid_dtype(dtype)) return BDM_ERR_DTYPE;
     if (ntok == 0) return BDM_OK;
     if (!q || !k || !v || !g || !b || !w || !write_w || !read_w || !event_grads || !d_write_value || !dq || !dk ||
-        !dv || !dg || !db || !dw || !d_write_w || !d_read_w)
+        !dv || !dg || !db || !dw || !d_write_w_heads || !d_read_w_heads)
         return BDM_ERR_INVALID;
-    if (ntok > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
     VjpParams p{};
     p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w; p.ww = write_w; p.rw = read_w;
     p.evg = event_grads; p.du = d_write_value;
-    p.nt = ntok; p.nw = ntok * kw; p.E = ntok * (kw + kr);
+    p.nt = ntok; p.nw = ntok * kw; p.E = ntok * (kw + kr); p.items = ntok * heads;
     p.H = heads; p.dv = head_value_width; p.kw = kw; p.kr = kr; p.routed_decay = routed_decay;
     p.tiles = scan_tiles(bank_size, head_value_width); p.scale = scale;
-    p.dq = dq; p.dk = dk; p.dv_out = dv; p.db = db; p.dw_out = dw; p.dww = d_write_w; p.drw = d_read_w; p.dg = dg;
+    p.dq = dq; p.dk = dk; p.dv_out = dv; p.db = db; p.dw_out = dw; p.dww_h = d_write_w_heads;
+    p.drw_h = d_read_w_heads; p.dg = dg;
+    const int64_t blocks = ceil_div(p.items, kVjpWarps);
+    if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;
+    const int cpl = (int)ceil_div(head_value_width, 32);
     const cudaStream_t st = as_stream(stream);
     BDM_DISPATCH_DTYPE(dtype, T, {
-        if (bank_size == 4) event_vjp_kernel<T, 4><<<(unsigned)ntok, 32 * heads, 0, st>>>(p);
-        else if (bank_size == 8) event_vjp_kernel<T, 8><<<(unsigned)ntok, 32 * heads, 0, st>>>(p);
-        else event_vjp_kernel<T, 16><<<(unsigned)ntok, 32 * heads, 0, st>>>(p);
+        if (bank_size == 4) launch_vjp<T, 4>(p, cpl, (unsigned)blocks, st);
+        else if (bank_size == 8) launch_vjp<T, 8>(p, cpl, (unsigned)blocks, st);
+        else launch_vjp<T, 16>(p, cpl, (unsigned)blocks, st);
     });
     return launch_status();
 }
@@ -1070,11 +1075,11 @@ extern "C" int bdm_product_state_backward(const float *d_initial, int64_t batch,
 }
 
 extern "C" int bdm_route_backward(const void *logits, int64_t ntok, int64_t ld, int64_t first, int64_t second, int j1,
-                                  int j2, int count, const int64_t *idx_first, const void *dw_first,
+                                  int j2, int count, int heads, const int64_t *idx_first, const void *dw_first,
                                   const int64_t *idx_second, const void *dw_second, int dtype, void *d_logits,
                                   int64_t ldd, void *stream) {
     using namespace bdm;
-    if (ntok < 0 || j1 <= 0 || j2 <= 0 || count <= 0 || first < 0 || second < first + j1 + j2 ||
+    if (ntok < 0 || j1 <= 0 || j2 <= 0 || count <= 0 || heads <= 0 || first < 0 || second < first + j1 + j2 ||
         ld < second + j1 + j2 || ldd < second + j1 + j2)
         return BDM_ERR_INVALID;
     if (count > 32) return BDM_ERR_UNSUPPORTED;
@@ -1083,7 +1088,8 @@ extern "C" int bdm_route_backward(const void *logits, int64_t ntok, int64_t ld, 
     if (!logits || !idx_first || !dw_first || !idx_second || !dw_second || !d_logits) return BDM_ERR_INVALID;
     RouteBwdParams p{};
     p.logits = logits; p.dlogits = d_logits; p.ntok = ntok; p.ld = ld; p.ldd = ldd; p.first = first;
-    p.second = second; p.j1 = j1; p.j2 = j2; p.count = count; p.idx1 = idx_first; p.idx2 = idx_second;
+    p.second = second; p.j1 = j1; p.j2 = j2; p.count = count; p.heads = heads; p.idx1 = idx_first;
+    p.idx2 = idx_second;
     p.dw1 = dw_first; p.dw2 = dw_second;
     const int64_t blocks = ceil_div(2 * ntok, 8);
     if (blocks > 0x7fffffffLL) return BDM_ERR_UNSUPPORTED;

@@ -508,7 +508,8 @@ def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, 
 
 def event_vjp(q, k, v, g, b, w, write_w, read_w, event_grads, d_write_value, *, heads: int, bank_size: int,
               head_value_width: int, routed_decay: bool, scale: float):
-    """Token gradients from the event gradients: (dq, dk, dv, dg, db, dw, d_write_w, d_read_w)."""
+    """Token gradients from the event gradients: (dq, dk, dv, dg, db, dw, d_write_w, d_read_w), the route
+    weight gradients per head ([NT, H, KW] / [NT, H, KR]; ``route_backward`` sums them)."""
     _cuda(q, event_grads, d_write_value)
     dt, dev = q.dtype, q.device
     nt = q.shape[0]
@@ -517,7 +518,8 @@ def event_vjp(q, k, v, g, b, w, write_w, read_w, event_grads, d_write_value, *, 
     dq, dk, db = (torch.empty_like(q) for _ in range(3))
     dg = torch.empty_like(g)
     dv, dw = torch.empty_like(v), torch.empty_like(w)
-    dww, drw = torch.empty_like(ww), torch.empty_like(rw)
+    dww = torch.empty((nt, heads, kw), dtype=dt, device=dev)
+    drw = torch.empty((nt, heads, kr), dtype=dt, device=dev)
     _lib.check(_lib.load().bdm_event_vjp(
         _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(ww), _ptr(rw), _ptr(event_grads),
         _ptr(d_write_value), nt, heads, bank_size, head_value_width, kw, kr, dtype_code(dt), int(routed_decay),
@@ -542,16 +544,21 @@ def product_state_backward(d_initial, *, batch: int, rows_p: int, cols_q: int, f
 
 def route_backward(proj, first: int, second: int, idx_first, dw_first, idx_second, dw_second, d_proj, *,
                    bank_count: int, factors=None):
-    """Both routers' logit gradients into ``d_proj`` (blocks at columns ``first`` and ``second``)."""
+    """Both routers' logit gradients into ``d_proj`` (blocks at columns ``first`` and ``second``).
+
+    ``dw_*``: weight gradients [NT, count] or per head [NT, H, count] (summed over heads here).
+    """
     _cuda(proj, idx_first, dw_first, idx_second, dw_second, d_proj)
     j1, j2 = factors or near_square_factors(bank_count)
     nt = proj.shape[0]
     count = idx_first.shape[-1]
+    heads = dw_first.shape[1] if dw_first.ndim == 3 else 1
     i1, i2 = idx_first.reshape(nt, count).contiguous(), idx_second.reshape(nt, count).contiguous()
-    w1, w2 = (t.reshape(nt, count).to(proj.dtype).contiguous() for t in (dw_first, dw_second))
+    w1, w2 = (t.reshape(nt, heads, count).to(proj.dtype).contiguous() for t in (dw_first, dw_second))
     ld = proj.stride(0) if nt > 1 else proj.shape[1]
     ldd = d_proj.stride(0) if nt > 1 else d_proj.shape[1]
-    _lib.check(_lib.load().bdm_route_backward(_ptr(proj), nt, ld, first, second, j1, j2, count, _ptr(i1), _ptr(w1),
+    _lib.check(_lib.load().bdm_route_backward(_ptr(proj), nt, ld, first, second, j1, j2, count, heads, _ptr(i1),
+                                              _ptr(w1),
                                               _ptr(i2), _ptr(w2), dtype_code(proj.dtype), _ptr(d_proj), ldd,
                                               _stream(proj.device)), 'bdm_route_backward')
 

@@ -242,15 +242,17 @@ BDM_API int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_id
  * bdm_event_vjp: per-token gather of the event gradients (role_bank_dispatch.py:
  *   76-132 plus the routed-decay dp term of routed_update.py:43-47): dq, dk, db
  *   [ntok, H*S], dv, dw [ntok, H*dv] (dtype), dg [ntok, H*S] (float), and the route
- *   weight gradients d_write_w [ntok, kw], d_read_w [ntok, kr] (dtype; per head,
- *   summed over heads).  H <= 32, dv <= 256, kw, kr <= 64.
+ *   weight gradients of each head, d_write_w_heads [ntok, H, kw] and
+ *   d_read_w_heads [ntok, H, kr] (dtype; the reference runs one routed update per
+ *   head).  dv <= 256.
  * bdm_product_state_backward: d_initial [batch, P*Q, dv] -> d_rows [P*Q, dv]
  *   (per logical row, batch-summed) and the factor gradients d_row_factor [P, dv],
  *   d_col_factor [Q, dv] (FP32 holding factor-dtype values).
  * bdm_route_backward: both routers' backward over one projection [ntok, ld]:
  *   blocks at columns first and second (J1+J2 logits each), selections idx_* [ntok,
- *   count] and weight gradients dw_* [ntok, count] (dtype) -> d_logits blocks of
- *   [ntok, ldd] (every logit of both blocks written).  count <= 32.
+ *   count] and per-head weight gradients dw_* [ntok, heads, count] (dtype; summed
+ *   over heads in ascending order) -> d_logits blocks of [ntok, ldd] (every logit of
+ *   both blocks written).  count <= 32.
  * bdm_controllers_backward: q, k, v, b, w column blocks of d_proj [ntok, ldd]
  *   (dtype), df [ntok, H*S] (dtype; gradient of f_proj's output) and the FP32
  *   d_dt_bias [H*S], d_a_log [H], from the forward's proj, f, g, b, w and the
@@ -278,12 +280,13 @@ BDM_API int bdm_event_vjp(const void *q, const void *k, const void *v, const flo
                           const void *write_w, const void *read_w, const float *event_grads,
                           const float *d_write_value, int64_t ntok, int heads, int bank_size, int head_value_width,
                           int kw, int kr, int dtype, int routed_decay, float scale, void *dq, void *dk, void *dv,
-                          float *dg, void *db, void *dw, void *d_write_w, void *d_read_w, void *stream);
+                          float *dg, void *db, void *dw, void *d_write_w_heads, void *d_read_w_heads,
+                          void *stream);
 BDM_API int bdm_product_state_backward(const float *d_initial, int64_t batch, int64_t rows_p, int64_t cols_q,
                                        int head_value_width, int factor_dtype, float *d_rows, float *d_row_factor,
                                        float *d_col_factor, void *stream);
 BDM_API int bdm_route_backward(const void *logits, int64_t ntok, int64_t ld, int64_t first, int64_t second, int j1,
-                               int j2, int count, const int64_t *idx_first, const void *dw_first,
+                               int j2, int count, int heads, const int64_t *idx_first, const void *dw_first,
                                const int64_t *idx_second, const void *dw_second, int dtype, void *d_logits,
                                int64_t ldd, void *stream);
 BDM_API int64_t bdm_controllers_backward_partial_floats(int64_t ntok, int heads, int bank_size);

@@ -64,7 +64,7 @@ def test_dispatch_workspace_sizing():
                                       *([None] * 5), 0, None),                         # null inputs
     lambda lib: lib.bdm_event_vjp(*([None] * 10), 4, 1, 8, 32, 4, 4, 1, 1, 0.35, *([None] * 8), None),
     lambda lib: lib.bdm_product_state_backward(None, 2, 0, 4, 32, 1, None, None, None, None),
-    lambda lib: lib.bdm_route_backward(None, 4, 32, 0, 4, 4, 4, 4, None, None, None, None, 1, None, 32, None),
+    lambda lib: lib.bdm_route_backward(None, 4, 32, 0, 4, 4, 4, 4, 1, None, None, None, None, 1, None, 32, None),
     lambda lib: lib.bdm_controllers_backward(None, 4, 64, 0, 8, 16, 48, 56, None, 8, *([None] * 11), 1, 8, 32, 0,
                                              1, None, 64, None, None, None, None, None),  # col_w + V > ld
 ])
@@ -106,10 +106,10 @@ def test_backward_sizing_and_limits():
     assert lib.bdm_scan_backward_tiles(6, 64) == -1
     assert lib.bdm_norm_gate_backward_partial_floats(33, 64) == 2 * 3 * 64
     assert lib.bdm_controllers_backward_partial_floats(65, 2, 8) == (2 * 2 + 1) * 16
-    # more heads than a VJP CTA's warps, more selected banks than a route warp's lanes
-    assert lib.bdm_event_vjp(*([dummy] * 10), 4, 33, 8, 32, 4, 4, 1, 1, 0.35, *([dummy] * 8), None) \
+    # head value width above 8 columns per lane, more selected banks than a route warp's lanes
+    assert lib.bdm_event_vjp(*([dummy] * 10), 4, 2, 8, 512, 4, 4, 1, 1, 0.35, *([dummy] * 8), None) \
         == _lib.BDM_ERR_UNSUPPORTED
-    assert lib.bdm_route_backward(dummy, 4, 200, 0, 100, 10, 10, 40, dummy, dummy, dummy, dummy, 1, dummy, 200,
+    assert lib.bdm_route_backward(dummy, 4, 200, 0, 100, 10, 10, 40, 1, dummy, dummy, dummy, dummy, 1, dummy, 200,
                                   None) == _lib.BDM_ERR_UNSUPPORTED
     # checkpoint scratch below the required size
     assert lib.bdm_scan_backward(*([dummy] * 10), 2, 4, 16, 1, 8, 32, 4, 4, 1, 1, 0.35, None, None, 0, 0, 0, dummy,
