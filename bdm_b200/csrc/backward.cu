@@ -20,12 +20,13 @@
 // dk_e = A - b_e c, db_e = -k c, dg_e = G, dq_e = scale * o follow in the VJP.
 //
 // One warp per (sequence, head, tile of 32 or 64 columns), one or two columns per
-// lane, so a column's S rows stay in registers.  States come back by replay at three levels:
-// HBM checkpoints every kBlock events (written by a first forward sweep), shared-
-// memory sub-checkpoints every kSub events inside a block, and a register history
-// of the kSub states inside a sub-block, walked in reverse.  Each pass over a block
-// first stages the block's event controls in shared memory (all loads of the block
-// in flight at once), so the replay and reverse steps read only shared memory.
+// lane, so a column's S rows stay in registers.  A first forward sweep writes the
+// state to HBM every kBlock events; the reverse sweep takes the blocks last to
+// first: it replays a block from its checkpoint into a lane-private shared-memory
+// history of the state before each event, then walks the block backwards.  Each
+// pass over a block first stages the block's event controls in shared memory (all
+// of the block's loads in flight at once), so replay and reverse read only shared
+// memory, and the loops stay rolled (compact code, no instruction-cache misses).
 #include "common.cuh"
 
 namespace bdm {
@@ -111,22 +112,20 @@ struct ScanBwdParams {
 };
 
 template <int S, int COLS> struct BwdGeom {
-    static constexpr int kSub = 64 / (S * COLS);  // register history depth (64 floats per lane)
-    static constexpr int kNSub = 4;               // shared-memory sub-checkpoints per block
-    static constexpr int kBlock = kSub * kNSub;   // events between HBM checkpoints (staged together)
-    static constexpr int kRec = 3 * S;            // floats per (event, head) record
+    static constexpr int kBlock = 128 / (S * COLS);  // events between HBM checkpoints (16 KB of history)
+    static constexpr int kRec = 3 * S;               // floats per (event, head) record
     static constexpr int kRedW = Pow2Ceil<3 * S>::value;
-    static constexpr int kTileCols = 32 * COLS;   // value columns per warp (lane l: l, l+32, ...)
+    static constexpr int kTileCols = 32 * COLS;      // value columns per warp (lane l: l, l+32, ...)
 };
 
 // One block of events staged in shared memory by the warp that owns the unit:
 // lane-uniform rows [k | a | e] per event (a = dtype(b*p)*k, e = exp(g_e); a read
 // keeps q_e = dtype(q*r) in the k slot), the lane's column values per event
 // (write: dtype(w*p)*v; read: the output gradient), the event ids, and the
-// sub-block checkpoints (lane-private).
+// lane-private history of the states before each event of the block.
 template <int S, int COLS> struct BlockStage {
     using G = BwdGeom<S, COLS>;
-    float sub[G::kNSub][S][COLS][32];
+    float hist[G::kBlock][S][COLS][32];
     alignas(16) float uni[G::kBlock][3 * S];
     float col[G::kBlock][COLS][32];
     int64_t id[G::kBlock];
@@ -167,7 +166,8 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
     for (int i = 0; i < n; ++i) {  // every lane over the events: its own columns
         const int64_t id = st.id[i];
         const bool wr = id < p.nw;
-        const int64_t row = (int64_t)(wr ? (uint32_t)id / (uint32_t)p.kw : (uint32_t)(id - p.nw) / (uint32_t)p.kr) * V;
+        const int64_t row =
+            (int64_t)(wr ? (uint32_t)id / (uint32_t)p.kw : (uint32_t)(id - p.nw) / (uint32_t)p.kr) * V;
         const float pw = wr ? ld_f(static_cast<const T *>(p.ww), id) : 0.f;
 #pragma unroll
         for (int c = 0; c < COLS; ++c) {
@@ -186,38 +186,50 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
     __syncwarp();
 }
 
+// Replays events [0, n) of the staged block from hs.  With `save` the state before each
+// event (after its storage rounding) goes to the block history; `rpos` = position of
+// event 0 modulo the storage interval.
 template <int S, int COLS>
-__device__ __forceinline__ void replay(const BlockStage<S, COLS> &st, int i, float (&hs)[S][COLS]) {
-    // (the caller skips reads: they leave the state unchanged)
+__device__ __forceinline__ void replay_block(const ScanBwdParams &p, BlockStage<S, COLS> &st, int n, int rpos,
+                                             bool save, float (&hs)[S][COLS]) {
     const unsigned lane = lane_id();
-    const float *u = st.uni[i];
-    float er[COLS][2];
+#pragma unroll 1
+    for (int i = 0; i < n; ++i) {
+        if (p.interval > 0) {
+            if (rpos == 0) {
 #pragma unroll
-    for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = 0.f;
+                for (int s = 0; s < S; ++s)
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-        const float e = u[2 * S + s], a = u[S + s];
+                    for (int c = 0; c < COLS; ++c) hs[s][c] = bf16_round(hs[s][c]);
+            }
+            rpos = rpos + 1 == p.interval ? 0 : rpos + 1;
+        }
+        if (save) {
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+#pragma unroll
+                for (int c = 0; c < COLS; ++c) st.hist[i][s][c][lane] = hs[s][c];
+        }
+        if (st.id[i] >= p.nw) continue;  // reads leave the state unchanged
+        const float *u = st.uni[i];
+        float er[COLS][2];
+#pragma unroll
+        for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = 0.f;
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const float e = u[2 * S + s], a = u[S + s];
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) {
+                hs[s][c] *= e;
+                er[c][s & 1] = fmaf(a, hs[s][c], er[c][s & 1]);
+            }
+        }
 #pragma unroll
         for (int c = 0; c < COLS; ++c) {
-            hs[s][c] *= e;
-            er[c][s & 1] = fmaf(a, hs[s][c], er[c][s & 1]);
+            const float uu = st.col[i][c][lane] - (er[c][0] + er[c][1]);
+#pragma unroll
+            for (int s = 0; s < S; ++s) hs[s][c] = fmaf(u[s], uu, hs[s][c]);
         }
-    }
-#pragma unroll
-    for (int c = 0; c < COLS; ++c) {
-        const float uu = st.col[i][c][lane] - (er[c][0] + er[c][1]);
-#pragma unroll
-        for (int s = 0; s < S; ++s) hs[s][c] = fmaf(u[s], uu, hs[s][c]);
-    }
-}
-
-template <int S, int COLS>
-__device__ __forceinline__ void storage_round(const ScanBwdParams &p, int64_t e, float (&hs)[S][COLS]) {
-    if (p.interval > 0 && (int)e % p.interval == 0) {  // e < 2^31: events of one sequence
-#pragma unroll
-        for (int s = 0; s < S; ++s)
-#pragma unroll
-            for (int c = 0; c < COLS; ++c) hs[s][c] = bf16_round(hs[s][c]);
     }
 }
 
@@ -248,71 +260,74 @@ __device__ __forceinline__ void initial_columns(const ScanBwdParams &p, int64_t 
     }
 }
 
+// Reverse pass over events [0, n) of the staged block (descending), from the history.
 template <int S, int COLS>
-__device__ __forceinline__ void reverse_event(const ScanBwdParams &p, const BlockStage<S, COLS> &st, int i,
-                                              const float (&h0)[S][COLS], int tile, int h, int col0,
-                                              float (&dh)[S][COLS]) {
+__device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const BlockStage<S, COLS> &st, int n, int tile,
+                                              int h, int col0, float (&dh)[S][COLS]) {
     using G = BwdGeom<S, COLS>;
     const unsigned lane = lane_id();
-    const int64_t id = st.id[i];
-    const float *u = st.uni[i];
-    float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
-    if (id < p.nw) {
-        float hd[S][COLS], er[COLS][2], du[COLS][2], uu[COLS], dus[COLS];
+#pragma unroll 1
+    for (int i = n - 1; i >= 0; --i) {
+        const int64_t id = st.id[i];
+        const float *u = st.uni[i];
+        float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
+        if (id < p.nw) {
+            float hd[S][COLS], er[COLS][2], du[COLS][2], uu[COLS], dus[COLS];
 #pragma unroll
-        for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = du[c][0] = du[c][1] = 0.f;
+            for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = du[c][0] = du[c][1] = 0.f;
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
+            for (int s = 0; s < S; ++s) {
+#pragma unroll
+                for (int c = 0; c < COLS; ++c) {
+                    hd[s][c] = st.hist[i][s][c][lane] * u[2 * S + s];
+                    er[c][s & 1] = fmaf(u[S + s], hd[s][c], er[c][s & 1]);
+                    du[c][s & 1] = fmaf(dh[s][c], u[s], du[c][s & 1]);
+                }
+            }
 #pragma unroll
             for (int c = 0; c < COLS; ++c) {
-                hd[s][c] = h0[s][c] * u[2 * S + s];
-                er[c][s & 1] = fmaf(u[S + s], hd[s][c], er[c][s & 1]);
-                du[c][s & 1] = fmaf(dh[s][c], u[s], du[c][s & 1]);
+                uu[c] = st.col[i][c][lane] - (er[c][0] + er[c][1]);
+                dus[c] = du[c][0] + du[c][1];
             }
-        }
+            float red[G::kRedW];
 #pragma unroll
-        for (int c = 0; c < COLS; ++c) {
-            uu[c] = st.col[i][c][lane] - (er[c][0] + er[c][1]);
-            dus[c] = du[c][0] + du[c][1];
-        }
-        float red[G::kRedW];
+            for (int s = 0; s < S; ++s) {
+                float A = 0.f, C = 0.f, Gs = 0.f;
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
-            float A = 0.f, C = 0.f, Gs = 0.f;
+                for (int c = 0; c < COLS; ++c) {
+                    A = fmaf(dh[s][c], uu[c], A);
+                    C = fmaf(hd[s][c], dus[c], C);
+                    const float dp = fmaf(-u[S + s], dus[c], dh[s][c]);
+                    Gs = fmaf(dp, hd[s][c], Gs);
+                    dh[s][c] = dp * u[2 * S + s];
+                }
+                red[s] = A;
+                red[S + s] = C;
+                red[2 * S + s] = Gs;
+            }
+#pragma unroll
+            for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
 #pragma unroll
             for (int c = 0; c < COLS; ++c) {
-                A = fmaf(dh[s][c], uu[c], A);
-                C = fmaf(hd[s][c], dus[c], C);
-                const float dp = fmaf(-u[S + s], dus[c], dh[s][c]);
-                Gs = fmaf(dp, hd[s][c], Gs);
-                dh[s][c] = dp * u[2 * S + s];
+                const int cc = col0 + 32 * c;
+                if (cc < p.dv) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + cc] = dus[c];
             }
-            red[s] = A;
-            red[S + s] = C;
-            red[2 * S + s] = Gs;
-        }
+            reduce_store<G::kRedW>(red, 3 * S, rec);
+        } else {
+            float red[S];
 #pragma unroll
-        for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
+            for (int s = 0; s < S; ++s) {
+                float o = 0.f;
 #pragma unroll
-        for (int c = 0; c < COLS; ++c) {
-            const int cc = col0 + 32 * c;
-            if (cc < p.dv) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + cc] = dus[c];
-        }
-        reduce_store<G::kRedW>(red, 3 * S, rec);
-    } else {
-        float red[S];
-#pragma unroll
-        for (int s = 0; s < S; ++s) {
-            float o = 0.f;
-#pragma unroll
-            for (int c = 0; c < COLS; ++c) {
-                const float cv = st.col[i][c][lane];
-                o = fmaf(h0[s][c], cv, o);
-                dh[s][c] = fmaf(u[s] * cv, p.scale, dh[s][c]);
+                for (int c = 0; c < COLS; ++c) {
+                    const float cv = st.col[i][c][lane];
+                    o = fmaf(st.hist[i][s][c][lane], cv, o);
+                    dh[s][c] = fmaf(u[s] * cv, p.scale, dh[s][c]);
+                }
+                red[s] = o;
             }
-            red[s] = o;
+            reduce_store<S>(red, S, rec);
         }
-        reduce_store<S>(red, S, rec);
     }
 }
 
@@ -335,19 +350,18 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
 #pragma unroll
         for (int c = 0; c < COLS; ++c) dh[s][c] = 0.f;
     const int64_t stride_state = (int64_t)S * p.dv;
+    const int interval = p.interval > 0 ? p.interval : 1;
     if (L > 0) {
         const int64_t nblk = (L + G::kBlock - 1) / G::kBlock;
         const int64_t slot0 = start / G::kBlock + seq;  // disjoint slot ranges across sequences
         float hs[S][COLS];
         if (nblk > 1) {  // sweep 1: checkpoints at the starts of blocks 1 .. nblk-1
             initial_columns<S, COLS>(p, seq, h, col0, hs);
+#pragma unroll 1
             for (int64_t m = 0; m + 1 < nblk; ++m) {
                 const int64_t e0 = m * G::kBlock;
                 stage_block<T, S, COLS>(p, st, start + e0, G::kBlock, h, col0, false);
-                for (int i = 0; i < G::kBlock; ++i) {
-                    storage_round<S, COLS>(p, e0 + i, hs);
-                    if (st.id[i] < p.nw) replay<S, COLS>(st, i, hs);
-                }
+                replay_block<S, COLS>(p, st, G::kBlock, (int)(e0 % interval), false, hs);
                 float *ck = p.ckpt + ((slot0 + m + 1) * p.H + h) * stride_state;
 #pragma unroll
                 for (int s = 0; s < S; ++s)
@@ -356,6 +370,7 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
                         if (col0 + 32 * c < p.dv) ck[(int64_t)s * p.dv + col0 + 32 * c] = hs[s][c];
             }
         }
+#pragma unroll 1
         for (int64_t m = nblk - 1; m >= 0; --m) {  // sweep 2: blocks in reverse
             if (m == 0) {
                 initial_columns<S, COLS>(p, seq, h, col0, hs);
@@ -369,43 +384,9 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
             }
             const int64_t e0 = m * G::kBlock;
             const int blen = (int)min((int64_t)G::kBlock, L - e0);
-            const int nsub = (blen + G::kSub - 1) / G::kSub;
             stage_block<T, S, COLS>(p, st, start + e0, blen, h, col0, true);
-            for (int n = 0; n < nsub; ++n) {  // sub-checkpoints (lane-private shared memory)
-#pragma unroll
-                for (int s = 0; s < S; ++s)
-#pragma unroll
-                    for (int c = 0; c < COLS; ++c) st.sub[n][s][c][lane] = hs[s][c];
-                if (n == nsub - 1) break;
-                for (int j = 0; j < G::kSub; ++j) {
-                    const int i = n * G::kSub + j;
-                    storage_round<S, COLS>(p, e0 + i, hs);
-                    if (st.id[i] < p.nw) replay<S, COLS>(st, i, hs);
-                }
-            }
-            for (int n = nsub - 1; n >= 0; --n) {
-#pragma unroll
-                for (int s = 0; s < S; ++s)
-#pragma unroll
-                    for (int c = 0; c < COLS; ++c) hs[s][c] = st.sub[n][s][c][lane];
-                const int slen = min(G::kSub, blen - n * G::kSub);
-                const int i0 = n * G::kSub;
-                float hist[G::kSub][S][COLS];
-#pragma unroll
-                for (int j = 0; j < G::kSub; ++j) {
-                    if (j < slen) {
-                        storage_round<S, COLS>(p, e0 + i0 + j, hs);
-#pragma unroll
-                        for (int s = 0; s < S; ++s)
-#pragma unroll
-                            for (int c = 0; c < COLS; ++c) hist[j][s][c] = hs[s][c];
-                        if (j + 1 < slen && st.id[i0 + j] < p.nw) replay<S, COLS>(st, i0 + j, hs);
-                    }
-                }
-#pragma unroll
-                for (int j = G::kSub - 1; j >= 0; --j)
-                    if (j < slen) reverse_event<S, COLS>(p, st, i0 + j, hist[j], tile, h, col0, dh);
-            }
+            replay_block<S, COLS>(p, st, blen, (int)(e0 % interval), true, hs);
+            reverse_block<S, COLS>(p, st, blen, tile, h, col0, dh);
         }
     }
     float *di = p.dinit + (seq * p.H + h) * stride_state;
