@@ -12,6 +12,8 @@ layer at N = 1, the bank-sharded forward (bdm_b200.sharded, NCCL all-gather /
 reduce-scatter) at N > 1.  Its total work is fixed, so it scales strongly.
 ``train``: one layer's forward + backward at the c5 layer geometry (batch 32 x
 2048 split over the ranks, gradients all-reduced over NCCL at N > 1).
+``c5``: a full training step (forward, backward, AdamW) of the 12-layer BDM
+language model, batch 32 x 2048 split over the ranks, DDP over NCCL at N > 1.
 
 Timed region (value): K forward steps of the public module call
 ``layer(hidden)`` with the input already in HBM; an L2 flush (256 MiB write)
@@ -52,6 +54,9 @@ C5 = dict(dim=768, bank_count=512, bank_size=8, selected_banks=8, value_width=76
 C5_BATCH, C5_TIME = 32, 2048
 C5_METRIC = ('BDM layer training step (forward + backward) tokens/sec, c5 layer geometry (batch 32 x seq 2048, '
              'd_model 768, H=12, J=512, S=8, B=8, d_v=64)')
+C5_LM = dict(vocab_size=32000, layers=12)
+C5_LM_METRIC = ('BDM language-model training tokens/sec (c5: 12 layers, d_model 768, 12 heads, vocab 32000, '
+                'J=512, S=8, B=8, d_v=64, SwiGLU; batch 32 x seq 2048, data parallel)')
 C4_METRIC = ('BDM layer prefill tokens/sec, bank-sharded large memory (c4: batch 16 x seq 8192, d_model 2048, '
              'H=16, J=16384, S=16, B=16, d_v=128, Zipf(1.1) bank popularity)')
 METRIC = 'BDM layer prefill tokens/sec (c2: batch 8 x seq 4096, d_model 1024, H=8, J=256, S=8, B=8, d_v=128)'
@@ -371,6 +376,11 @@ def run_ours(args, world, rank, local):
             line['train'] = run_train(dev, rank, world, args)
         except Exception as e:  # keep the headline line even if the extra workload fails
             line['train'] = {'error': repr(e)[:300]}
+    if not args.skip_c5:
+        try:
+            line['c5'] = run_c5(dev, rank, world, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['c5'] = {'error': repr(e)[:300]}
     if rank == 0 and world == 1 and not args.skip_cpu:
         tps, dt, threads = cpu_forward_sample(C2_BATCH, args.cpu_time)
         line['cpu_baseline'] = {'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
@@ -514,6 +524,80 @@ def run_train(dev, rank, world, args):
             'clocks': clocks.summary()}
 
 
+def run_c5(dev, rank, world, args):
+    """c5: one training step (forward, backward, fused AdamW) of the 12-layer BDM language model in BF16,
+    the global batch of uniform-random token ids split over the ranks; DDP (NCCL) at N > 1."""
+    from bdm_b200 import BSDMConfig, _lib
+    from bdm_b200.lm import BDMLanguageModel, LanguageModelConfig
+    batch = args.c5_batch
+    if batch % world:
+        return {'skipped': f'batch {batch} does not split over {world} ranks'}
+    lib = _lib.load()
+    rows = batch // world
+    cfg = LanguageModelConfig(memory=BSDMConfig(**C5), vocab_size=C5_LM['vocab_size'], layers=C5_LM['layers'],
+                              seed=4)
+    model = BDMLanguageModel(cfg).to(torch.bfloat16).to(dev)
+    params = sum(p.numel() for p in model.parameters())
+    gemm_params = sum(m.weight.numel() for m in model.modules() if isinstance(m, torch.nn.Linear))
+    net = model
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[dev.index])
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True)
+    gen = torch.Generator(device=dev).manual_seed(4000 + rank)
+    tokens = torch.randint(0, cfg.vocab_size, (rows, C5_TIME + 1), generator=gen, device=dev)
+    inp, tgt = tokens[:, :-1].contiguous(), tokens[:, 1:].contiguous()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    steps = args.c5_steps
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        loss = net(inp, tgt)
+        loss.backward()
+        opt.step()
+        return loss
+
+    clocks = ClockSampler(dev.index).start()
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = lib.bdm_kernel_launches()
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        loss = step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    clocks.stop()
+    launches = lib.bdm_kernel_launches() - launches0
+    barrier(world)
+    ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)), world) / steps
+    tokens_step = batch * C5_TIME
+    _, bf16_peak, peak_kind = load_peaks()
+    dense_flops = 6 * gemm_params * tokens_step  # every GEMM weight: forward + two backward products
+    floor_ms = dense_flops / world / (bf16_peak * 1e12) * 1000
+    out = {'metric': C5_LM_METRIC, 'value': tokens_step / (ms / 1000), 'unit': 'tokens/s', 'n_gpus': world,
+           'steps': steps, 'warmup': 2, 'ms_per_step': ms, 'scaling': 'strong', 'dtype': 'bf16',
+           'loss': float(loss.item()),
+           'path': 'bdm_b200.lm.BDMLanguageModel (B200 BDM layers, cuBLAS SwiGLU/head), fused AdamW'
+                   + (', DistributedDataParallel over NCCL' if world > 1 else ''),
+           'config': {'workload': 'c5: 12 x BSDMConfig(dim=768, bank_count=512, bank_size=8, selected_banks=8, '
+                                  'value_width=768, num_heads=12) + SwiGLU FFN, vocab 32000, seed 4, random init',
+                      'parameters': params, 'global_batch': batch, 'seq_len': C5_TIME, 'rows_per_rank': rows,
+                      'data': 'uniform-random token ids (seed 4000 + rank), next-token targets',
+                      'l2': 'working set larger than L2; 256 MiB flush between steps'},
+           'gpu_launches': int(launches),
+           'roofline': {'bound': 'tensor', 'what': '6 x GEMM parameters x tokens at the measured bf16 peak',
+                        'dense_floor_ms': floor_ms, 'peak': bf16_peak, 'unit': 'TFLOP/s', 'peak_source': peak_kind,
+                        'achieved': dense_flops / world / (ms / 1000) / 1e12, 'frac': floor_ms / ms},
+           'clocks': clocks.summary()}
+    del net, model, opt
+    return out
+
+
 def c4_hidden(rows, dev):
     """c4 input rows: row b of the global batch is N(0,1) from seed 3000 + b, for any rank count."""
     out = torch.empty(len(rows), C4_TIME, C4['dim'], dtype=torch.bfloat16, device=dev)
@@ -606,6 +690,9 @@ def main():
     ap.add_argument('--c4-steps', type=int, default=5)
     ap.add_argument('--c4-ownership', choices=('balanced', 'contiguous'), default='balanced')
     ap.add_argument('--skip-train', action='store_true')
+    ap.add_argument('--skip-c5', action='store_true')
+    ap.add_argument('--c5-steps', type=int, default=2)
+    ap.add_argument('--c5-batch', type=int, default=32, help='c5 global batch (32 is the benchmark)')
     ap.add_argument('--train-steps', type=int, default=3)
     ap.add_argument('--train-batch', type=int, default=C5_BATCH, help='c5 batch (32 is the benchmark)')
     args = ap.parse_args()

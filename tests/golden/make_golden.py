@@ -19,6 +19,8 @@ Fixtures:
   layer_*.pt    BlockSparseDeltaMemory(backend='reference').forward on small
                 configs (FP32 and BF16, H=1 and H=2) with their state_dicts,
                 controller tensors and router logits; plus c1 at T=64.
+  lm_small.pt   BDMLanguageModel(backend='reference') at a small geometry: its seeded
+                initial state_dict, and the loss and gradients of one training step.
   grad_*.pt     torch autograd through the same reference forward (backend='reference'):
                 the gradients of every parameter and of the input for a seeded
                 output cotangent, on BSDMConfig (routed decay, 'nvidia' q/k norm,
@@ -37,7 +39,7 @@ sys.path.insert(0, REF)
 
 from bdm.gdn2_banks import (pack_bank_events, product_key_route, reference_packed_gdn2,  # noqa: E402
                             scatter_bank_outputs, serial_banked_gdn2)
-from bdm import BankedDeltaMemory, BDMConfig  # noqa: E402
+from bdm import BankedDeltaMemory, BDMConfig, BDMLanguageModel, LanguageModelConfig  # noqa: E402
 from bsdm import BlockSparseDeltaMemory, BSDMConfig  # noqa: E402
 
 
@@ -180,6 +182,27 @@ def make_grad(name, cls, cfg, batch, time, dtype, seed=0, x_seed=0):
                os.path.join(HERE, f'grad_{name}.pt'))
 
 
+def make_lm():
+    """Small LM: seeded initial parameters, loss and gradients of one step (FP32, FP32 state storage)."""
+    mem = BSDMConfig(dim=64, bank_count=64, bank_size=8, selected_banks=4, value_width=32, num_heads=2,
+                     training_state_dtype='float32')
+    cfg = LanguageModelConfig(memory=mem, vocab_size=96, layers=2, seed=1)
+    m = BDMLanguageModel(cfg, backend='reference')
+    init = {k: v.detach().clone() for k, v in m.state_dict().items()}
+    gen = torch.Generator().manual_seed(44)
+    tokens = torch.randint(0, cfg.vocab_size, (2, 24), generator=gen)
+    target = torch.randint(0, cfg.vocab_size, (2, 24), generator=gen)
+    loss = m(tokens, target)
+    loss.backward()
+    grads = {n: p.grad.detach().clone() for n, p in m.named_parameters() if p.grad is not None}
+    mem_dict = {k: getattr(mem, k) for k in mem.__dataclass_fields__}
+    torch.save(dict(memory=mem_dict, vocab_size=cfg.vocab_size, layers=cfg.layers, seed=cfg.seed,
+                    ffn_multiple_of=cfg.ffn_multiple_of, state_dict=init, tokens=tokens, target=target,
+                    loss=loss.detach(), grads=grads,
+                    source='bdm.BDMLanguageModel(backend="reference"): init, cross-entropy loss and its gradients'),
+               os.path.join(HERE, 'lm_small.pt'))
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     torch.save(dict(cases=_route_cases(), source='bdm.gdn2_banks.product_key_route'), os.path.join(HERE, 'router.pt'))
@@ -198,6 +221,7 @@ def main():
                torch.float32, seed=3)
     c1 = BSDMConfig(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=64, num_heads=1)
     make_layer('c1_t64', c1, 2, 64, torch.float32, seed=0, x_seed=0, factor_std=0.02 / 2 ** 0.5)
+    make_lm()
     make_grad('h1_fp32_state32', BlockSparseDeltaMemory,
               BSDMConfig(**small, num_heads=1, training_state_dtype='float32'), 2, 40, torch.float32, seed=1)
     make_grad('h2_fp32_state32', BlockSparseDeltaMemory,
