@@ -129,6 +129,7 @@ template <int S, int COLS> struct BlockStage {
     alignas(16) float uni[G::kBlock][3 * S];
     float col[G::kBlock][COLS][32];
     int64_t id[G::kBlock];
+    int tok[G::kBlock];
 };
 
 template <typename T, int S, int COLS>
@@ -143,6 +144,7 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
         float *u = st.uni[i];
         if (id < p.nw) {
             const int64_t tok = (uint32_t)id / (uint32_t)p.kw;  // event ids < 2^31 (checked on the host)
+            st.tok[i] = (int)tok;
             const float pw = ld_f(static_cast<const T *>(p.ww), id);
             const int64_t base = (tok * p.H + h) * S;
 #pragma unroll
@@ -153,9 +155,11 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
                 u[S + s] = rnd<T>(ld_f(static_cast<const T *>(p.b), base + s) * pw) * kk;
                 u[2 * S + s] = expf(p.routed_decay ? gg * pw : gg);
             }
-        } else {
+        } else if (want_dout) {  // reads matter only to the reverse pass
             const int64_t rid = id - p.nw;
-            const int64_t base = ((int64_t)((uint32_t)rid / (uint32_t)p.kr) * p.H + h) * S;
+            const int rtok = (int)((uint32_t)rid / (uint32_t)p.kr);
+            st.tok[i] = rtok;
+            const int64_t base = ((int64_t)rtok * p.H + h) * S;
             const float r = ld_f(static_cast<const T *>(p.rw), rid);
 #pragma unroll
             for (int s = 0; s < S; ++s) u[s] = rnd<T>(ld_f(static_cast<const T *>(p.q), base + s) * r);
@@ -166,8 +170,8 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
     for (int i = 0; i < n; ++i) {  // every lane over the events: its own columns
         const int64_t id = st.id[i];
         const bool wr = id < p.nw;
-        const int64_t row =
-            (int64_t)(wr ? (uint32_t)id / (uint32_t)p.kw : (uint32_t)(id - p.nw) / (uint32_t)p.kr) * V;
+        if (!wr && !want_dout) continue;
+        const int64_t row = (int64_t)st.tok[i] * V;
         const float pw = wr ? ld_f(static_cast<const T *>(p.ww), id) : 0.f;
 #pragma unroll
         for (int c = 0; c < COLS; ++c) {
