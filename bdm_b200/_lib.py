@@ -39,7 +39,7 @@ SIGNATURES = {
     'bdm_bank_scan_workspace_bytes': (_i64, [_i64, _i64]),
     'bdm_bank_scan': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int,
                              _int, _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _vp, _i64, _int, _int, _vp,
-                             _int, _int, _int, _vp, _vp, _i64, _vp]),
+                             _int, _int, _int, _vp, _vp, _i64, _vp, _int, _vp]),
     'bdm_combine_norm_gate': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _int, _vp,
                                      _vp]),
     'bdm_combine_norm_gate_save': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _int,
@@ -48,10 +48,11 @@ SIGNATURES = {
     'bdm_norm_gate_backward': (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _vp, _vp, _i64,
                                       _vp, _vp, _vp, _vp]),
     'bdm_scan_backward_tiles': (_int, [_int, _int]),
+    'bdm_scan_backward_block_events': (_int, [_int, _int]),
     'bdm_scan_backward_checkpoint_bytes': (_i64, [_i64, _i64, _int, _int, _i64, _int, _int, _int]),
     'bdm_scan_backward': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _int,
                                  _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _int, _vp, _vp, _vp, _vp, _vp,
-                                 _i64, _vp]),
+                                 _i64, _int, _vp]),
     'bdm_event_vjp': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int,
                              _int, _int, _flt, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     'bdm_product_state_backward': (_int, [_vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp]),

@@ -109,7 +109,10 @@ struct ScanBwdParams {
     float *evg;         // [tiles, E, H, 3S] per-(event, head) column sums (A | c | G; o for reads)
     float *du;          // [nt*kw, H*dv] write-event du per column
     float *dinit;       // [nseq, H, S, dv] gradient of each sequence's initial state
+    int ckpt_ready;     // the forward recurrence wrote the block checkpoints (sequences < kLongSeq events)
 };
+
+constexpr int64_t kLongSeq = 2048;  // the forward's long-sequence kernel (>= this many events) writes none
 
 template <int S, int COLS> struct BwdGeom {
     static constexpr int kBlock = 128 / (S * COLS);  // events between HBM checkpoints (16 KB of history)
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
         const int64_t nblk = (L + G::kBlock - 1) / G::kBlock;
         const int64_t slot0 = start / G::kBlock + seq;  // disjoint slot ranges across sequences
         float hs[S][COLS];
-        if (nblk > 1) {  // sweep 1: checkpoints at the starts of blocks 1 .. nblk-1
+        if (nblk > 1 && (!p.ckpt_ready || L >= kLongSeq)) {  // sweep 1: checkpoints at blocks 1 .. nblk-1
             initial_columns<S, COLS>(p, seq, h, col0, hs);
 #pragma unroll 1
             for (int64_t m = 0; m + 1 < nblk; ++m) {
@@ -954,6 +957,11 @@ extern "C" int64_t bdm_scan_backward_checkpoint_bytes(int64_t batch, int64_t tim
     return slots * heads * bank_size * head_value_width * (int64_t)sizeof(float);
 }
 
+extern "C" int bdm_scan_backward_block_events(int bank_size, int head_value_width) {
+    if ((bank_size != 4 && bank_size != 8 && bank_size != 16) || head_value_width <= 0) return -1;
+    return (int)bdm::block_events(bank_size, head_value_width);
+}
+
 extern "C" int bdm_scan_backward_tiles(int bank_size, int head_value_width) {
     if ((bank_size != 4 && bank_size != 8 && bank_size != 16) || head_value_width <= 0) return -1;
     return bdm::scan_tiles(bank_size, head_value_width);
@@ -966,7 +974,7 @@ extern "C" int bdm_scan_backward(const void *q, const void *k, const void *v, co
                                  float scale, const void *row_factor, const void *col_factor, int64_t factor_cols,
                                  int factor_dtype, int state_interval, const void *d_read, float *event_grads,
                                  float *d_write_value, float *d_initial, float *checkpoints, int64_t checkpoint_bytes,
-                                 void *stream) {
+                                 int checkpoints_ready, void *stream) {
     using namespace bdm;
     if (batch < 0 || time < 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0 ||
         state_interval < 0)
@@ -991,6 +999,7 @@ extern "C" int bdm_scan_backward(const void *q, const void *k, const void *v, co
     p.interval = state_interval; p.tiles = scan_tiles(bank_size, head_value_width); p.scale = scale;
     p.row_factor = row_factor; p.col_factor = col_factor; p.factor_cols = factor_cols; p.factor_dtype = factor_dtype;
     p.dread = d_read; p.ckpt = checkpoints; p.evg = event_grads; p.du = d_write_value; p.dinit = d_initial;
+    p.ckpt_ready = checkpoints_ready;
     p.units = p.nseq * heads * p.tiles;
     const cudaStream_t st = as_stream(stream);
     const bool two = scan_cols(bank_size, head_value_width) == 2;

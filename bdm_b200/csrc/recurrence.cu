@@ -76,6 +76,11 @@ struct ScanParams {
     int ws_classes;            // length classes run by warp-specialised CTAs (0: none)
     int64_t ws_ctas;           // CTAs [0, ws_ctas) run those units
     int64_t nseq;
+    // Training: the state before every ckpt_block-th event of a sequence (position > 0) is
+    // written to ckpt[(start / ckpt_block + seq + pos / ckpt_block), head, S, dv] for the
+    // recurrence backward (short-kernel sequences only; null / 0 when off).
+    float *ckpt;
+    int ckpt_block;
 };
 
 // Length classes of the work list (events per sequence, lower bounds), longest first.
@@ -274,7 +279,8 @@ __device__ __forceinline__ void load_initial_state(const ScanParams &p, int64_t 
 template <typename T, int S, int NC>
 __device__ __forceinline__ void event_step(const float2 *row, bool round_point, bool is_write, bool is_read,
                                            bool active, const Row<T, NC> &vr, const Row<T, NC> &wr, float scale,
-                                           T *out_row, float2 (&N)[S][NC / 2]) {
+                                           T *out_row, float2 (&N)[S][NC / 2], bool ck_point = false,
+                                           float *ck_row = nullptr, int64_t ck_stride = 0) {
     using Ctl = CtlLayout<S>;
     constexpr int NP = NC / 2;
     constexpr int NCH = NP >= 2 ? 2 : 4;
@@ -285,6 +291,19 @@ __device__ __forceinline__ void event_step(const float2 *row, bool round_point, 
 #pragma unroll
             for (int c = 0; c < NP; ++c) N[s][c] = bf16_round_pair(__fmul2_rn(N[s][c], d2));
         }
+    } else if (ck_point) {  // checkpoint only: materialise
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const float2 d2 = row[Ctl::dprev + s];
+#pragma unroll
+            for (int c = 0; c < NP; ++c) N[s][c] = __fmul2_rn(N[s][c], d2);
+        }
+    }
+    if (ck_point && active) {  // the state before this event, for the recurrence backward
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+#pragma unroll
+            for (int c = 0; c < NP; ++c) store_pair<float>(ck_row + (int64_t)s * ck_stride + 2 * c, N[s][c]);
     }
     const float4 *crow = reinterpret_cast<const float4 *>(row + Ctl::c);
     if (is_write) {
@@ -352,7 +371,9 @@ __device__ __forceinline__ void event_step(const float2 *row, bool round_point, 
 // Short sequences: one warp per (sequence, head, column tile) unit, kScanWarps
 // units per CTA; each warp stages and runs its own batches.  Takes the length
 // classes from p.ws_classes on (all of them when the long kernel does not run).
-template <typename T, int S, int NC>
+// CK: the launch writes the recurrence backward's state checkpoints (training forwards only;
+// the inference instantiation keeps none of that code).
+template <typename T, int S, int NC, bool CK>
 __global__ void __launch_bounds__(kScanWarps * 32, BDM_SCAN_MIN_BLOCKS)
 bank_scan_kernel(const ScanParams p) {
     constexpr int NP = NC / 2;
@@ -470,11 +491,12 @@ bank_scan_kernel(const ScanParams p) {
     // pos0 = position of the batch's first event in its sequence.  Sets the
     // number of events to run (<= bn, cut where the log-decay range ends), the
     // storage-point mask, and returns the write mask.
-    auto stage_finish = [&](int64_t pos0, int bn, int &n_out, unsigned &round_out) -> unsigned {
+    auto stage_finish = [&](int64_t pos0, int bn, int &n_out, unsigned &round_out, unsigned &ck_out) -> unsigned {
         cp_async_wait_all();
         const bool valid = lane < bn;
         const int64_t pos = pos0 + lane;
         const bool head = valid && p.interval > 0 && pos > 0 && (pos % p.interval) == 0;
+        const bool ckp = CK && valid && pos > 0 && (pos % p.ckpt_block) == 0;
         const T *rk = reinterpret_cast<const T *>(raw[lane] + Raw::kOff);
         const float *rg = reinterpret_cast<const float *>(raw[lane] + Raw::gOff);
         // segmented inclusive scan of log-decays; segments start at lane 0 and at storage points
@@ -485,7 +507,7 @@ bank_scan_kernel(const ScanParams p) {
             if (my_write && my_tok >= 0) ge = fmaxf(p.routed_decay ? rg[s] * my_wt : rg[s], kMinLogDecay);
             L[s] = ge;
         }
-        bool f = head || lane == 0;
+        bool f = head || ckp || lane == 0;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
             const bool fu = __shfl_up_sync(0xffffffffu, f, d);
@@ -527,7 +549,7 @@ bank_scan_kernel(const ScanParams p) {
 #pragma unroll
         for (int s = 0; s < S; ++s) {
             const float before = __shfl_up_sync(0xffffffffu, D[s], 1);
-            if (use && head) ctl[lane][Ctl::dprev + s] = dup(lane == 0 ? 1.0f : before);
+            if (use && (head || ckp)) ctl[lane][Ctl::dprev + s] = dup(lane == 0 ? 1.0f : before);
             if (lane == n - 1) dend[s] = dup(D[s]);
         }
         if (lane < EB) {
@@ -536,18 +558,19 @@ bank_scan_kernel(const ScanParams p) {
         }
         n_out = n;
         round_out = __ballot_sync(0xffffffffu, use && head);
+        ck_out = __ballot_sync(0xffffffffu, use && ckp);
         const unsigned wm = __ballot_sync(0xffffffffu, use && my_write && my_tok >= 0);
         __syncwarp();
         return wm;
     };
 
     int n = 0;
-    unsigned wmask = 0, rmask = 0;
+    unsigned wmask = 0, rmask = 0, cmask = 0;
     {
         const int bn = (int)min((int64_t)EB, end - start);
         if (bn > 0) {
             stage_issue(start, bn);
-            wmask = stage_finish(0, bn, n, rmask);
+            wmask = stage_finish(0, bn, n, rmask, cmask);
         }
     }
     Row<T, NC> vr[PD], wr[PD];
@@ -574,8 +597,15 @@ bank_scan_kernel(const ScanParams p) {
             for (int j = 0; j < PD; ++j) {
                 const int ev = e0 + j;
                 if (ev >= n) break;
+                float *ck_row = nullptr;
+                const bool ck_here = CK && ((cmask >> ev) & 1u);
+                if (ck_here) {
+                    const int64_t pos = base - start + ev;
+                    ck_row = p.ckpt + ((start / p.ckpt_block + seq + pos / p.ckpt_block) * p.H + hh) * (int64_t)S * p.dv +
+                             col0;
+                }
                 event_step<T, S, NC>(ctl[ev], (rmask >> ev) & 1u, (wmask >> ev) & 1u, tok_s[ev] >= 0, active, vr[j],
-                                     wr[j], p.scale, outp + (int64_t)rid_s[ev] * V, N);
+                                     wr[j], p.scale, outp + (int64_t)rid_s[ev] * V, N, ck_here, ck_row, p.dv);
                 prefetch(ev + PD, j);
             }
         }
@@ -589,7 +619,7 @@ bank_scan_kernel(const ScanParams p) {
         if (nn > 0) {
             if (!issued) stage_issue(nbase, nn);
             __syncwarp();
-            wmask = stage_finish(nbase - start, nn, n, rmask);
+            wmask = stage_finish(nbase - start, nn, n, rmask, cmask);
         }
         base = nbase;
     }
@@ -1238,8 +1268,8 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
         if (rc) return rc;
     }
     int per_sm = 1;
-    rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bank_scan_kernel<T, S, NC>,
-                                                                   kScanWarps * 32, 0));
+    auto sk = p.ckpt ? bank_scan_kernel<T, S, NC, true> : bank_scan_kernel<T, S, NC, false>;
+    rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sk, kScanWarps * 32, 0));
     if (rc) return rc;
     const int64_t want = ceil_div(q.units, kScanWarps);
     const int64_t blocks = BDM_SCAN_DYNAMIC ? min((int64_t)sms * (per_sm > 0 ? per_sm : 1), want)
@@ -1257,7 +1287,7 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = long_mode ? 1 : 0;
-    rc = cuda_status(cudaLaunchKernelEx(&cfg, bank_scan_kernel<T, S, NC>, q));
+    rc = cuda_status(cudaLaunchKernelEx(&cfg, sk, q));
     count_launch();
     return rc;
 }
@@ -1299,7 +1329,7 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
                              const int32_t *bank_ids, int64_t total_banks, int head_offset, int total_heads,
                              void *cache, int cache_dtype,
                              int store_final, int state_interval, void *reads, void *workspace,
-                             int64_t workspace_bytes, void *stream) {
+                             int64_t workspace_bytes, float *checkpoints, int checkpoint_block, void *stream) {
     using namespace bdm;
     if (batch <= 0 || time <= 0 || bank_count <= 0 || heads <= 0 || head_value_width <= 0 || kw <= 0 || kr <= 0)
         return BDM_ERR_INVALID;
@@ -1323,6 +1353,8 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     }
     const int64_t nseq = batch * bank_count;
     if (!workspace || workspace_bytes < scan_workspace_bytes(nseq)) return BDM_ERR_WORKSPACE;
+    if (checkpoints && (checkpoint_block <= 0 || cache || bank_ids || head_offset != 0 || total_heads != heads))
+        return BDM_ERR_INVALID;
     ScanParams p{};
     p.q = q; p.k = k; p.v = v; p.g = g; p.b = b; p.w = w;
     p.wi = write_idx; p.ri = read_idx; p.ww = write_w; p.rw = read_w;
@@ -1338,6 +1370,8 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.head_offset = head_offset; p.total_heads = total_heads;
     p.cache = cache; p.cache_dtype = cache_dtype; p.store_final = store_final; p.interval = state_interval;
     p.reads = reads;
+    p.ckpt = checkpoints;
+    p.ckpt_block = checkpoints ? checkpoint_block : 0;
     char *ws = static_cast<char *>(workspace);
     int *counts = reinterpret_cast<int *>(ws);
     int *lists = reinterpret_cast<int *>(ws + kWsHeader);

@@ -474,25 +474,29 @@ class _BankTraining(torch.autograd.Function):
         shape = (batch, time, -1)
         meta = ops.dispatch(wi.reshape(shape), ri.reshape(shape), J)
         interval = state_interval(S) if m.config.training_state_dtype == 'bfloat16' else 0
+        # the recurrence also writes the backward's state checkpoints (no replay sweep in the backward)
+        ckpt, block = ops.checkpoint_buffer(batch=batch, time=time, kw=wi.shape[-1], kr=ri.shape[-1], bank_count=J,
+                                            heads=H, bank_size=S, head_value_width=dv, device=proj.device)
         reads = ops.bank_scan(q, k, v, g, b, w, wi.reshape(shape), ww.reshape(shape), ri.reshape(shape),
                               rw.reshape(shape), meta['order'], meta['cu_seqlens'], batch=batch, time=time,
                               bank_count=J, heads=H, bank_size=S, head_value_width=dv,
                               routed_decay=m.config.routed_decay, scale=S ** -0.5, row_factor=row_factor,
-                              col_factor=col_factor, state_interval=interval)
+                              col_factor=col_factor, state_interval=interval, checkpoints=ckpt,
+                              checkpoint_block=block)
         gate = proj[:, cols['gate']:cols['gate'] + V]
         layer_norm = m.config.output_normalization == 'layer'
         normed, raw = ops.combine_norm_gate(reads, ri, gate, norm_w, norm_b if layer_norm else None, eps=m.norm_eps,
                                             layer_norm=layer_norm, round_each=False, save_raw=True)
         del reads
         ctx.save_for_backward(proj, f, wf2, a_log, dt_bias, row_factor, col_factor, norm_w, norm_b, q, k, v, g, b, w,
-                              ww, wi, rw, ri, meta['order'], meta['cu_seqlens'], raw)
+                              ww, wi, rw, ri, meta['order'], meta['cu_seqlens'], raw, ckpt)
         ctx.layer, ctx.cols, ctx.batch, ctx.time, ctx.interval = m, cols, batch, time, interval
         return normed
 
     @staticmethod
     def backward(ctx, d_normed):
         (proj, f, wf2, a_log, dt_bias, row_factor, col_factor, norm_w, norm_b, q, k, v, g, b, w, ww, wi, rw, ri,
-         order, cu, raw) = ctx.saved_tensors
+         order, cu, raw, ckpt) = ctx.saved_tensors
         m, cols, batch, time = ctx.layer, ctx.cols, ctx.batch, ctx.time
         H, S, dv, V, J = m.num_heads, m.bank_size, m.head_value_width, m.value_width, m.bank_count
         layer_norm = m.config.output_normalization == 'layer'
@@ -510,7 +514,7 @@ class _BankTraining(torch.autograd.Function):
                                            bank_count=J, heads=H, bank_size=S, head_value_width=dv, kw=kw, kr=kr,
                                            routed_decay=m.config.routed_decay, scale=S ** -0.5,
                                            row_factor=row_factor, col_factor=col_factor,
-                                           state_interval=ctx.interval)
+                                           state_interval=ctx.interval, checkpoints=ckpt)
         if timing:
             end.record()
             m.backward_events.append((start, end))

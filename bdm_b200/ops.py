@@ -201,7 +201,8 @@ def product_state(row_factor, col_factor, *, batch: int, bank_count: int, heads:
 def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_seqlens, *, batch: int, time: int,
               bank_count: int, heads: int, bank_size: int, head_value_width: int, routed_decay: bool, scale: float,
               row_factor=None, col_factor=None, cache=None, store_final=False, state_interval=0,
-              bank_ids=None, total_banks=0, head_offset=0, total_heads=0, check_status=False):
+              bank_ids=None, total_banks=0, head_offset=0, total_heads=0, check_status=False,
+              checkpoints=None, checkpoint_block=0):
     """Per-bank recurrence over dispatched events; returns reads [NT, KR, V] in the activation dtype.
 
     With ``cache`` ([batch, J, H, S, dv]) the state starts from it and, with
@@ -210,6 +211,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
     local bank count and ``bank_ids`` (int32 [bank_count]) maps local banks into
     the full table of ``total_banks`` banks.  ``heads`` may be a head group
     [head_offset, head_offset + heads) of a layer with ``total_heads`` heads.
+    ``checkpoints`` (float32, training): receives the states the recurrence backward
+    replays from, every ``checkpoint_block`` events (see ``scan_backward``).
     """
     _cuda(q, k, v, g, b, w, write_idx, read_idx, order, cu_seqlens, cache, bank_ids)
     if bank_ids is not None and (bank_ids.dtype != torch.int32 or bank_ids.numel() != bank_count
@@ -244,7 +247,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         dtype_code(u.dtype) if u is not None else 0, _ptr(bank_ids), int(total_banks) if bank_ids is not None else 0,
         int(head_offset), int(total_heads),
         _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
-        int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _stream(q.device)), 'bdm_bank_scan')
+        int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _ptr(checkpoints),
+        int(checkpoint_block) if checkpoints is not None else 0, _stream(q.device)), 'bdm_bank_scan')
     if check_status:  # synchronises: the kernel's error bits (a bounded producer/consumer wait that gave up)
         status = int(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32).item())
         if status:
@@ -471,10 +475,12 @@ def norm_gate_backward(d_out, raw, gate, norm_weight, norm_bias, *, eps: float, 
 
 def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, *, batch: int, time: int,
                   bank_count: int, heads: int, bank_size: int, head_value_width: int, kw: int, kr: int,
-                  routed_decay: bool, scale: float, row_factor=None, col_factor=None, state_interval=0):
+                  routed_decay: bool, scale: float, row_factor=None, col_factor=None, state_interval=0,
+                  checkpoints=None):
     """Recurrence backward over the dispatched events of a factor-initialised training forward.
 
-    ``d_read`` [NT, H*dv] is the gradient of the combined read sum.  Returns
+    ``d_read`` [NT, H*dv] is the gradient of the combined read sum.  ``checkpoints``: the buffer
+    the forward filled (``checkpoint_buffer``), or None to replay them here.  Returns
     (event_grads [tiles, E, H, 3S], d_write_value [NT*KW, H*dv], d_initial [B*J, H, S, dv]), FP32.
     """
     _cuda(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read)
@@ -488,7 +494,13 @@ def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, 
                                                       head_value_width)
     if ck_bytes < 0:
         raise NotImplementedError('scan backward supports bank_size 4, 8 or 16')
-    ck = torch.empty(max(ck_bytes // 4, 1), dtype=torch.float32, device=dev)
+    ready = checkpoints is not None
+    if ready:
+        if checkpoints.dtype != torch.float32 or checkpoints.numel() * 4 < ck_bytes:
+            raise ValueError('checkpoints must be the float32 buffer of checkpoint_buffer()')
+        ck = checkpoints
+    else:
+        ck = torch.empty(max(ck_bytes // 4, 1), dtype=torch.float32, device=dev)
     evg = torch.empty((tiles, e, heads, 3 * bank_size), dtype=torch.float32, device=dev)
     du = torch.empty((nt * kw, v_width), dtype=torch.float32, device=dev)
     dinit = torch.empty((batch * bank_count, heads, bank_size, head_value_width), dtype=torch.float32, device=dev)
@@ -502,8 +514,20 @@ def scan_backward(q, k, v, g, b, w, write_w, read_w, order, cu_seqlens, d_read, 
         batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt), int(routed_decay),
         float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
         dtype_code(u.dtype) if u is not None else 0, int(state_interval), _ptr(dr), _ptr(evg), _ptr(du),
-        _ptr(dinit), _ptr(ck), ck_bytes, _stream(dev)), 'bdm_scan_backward')
+        _ptr(dinit), _ptr(ck), ck_bytes, int(ready), _stream(dev)), 'bdm_scan_backward')
     return evg, du, dinit
+
+
+def checkpoint_buffer(*, batch: int, time: int, kw: int, kr: int, bank_count: int, heads: int, bank_size: int,
+                      head_value_width: int, device):
+    """(float32 buffer, block) for a training forward's ``bank_scan(checkpoints=, checkpoint_block=)``."""
+    lib = _lib.load()
+    nbytes = lib.bdm_scan_backward_checkpoint_bytes(batch, time, kw, kr, bank_count, heads, bank_size,
+                                                    head_value_width)
+    block = lib.bdm_scan_backward_block_events(bank_size, head_value_width)
+    if nbytes < 0 or block <= 0:
+        raise NotImplementedError('the training backward supports bank_size 4, 8 or 16')
+    return torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=device), block
 
 
 def event_vjp(q, k, v, g, b, w, write_w, read_w, event_grads, d_write_value, *, heads: int, bank_size: int,

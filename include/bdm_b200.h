@@ -178,6 +178,13 @@ BDM_API int bdm_product_state(const void *row_factor, const void *col_factor, in
  * 128 of the workspace holds error bits after the kernel: 1 = a wait between
  * the staging warp and the state warps of a CTA gave up (bounded at ~2 s; the
  * CTA's outputs are then incomplete).
+ * checkpoints (training; NULL otherwise): the state before every
+ * checkpoint_block-th event (position > 0) of a sequence is written to
+ * checkpoints[(start / checkpoint_block + seq + pos / checkpoint_block), head, S, dv]
+ * (float), the layout bdm_scan_backward reads with checkpoints_ready = 1
+ * (checkpoint_block = bdm_scan_backward_block_events(S, dv)); sequences of 2048 or
+ * more events may run on the long-sequence kernel, which writes none.  Needs the
+ * factor-initialised whole-layer form (no cache, bank_ids or head group).
  * Supported: bank_size in {4, 8, 16}; head_value_width a multiple of 8.
  */
 BDM_API int64_t bdm_bank_scan_workspace_bytes(int64_t batch, int64_t bank_count);
@@ -189,7 +196,8 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
                           int64_t factor_cols, int factor_dtype, const int32_t *bank_ids, int64_t total_banks,
                           int head_offset, int total_heads, void *cache, int cache_dtype, int store_final,
                           int state_interval, void *reads,
-                          void *workspace, int64_t workspace_bytes, void *stream);
+                          void *workspace, int64_t workspace_bytes, float *checkpoints, int checkpoint_block,
+                          void *stream);
 
 /*
  * Read combine + output normalisation + sigmoid gate.  Replaces
@@ -238,7 +246,9 @@ BDM_API int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_id
  *   sum_x dh*u | sum_x hd*du | sum_x dh'*hd; per read event id: sum_x h*do),
  *   d_write_value [ntok*kw, H*dv] (du per write event id) and d_initial
  *   [batch*J, H, S, dv].  checkpoints: bdm_scan_backward_checkpoint_bytes() bytes
- *   of scratch (states replayed at block starts).  S in {4, 8, 16}.
+ *   holding the states at block starts; with checkpoints_ready = 1 the training forward
+ *   (bdm_bank_scan with these checkpoints) already wrote them, except for sequences of
+ *   2048 or more events, whose checkpoints this call replays itself.  S in {4, 8, 16}.
  * bdm_event_vjp: per-token gather of the event gradients (role_bank_dispatch.py:
  *   76-132 plus the routed-decay dp term of routed_update.py:43-47): dq, dk, db
  *   [ntok, H*S], dv, dw [ntok, H*dv] (dtype), dg [ntok, H*S] (float), and the route
@@ -266,6 +276,9 @@ BDM_API int bdm_norm_gate_backward(const void *d_out, const void *raw, int64_t n
                                    float *partials, float *d_norm_weight, float *d_norm_bias, void *stream);
 /* Column tiles of bdm_scan_backward's event_grads (its leading dimension); -1 if unsupported. */
 BDM_API int bdm_scan_backward_tiles(int bank_size, int head_value_width);
+/* Events between the backward's state checkpoints (the checkpoint_block a training
+ * forward passes to bdm_bank_scan); -1 if unsupported. */
+BDM_API int bdm_scan_backward_block_events(int bank_size, int head_value_width);
 BDM_API int64_t bdm_scan_backward_checkpoint_bytes(int64_t batch, int64_t time, int kw, int kr, int64_t bank_count,
                                                    int heads, int bank_size, int head_value_width);
 BDM_API int bdm_scan_backward(const void *q, const void *k, const void *v, const float *g, const void *b,
@@ -275,7 +288,7 @@ BDM_API int bdm_scan_backward(const void *q, const void *k, const void *v, const
                               float scale, const void *row_factor, const void *col_factor, int64_t factor_cols,
                               int factor_dtype, int state_interval, const void *d_read, float *event_grads,
                               float *d_write_value, float *d_initial, float *checkpoints, int64_t checkpoint_bytes,
-                              void *stream);
+                              int checkpoints_ready, void *stream);
 BDM_API int bdm_event_vjp(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
                           const void *write_w, const void *read_w, const float *event_grads,
                           const float *d_write_value, int64_t ntok, int heads, int bank_size, int head_value_width,

@@ -61,7 +61,7 @@ def test_dispatch_workspace_sizing():
     lambda lib: lib.bdm_norm_gate_backward(None, None, 4, 64, None, 32, None, None, 1e-5, 1, 1, None, None, 64, None,
                                            None, None, None),                          # ld_gate < width
     lambda lib: lib.bdm_scan_backward(*([None] * 10), 2, 4, 16, 1, 8, 32, 4, 4, 1, 1, 0.35, None, None, 0, 0, 0,
-                                      *([None] * 5), 0, None),                         # null inputs
+                                      *([None] * 5), 0, 0, None),                      # null inputs
     lambda lib: lib.bdm_event_vjp(*([None] * 10), 4, 1, 8, 32, 4, 4, 1, 1, 0.35, *([None] * 8), None),
     lambda lib: lib.bdm_product_state_backward(None, 2, 0, 4, 32, 1, None, None, None, None),
     lambda lib: lib.bdm_route_backward(None, 4, 32, 0, 4, 4, 4, 4, 1, None, None, None, None, 1, None, 32, None),
@@ -88,7 +88,7 @@ def test_unsupported_geometry_is_reported():
     lib = _lib.load()
     dummy = ctypes.c_void_p(16)
     rc = lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 32, 64, 8, 8, 1, 1, 0.25, None, None, 0, 0, None, 0, 0, 0,
-                           None, 0, 0, 0, dummy, dummy, 1 << 20, None)
+                           None, 0, 0, 0, dummy, dummy, 1 << 20, None, 0, None)
     assert rc == _lib.BDM_ERR_UNSUPPORTED  # bank_size 32 is not implemented
     with pytest.raises(NotImplementedError):
         _lib.check(rc, 'bdm_bank_scan')
@@ -113,4 +113,10 @@ def test_backward_sizing_and_limits():
                                   None) == _lib.BDM_ERR_UNSUPPORTED
     # checkpoint scratch below the required size
     assert lib.bdm_scan_backward(*([dummy] * 10), 2, 4, 16, 1, 8, 32, 4, 4, 1, 1, 0.35, None, None, 0, 0, 0, dummy,
-                                 dummy, dummy, dummy, dummy, 16, None) == _lib.BDM_ERR_WORKSPACE
+                                 dummy, dummy, dummy, dummy, 16, 0, None) == _lib.BDM_ERR_WORKSPACE
+    # checkpoint blocks: 128 / (S * columns per lane) events
+    assert [lib.bdm_scan_backward_block_events(8, d) for d in (32, 64)] == [16, 8]
+    assert lib.bdm_scan_backward_block_events(16, 128) == 8 and lib.bdm_scan_backward_block_events(5, 64) == -1
+    # a training forward's checkpoints need the whole-layer, factor-initialised form
+    assert lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 8, 64, 8, 8, 1, 1, 0.35, None, None, 0, 0, None, 0, 0, 0,
+                             dummy, 1, 0, 0, dummy, dummy, 1 << 20, dummy, 8, None) == _lib.BDM_ERR_INVALID
