@@ -444,23 +444,18 @@ constexpr int kVjpWarps = 4;
 // then the read slots, with its rounding points.  The route-weight gradients stay
 // per head (the reference runs one routed update per head); the router backward
 // sums them over heads.  CPL = value columns per lane (lane l: l, l+32, ...).
-// Slots go in chunks of kVjpChunk: the chunk's loads are issued together and its
-// per-slot warp sums are reduced in one halving butterfly.
-constexpr int kVjpChunk = 8;
-
 template <typename T, int S, int CPL>
 __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpParams p) {
     const int64_t item = (int64_t)blockIdx.x * kVjpWarps + (threadIdx.x >> 5);
     if (item >= p.items) return;
     const int64_t t = item / p.H;
     const int h = (int)(item % p.H);
-    const unsigned lane = lane_id();
+    const int lane = (int)lane_id();
     const int dv = p.dv;
     const int64_t V = (int64_t)p.H * dv;
     const int64_t hs0 = (t * p.H + h) * S;
     const bool nl = lane < S;
     constexpr int R = 3 * S;
-    constexpr int CH = kVjpChunk;
     float k0 = 0.f, b0 = 0.f, g0 = 0.f, q0 = 0.f;
     if (nl) {
         k0 = ld_f(static_cast<const T *>(p.k), hs0 + lane);
@@ -472,7 +467,7 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     float v0[CPL], w0[CPL], accv[CPL], accw[CPL];
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
-        const int c = (int)lane + 32 * i;
+        const int c = lane + 32 * i;
         const bool on = c < dv;
         v0[i] = on ? ld_f(static_cast<const T *>(p.v), vrow + c) : 0.f;
         w0[i] = on ? ld_f(static_cast<const T *>(p.w), vrow + c) : 0.f;
@@ -481,100 +476,67 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     float dk_acc = 0.f, db_acc = 0.f, dg_acc = 0.f, dq_acc = 0.f;
     T *dwwh = static_cast<T *>(p.dww_h) + (t * p.H + h) * p.kw;
     T *drwh = static_cast<T *>(p.drw_h) + (t * p.H + h) * p.kr;
-    for (int j0 = 0; j0 < p.kw; j0 += CH) {
-        float pw[CH], du[CH][CPL], A[CH], C[CH], Gs[CH];
+#pragma unroll 2
+    for (int j = 0; j < p.kw; ++j) {
+        const int64_t id = t * p.kw + j;
+        const float pw = ld_f(static_cast<const T *>(p.ww), id);
+        float wvp = 0.f;
+        const float *durow = p.du + id * V + (int64_t)h * dv;
 #pragma unroll
-        for (int jj = 0; jj < CH; ++jj) {  // the chunk's loads
-            const int j = j0 + jj;
-            const bool on = j < p.kw;
-            const int64_t id = t * p.kw + j;
-            pw[jj] = on ? ld_f(static_cast<const T *>(p.ww), id) : 0.f;
-#pragma unroll
-            for (int i = 0; i < CPL; ++i) {
-                const int c = (int)lane + 32 * i;
-                du[jj][i] = (on && c < dv) ? p.du[id * V + (int64_t)h * dv + c] : 0.f;
-            }
-            A[jj] = C[jj] = Gs[jj] = 0.f;
-            if (on && nl) {
-                for (int tile = 0; tile < p.tiles; ++tile) {
-                    const float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * R;
-                    A[jj] += rec[lane];
-                    C[jj] += rec[S + lane];
-                    Gs[jj] += rec[2 * S + lane];
-                }
+        for (int i = 0; i < CPL; ++i) {
+            const int c = lane + 32 * i;
+            if (c < dv) {
+                const float du = durow[c];
+                const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
+                const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
+                accv[i] = rnd<T>(accv[i] + dve);
+                accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
+                wvp += rnd<T>(dwe * w0[i]);
             }
         }
-        float red[32];  // per slot: [sum_x dw*w | sum_s db*b | sum_s dg*g] partials of this lane
-#pragma unroll
-        for (int jj = 0; jj < CH; ++jj) {
-            float wvp = 0.f, wbp = 0.f, dec = 0.f;
-            if (j0 + jj < p.kw) {
-#pragma unroll
-                for (int i = 0; i < CPL; ++i) {
-                    if ((int)lane + 32 * i < dv) {
-                        const float dve = rnd<T>(du[jj][i] * rnd<T>(w0[i] * pw[jj]));  // event dv (dtype)
-                        const float dwe = rnd<T>(du[jj][i] * v0[i]);                  // event dw (dtype)
-                        accv[i] = rnd<T>(accv[i] + dve);
-                        accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw[jj]));
-                        wvp += rnd<T>(dwe * w0[i]);
-                    }
-                }
-                if (nl) {
-                    const float be = rnd<T>(b0 * pw[jj]);
-                    const float dke = rnd<T>(A[jj] - be * C[jj]);
-                    const float dbe = rnd<T>(-k0 * C[jj]);
-                    dk_acc += dke;
-                    db_acc += rnd<T>(dbe * pw[jj]);
-                    if (p.routed_decay) {
-                        dg_acc += Gs[jj] * pw[jj];
-                        dec = Gs[jj] * g0;
-                    } else {
-                        dg_acc += Gs[jj];
-                    }
-                    wbp = rnd<T>(dbe * b0);
-                }
+        float wbp = 0.f, dec = 0.f;
+        if (nl) {
+            float A = 0.f, C = 0.f, Gs = 0.f;
+            for (int tile = 0; tile < p.tiles; ++tile) {
+                const float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * R;
+                A += rec[lane];
+                C += rec[S + lane];
+                Gs += rec[2 * S + lane];
             }
-            red[jj] = wvp;
-            red[CH + jj] = wbp;
-            red[2 * CH + jj] = dec;
+            const float be = rnd<T>(b0 * pw);
+            const float dke = rnd<T>(A - be * C);
+            const float dbe = rnd<T>(-k0 * C);
+            dk_acc += dke;
+            db_acc += rnd<T>(dbe * pw);
+            if (p.routed_decay) {
+                dg_acc += Gs * pw;
+                dec = Gs * g0;
+            } else {
+                dg_acc += Gs;
+            }
+            wbp = rnd<T>(dbe * b0);
         }
-#pragma unroll
-        for (int k = 3 * CH; k < 32; ++k) red[k] = 0.f;
-        HalvingReduce<32, 16, 32>::run(red, lane);  // lane l: the warp total of value l
-        const float tot = red[0];
-        const float wb = __shfl_sync(kFull, tot, (int)(lane & (CH - 1)) + CH);
-        const float decs = __shfl_sync(kFull, tot, (int)(lane & (CH - 1)) + 2 * CH);
-        if (lane < CH && j0 + (int)lane < p.kw)
-            dwwh[j0 + lane] = Elem<T>::from_float(rnd<T>(rnd<T>(wb) + rnd<T>(tot)) + decs);
+        const float wv = rnd<T>(warp_sum(wvp));
+        const float wb = rnd<T>(warp_sum(wbp));
+        const float decs = warp_sum(dec);
+        if (lane == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
     }
-    for (int j0 = 0; j0 < p.kr; j0 += CH) {
-        float r[CH], o[CH];
-#pragma unroll
-        for (int jj = 0; jj < CH; ++jj) {  // the chunk's loads
-            const int j = j0 + jj;
-            const bool on = j < p.kr;
-            const int64_t rid = t * p.kr + j;
-            r[jj] = on ? ld_f(static_cast<const T *>(p.rw), rid) : 0.f;
-            o[jj] = 0.f;
-            if (on && nl) {
-                for (int tile = 0; tile < p.tiles; ++tile)
-                    o[jj] += p.evg[(((int64_t)tile * p.E + p.nw + rid) * p.H + h) * R + lane] * p.scale;
-            }
+#pragma unroll 2
+    for (int j = 0; j < p.kr; ++j) {
+        const int64_t rid = t * p.kr + j;
+        const int64_t id = p.nw + rid;
+        const float r = ld_f(static_cast<const T *>(p.rw), rid);
+        float wrp = 0.f;
+        if (nl) {
+            float o = 0.f;
+            for (int tile = 0; tile < p.tiles; ++tile)
+                o += p.evg[(((int64_t)tile * p.E + id) * p.H + h) * R + lane] * p.scale;
+            const float dqe = rnd<T>(o);
+            dq_acc += rnd<T>(dqe * r);
+            wrp = rnd<T>(dqe * q0);
         }
-        float red[CH];
-#pragma unroll
-        for (int jj = 0; jj < CH; ++jj) {
-            float wrp = 0.f;
-            if (nl && j0 + jj < p.kr) {
-                const float dqe = rnd<T>(o[jj]);
-                dq_acc += rnd<T>(dqe * r[jj]);
-                wrp = rnd<T>(dqe * q0);
-            }
-            red[jj] = wrp;
-        }
-        HalvingReduce<CH, 16, CH>::run(red, lane);  // lane l: the total of slot l >> 2 (lanes 4s .. 4s+3)
-        const int slot = (int)(lane >> 2);
-        if ((lane & 3) == 0 && j0 + slot < p.kr) drwh[j0 + slot] = Elem<T>::from_float(red[0]);
+        const float wr = warp_sum(wrp);
+        if (lane == 0) drwh[j] = Elem<T>::from_float(wr);
     }
     if (nl) {
         st_f(static_cast<T *>(p.dq), hs0 + lane, dq_acc);
@@ -584,7 +546,7 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     }
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
-        const int c = (int)lane + 32 * i;
+        const int c = lane + 32 * i;
         if (c < dv) {
             st_f(static_cast<T *>(p.dv_out), vrow + c, accv[i]);
             st_f(static_cast<T *>(p.dw_out), vrow + c, accw[i]);
