@@ -1,7 +1,8 @@
 """Generate golden vectors from the reference implementation itself.
 
-Run in a container that holds the reference checkout (it is imported from
-``$BDM_REFERENCE/implementation``, default ``/root/reference/implementation``):
+Run where the reference checkout is present.  Its ``implementation`` directory is
+imported from ``$BDM_REFERENCE``, by default ``reference/implementation`` beside this
+repository's root directory:
 
     python tests/golden/make_golden.py
 
@@ -34,7 +35,9 @@ import sys
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get('BDM_REFERENCE', '/root/reference/implementation')
+REF = os.environ.get('BDM_REFERENCE',
+                     os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))), 'reference',
+                                  'implementation'))
 sys.path.insert(0, REF)
 
 from bdm.gdn2_banks import (pack_bank_events, product_key_route, reference_packed_gdn2,  # noqa: E402
