@@ -251,6 +251,24 @@ def cpu_forward_sample(batch, time_, seed=1):
     return batch * time_ / dt, dt, threads
 
 
+def cpu_train_sample(batch, time_, seed=4):
+    """Time one forward + backward of the c5 layer (BF16) with the gradient oracle (torch autograd
+    over the CPU restatement, oracle/grad.py) on batch x time_ tokens, on the host cores."""
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
+    from oracle.grad import layer_grads
+    cfg = BSDMConfig(**C5)
+    m = BlockSparseDeltaMemory(cfg, seed=seed).to(torch.bfloat16)
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(batch, time_, cfg.dim, generator=gen).to(torch.bfloat16)
+    dy = torch.randn(batch, time_, cfg.dim, generator=gen).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    grads, _, _ = layer_grads(sd, x, dy, {k: getattr(cfg, k) for k in cfg.__dataclass_fields__})
+    dt = time.perf_counter() - t0
+    assert all(torch.isfinite(g.float()).all() for g in grads.values())
+    return batch * time_ / dt, dt, torch.get_num_threads()
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
@@ -381,6 +399,13 @@ def run_ours(args, world, rank, local):
             line['c5'] = run_c5(dev, rank, world, args)
         except Exception as e:  # keep the headline line even if the extra workload fails
             line['c5'] = {'error': repr(e)[:300]}
+    if rank == 0 and world == 1 and not args.skip_cpu and isinstance(line.get('train'), dict) \
+            and 'value' in line['train']:
+        tps, dt, threads = cpu_train_sample(args.cpu_train_batch, C5_TIME)
+        line['train']['cpu_baseline'] = {
+            'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+            'sample': f'c5 layer forward + backward, batch {args.cpu_train_batch} x seq {C5_TIME} ({dt:.1f} s), '
+                      f'torch autograd over the CPU restatement oracle/grad.py'}
     if rank == 0 and world == 1 and not args.skip_cpu:
         tps, dt, threads = cpu_forward_sample(C2_BATCH, args.cpu_time)
         line['cpu_baseline'] = {'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
@@ -690,6 +715,7 @@ def main():
     ap.add_argument('--c4-steps', type=int, default=5)
     ap.add_argument('--c4-ownership', choices=('balanced', 'contiguous'), default='balanced')
     ap.add_argument('--skip-train', action='store_true')
+    ap.add_argument('--cpu-train-batch', type=int, default=2, help='rows (x 2048 tokens) of the training CPU sample')
     ap.add_argument('--skip-c5', action='store_true')
     ap.add_argument('--c5-steps', type=int, default=2)
     ap.add_argument('--c5-batch', type=int, default=32, help='c5 global batch (32 is the benchmark)')
