@@ -267,45 +267,17 @@ __device__ __forceinline__ void initial_columns(const ScanBwdParams &p, int64_t 
     }
 }
 
-// Stores the first `used` values of an N-value halving reduction (see HalvingReduce).
-template <int N>
-__device__ __forceinline__ void store_reduced(const float (&v)[N], int used, float *out) {
-    const unsigned lane = lane_id();
-    if constexpr (N >= 32) {
-#pragma unroll
-        for (int i = 0; i < N / 32; ++i) {
-            const int idx = (int)lane * (N / 32) + i;
-            if (idx < used) out[idx] = v[i];
-        }
-    } else {
-        constexpr int shift = 5 - ilog2(N);
-        const int idx = (int)(lane >> shift);
-        if ((lane & ((1u << shift) - 1u)) == 0 && idx < used) out[idx] = v[0];
-    }
-}
-
 // Reverse pass over events [0, n) of the staged block (descending), from the history.
-// Software-pipelined: an iteration computes event i's per-lane sums and reduces event
-// i+1's across the warp (two independent instruction streams in one basic block).
 template <int S, int COLS>
 __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const BlockStage<S, COLS> &st, int n, int tile,
                                               int h, int col0, float (&dh)[S][COLS]) {
     using G = BwdGeom<S, COLS>;
-    constexpr int W = G::kRedW;
     const unsigned lane = lane_id();
-    float pend[W];  // the previous event's per-lane sums, reduced one iteration later
-#pragma unroll
-    for (int k = 0; k < W; ++k) pend[k] = 0.f;
-    float *pend_rec = nullptr;
-    int pend_used = 0;
 #pragma unroll 1
     for (int i = n - 1; i >= 0; --i) {
         const int64_t id = st.id[i];
         const float *u = st.uni[i];
         float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
-        float red[W];
-#pragma unroll
-        for (int k = 0; k < W; ++k) red[k] = 0.f;
         if (id < p.nw) {
             float hd[S][COLS], er[COLS][2], du[COLS][2], uu[COLS], dus[COLS];
 #pragma unroll
@@ -324,6 +296,7 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
                 uu[c] = st.col[i][c][lane] - (er[c][0] + er[c][1]);
                 dus[c] = du[c][0] + du[c][1];
             }
+            float red[G::kRedW];
 #pragma unroll
             for (int s = 0; s < S; ++s) {
                 float A = 0.f, C = 0.f, Gs = 0.f;
@@ -340,16 +313,15 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
                 red[2 * S + s] = Gs;
             }
 #pragma unroll
+            for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
+#pragma unroll
             for (int c = 0; c < COLS; ++c) {
                 const int cc = col0 + 32 * c;
                 if (cc < p.dv) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + cc] = dus[c];
             }
-            HalvingReduce<W, 16, W>::run(pend, lane);
-            if (pend_rec) store_reduced<W>(pend, pend_used, pend_rec);
-#pragma unroll
-            for (int k = 0; k < W; ++k) pend[k] = red[k];
-            pend_used = 3 * S;
+            reduce_store<G::kRedW>(red, 3 * S, rec);
         } else {
+            float red[S];
 #pragma unroll
             for (int s = 0; s < S; ++s) {
                 float o = 0.f;
@@ -361,16 +333,9 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
                 }
                 red[s] = o;
             }
-            HalvingReduce<W, 16, W>::run(pend, lane);
-            if (pend_rec) store_reduced<W>(pend, pend_used, pend_rec);
-#pragma unroll
-            for (int k = 0; k < W; ++k) pend[k] = red[k];
-            pend_used = S;
+            reduce_store<S>(red, S, rec);
         }
-        pend_rec = rec;
     }
-    HalvingReduce<W, 16, W>::run(pend, lane);
-    if (pend_rec) store_reduced<W>(pend, pend_used, pend_rec);
 }
 
 // One warp (one CTA) per (sequence, head, tile of 32*COLS columns).
