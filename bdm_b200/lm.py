@@ -152,3 +152,63 @@ class BDMLanguageModel(nn.Module):
         if target is not None:
             return F.cross_entropy(logits.float().flatten(0, -2), target.flatten())
         return logits
+
+    # ---------------------------------------------------- stateful inference
+    def prefill(self, tokens, caches=None, *, state_dtype=None):
+        """Process a prefix [B, T] -> (logits [B, T, vocab], per-layer bank caches).
+
+        Every block's mixer runs ``BankedDeltaMemory.prefill`` (inference.py:110-131): FP32
+        recurrence, the cache rounded once to its storage dtype (BF16 unless ``state_dtype`` or the
+        given caches say otherwise).  Requires no_grad / inference_mode.
+        """
+        hidden = self.tok_embeddings(tokens)
+        out = []
+        for i, block in enumerate(self.layers):
+            mix, cache = block.attention.prefill(block.attention_norm(hidden), None if caches is None else caches[i],
+                                                 state_dtype=state_dtype)
+            hidden = hidden + mix
+            hidden = hidden + block.feed_forward(block.ffn_norm(hidden))
+            out.append(cache)
+        return self.output(self.norm(hidden)), out
+
+    def step(self, tokens, caches):
+        """One token per row [B, 1] -> logits [B, 1, vocab]; advances ``caches`` in place."""
+        hidden = self.tok_embeddings(tokens)
+        for block, cache in zip(self.layers, caches):
+            mix, _ = block.attention.step(block.attention_norm(hidden), cache)
+            hidden = hidden + mix
+            hidden = hidden + block.feed_forward(block.ffn_norm(hidden))
+        return self.output(self.norm(hidden))
+
+    def capture_step(self, caches, *, warmup=2):
+        """CUDA-graph one decode step of the whole model bound to ``caches`` (from ``prefill``).
+
+        Returns ``run(tokens[B, 1]) -> logits[B, 1, vocab]``: copies the tokens into the graph's
+        input, replays the step (advancing ``caches`` in place, as ``step`` does) and returns the
+        graph's logits buffer, which the next call overwrites.  Warm-up runs on clones of the
+        caches.  Parameters must not change afterwards.
+        """
+        if torch.is_grad_enabled():
+            raise RuntimeError('capture_step requires no_grad or inference_mode')
+        batch = caches[0].shape[0]
+        dev = caches[0].device
+        tokens_in = torch.zeros(batch, 1, dtype=torch.long, device=dev)
+        scratch = [c.clone() for c in caches]
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(tokens_in, scratch)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        del scratch
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            logits = self.step(tokens_in, caches)
+
+        def run(tokens):
+            tokens_in.copy_(tokens)
+            graph.replay()
+            return logits
+
+        run.graph = graph
+        return run

@@ -58,3 +58,26 @@ def test_lm_training_step_matches_reference():
         if not err <= 1e-4:
             bad[n] = err
     assert not bad, bad
+
+
+@pytest.mark.gpu
+def test_lm_prefill_step_and_graphed_step_match_forward():
+    """FP32 model and caches: prefill over T tokens then one step reproduce the full forward's
+    logits (same recurrence, no storage rounding); the CUDA-graphed step equals the eager one."""
+    d = _golden()
+    m = _model(d).cuda()
+    gen = torch.Generator().manual_seed(8)
+    tokens = torch.randint(0, d['vocab_size'], (2, 25), generator=gen).cuda()
+    with torch.inference_mode():
+        full = m(tokens)
+        logits_p, caches = m.prefill(tokens[:, :24], state_dtype=torch.float32)
+        eager_caches = [c.clone() for c in caches]
+        logits_s = m.step(tokens[:, 24:], eager_caches)
+        run = m.capture_step(caches)
+        logits_g = run(tokens[:, 24:]).clone()
+    scale = full.abs().max()
+    assert ((logits_p - full[:, :24]).abs().max() / scale).item() <= 1e-4
+    assert ((logits_s[:, 0] - full[:, 24]).abs().max() / scale).item() <= 1e-4
+    assert torch.equal(logits_g, logits_s)
+    for a, b in zip(caches, eager_caches):
+        assert torch.equal(a, b)
