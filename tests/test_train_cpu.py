@@ -1,13 +1,20 @@
 """Host logic of the training path (bdm_b200.layer._BankTraining) on the CPU.
 
 The CUDA ops are replaced by shape-checking stand-ins, so only the autograd plumbing runs:
-every parameter of the layer receives a gradient, and the backward writes each column of
-the fused projection's gradient exactly once (q, k, v, b, w by the controllers backward,
-f1 by the f_proj.1 GEMM, the router blocks by the router backward, the gate block by the
-norm/gate backward).
+* every parameter of the layer receives a gradient, and the backward writes each column of
+  the fused projection's gradient exactly once (q, k, v, b, w by the controllers backward,
+  f1 by the f_proj.1 GEMM, the router blocks by the router backward, the gate block by the
+  norm/gate backward);
+* data parallelism: the LM shell under DistributedDataParallel (gloo, world size 2)
+  all-reduces to the mean of the ranks' local gradients.
 """
+import os
+import socket
+
 import pytest
 import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
 
 from bdm_b200 import BDMConfig, BSDMConfig, BankedDeltaMemory
 from bdm_b200 import layer as layer_mod
@@ -23,7 +30,8 @@ class _Recorder:
         self.writes.append((first, width))
 
 
-def _install(monkeypatch, rec):
+def _install(set_attr, rec):
+    """Replace the CUDA ops with CPU stand-ins; ``set_attr(obj, name, value)``."""
     def controllers(proj, cols, f, a_log, dt_bias, *, heads, bank_size, head_value_width, qk_norm, f_weight=None,
                     f1_width=0):
         nt, hs, v = proj.shape[0], heads * bank_size, heads * head_value_width
@@ -34,8 +42,8 @@ def _install(monkeypatch, rec):
 
     def route_pair(proj, first, second, *, bank_count, selected_banks, factors):
         nt = proj.shape[0]
-        idx = torch.randint(0, bank_count, (nt, selected_banks))
-        w = torch.rand(nt, selected_banks).to(proj.dtype)
+        idx = (torch.arange(nt)[:, None] * 7 + torch.arange(selected_banks)[None, :]) % bank_count
+        w = torch.softmax(proj[:, first:first + selected_banks].float(), -1).to(proj.dtype)
         return (w, idx), (w.clone(), idx.clone())
 
     def dispatch(wi, ri, bank_count):
@@ -93,14 +101,14 @@ def _install(monkeypatch, rec):
                          scan_backward=scan_backward, event_vjp=event_vjp, route_backward=route_backward,
                          controllers_backward=controllers_backward,
                          product_state_backward=product_state_backward).items():
-        monkeypatch.setattr(ops, name, fn)
+        set_attr(ops, name, fn)
 
 
 @pytest.mark.parametrize('cfg_cls,heads,dtype', [(BSDMConfig, 2, torch.float32), (BSDMConfig, 1, torch.bfloat16),
                                                   (BDMConfig, 1, torch.float32)])
 def test_training_plumbing_covers_every_gradient(monkeypatch, cfg_cls, heads, dtype):
     rec = _Recorder()
-    _install(monkeypatch, rec)
+    _install(monkeypatch.setattr, rec)
     cfg = cfg_cls(dim=64, bank_count=64, bank_size=8, selected_banks=4, value_width=32, num_heads=heads)
     m = BankedDeltaMemory(cfg, seed=1).to(dtype)
     x = torch.randn(2, 5, 64).to(dtype).requires_grad_(True)
@@ -121,3 +129,59 @@ def test_training_plumbing_covers_every_gradient(monkeypatch, cfg_cls, heads, dt
             covered[first:first + width] += 1
     covered[cols['f']:cols['f'] + m.head_value_width] += 1  # torch.mm(df, f_proj.1 weight)
     assert torch.equal(covered, torch.ones_like(covered))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+def _lm():
+    from bdm_b200 import LanguageModelConfig
+    from bdm_b200.lm import BDMLanguageModel
+    mem = BSDMConfig(dim=32, bank_count=16, bank_size=8, selected_banks=4, value_width=32, num_heads=2,
+                     training_state_dtype='float32')
+    return BDMLanguageModel(LanguageModelConfig(memory=mem, vocab_size=40, layers=2, seed=3, ffn_multiple_of=32))
+
+
+def _tokens(rank):
+    gen = torch.Generator().manual_seed(100 + rank)
+    return torch.randint(0, 40, (2, 6), generator=gen), torch.randint(0, 40, (2, 6), generator=gen)
+
+
+def _allow_cpu(set_attr):
+    """The layer refuses CPU tensors (it has no CPU path); with the ops stubbed, let them through."""
+    set_attr(BankedDeltaMemory, '_check_hidden', lambda self, hidden: None)
+
+
+def _ddp_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port))
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        _install(setattr, _Recorder())
+        _allow_cpu(setattr)
+        model = torch.nn.parallel.DistributedDataParallel(_lm())
+        tokens, target = _tokens(rank)
+        model(tokens, target).backward()
+        torch.save({n: p.grad for n, p in model.module.named_parameters()}, os.path.join(out_dir, f'g{rank}.pt'))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_lm_data_parallel_gloo_world2(monkeypatch, tmp_path):
+    world = 2
+    mp.spawn(_ddp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    _install(monkeypatch.setattr, _Recorder())
+    _allow_cpu(monkeypatch.setattr)
+    local = []
+    for rank in range(world):  # each rank's local gradients, without DDP
+        m = _lm()
+        tokens, target = _tokens(rank)
+        m(tokens, target).backward()
+        local.append({n: p.grad for n, p in m.named_parameters()})
+    got = [torch.load(tmp_path / f'g{r}.pt') for r in range(world)]
+    for n in local[0]:
+        want = (local[0][n] + local[1][n]) / world
+        assert torch.equal(got[0][n], got[1][n]), n  # every rank holds the same all-reduced gradient
+        assert torch.allclose(got[0][n], want, rtol=1e-5, atol=1e-7), n
