@@ -23,6 +23,9 @@
 // the end of a batch, a BF16 state-storage point (gdn2_banks.py:35-36), or
 // where the cumulative log-decay would leave the FP32 range (the batch is cut).
 #include "common.cuh"
+#include "scan.cuh"
+
+#include <type_traits>
 
 namespace bdm {
 namespace {
@@ -45,51 +48,7 @@ namespace {
 
 constexpr int kScanWarps = 4;
 constexpr int kPrefetch = BDM_SCAN_PREFETCH;
-constexpr float kMinLogDecay = -60.0f;   // per-segment floor of the cumulative log-decay
 
-struct ScanParams {
-    const void *q, *k, *v;
-    const float *g;
-    const void *b, *w;
-    const int64_t *wi, *ri;
-    const void *ww, *rw;
-    const int64_t *order, *cu;
-    int64_t batch, time, J, nt, nw, E;
-    int H, dv, kw, kr, routed_decay, ctiles;
-    float scale;
-    const void *row_factor, *col_factor;
-    int64_t factor_cols;
-    int factor_dtype;
-    const int32_t *bank_ids;  // local bank -> bank of the full table (bank-sharded ranks), or null
-    int64_t total_banks;
-    int head_offset, total_heads;  // this call's heads are [head_offset, head_offset + H) of total_heads
-    void *cache;
-    int cache_dtype, store_final, interval;
-    void *reads;
-    int64_t units;        // (sequence, head, column tile) units when every sequence runs
-    // Work list: non-empty sequences grouped by length class, longest class first.
-    const int *lists;     // kLenClasses lists of capacity nseq
-    const int *counts;    // [kLenClasses] list lengths
-    unsigned long long *next;  // dynamic work counter (zero at launch)
-    unsigned long long *long_next;  // the long kernel's work counter (zero at launch)
-    int *status;               // error bits (BDM_SCAN_ERR_*), zero at launch
-    int ws_classes;            // length classes run by warp-specialised CTAs (0: none)
-    int64_t ws_ctas;           // CTAs [0, ws_ctas) run those units
-    int64_t nseq;
-    // Training: the state before every ckpt_block-th event of a sequence (position > 0) is
-    // written to ckpt[(start / ckpt_block + seq + pos / ckpt_block), head, S, dv] for the
-    // recurrence backward (short-kernel sequences only; null / 0 when off).
-    float *ckpt;
-    int ckpt_block;
-};
-
-// Length classes of the work list (events per sequence, lower bounds), longest first.
-// Inside a class sequences keep ascending (batch, bank) order, so warps running
-// at the same time mostly read the same batch row's token rows (L2 locality).
-constexpr int kLenClasses = 4;
-constexpr int kWsClasses = 1;           // class 0 (the long sequences) runs warp-specialised
-constexpr int64_t kLongEvents = 2048;   // a long sequence has at least this many events
-constexpr int BDM_SCAN_ERR_TIMEOUT = 1;  // a producer/consumer wait gave up
 // Lower bounds of classes 1..3; class 0 starts at the launch's long-sequence bound.
 __device__ __constant__ int kLenLower[kLenClasses] = {0, 2048, 512, 1};
 
@@ -1267,6 +1226,9 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
         rc = launch_status();
         if (rc) return rc;
     }
+    // bdm_bank_scan_chunked: the remaining classes on the tensor-core chunked kernel
+    // (chunk_scan.cu), as the long kernel's programmatic dependent.
+    if (q.chunked) return launch_chunk_scan(q, S, st, long_mode);
     int per_sm = 1;
     auto sk = p.ckpt ? bank_scan_kernel<T, S, NC, true> : bank_scan_kernel<T, S, NC, false>;
     rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sk, kScanWarps * 32, 0));
@@ -1309,7 +1271,7 @@ int launch_scan_shape(const ScanParams &p, int S, cudaStream_t st) {
 namespace bdm {
 namespace {
 // Workspace: 256-byte header [counts (kLenClasses int32) at 0 | dynamic counters (uint64) at 64
-// (short kernel) and 72 (long kernel) | status word (int32, BDM_SCAN_ERR_* bits) at 128], then the lists.
+// (short kernel), 72 (long kernel) and 80 (chunked kernel) | status word (int32, BDM_SCAN_ERR_* bits) at 128], then the lists.
 constexpr int64_t kWsHeader = 256;
 inline int64_t scan_workspace_bytes(int64_t nseq) { return kWsHeader + (int64_t)kLenClasses * nseq * 4; }
 }  // namespace
@@ -1320,7 +1282,8 @@ extern "C" int64_t bdm_bank_scan_workspace_bytes(int64_t batch, int64_t bank_cou
     return bdm::scan_workspace_bytes(batch * bank_count);
 }
 
-extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
+namespace {
+int bank_scan_impl(bool chunked, const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,
                              const int64_t *write_idx, const void *write_w, const int64_t *read_idx,
                              const void *read_w, const int64_t *order, const int64_t *cu_seqlens, int64_t batch,
                              int64_t time, int64_t bank_count, int heads, int bank_size, int head_value_width, int kw,
@@ -1372,6 +1335,8 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.reads = reads;
     p.ckpt = checkpoints;
     p.ckpt_block = checkpoints ? checkpoint_block : 0;
+    p.chunked = chunked ? 1 : 0;
+    if (chunked && !chunk_scan_eligible(p, dtype, bank_size)) return BDM_ERR_UNSUPPORTED;
     char *ws = static_cast<char *>(workspace);
     int *counts = reinterpret_cast<int *>(ws);
     int *lists = reinterpret_cast<int *>(ws + kWsHeader);
@@ -1379,6 +1344,7 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     p.next = reinterpret_cast<unsigned long long *>(ws + 64);
     p.status = reinterpret_cast<int *>(ws + 128);
     p.long_next = reinterpret_cast<unsigned long long *>(ws + 72);
+    p.chunk_next = reinterpret_cast<unsigned long long *>(ws + 80);
     p.lists = lists;
     p.nseq = nseq;
     cudaStream_t st = as_stream(stream);
@@ -1387,3 +1353,22 @@ extern "C" int bdm_bank_scan(const void *q, const void *k, const void *v, const 
     BDM_DISPATCH_DTYPE(dtype, T, { return launch_scan_shape<T>(p, bank_size, st); });
     return BDM_OK;
 }
+}  // namespace
+
+#define BDM_SCAN_ARGS                                                                                                  \
+    const void *q, const void *k, const void *v, const float *g, const void *b, const void *w,                         \
+        const int64_t *write_idx, const void *write_w, const int64_t *read_idx, const void *read_w,                    \
+        const int64_t *order, const int64_t *cu_seqlens, int64_t batch, int64_t time, int64_t bank_count, int heads,   \
+        int bank_size, int head_value_width, int kw, int kr, int dtype, int routed_decay, float scale,                 \
+        const void *row_factor, const void *col_factor, int64_t factor_cols, int factor_dtype,                         \
+        const int32_t *bank_ids, int64_t total_banks, int head_offset, int total_heads, void *cache, int cache_dtype,  \
+        int store_final, int state_interval, void *reads, void *workspace, int64_t workspace_bytes,                    \
+        float *checkpoints, int checkpoint_block, void *stream
+#define BDM_SCAN_PASS                                                                                                  \
+    q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_seqlens, batch, time, bank_count, heads,         \
+        bank_size, head_value_width, kw, kr, dtype, routed_decay, scale, row_factor, col_factor, factor_cols,          \
+        factor_dtype, bank_ids, total_banks, head_offset, total_heads, cache, cache_dtype, store_final,                \
+        state_interval, reads, workspace, workspace_bytes, checkpoints, checkpoint_block, stream
+
+extern "C" int bdm_bank_scan(BDM_SCAN_ARGS) { return bank_scan_impl(false, BDM_SCAN_PASS); }
+extern "C" int bdm_bank_scan_chunked(BDM_SCAN_ARGS) { return bank_scan_impl(true, BDM_SCAN_PASS); }

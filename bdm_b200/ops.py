@@ -202,7 +202,7 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
               bank_count: int, heads: int, bank_size: int, head_value_width: int, routed_decay: bool, scale: float,
               row_factor=None, col_factor=None, cache=None, store_final=False, state_interval=0,
               bank_ids=None, total_banks=0, head_offset=0, total_heads=0, check_status=False,
-              checkpoints=None, checkpoint_block=0):
+              checkpoints=None, checkpoint_block=0, chunked=False):
     """Per-bank recurrence over dispatched events; returns reads [NT, KR, V] in the activation dtype.
 
     With ``cache`` ([batch, J, H, S, dv]) the state starts from it and, with
@@ -213,6 +213,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
     [head_offset, head_offset + heads) of a layer with ``total_heads`` heads.
     ``checkpoints`` (float32, training): receives the states the recurrence backward
     replays from, every ``checkpoint_block`` events (see ``scan_backward``).
+    ``chunked``: run the sequences on the tensor-core chunked kernel (``bdm_bank_scan_chunked``;
+    BF16, head_value_width a multiple of 128, no checkpoints).
     """
     _cuda(q, k, v, g, b, w, write_idx, read_idx, order, cu_seqlens, cache, bank_ids)
     if bank_ids is not None and (bank_ids.dtype != torch.int32 or bank_ids.numel() != bank_count
@@ -240,7 +242,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
     lib = _lib.load()
     nbytes = lib.bdm_bank_scan_workspace_bytes(batch, bank_count)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
-    _lib.check(lib.bdm_bank_scan(
+    entry = lib.bdm_bank_scan_chunked if chunked else lib.bdm_bank_scan
+    _lib.check(entry(
         _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(b), _ptr(w), _ptr(wi), _ptr(ww), _ptr(ri), _ptr(rw), _ptr(order),
         _ptr(cu_seqlens), batch, time, bank_count, heads, bank_size, head_value_width, kw, kr, dtype_code(dt),
         int(routed_decay), float(scale), _ptr(u), _ptr(z), z.shape[0] if z is not None else 0,
@@ -248,7 +251,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         int(head_offset), int(total_heads),
         _ptr(cache), dtype_code(cache.dtype) if cache is not None else 0,
         int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _ptr(checkpoints),
-        int(checkpoint_block) if checkpoints is not None else 0, _stream(q.device)), 'bdm_bank_scan')
+        int(checkpoint_block) if checkpoints is not None else 0, _stream(q.device)),
+        'bdm_bank_scan_chunked' if chunked else 'bdm_bank_scan')
     if check_status:  # synchronises: the kernel's error bits (a bounded producer/consumer wait that gave up)
         status = int(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32).item())
         if status:

@@ -198,6 +198,27 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
                           int state_interval, void *reads,
                           void *workspace, int64_t workspace_bytes, float *checkpoints, int checkpoint_block,
                           void *stream);
+/*
+ * bdm_bank_scan with the sequences below the long-sequence bound run in chunks on the tensor
+ * cores (tcgen05.mma kind::tf32, accumulators in tensor memory): per chunk of C events (the
+ * reference's BF16 storage interval, role_bank_kernel.py:153: 16 for bank_size <= 8, 8 for 16)
+ * U = (I + Z)^-1 (X - Y M0) and the state carry are tensor-core products; the inter-chunk state
+ * stays in FP32 registers.  Same arguments, outputs and storage policy as bdm_bank_scan.
+ * BF16 only, head_value_width a multiple of 128, state_interval 0 or C, no checkpoints;
+ * anything else returns BDM_ERR_UNSUPPORTED.  Outputs agree with bdm_bank_scan within the BF16
+ * tolerance (tf32 operands), not bit for bit.
+ */
+BDM_API int bdm_bank_scan_chunked(const void *q, const void *k, const void *v, const float *g, const void *b,
+                                  const void *w, const int64_t *write_idx, const void *write_w,
+                                  const int64_t *read_idx, const void *read_w, const int64_t *order,
+                                  const int64_t *cu_seqlens, int64_t batch, int64_t time, int64_t bank_count,
+                                  int heads, int bank_size, int head_value_width, int kw, int kr, int dtype,
+                                  int routed_decay, float scale, const void *row_factor, const void *col_factor,
+                                  int64_t factor_cols, int factor_dtype, const int32_t *bank_ids,
+                                  int64_t total_banks, int head_offset, int total_heads, void *cache,
+                                  int cache_dtype, int store_final, int state_interval, void *reads,
+                                  void *workspace, int64_t workspace_bytes, float *checkpoints,
+                                  int checkpoint_block, void *stream);
 
 /*
  * Read combine + output normalisation + sigmoid gate.  Replaces

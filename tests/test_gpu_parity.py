@@ -169,7 +169,7 @@ def _controls(gen, nt, heads, s, dv, dtype, decay=0.3):
 
 
 def _run_scan(batch, time, bank_count, selected, heads, s, dv, dtype, *, interval, routed, cache_dtype=None,
-              seed=0, decay=0.3):
+              seed=0, decay=0.3, chunked=False):
     gen = torch.Generator().manual_seed(seed)
     nt = batch * time
     ctl = _controls(gen, nt, heads, s, dv, dtype, decay)
@@ -187,14 +187,14 @@ def _run_scan(batch, time, bank_count, selected, heads, s, dv, dtype, *, interva
               routed_decay=routed, scale=s ** -0.5)
     if cache_dtype is None:
         reads = ops.bank_scan(*args, **kw, row_factor=u.to(DEV), col_factor=z.to(DEV), state_interval=interval,
-                              check_status=True)
+                              check_status=True, chunked=chunked)
         final = None
         init_b = init[None]
     else:
         cache = torch.from_numpy(np.broadcast_to(init, (batch,) + init.shape).copy()).to(cache_dtype).to(DEV)
         init_b = npf(cache)
         reads = ops.bank_scan(*args, **kw, cache=cache, store_final=True, state_interval=interval,
-                              check_status=True)
+                              check_status=True, chunked=chunked)
         final = cache
     q, k, v, g, b, w = (npf(t) for t in ctl)
     sh = lambda x, last: x.reshape(batch, time, heads, last)
@@ -274,6 +274,47 @@ def test_bank_scan_c2_full_size_bf16():
     ours, ref, _, _ = _run_scan(8, 4096, 256, 8, 8, 8, 128, torch.bfloat16, interval=16, routed=True, seed=11)
     assert max_rel(ours, ref) <= BF16_TOL, max_rel(ours, ref)
     assert np.mean(ours == ref) > 0.5
+
+
+# ------------------------------------------------- tensor-core chunked recurrence
+@pytest.mark.parametrize('s,heads', [(8, 1), (8, 2), (4, 1), (4, 2), (16, 1), (16, 2), (8, 3)])
+def test_bank_scan_chunked_matches_oracle(s, heads):
+    # training storage policy (BF16 state rounded every C = 16 / 8 events, the chunk length)
+    ours, ref, _, _ = _run_scan(2, 200, 64, 4, heads, s, 128, torch.bfloat16, interval=state_interval(s),
+                                routed=True, seed=40 + s + heads, chunked=True)
+    assert max_rel(ours, ref) <= BF16_TOL, max_rel(ours, ref)
+
+
+@pytest.mark.parametrize('cache_dtype', [torch.float32, torch.bfloat16])
+def test_bank_scan_chunked_prefill_final_state_and_strong_decay(cache_dtype):
+    # prefill policy (no rounding until the cache store), two column tiles (dv = 256), and decays
+    # strong enough that chunks exceed the split pair factor's range (the direct exp path)
+    for decay, seed in ((0.3, 7), (40.0, 8)):
+        ours, ref, final, ofinal = _run_scan(3, 150, 64, 8, 2, 8, 256, torch.bfloat16, interval=0, routed=True,
+                                             cache_dtype=cache_dtype, seed=seed, decay=decay, chunked=True)
+        assert max_rel(ours, ref) <= BF16_TOL, (decay, max_rel(ours, ref))
+        ofinal_c = oracle.bf16_round(ofinal) if cache_dtype == torch.bfloat16 else ofinal
+        assert max_rel(final.reshape(ofinal_c.shape), ofinal_c) <= BF16_TOL
+
+
+def test_bank_scan_chunked_c2_full_size():
+    """c2 geometry (8 x 4096 tokens, H=8, S=8, dv=128, J=256, B=8) against the oracle."""
+    ours, ref, _, _ = _run_scan(8, 4096, 256, 8, 8, 8, 128, torch.bfloat16, interval=16, routed=True, seed=11,
+                                chunked=True)
+    assert max_rel(ours, ref) <= BF16_TOL, max_rel(ours, ref)
+
+
+def test_bank_scan_chunked_rejects_unsupported():
+    gen = torch.Generator().manual_seed(0)
+    for dtype, dv, interval in ((torch.float32, 128, 0), (torch.bfloat16, 64, 16), (torch.bfloat16, 128, 4)):
+        ctl = [t.to(DEV) for t in _controls(gen, 32, 1, 8, dv, dtype)]
+        ww, wi, rw, ri = _random_routes(gen, 1, 32, 16, 2)
+        meta = ops.dispatch(wi.to(DEV), ri.to(DEV), 16)
+        with pytest.raises(NotImplementedError):
+            ops.bank_scan(*ctl, wi.to(DEV), ww.to(dtype).to(DEV), ri.to(DEV), rw.to(dtype).to(DEV), meta['order'],
+                          meta['cu_seqlens'], batch=1, time=32, bank_count=16, heads=1, bank_size=8,
+                          head_value_width=dv, routed_decay=True, scale=8 ** -0.5, state_interval=interval,
+                          chunked=True)
 
 
 # ------------------------------------------------------------------ layer
