@@ -28,6 +28,7 @@
 // of the block's loads in flight at once), so replay and reverse read only shared
 // memory, and the loops stay rolled (compact code, no instruction-cache misses).
 #include "common.cuh"
+#include "scan.cuh"
 
 namespace bdm {
 namespace {
@@ -112,7 +113,9 @@ struct ScanBwdParams {
     int ckpt_ready;     // the forward recurrence wrote the block checkpoints (sequences < kLongSeq events)
 };
 
-constexpr int64_t kLongSeq = 2048;  // the forward's long-sequence kernel (>= this many events) writes none
+// Sequences the forward may run on its long-sequence kernel, which writes no checkpoints: the
+// forward's long bound is at least kLongEvents, so every shorter sequence has them.
+constexpr int64_t kLongSeq = kLongEvents;
 
 template <int S, int COLS> struct BwdGeom {
     static constexpr int kBlock = 128 / (S * COLS);  // events between HBM checkpoints (16 KB of history)

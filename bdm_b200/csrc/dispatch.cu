@@ -19,6 +19,8 @@
 // and cu_seqlens[B*J_local] is the owned event count.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace bdm {
 namespace {
 
@@ -461,8 +463,9 @@ extern "C" int bdm_dispatch_owned(const int64_t *write_idx, const int64_t *read_
 // (32 MiB).  Every GPU that loads the library holds it until the process
 // exits.  Host code cannot use the array's name as a device address; the
 // first call on each device looks the address up with cudaGetSymbolAddress
-// while that device is current and caches it, so make that first call before
-// any stream capture.  All calls share the one array: calls whose kernels can
+// while that device is current and caches it with the id of the device's
+// context, so make that first call before any stream capture.  A call after
+// the context was re-created (cudaDeviceReset) looks the address up again.  All calls share the one array: calls whose kernels can
 // overlap on the GPU (different streams, or different host threads on one
 // device) race on it and must be ordered by the caller.  The sort writes every
 // scratch byte it reads, so no clearing is needed between calls.
@@ -475,7 +478,36 @@ constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_dispatch_scratch[kNoAllocScratchBytes];
 
-void *g_scratch_ptr[kMaxDevices] = {};
+// The looked-up address per device, with the id of the context it belongs to: after
+// cudaDeviceReset the device's primary context (and with it the array's address) is new, so
+// a cached address is only used while the current context id matches.
+struct ScratchSlot {
+    unsigned long long context = 0;
+    void *ptr = nullptr;
+};
+ScratchSlot g_scratch[kMaxDevices];
+std::mutex g_scratch_mu;
+
+// Id of the calling thread's current context (driver entry points reached through the runtime,
+// so the library needs no link against the driver library); 0 when unknown.
+unsigned long long current_context_id() {
+    using GetCurrentFn = int (*)(void **);
+    using GetIdFn = int (*)(void *, unsigned long long *);
+    static GetCurrentFn get_current = [] {
+        void *f = nullptr;
+        return cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault) == cudaSuccess
+                   ? reinterpret_cast<GetCurrentFn>(f) : nullptr;
+    }();
+    static GetIdFn get_id = [] {
+        void *f = nullptr;
+        return cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault) == cudaSuccess
+                   ? reinterpret_cast<GetIdFn>(f) : nullptr;
+    }();
+    void *ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+    return id;
+}
 
 }  // namespace
 }  // namespace bdm
@@ -491,11 +523,19 @@ extern "C" int bdm_dispatch_noalloc(const int64_t *write_idx, const int64_t *rea
     int rc = cuda_status(cudaGetDevice(&dev));
     if (rc) return rc;
     if (dev < 0 || dev >= kMaxDevices) return BDM_ERR_UNSUPPORTED;
-    void *ptr = __atomic_load_n(&g_scratch_ptr[dev], __ATOMIC_ACQUIRE);
-    if (!ptr) {
-        rc = cuda_status(cudaGetSymbolAddress(&ptr, g_dispatch_scratch));
-        if (rc) return rc;
-        __atomic_store_n(&g_scratch_ptr[dev], ptr, __ATOMIC_RELEASE);
+    void *ptr = nullptr;
+    {
+        const unsigned long long context = current_context_id();
+        std::lock_guard<std::mutex> lock(g_scratch_mu);
+        ScratchSlot &slot = g_scratch[dev];
+        if (slot.ptr && context != 0 && slot.context == context) {
+            ptr = slot.ptr;
+        } else {  // first call on this device, or its context was re-created (or its id is unknown)
+            rc = cuda_status(cudaGetSymbolAddress(&ptr, g_dispatch_scratch));
+            if (rc) return rc;
+            slot.ptr = ptr;
+            slot.context = current_context_id();
+        }
     }
     return bdm_dispatch(write_idx, read_idx, batch, time, kw, kr, bank_count, order, cu_seqlens, inverse, tokens,
                         error_word, ptr, kNoAllocScratchBytes, stream);

@@ -332,17 +332,22 @@ class BankedDeltaMemory(nn.Module):
         reads = self._bank_pass(controls, routes, batch, time, row_factor=self.initial_row_factor,
                                 col_factor=self.initial_column_factor, state_interval=interval)
         ri = routes[3].reshape(batch * time, -1)
-        return self._output(hidden, reads, ri, gate, round_each=False)
+        out = self._output(hidden, reads, ri, gate, round_each=False)
+        ops.check_scan_status(hidden.device)  # non-blocking: raises once an earlier timeout is seen
+        return out
 
     def _forward_train(self, hidden):
         batch, time, _ = hidden.shape
         if self.bank_size not in (4, 8, 16):
             raise NotImplementedError('the training backward supports bank_size 4, 8 or 16')
+        if self.head_value_width > 256:  # the event VJP keeps a head's value row in one warp
+            raise NotImplementedError('the training backward supports head_value_width <= 256')
         weight, bias, cols = self._fused_projection_autograd()
         proj = torch.addmm(bias, hidden.reshape(batch * time, self.hidden_size), weight.t())
         normed = _BankTraining.apply(proj, self.f_proj[1].weight, self.A_log, self.dt_bias, self.initial_row_factor,
                                      self.initial_column_factor, self.output_norm_weight,
                                      getattr(self, 'output_norm_bias', None), self, cols, batch, time)
+        ops.check_scan_status(hidden.device)
         return F.linear(normed, self.o_proj.weight, self.o_proj.bias).reshape(batch, time, self.hidden_size)
 
     # ---------------------------------------------------- stateful inference
@@ -384,7 +389,9 @@ class BankedDeltaMemory(nn.Module):
         if state.dtype != cache_dtype:
             state = state.to(cache_dtype)
         ri = routes[3].reshape(batch * time, -1)
-        return self._output(hidden, reads, ri, gate, round_each=True), state
+        out = self._output(hidden, reads, ri, gate, round_each=True)
+        ops.check_scan_status(hidden.device)
+        return out, state
 
     def prefill(self, hidden, state=None, *, state_dtype=None):
         """Process a prefix (inference.py:110-131); BF16 cache storage rounds once, at handoff."""
@@ -498,6 +505,7 @@ class _BankTraining(torch.autograd.Function):
         (proj, f, wf2, a_log, dt_bias, row_factor, col_factor, norm_w, norm_b, q, k, v, g, b, w, ww, wi, rw, ri,
          order, cu, raw, ckpt) = ctx.saved_tensors
         m, cols, batch, time = ctx.layer, ctx.cols, ctx.batch, ctx.time
+        ops.check_scan_status(proj.device)  # the forward's reads and checkpoints feed everything below
         H, S, dv, V, J = m.num_heads, m.bank_size, m.head_value_width, m.value_width, m.bank_count
         layer_norm = m.config.output_normalization == 'layer'
         d_proj = torch.empty_like(proj)

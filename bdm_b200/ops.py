@@ -54,6 +54,80 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+# --------------------------------------------------------------- recurrence status
+class _ScanStatus:
+    """Sticky error bits of the bank recurrence on one device.
+
+    Every bank_scan ORs its launch's status word into ``word`` on the launch stream (no host
+    sync).  A bit means a bounded wait inside the recurrence gave up (a producer / consumer
+    staging wait or a tensor-core completion wait); the reads and final states of that launch
+    are then unspecified.  The bits stay set until reset_scan_status.
+    """
+
+    def __init__(self, device):
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = None
+        self.last = 0
+
+
+_SCAN_STATUS: dict = {}
+
+
+def _scan_status_of(device) -> _ScanStatus:
+    device = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+    if device.index is None:
+        device = torch.device('cuda', torch.cuda.current_device())
+    st = _SCAN_STATUS.get(device.index)
+    if st is None:
+        st = _SCAN_STATUS[device.index] = _ScanStatus(device)
+    return st
+
+
+def scan_status(device=None, *, wait: bool = False) -> int:
+    """Error bits the bank recurrence has recorded on ``device`` (0 = none).
+
+    Without ``wait`` this never blocks: it returns the latest snapshot that has reached the
+    host and starts the next asynchronous snapshot, so an error shows up at most one poll
+    late.  With ``wait`` it synchronises the current stream and returns the current bits.
+    """
+    st = _scan_status_of(device)
+    if torch.cuda.is_current_stream_capturing():
+        return st.last
+    stream = torch.cuda.current_stream(st.word.device)
+    if wait:
+        stream.synchronize()
+        st.last = int(st.word.item())
+        return st.last
+    if st.event is not None and st.event.query():
+        st.last = int(st.host.item())
+        st.event = None
+    if st.event is None:
+        st.host.copy_(st.word, non_blocking=True)
+        st.event = torch.cuda.Event()
+        st.event.record(stream)
+    return st.last
+
+
+def check_scan_status(device=None, *, wait: bool = False) -> None:
+    """Raises BDMError if the recurrence recorded an error (see scan_status).  No-op off CUDA."""
+    if device is not None and torch.device(device).type != 'cuda':
+        return
+    bits = scan_status(device, wait=wait)
+    if bits:
+        raise _lib.BDMError(f'bank recurrence: device status {bits:#x} (a bounded wait inside the kernel gave up; '
+                            f'outputs since then are unspecified; reset with ops.reset_scan_status)')
+
+
+def reset_scan_status(device=None) -> None:
+    st = _scan_status_of(device)
+    st.word.zero_()
+    if st.event is not None:
+        st.event.synchronize()
+        st.event = None
+    st.last = 0
+
+
 def route(logits: torch.Tensor, *, bank_count: int, selected_banks: int, factors=None):
     """Product-key top-B routing of ``logits[..., J1+J2]`` (last dim may be a strided view).
 
@@ -253,6 +327,8 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _ptr(checkpoints),
         int(checkpoint_block) if checkpoints is not None else 0, _stream(q.device)),
         'bdm_bank_scan_chunked' if chunked else 'bdm_bank_scan')
+    sticky = _scan_status_of(q.device).word
+    sticky.bitwise_or_(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32))
     if check_status:  # synchronises: the kernel's error bits (a bounded producer/consumer wait that gave up)
         status = int(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32).item())
         if status:
@@ -350,6 +426,9 @@ def bank_histogram(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: 
 
 
 OWNERSHIP_MODES = {'contiguous': 0, 'balanced': 1}
+# Limits of the balanced partition (one CTA sorts the whole bank table in shared memory, one
+# lane per rank); larger tables or worlds use contiguous ranges.
+MAX_BALANCED_BANKS, MAX_BALANCED_WORLD = 16384, 32
 
 
 def bank_owners(counts: torch.Tensor | None, bank_count: int, world: int, *, mode: str = 'balanced',

@@ -41,6 +41,8 @@ choreography in ``forward`` can be exercised with other stage implementations
 """
 from __future__ import annotations
 
+import warnings
+
 import torch
 import torch.distributed as dist
 from torch.nn import functional as F
@@ -156,6 +158,12 @@ class BankShardedMemory:
         self.rank, self.world = self.comm.rank, self.comm.world
         if layer.bank_count % self.world:
             raise NotImplementedError(f'{layer.bank_count} banks do not divide over {self.world} ranks')
+        if ownership == 'balanced' and (layer.bank_count > ops.MAX_BALANCED_BANKS
+                                        or self.world > ops.MAX_BALANCED_WORLD):
+            warnings.warn(f'the balanced bank partition supports at most {ops.MAX_BALANCED_BANKS} banks and '
+                          f'{ops.MAX_BALANCED_WORLD} ranks; {layer.bank_count} banks over {self.world} ranks use '
+                          'contiguous ranges', stacklevel=2)
+            self.ownership = 'contiguous'
         self.local_banks = layer.bank_count // self.world
         self.last_partition = None  # (owner, slot, members, counts) of the latest call
         self._chunk_streams = None
@@ -275,6 +283,7 @@ class BankShardedMemory:
                               col_factor=lay.initial_column_factor, state_interval=interval,
                               bank_ids=members[self.rank], total_banks=lay.bank_count)
         self._mark('recurrence', reads)
+        ops.check_scan_status(reads.device)  # non-blocking: raises once an earlier timeout is seen
         part = ops.combine_partial(reads, ri.reshape(batch * time, -1), owner, self.rank)
         self._mark('partial_combine', part)
         return part

@@ -1,4 +1,4 @@
-"""Benchmark: BDM layer prefill tokens/s on B200 (BASELINE config c2), plus c3 decode, c4 and training.
+"""Benchmark: BDM layer prefill tokens/s on B200 (config c2), plus c3 decode, c4 and training.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 

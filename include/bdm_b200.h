@@ -108,8 +108,9 @@ BDM_API int bdm_dispatch(const int64_t *write_idx, const int64_t *read_idx, int6
  * fixed 32 MiB array inside the library (held on every GPU that loads it until
  * exit).  Needs bdm_dispatch_workspace_bytes(...) <= 32 MiB, else returns
  * BDM_ERR_WORKSPACE.  The first call on a device looks the array up (make it
- * before any stream capture).  Calls share the array: calls that may overlap
- * on the GPU race and must be ordered by the caller.
+ * before any stream capture), and so does the first call after the device's
+ * context was re-created (cudaDeviceReset).  Calls share the array: calls that
+ * may overlap on the GPU race and must be ordered by the caller.
  */
 BDM_API int bdm_dispatch_noalloc(const int64_t *write_idx, const int64_t *read_idx, int64_t batch, int64_t time,
                                  int kw, int kr, int64_t bank_count, int64_t *order, int64_t *cu_seqlens,

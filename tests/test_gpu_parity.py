@@ -2,7 +2,7 @@
 
 Bit-exact: routing indices, dispatch order / cu_seqlens / inverse / tokens.
 Floating point, max-relative error max|a-b| / max|b|:
-  FP32 runs            1e-4   ("within 1e-4 against an FP32 run")
+  FP32 runs            1e-4   (north star: "within 1e-4 against an FP32 run")
   BF16 runs            2e-2   (north star: "2e-2 max-relative error in BF16")
 """
 import os
@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import oracle
-from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, near_square_factors, ops, state_interval
+from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory, _lib, near_square_factors, ops, state_interval
 
 pytestmark = pytest.mark.gpu
 
@@ -270,7 +270,7 @@ def test_bank_scan_plain_decay_and_fp32_against_golden(golden_dir):
 
 
 def test_bank_scan_c2_full_size_bf16():
-    """BASELINE c2 geometry (8 x 4096 tokens, H=8, S=8, dv=128, J=256, B=8) against the oracle."""
+    """c2 geometry (8 x 4096 tokens, H=8, S=8, dv=128, J=256, B=8) against the oracle."""
     ours, ref, _, _ = _run_scan(8, 4096, 256, 8, 8, 8, 128, torch.bfloat16, interval=16, routed=True, seed=11)
     assert max_rel(ours, ref) <= BF16_TOL, max_rel(ours, ref)
     assert np.mean(ours == ref) > 0.5
@@ -315,6 +315,26 @@ def test_bank_scan_chunked_rejects_unsupported():
                           meta['cu_seqlens'], batch=1, time=32, bank_count=16, heads=1, bank_size=8,
                           head_value_width=dv, routed_decay=True, scale=8 ** -0.5, state_interval=interval,
                           chunked=True)
+
+
+def test_scan_status_is_sticky_and_polled_without_blocking():
+    dev = torch.device(DEV, torch.cuda.current_device())
+    ops.reset_scan_status(dev)
+    _run_scan(1, 64, 16, 2, 1, 8, 128, torch.bfloat16, interval=16, routed=True, seed=2)
+    assert ops.scan_status(dev, wait=True) == 0
+    ops.check_scan_status(dev)
+    # a launch's error bits (set here by hand: a wait that gave up) stay until reset; the
+    # non-blocking poll reports them once its snapshot has reached the host
+    ops._scan_status_of(dev).word.fill_(1)
+    torch.cuda.synchronize()
+    ops.scan_status(dev)
+    torch.cuda.synchronize()
+    with pytest.raises(_lib.BDMError):
+        ops.check_scan_status(dev)
+    with pytest.raises(_lib.BDMError):
+        ops.check_scan_status(dev, wait=True)
+    ops.reset_scan_status(dev)
+    assert ops.scan_status(dev, wait=True) == 0
 
 
 # ------------------------------------------------------------------ layer

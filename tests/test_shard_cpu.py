@@ -57,6 +57,24 @@ def test_partition_rules(world):
     assert lb.max() - lb.mean() <= counts.max()
 
 
+class _FakeComm:
+    def __init__(self, rank, world):
+        self.rank, self.world = rank, world
+
+
+@pytest.mark.parametrize('bank_count,world', [(32768, 2), (16384 * 4, 8), (16384, 64)])
+def test_balanced_partition_beyond_its_limits_uses_contiguous_ranges(bank_count, world):
+    cfg = BSDMConfig(dim=64, bank_count=bank_count, bank_size=8, selected_banks=4, value_width=32, num_heads=1)
+    m = BlockSparseDeltaMemory(cfg, seed=0)
+    with pytest.warns(UserWarning, match='contiguous'):
+        sharded = BankShardedMemory(m, comm=_FakeComm(0, world), ownership='balanced')
+    assert sharded.ownership == 'contiguous' and sharded.local_banks == bank_count // world
+    # within the limits the requested partition stays
+    small = BlockSparseDeltaMemory(BSDMConfig(dim=64, bank_count=256, bank_size=8, selected_banks=4, value_width=32,
+                                              num_heads=1), seed=0)
+    assert BankShardedMemory(small, comm=_FakeComm(0, 2), ownership='balanced').ownership == 'balanced'
+
+
 class OracleStages(BankShardedMemory):
     """The sharded forward with every compute stage done by the CPU oracle."""
 

@@ -131,6 +131,15 @@ def test_training_plumbing_covers_every_gradient(monkeypatch, cfg_cls, heads, dt
     assert torch.equal(covered, torch.ones_like(covered))
 
 
+def test_training_rejects_wide_heads_before_any_work():
+    # H = 1 with value_width 512: the backward's event VJP supports head_value_width <= 256, so the
+    # training forward refuses up front instead of failing in backward after the forward ran
+    cfg = BSDMConfig(dim=64, bank_count=64, bank_size=8, selected_banks=4, value_width=512, num_heads=1)
+    m = BankedDeltaMemory(cfg, seed=1)
+    with pytest.raises(NotImplementedError, match='head_value_width'):
+        m._forward_train(torch.randn(1, 4, 64, requires_grad=True))
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(('127.0.0.1', 0))
