@@ -65,8 +65,11 @@ class _ScanStatus:
     """
 
     def __init__(self, device):
-        self.word = torch.zeros(1, dtype=torch.int32, device=device)
-        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        # normal tensors even when the first call runs under inference_mode, so later calls
+        # outside it may update them in place
+        with torch.inference_mode(False):
+            self.word = torch.zeros(1, dtype=torch.int32, device=device)
+            self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.event = None
         self.last = 0
 

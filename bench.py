@@ -44,6 +44,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 # ----------------------------------------------------------------- workloads
+C1 = dict(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=64, num_heads=1)
+C1_BATCH, C1_TIME = 2, 512
 C2 = dict(dim=1024, bank_count=256, bank_size=8, selected_banks=8, value_width=1024, num_heads=8)
 C2_BATCH, C2_TIME, C2_CHUNK = 8, 4096, 64
 C3 = dict(dim=1024, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
@@ -251,6 +253,111 @@ def cpu_forward_sample(batch, time_, seed=1):
     return batch * time_ / dt, dt, threads
 
 
+def cpu_decode_sample(steps=8, seed=2):
+    """Time ``steps`` decode steps of the CPU restatement (oracle/) at c3 (batch 64, J = 2048) on a c3-shaped
+    BF16 cache (the product-key initial state: a step's cost does not depend on the cache values)."""
+    import numpy as np
+
+    import oracle
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
+    threads = oracle.set_threads(0)
+    cfg = BSDMConfig(**C3)
+    m = BlockSparseDeltaMemory(cfg, seed=2).to(torch.bfloat16)
+    params = {k: v.float().numpy() for k, v in m.state_dict().items()}
+    layer = oracle.OracleLayer({k: getattr(cfg, k) for k in cfg.__dataclass_fields__}, params, bf16=True)
+    state = np.ascontiguousarray(np.broadcast_to(layer.initial_state()[None], (C3_BATCH,) +
+                                                 layer.initial_state().shape))
+    gen = torch.Generator().manual_seed(seed)
+    xs = [torch.randn(C3_BATCH, 1, cfg.dim, generator=gen).to(torch.bfloat16).float().numpy() for _ in range(steps)]
+    layer.step(xs[0], state)  # warm-up
+    t0 = time.perf_counter()
+    for x in xs:
+        y, state = layer.step(x, state)
+    dt = time.perf_counter() - t0
+    assert np.isfinite(y).all()
+    return C3_BATCH * steps / dt, dt, threads
+
+
+def cpu_c4_sample(time_=256, seed=3):
+    """Time the CPU restatement of the c4 layer forward (Zipf-skewed router) on one row of time_ tokens."""
+    import numpy as np
+
+    import oracle
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
+    threads = oracle.set_threads(0)
+    cfg = BSDMConfig(**C4)
+    m = BlockSparseDeltaMemory(cfg, seed=3)
+    zipf_router_bias(m)
+    m = m.to(torch.bfloat16)
+    params = {k: v.float().numpy() for k, v in m.state_dict().items()}
+    layer = oracle.OracleLayer({k: getattr(cfg, k) for k in cfg.__dataclass_fields__}, params, bf16=True)
+    gen = torch.Generator().manual_seed(3000 + seed)
+    x = torch.randn(1, time_, cfg.dim, generator=gen).to(torch.bfloat16).float().numpy()
+    t0 = time.perf_counter()
+    y = layer.forward(x)
+    dt = time.perf_counter() - t0
+    assert np.isfinite(y).all()
+    return time_ / dt, dt, threads
+
+
+def c1_layer(dtype=torch.float32):
+    """c1: BSDMConfig(256, 256, 8, 8, 64, 1), seed 0, initial memory N(0, 0.02) (factors N(0, 0.02 / sqrt 2))."""
+    from bdm_b200 import BSDMConfig, BlockSparseDeltaMemory
+    m = BlockSparseDeltaMemory(BSDMConfig(**C1), seed=0)
+    gen = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        for f in (m.initial_row_factor, m.initial_column_factor):
+            f.copy_(torch.randn(f.shape, generator=gen) * (0.02 / 2 ** 0.5))
+    return m.to(dtype)
+
+
+def cpu_c1_sample():
+    """The CPU restatement of the c1 layer forward in full (batch 2 x 512, FP32)."""
+    import numpy as np
+
+    import oracle
+    threads = oracle.set_threads(0)
+    m = c1_layer()
+    params = {k: v.float().numpy() for k, v in m.state_dict().items()}
+    layer = oracle.OracleLayer({k: getattr(m.config, k) for k in m.config.__dataclass_fields__}, params, bf16=False)
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(C1_BATCH, C1_TIME, C1['dim'], generator=gen).numpy()
+    t0 = time.perf_counter()
+    y = layer.forward(x)
+    dt = time.perf_counter() - t0
+    assert np.isfinite(y).all()
+    return C1_BATCH * C1_TIME / dt, dt, threads
+
+
+def run_c1(dev, rank, world, args):
+    """c1 (the reference's CPU-runnable case) on one GPU: forward of batch 2 x 512, FP32, CUDA events."""
+    m = c1_layer().to(dev)
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(C1_BATCH, C1_TIME, C1['dim'], generator=gen).to(dev)
+    steps = 20
+    with torch.inference_mode():
+        for _ in range(3):
+            m(x)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            m(x)
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    out = {'metric': 'BDM layer forward tokens/sec (c1: batch 2 x seq 512, d_model 256, J=256, S=8, B=8, d_v=64, '
+                     'FP32 activations, BF16 state storage policy)',
+           'value': C1_BATCH * C1_TIME / (ms / 1000), 'unit': 'tokens/s', 'steps': steps, 'warmup': 3,
+           'ms_per_step': ms, 'path': 'BlockSparseDeltaMemory.forward (one GPU; launch-bound at 1024 tokens)'}
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        tps, dt, threads = cpu_c1_sample()
+        out['cpu_baseline'] = {'value': tps, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+                               'sample': f'full c1 forward, batch {C1_BATCH} x seq {C1_TIME} ({dt:.2f} s), '
+                                         'CPU restatement oracle/'}
+    return out
+
+
 def cpu_train_sample(batch, time_, seed=4):
     """Time one forward + backward of the c5 layer (BF16) with the gradient oracle (torch autograd
     over the CPU restatement, oracle/grad.py) on batch x time_ tokens, on the host cores."""
@@ -379,6 +486,16 @@ def run_ours(args, world, rank, local):
                      'layer_frac': roof_ms / (total_ms / args.steps), 'layer_roofline_ms': roof_ms},
         'clocks': clocks.summary(),
     }
+    if not args.skip_scan_variants:
+        try:
+            line['scan_variants'] = run_scan_variants(layer, x, dev, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['scan_variants'] = {'error': repr(e)[:300]}
+    if not args.skip_c1 and world == 1:
+        try:
+            line['c1'] = run_c1(dev, rank, world, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['c1'] = {'error': repr(e)[:300]}
     if not args.skip_decode:
         try:
             line['decode'] = run_decode(dev, rank, world, args)
@@ -415,6 +532,46 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_scan_variants(layer, x, dev, args):
+    """The c2 recurrence alone on the layer's own controls and routes: the default per-event kernel
+    (bdm_bank_scan) and the tensor-core chunked kernel (bdm_bank_scan_chunked), CUDA events around
+    each call, the 256 MiB L2 flush between calls."""
+    from bdm_b200 import ops, state_interval
+    batch, time_ = x.shape[0], x.shape[1]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    with torch.inference_mode():
+        controls, routes, _ = layer._controls_and_routes(x)
+        ww, wi, rw, ri = routes
+        meta = ops.dispatch(wi, ri, layer.bank_count)
+        args_ = (*controls, wi, ww, ri, rw, meta['order'], meta['cu_seqlens'])
+        kw = dict(batch=batch, time=time_, bank_count=layer.bank_count, heads=layer.num_heads,
+                  bank_size=layer.bank_size, head_value_width=layer.head_value_width,
+                  routed_decay=layer.config.routed_decay, scale=layer.bank_size ** -0.5,
+                  row_factor=layer.initial_row_factor, col_factor=layer.initial_column_factor,
+                  state_interval=state_interval(layer.bank_size))
+        out = {}
+        for name, chunked in (('per_event', False), ('chunked_tensor_core', True)):
+            for _ in range(3):
+                ops.bank_scan(*args_, **kw, chunked=chunked)
+            times = []
+            for _ in range(max(args.steps, 3)):
+                flush.zero_()
+                s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_.record()
+                ops.bank_scan(*args_, **kw, chunked=chunked)
+                e_.record()
+                torch.cuda.synchronize()
+                times.append(s_.elapsed_time(e_))
+            out[name] = {'kernel_ms': statistics.mean(times), 'min_ms': min(times)}
+    hbm_peak, _, _ = load_peaks()
+    kernel_bytes, _ = c2_bytes_per_token(batch=batch)
+    for v in out.values():
+        v['achieved_gbs'] = kernel_bytes * batch * time_ / (v['kernel_ms'] / 1000) / 1e9
+        v['frac'] = v['achieved_gbs'] / hbm_peak
+    return {'what': 'c2 recurrence alone (bdm_bank_scan vs bdm_bank_scan_chunked), same inputs, BF16 storage policy',
+            **out}
+
+
 def run_decode(dev, rank, world, args):
     """c3: 1024 single-token steps at batch 64 on a state pre-filled by a 2048-token prefill.
 
@@ -441,7 +598,7 @@ def run_decode(dev, rank, world, args):
             run(toks[i])
         end.record()
         torch.cuda.synchronize()
-        eager_n = 64
+        eager_n = min(64, steps + 8)
         es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         es.record()
         for i in range(eager_n):
@@ -450,6 +607,13 @@ def run_decode(dev, rank, world, args):
         torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end), world)
     eager_ms = es.elapsed_time(ee) / eager_n
+    del state, run
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        tps_cpu, dt, threads = cpu_decode_sample()
+        cpu = {'value': tps_cpu, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+               'sample': f'8 decode steps at batch {C3_BATCH} ({dt:.2f} s) on a c3-shaped BF16 cache, '
+                         'CPU restatement oracle/ (controllers, routers, the per-bank step and the output)'}
     weight_bytes = sum(p.numel() * p.element_size() for p in layer.parameters())
     hbm_peak, _, _ = load_peaks()
     bpt = c3_bytes_per_token(weight_bytes=weight_bytes)
@@ -457,7 +621,8 @@ def run_decode(dev, rank, world, args):
     return {'metric': 'BDM decode tokens/sec (c3: batch 64, J=2048, S=8, B=8, d_v=128, 2048-token prefill)',
             'value': tps, 'unit': 'tokens/s', 'steps': steps, 'ms_per_step': ms / steps,
             'path': 'CUDA-graphed step (BlockSparseDeltaMemory.capture_step)',
-            'eager_step_ms': eager_ms, 'state_bytes': state.numel() * state.element_size(),
+            'eager_step_ms': eager_ms, 'state_bytes': C3_BATCH * C3['bank_count'] * C3['bank_size'] * C3['value_width'] * 2,
+            **({'cpu_baseline': cpu} if cpu else {}),
             'roofline': {'bound': 'hbm', 'bytes_per_token': bpt, 'achieved': bpt * tps / world / 1e9,
                          'peak': hbm_peak, 'unit': 'GB/s', 'frac': bpt * tps / world / 1e9 / hbm_peak}}
 
@@ -684,6 +849,30 @@ def run_c4(dev, rank, world, args):
                         'unit': 'GB/s', 'achieved': layer_bytes * tokens / (ms / 1000) / 1e9 / world,
                         'frac': roof_ms / ms, 'roofline_ms': roof_ms},
            'clocks': clocks.summary()}
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        tps_cpu, dt, threads = cpu_c4_sample()
+        out['cpu_baseline'] = {'value': tps_cpu, 'unit': 'tokens/s', 'cores': threads, 'kind': 'port',
+                               'sample': f'c4 layer forward truncated to batch 1 x seq 256 ({dt:.1f} s; truncated T), '
+                                         'CPU restatement oracle/'}
+    if world > 1 and args.c4_ownership == 'balanced':
+        # the bank table as contiguous index ranges (rank r owns [r J/R, (r+1) J/R)), timed the same way
+        ranges = BankShardedMemory(layer, ownership='contiguous')
+        with torch.inference_mode():
+            ranges(x)
+            torch.cuda.synchronize()
+            barrier(world)
+            cs, ce = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            cs.record()
+            for _ in range(steps):
+                ranges(x)
+            ce.record()
+            torch.cuda.synchronize()
+            barrier(world)
+        c_ms = max_over_ranks(cs.elapsed_time(ce), world) / steps
+        owner, _, _, counts = ranges.last_partition
+        load = torch.zeros(world, dtype=torch.float64, device=dev).index_add_(0, owner.long(), counts.double())
+        out['contiguous_partition'] = {'ms_per_step': c_ms, 'value': tokens / (c_ms / 1000),
+                                       'partition_load_max_over_mean': (load.max() / load.mean()).item()}
     if world > 1 and fwd.last_partition is not None:
         owner, _, _, counts = fwd.last_partition
         load = torch.zeros(world, dtype=torch.float64, device=dev).index_add_(0, owner.long(), counts.double())
@@ -710,6 +899,8 @@ def main():
     ap.add_argument('--decode-steps', type=int, default=C3_STEPS)
     ap.add_argument('--cpu-time', type=int, default=C2_TIME, help='sequence length of the CPU baseline sample')
     ap.add_argument('--skip-decode', action='store_true')
+    ap.add_argument('--skip-c1', action='store_true')
+    ap.add_argument('--skip-scan-variants', action='store_true')
     ap.add_argument('--skip-cpu', action='store_true')
     ap.add_argument('--skip-c4', action='store_true')
     ap.add_argument('--c4-steps', type=int, default=5)

@@ -319,6 +319,9 @@ def test_bank_scan_chunked_rejects_unsupported():
 
 def test_scan_status_is_sticky_and_polled_without_blocking():
     dev = torch.device(DEV, torch.cuda.current_device())
+    ops._SCAN_STATUS.pop(dev.index, None)
+    with torch.inference_mode():  # first use under inference_mode, later use outside it
+        _run_scan(1, 32, 16, 2, 1, 8, 128, torch.bfloat16, interval=16, routed=True, seed=1)
     ops.reset_scan_status(dev)
     _run_scan(1, 64, 16, 2, 1, 8, 128, torch.bfloat16, interval=16, routed=True, seed=2)
     assert ops.scan_status(dev, wait=True) == 0
