@@ -43,6 +43,9 @@ SIGNATURES = {
     'bdm_bank_scan_chunked': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int,
                                      _int, _int, _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _vp, _i64, _int,
                                      _int, _vp, _int, _int, _int, _vp, _vp, _i64, _vp, _int, _vp]),
+    'bdm_decode_token_step': (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _int,
+                                     _vp, _vp, _int, _int, _int, _int, _i64, _int, _int, _int, _int, _int, _flt, _vp,
+                                     _int, _vp, _vp, _flt, _int, _vp, _vp]),
     'bdm_combine_norm_gate': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _int, _vp,
                                      _vp]),
     'bdm_combine_norm_gate_save': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _int,

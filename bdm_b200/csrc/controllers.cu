@@ -15,6 +15,7 @@
 // g (and f_proj.1's dot product when the kernel computes f), one per 8-element
 // chunk of the wide v / w rows (streamed with 16-byte accesses).
 #include "common.cuh"
+#include "controller_math.cuh"
 
 namespace bdm {
 namespace {
@@ -22,13 +23,7 @@ namespace {
 constexpr int kCtlThreads = 256;
 constexpr int kMaxS = 16;
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
-__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
-// Wide activations use the hardware exp and an approximate divide (relative error
-// ~1e-6: below one BF16 ulp and far below the FP32 tolerance).
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+using namespace ctl;
 
 struct CtlArgs {
     const void *proj;
@@ -57,9 +52,9 @@ __device__ __forceinline__ void narrow_item(const CtlArgs &a, int64_t t, int h) 
         float ss = 0.f;
         for (int s = 0; s < S; ++s) {
             x[s] = rnd<T>(silu_f(Elem<T>::to_float(src[s])));
-            ss += x[s] * x[s];
+            ss = fmaf(x[s], x[s], ss);
         }
-        const float scale = a.qk_norm ? 1.0f / sqrtf(ss + 1e-6f) : 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+        const float scale = qk_scale(ss, a.qk_norm);
         T *dst = static_cast<T *>(role ? a.k : a.q) + o;
         for (int s = 0; s < S; ++s) dst[s] = Elem<T>::from_float(x[s] * scale);
     }
@@ -83,7 +78,7 @@ __device__ __forceinline__ void gate_item(const CtlArgs &a, int64_t t, int hs) {
     }
     const int h = hs / a.S;
     static_cast<T *>(a.b)[o] = Elem<T>::from_float(sigmoid_f(Elem<T>::to_float(row[a.col_b + hs])));
-    a.g[o] = -expf(a.a_log[h]) * softplus_f(fv + a.dt_bias[hs]);
+    a.g[o] = decay_gate(a.a_log[h], fv, a.dt_bias[hs]);
 }
 
 template <typename T>

@@ -408,6 +408,18 @@ class BankedDeltaMemory(nn.Module):
         if torch.is_grad_enabled() or hidden.shape[1] != 1:
             raise ValueError('step requires one token under no_grad/inference_mode')
         batch = hidden.shape[0]
+        if self.num_reads == self.num_writes:
+            # controllers, both routers and the bank step in one kernel after the projection GEMM
+            proj, cols = self._project(hidden.reshape(batch, self.hidden_size))
+            normed = ops.decode_token_step(
+                proj, cols, self.f_proj[1].weight, self.A_log, self.dt_bias, state, bank_count=self.bank_count,
+                selected_banks=self.num_reads, factors=self.factors, heads=self.num_heads, bank_size=self.bank_size,
+                head_value_width=self.head_value_width, qk_norm=self.config.qk_normalization,
+                routed_decay=self.config.routed_decay, scale=self.bank_size ** -0.5,
+                norm_weight=self.output_norm_weight, norm_bias=getattr(self, 'output_norm_bias', None),
+                eps=self.norm_eps, layer_norm=self.config.output_normalization == 'layer')
+            out = F.linear(normed, self.o_proj.weight, self.o_proj.bias)
+            return out.reshape(batch, 1, self.hidden_size), state
         controls, routes, gate = self._controls_and_routes(hidden)
         ww, wi, rw, ri = (r.reshape(batch, -1) for r in routes)
         # the step kernel also applies the output norm and gate (one launch instead of two)

@@ -409,6 +409,33 @@ def decode_step(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, state, *
     return raw if gate is None else out
 
 
+def decode_token_step(proj, cols, f_weight, a_log, dt_bias, state, *, bank_count: int, selected_banks: int,
+                      factors, heads: int, bank_size: int, head_value_width: int, qk_norm: str, routed_decay: bool,
+                      scale: float, norm_weight, norm_bias=None, eps: float = 1e-5, layer_norm: bool = True):
+    """A whole decode step from the fused projection ``proj`` [B, ld] (one token per row): controllers,
+    both routers and the bank step with combine, norm and gate in one launch; ``state`` updated in place.
+    Returns the normalised, gated [B, H*dv] (o_proj's input)."""
+    _cuda(proj, state)
+    if proj.stride(-1) != 1 or not state.is_contiguous():
+        raise ValueError('proj rows and the state must be contiguous')
+    batch = proj.shape[0]
+    ld = proj.stride(0) if batch > 1 else proj.shape[-1]
+    j1, j2 = factors
+    out = torch.empty((batch, heads * head_value_width), dtype=proj.dtype, device=proj.device)
+    wf2 = f_weight.detach().to(proj.dtype).contiguous()
+    nw = norm_weight.detach().to(proj.dtype).contiguous()
+    nb = norm_bias.detach().to(proj.dtype).contiguous() if norm_bias is not None else None
+    al = a_log.detach().float().contiguous()
+    dt = dt_bias.detach().float().contiguous()
+    _lib.check(_lib.load().bdm_decode_token_step(
+        _ptr(proj), batch, ld, cols['q'], cols['k'], cols['v'], cols['f'], cols['b'], cols['w'], cols['read'],
+        cols['write'], cols['gate'], _ptr(wf2), head_value_width, _ptr(al), _ptr(dt),
+        1 if qk_norm == 'nvidia' else 0, j1, j2, selected_banks, bank_count, heads, bank_size, head_value_width,
+        dtype_code(proj.dtype), int(routed_decay), float(scale), _ptr(state), dtype_code(state.dtype), _ptr(nw),
+        _ptr(nb), float(eps), 1 if layer_norm else 0, _ptr(out), _stream(proj.device)), 'bdm_decode_token_step')
+    return out
+
+
 # ------------------------------------------------------------ bank sharding
 
 def bank_histogram(write_idx: torch.Tensor, read_idx: torch.Tensor, bank_count: int,

@@ -491,6 +491,8 @@ def run_ours(args, world, rank, local):
             line['scan_variants'] = run_scan_variants(layer, x, dev, args)
         except Exception as e:  # keep the headline line even if the extra workload fails
             line['scan_variants'] = {'error': repr(e)[:300]}
+    if args.reference_gpu and rank == 0 and world == 1:
+        line['reference_gpu'] = run_reference_gpu(dev, args)
     if not args.skip_c1 and world == 1:
         try:
             line['c1'] = run_c1(dev, rank, world, args)
@@ -570,6 +572,75 @@ def run_scan_variants(layer, x, dev, args):
         v['frac'] = v['achieved_gbs'] / hbm_peak
     return {'what': 'c2 recurrence alone (bdm_bank_scan vs bdm_bank_scan_chunked), same inputs, BF16 storage policy',
             **out}
+
+
+def run_reference_gpu(dev, args):
+    """The reference's own GPU path on this GPU (its Triton 'role' backend, unmodified, from the copy
+    installed in baseline/_ref): the c2 forward and the c3 prefill + eager steps, CUDA events."""
+    ref_dir = os.path.join(ROOT, 'baseline', '_ref')
+    if not os.path.isdir(os.path.join(ref_dir, 'bsdm')):
+        return {'unavailable': 'reference not installed in baseline/_ref'}
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        import bsdm
+    except Exception as e:  # noqa: BLE001
+        return {'unavailable': f'import failed: {e!r}'[:300]}
+    out = {'path': "bsdm.BlockSparseDeltaMemory(backend='role') (reference Triton kernels), unmodified"}
+    try:
+        cfg = bsdm.BSDMConfig(**C2)
+        layer = bsdm.BlockSparseDeltaMemory(cfg, seed=1, backend='role').to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            layer.initial_row_factor.zero_()
+            layer.initial_column_factor.zero_()
+        gen = torch.Generator().manual_seed(1)
+        x = torch.randn(C2_BATCH, C2_TIME, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            layer(x)
+            torch.cuda.synchronize()
+            n = 3
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            for _ in range(n):
+                layer(x)
+            e_.record()
+            torch.cuda.synchronize()
+        ms = s_.elapsed_time(e_) / n
+        out['c2_forward'] = {'ms_per_step': ms, 'value': C2_BATCH * C2_TIME / (ms / 1000), 'unit': 'tokens/s',
+                             'steps': n, 'warmup': 1}
+        del layer, x
+    except Exception as e:  # noqa: BLE001
+        out['c2_forward'] = {'error': repr(e)[:300]}
+    try:
+        cfg = bsdm.BSDMConfig(**C3)
+        layer = bsdm.BlockSparseDeltaMemory(cfg, seed=2, backend='role').to(torch.bfloat16).to(dev)
+        gen = torch.Generator().manual_seed(2)
+        prefix = torch.randn(C3_BATCH, C3_PREFIX, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
+        toks = torch.randn(72, C3_BATCH, 1, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
+        with torch.no_grad():
+            layer.prefill(prefix[:1, :64])  # compiles its kernels
+            torch.cuda.synchronize()
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            _, state = layer.prefill(prefix)
+            e_.record()
+            torch.cuda.synchronize()
+            prefill_ms = s_.elapsed_time(e_)
+            for i in range(8):
+                _, state = layer.step(toks[64 + i], state)
+            torch.cuda.synchronize()
+            s_.record()
+            for i in range(64):
+                _, state = layer.step(toks[i], state)
+            e_.record()
+            torch.cuda.synchronize()
+        step_ms = s_.elapsed_time(e_) / 64
+        out['c3'] = {'prefill_ms': prefill_ms, 'step_ms': step_ms,
+                     'decode_value': C3_BATCH / (step_ms / 1000), 'unit': 'tokens/s', 'steps': 64, 'warmup': 8,
+                     'note': 'eager steps (the reference records cuda_graph=False for its sustained decode)'}
+    except Exception as e:  # noqa: BLE001
+        out['c3'] = {'error': repr(e)[:300]}
+    return out
 
 
 def run_decode(dev, rank, world, args):
@@ -900,6 +971,8 @@ def main():
     ap.add_argument('--cpu-time', type=int, default=C2_TIME, help='sequence length of the CPU baseline sample')
     ap.add_argument('--skip-decode', action='store_true')
     ap.add_argument('--skip-c1', action='store_true')
+    ap.add_argument('--reference-gpu', action='store_true',
+                    help="also time the reference's own Triton GPU path (installed in baseline/_ref)")
     ap.add_argument('--skip-scan-variants', action='store_true')
     ap.add_argument('--skip-cpu', action='store_true')
     ap.add_argument('--skip-c4', action='store_true')

@@ -403,6 +403,28 @@ BDM_API int bdm_decode_step(const void *q, const void *k, const void *v, const f
                     const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias, float eps,
                     int norm_mode, void *out, void *stream);
 
+/*
+ * One whole decode step from the fused input projection, in one launch: the controllers
+ * (_parameters.py:189-220, f_proj.1 computed in-kernel), both product-key routers
+ * (gdn2_banks.py:74-114) and the bank step with the ordered read sum, norm and gate (as
+ * bdm_decode_step, inference.py:161-194).  The step is then the projection GEMM, this call and
+ * o_proj.  Results equal bdm_controllers + bdm_route_pair + bdm_decode_step bit for bit.
+ *   proj [batch, ld] (dtype): one token per row; the column offsets name its q, k, v, f1
+ *   (f1_width), b, w, read and write router logits (j1 + j2 each) and output-gate blocks.
+ *   wf2 [H*S, f1_width] (dtype): f_proj.1's weight.  a_log [H], dt_bias [H*S] float.
+ *   qk_norm 1 = 'nvidia', 0 = 'original'.  selected: banks per role (j1 * j2 == bank_count).
+ *   state [batch, J, H, S, dv] (state_dtype) is updated in place.
+ *   out [batch, H*dv] (dtype): the normalised and gated read sum, o_proj's input.
+ */
+BDM_API int bdm_decode_token_step(const void *proj, int64_t batch, int64_t ld, int64_t col_q, int64_t col_k,
+                                  int64_t col_v, int64_t col_f1, int64_t col_b, int64_t col_w, int64_t col_read,
+                                  int64_t col_write, int64_t col_gate, const void *wf2, int f1_width,
+                                  const float *a_log, const float *dt_bias, int qk_norm, int j1, int j2,
+                                  int selected, int64_t bank_count, int heads, int bank_size, int head_value_width,
+                                  int dtype, int routed_decay, float scale, void *state, int state_dtype,
+                                  const void *norm_weight, const void *norm_bias, float eps, int norm_mode,
+                                  void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -561,6 +561,37 @@ def test_decode_step_fused_norm_gate(dtype, layer_norm):
         assert diff.max() <= 1e-6 * want.float().abs().max()
 
 
+@pytest.mark.parametrize('dtype,cache_dtype', [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+                                               (torch.bfloat16, torch.float32)])
+@pytest.mark.parametrize('heads,bank_size,norm,qk', [(1, 8, 'layer', 'nvidia'), (2, 16, 'rms', 'original'),
+                                                     (4, 4, 'layer', 'original')])
+def test_fused_decode_step_equals_separate_kernels(dtype, cache_dtype, heads, bank_size, norm, qk):
+    # bdm_decode_token_step (controllers + routers + bank step in one launch) against
+    # bdm_controllers + bdm_route_pair + bdm_decode_step on the same cache: bit for bit
+    cfg = BSDMConfig(dim=256, bank_count=512, bank_size=bank_size, selected_banks=8, value_width=64 * heads,
+                     num_heads=heads, output_normalization=norm, qk_normalization=qk)
+    torch.manual_seed(21)
+    m = BlockSparseDeltaMemory(cfg, seed=3).to(dtype).to(DEV)
+    with torch.no_grad():
+        x0 = torch.randn(6, 40, 256).to(dtype).to(DEV)
+        _, state = m.prefill(x0, state_dtype=cache_dtype)
+        for i in range(3):
+            xt = torch.randn(6, 1, 256).to(dtype).to(DEV)
+            ref_state = state.clone()
+            controls, routes, gate = m._controls_and_routes(xt)
+            ww, wi, rw, ri = (r.reshape(6, -1) for r in routes)
+            normed = ops.decode_step(*controls, wi, ww, ri, rw, ref_state, bank_count=m.bank_count, heads=heads,
+                                     bank_size=bank_size, head_value_width=m.head_value_width,
+                                     routed_decay=m.config.routed_decay, scale=bank_size ** -0.5, gate=gate,
+                                     norm_weight=m.output_norm_weight,
+                                     norm_bias=getattr(m, 'output_norm_bias', None), eps=m.norm_eps,
+                                     layer_norm=norm == 'layer')
+            ref = torch.nn.functional.linear(normed, m.o_proj.weight, m.o_proj.bias).reshape(6, 1, 256)
+            y, state = m.step(xt, state)
+            assert torch.equal(y, ref), i
+            assert torch.equal(state, ref_state), i
+
+
 def test_captured_decode_step_matches_eager_step():
     cfg = BSDMConfig(dim=256, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
     m = BlockSparseDeltaMemory(cfg, seed=2).to(torch.bfloat16).to(DEV)
