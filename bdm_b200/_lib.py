@@ -40,6 +40,7 @@ SIGNATURES = {
     'bdm_bank_scan': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int,
                              _int, _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _vp, _i64, _int, _int, _vp,
                              _int, _int, _int, _vp, _vp, _i64, _vp, _int, _vp]),
+    'bdm_scan_test_fault': (_int, [_int, ctypes.c_ulonglong]),
     'bdm_bank_scan_chunked': (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int,
                                      _int, _int, _int, _int, _int, _int, _flt, _vp, _vp, _i64, _int, _vp, _i64, _int,
                                      _int, _vp, _int, _int, _int, _vp, _vp, _i64, _vp, _int, _vp]),

@@ -25,6 +25,7 @@
 #include "common.cuh"
 #include "scan.cuh"
 
+#include <atomic>
 #include <type_traits>
 
 namespace bdm {
@@ -655,13 +656,13 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
     return t;
 }
-// Bounded wait for the phase of `parity` to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+// Bounded wait for the phase of `parity` to complete; false on timeout (after limit_ns).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned long long limit_ns) {
     if (mbar_test(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     for (long long i = 0; i < kWaitPolls; ++i) {
         if (mbar_test(bar, parity)) return true;
-        if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) break;
+        if ((i & 255) == 255 && global_ns() - t0 > limit_ns) break;
     }
     return false;
 }
@@ -727,6 +728,8 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
     __syncthreads();
 
     volatile int *abort_flag = &sh.abort;
+    const unsigned long long wait_ns = p.wait_ns ? p.wait_ns : kWaitNs;
+    bool withhold = p.test_fault == 1;  // diagnostics: skip the first hand-off of this CTA
     auto fail = [&]() {
         if (lane == 0) atomicOr(p.status, BDM_SCAN_ERR_TIMEOUT);
         *abort_flag = 1;
@@ -929,7 +932,7 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
             bool ok = true;
             // A batch's slot frees when the consumers finish the batch kWsSlots before it.
             auto acquire = [&](unsigned j) {
-                return j < kWsSlots || mbar_wait(&sh.empty[ring_slot(j)], use_parity(j - kWsSlots));
+                return j < kWsSlots || mbar_wait(&sh.empty[ring_slot(j)], use_parity(j - kWsSlots), wait_ns);
             };
             issue_rows(base, bn, sh.raw[it & 1], cur);
             if (!acquire(it)) ok = false;
@@ -944,7 +947,8 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
                 }
                 const int b = ring_slot(it);
                 const int n = finish(base - start, bn, sh.raw[it & 1], cur, b, sbn > 0);
-                mbar_arrive(&sh.full[b]);
+                if (withhold) withhold = false;  // the consumers' wait for this batch runs out
+                else mbar_arrive(&sh.full[b]);
                 if (n < bn) {  // cut: the next batch starts right after the n-th event
                     cp_async_wait_all();
                     base += n;
@@ -980,7 +984,7 @@ __device__ __forceinline__ void scan_long_units(const ScanParams &p, unsigned ch
             bool ok = true;
             while (base < end) {
                 const int b = ring_slot(it);
-                if (!mbar_wait(&sh.full[b], use_parity(it))) {
+                if (!mbar_wait(&sh.full[b], use_parity(it), wait_ns)) {
                     ok = false;
                     break;
                 }
@@ -1270,6 +1274,9 @@ int launch_scan_shape(const ScanParams &p, int S, cudaStream_t st) {
 
 namespace bdm {
 namespace {
+// Diagnostics set by bdm_scan_test_fault (process-wide; off unless a test turns them on).
+std::atomic<unsigned long long> g_scan_wait_ns{0};
+std::atomic<int> g_scan_test_fault{0};
 // Workspace: 256-byte header [counts (kLenClasses int32) at 0 | dynamic counters (uint64) at 64
 // (short kernel), 72 (long kernel) and 80 (chunked kernel) | status word (int32, BDM_SCAN_ERR_* bits) at 128], then the lists.
 constexpr int64_t kWsHeader = 256;
@@ -1336,6 +1343,8 @@ int bank_scan_impl(bool chunked, const void *q, const void *k, const void *v, co
     p.ckpt = checkpoints;
     p.ckpt_block = checkpoints ? checkpoint_block : 0;
     p.chunked = chunked ? 1 : 0;
+    p.wait_ns = g_scan_wait_ns.load(std::memory_order_relaxed);
+    p.test_fault = g_scan_test_fault.load(std::memory_order_relaxed);
     if (chunked && !chunk_scan_eligible(p, dtype, bank_size)) return BDM_ERR_UNSUPPORTED;
     char *ws = static_cast<char *>(workspace);
     int *counts = reinterpret_cast<int *>(ws);
@@ -1372,3 +1381,10 @@ int bank_scan_impl(bool chunked, const void *q, const void *k, const void *v, co
 
 extern "C" int bdm_bank_scan(BDM_SCAN_ARGS) { return bank_scan_impl(false, BDM_SCAN_PASS); }
 extern "C" int bdm_bank_scan_chunked(BDM_SCAN_ARGS) { return bank_scan_impl(true, BDM_SCAN_PASS); }
+
+extern "C" int bdm_scan_test_fault(int fault, unsigned long long wait_ns) {
+    if (fault != 0 && fault != 1) return BDM_ERR_INVALID;
+    bdm::g_scan_test_fault.store(fault, std::memory_order_relaxed);
+    bdm::g_scan_wait_ns.store(wait_ns, std::memory_order_relaxed);
+    return BDM_OK;
+}

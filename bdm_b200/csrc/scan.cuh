@@ -43,6 +43,10 @@ struct ScanParams {
     float *ckpt;
     int ckpt_block;
     int chunked;  // run the non-long classes on the tensor-core chunked kernel (chunk_scan.cu)
+    // Diagnostics (bdm_scan_test_fault): the long kernel's bounded-wait limit in ns (0: 2 s) and
+    // a test fault (1: its producer withholds the first batch hand-off, so the waits run out).
+    unsigned long long wait_ns;
+    int test_fault;
 };
 
 // Length classes of the work list (events per sequence, lower bounds), longest first.

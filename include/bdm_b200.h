@@ -200,6 +200,17 @@ BDM_API int bdm_bank_scan(const void *q, const void *k, const void *v, const flo
                           void *workspace, int64_t workspace_bytes, float *checkpoints, int checkpoint_block,
                           void *stream);
 /*
+ * Diagnostics, no counterpart in the reference: makes the recurrence's bounded waits testable
+ * without a GPU fault.  wait_ns (0 = the default 2 s) bounds the long-sequence kernel's
+ * producer / consumer waits; fault = 1 makes its producer withhold each CTA's first batch
+ * hand-off, so the consumers' wait runs out, they set BDM_SCAN_ERR_TIMEOUT (bit 1) in the
+ * workspace status word and every warp returns.  Applies to bdm_bank_scan calls made after it,
+ * process-wide; outputs of a call that timed out are unspecified.  bdm_scan_test_fault(0, 0)
+ * restores normal operation.
+ */
+BDM_API int bdm_scan_test_fault(int fault, unsigned long long wait_ns);
+
+/*
  * bdm_bank_scan with the sequences below the long-sequence bound run in chunks on the tensor
  * cores (tcgen05.mma kind::tf32, accumulators in tensor memory): per chunk of C events (the
  * reference's BF16 storage interval, role_bank_kernel.py:153: 16 for bank_size <= 8, 8 for 16)

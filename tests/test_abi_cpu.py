@@ -120,3 +120,9 @@ def test_backward_sizing_and_limits():
     # a training forward's checkpoints need the whole-layer, factor-initialised form
     assert lib.bdm_bank_scan(*([dummy] * 12), 1, 4, 16, 1, 8, 64, 8, 8, 1, 1, 0.35, None, None, 0, 0, None, 0, 0, 0,
                              dummy, 1, 0, 0, dummy, dummy, 1 << 20, dummy, 8, None) == _lib.BDM_ERR_INVALID
+
+
+def test_scan_test_fault_validates_its_flag():
+    lib = _lib.load()
+    assert lib.bdm_scan_test_fault(2, 0) == _lib.BDM_ERR_INVALID
+    assert lib.bdm_scan_test_fault(0, 0) == _lib.BDM_OK

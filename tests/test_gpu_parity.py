@@ -340,6 +340,26 @@ def test_scan_status_is_sticky_and_polled_without_blocking():
     assert ops.scan_status(dev, wait=True) == 0
 
 
+def test_long_kernel_wait_runs_out_sets_status_and_returns():
+    # The long-sequence kernel's producer withholds its first batch hand-off (a test flag that
+    # nothing sets in normal use), with a 2 ms wait limit: the consumers' bounded wait runs out,
+    # the launch records BDM_SCAN_ERR_TIMEOUT and every warp returns; the context stays usable.
+    lib = _lib.load()
+    dev = torch.device(DEV, torch.cuda.current_device())
+    try:
+        assert lib.bdm_scan_test_fault(1, 2_000_000) == 0
+        with pytest.raises(_lib.BDMError, match='status 0x1'):
+            _run_scan(2, 2600, 4, 2, 1, 8, 128, torch.bfloat16, interval=16, routed=True, seed=5)
+        with pytest.raises(_lib.BDMError):  # the sticky word reports it to later callers too
+            ops.check_scan_status(dev, wait=True)
+    finally:
+        lib.bdm_scan_test_fault(0, 0)
+        ops.reset_scan_status(dev)
+    ours, ref, _, _ = _run_scan(2, 2600, 4, 2, 1, 8, 128, torch.bfloat16, interval=16, routed=True, seed=5)
+    assert max_rel(ours, ref) <= BF16_TOL
+    assert ops.scan_status(dev, wait=True) == 0
+
+
 # ------------------------------------------------------------------ layer
 LAYER_GOLDEN = [('h1_fp32', 2e-2), ('h1_fp32_state32', FP32_TOL), ('h2_fp32_state32', FP32_TOL),
                 ('c1_t64', 2e-2)]
