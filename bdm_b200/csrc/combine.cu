@@ -11,6 +11,7 @@
 // summed by a reduce-scatter, and bdm_norm_gate_f32 rounds that FP32 sum once to
 // the activation dtype (the forward's round-once combine) before norm and gate.
 #include "common.cuh"
+#include "norm_gate.cuh"
 
 namespace bdm {
 namespace {
@@ -138,28 +139,28 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
         float sq = 0.f;
 #pragma unroll
         for (int i = 0; i < kCols; ++i)
-            if (act && c0 + i < width) sq += (x[i] - mean) * (x[i] - mean);
+            if (act && c0 + i < width) sq = ng::sq_dev(x[i], mean, sq);
         const float var = block_sum(sq, red) * inv_w;
-        const float rstd = 1.0f / sqrtf(var + eps);
+        const float rstd = ng::inv_std(var, eps);
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
             float y = 0.f;
             if (act && c0 + i < width) {
-                y = (x[i] - mean) * rstd * Elem<T>::to_float(nw[c0 + i]);
-                if (nb) y += Elem<T>::to_float(nb[c0 + i]);
+                const float b = nb ? Elem<T>::to_float(nb[c0 + i]) : 0.f;
+                y = ng::layer_norm_col(x[i], mean, rstd, Elem<T>::to_float(nw[c0 + i]), nb ? &b : nullptr);
             }
             n[i] = rnd<T>(y);
         }
     } else {
         float sq = 0.f;
 #pragma unroll
-        for (int i = 0; i < kCols; ++i) sq += x[i] * x[i];
+        for (int i = 0; i < kCols; ++i) sq = fmaf(x[i], x[i], sq);
         const float var = block_sum(sq, red) * inv_w;
-        const float sc = rnd<T>(1.0f / sqrtf(var + eps));
+        const float sc = rnd<T>(ng::inv_std(var, eps));
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
             n[i] = 0.f;
-            if (act && c0 + i < width) n[i] = rnd<T>(rnd<T>(x[i] * sc) * Elem<T>::to_float(nw[c0 + i]));
+            if (act && c0 + i < width) n[i] = ng::rms_col<T>(x[i], sc, Elem<T>::to_float(nw[c0 + i]));
         }
     }
     if (act) {
@@ -171,21 +172,16 @@ __global__ void combine_norm_gate_kernel(const T *__restrict__ reads, const int6
                 uint4 u;
                 __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float g0 = rnd<T>(__fdividef(1.0f, 1.0f + __expf(-gv[2 * i])));
-                    const float g1 = rnd<T>(__fdividef(1.0f, 1.0f + __expf(-gv[2 * i + 1])));
-                    h[i] = __floats2bfloat162_rn(n[2 * i] * g0, n[2 * i + 1] * g1);
-                }
+                for (int i = 0; i < 4; ++i)
+                    h[i] = __floats2bfloat162_rn(n[2 * i] * ng::gate_sigmoid<T>(gv[2 * i]),
+                                                 n[2 * i + 1] * ng::gate_sigmoid<T>(gv[2 * i + 1]));
                 *reinterpret_cast<uint4 *>(orow) = u;
                 return;
             }
         }
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
-            if (c0 + i < width) {
-                const float gt = rnd<T>(1.0f / (1.0f + expf(-gv[i])));
-                orow[i] = Elem<T>::from_float(n[i] * gt);
-            }
+            if (c0 + i < width) orow[i] = Elem<T>::from_float(n[i] * ng::gate_sigmoid<T>(gv[i]));
         }
     }
 }

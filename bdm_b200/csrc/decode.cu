@@ -14,6 +14,7 @@
 // plus the KR bank tiles read.
 #include "common.cuh"
 #include "controller_math.cuh"
+#include "norm_gate.cuh"
 #include "route_select.cuh"
 
 namespace bdm {
@@ -41,12 +42,9 @@ __device__ __forceinline__ float dec_block_sum(float x, float *red) {
     return warp_sum(t);
 }
 
-// Output gate, as bdm_combine_norm_gate computes it: BF16 rows on the fast
-// exponential and divide, FP32 rows on expf and an IEEE divide.
-template <typename T> __device__ __forceinline__ float gate_sigmoid(float x) {
-    if constexpr (sizeof(T) == 2) return rnd<T>(__fdividef(1.0f, 1.0f + __expf(-x)));
-    else return rnd<T>(1.0f / (1.0f + expf(-x)));
-}
+// Output norm and gate: the combine kernels' arithmetic (norm_gate.cuh).
+using ng::gate_sigmoid;
+using ng::layer_norm_col;
 
 // The arithmetic both step kernels share, with explicit roundings (no multiply-add
 // contraction), so the fused step and the separate kernels agree bit for bit.
@@ -69,11 +67,6 @@ template <typename T, int S> __device__ __forceinline__ float read_value(const f
         for (int s = 0; s < S; ++s) sum = __fadd_rn(sum, x[s]);
     }
     return rnd<T>(__fmul_rn(sum, scale));
-}
-// LayerNorm output of one column: (x - mean) * rstd * w (+ b).
-__device__ __forceinline__ float layer_norm_col(float x, float mean, float rstd, float w, const float *b) {
-    const float y = __fmul_rn(__fmul_rn(__fsub_rn(x, mean), rstd), w);
-    return b ? __fadd_rn(y, *b) : y;
 }
 
 struct DecNorm {

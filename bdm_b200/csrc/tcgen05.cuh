@@ -47,6 +47,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsign
     return false;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// One arrival that also expects `bytes` of asynchronous (TMA) transactions on this phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// ------------------------------------------------------------------ TMA
+// 2-D tiled load of one box of the tensor map `map` (a __grid_constant__ kernel parameter) at
+// element coordinates (x, y) into shared memory; completes its bytes as transactions on *bar.
+// x times the element size must be a multiple of 16 bytes.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ----------------------------------------------------------- tensor memory
 // Executed by one whole warp.  The allocated base address is written to *slot (shared).
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {
@@ -92,6 +114,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
     d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
     d |= (uint64_t)1 << 46;
     return d;
+}
+// K-major operand in the 128-byte swizzle layout (what a TMA box of 64 BF16 columns with
+// SWIZZLE_128B writes): rows of 128 bytes, 8-row groups 1024 bytes apart, the 16-byte chunk c of
+// row r stored at chunk c ^ (r % 8); the group must start on a 1024-byte boundary.  One K = 16
+// step of kind::f16 advances the start address by 32 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    return smem_desc(addr, 16, 1024) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor of a dense kind::tf32 MMA with FP32 accumulation, A and B K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {

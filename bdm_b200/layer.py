@@ -137,6 +137,10 @@ class BankedDeltaMemory(nn.Module):
         # (forward) and every recurrence-backward launch.
         self.scan_events = None
         self.backward_events = None
+        # True: inference forwards / prefills of BF16 layers whose shapes fit run the read combine,
+        # norm, gate and o_proj as one tensor-core kernel (ops.combine_project); False (default):
+        # the combine_norm_gate kernel followed by a cuBLAS o_proj.
+        self.fused_output = False
         self.init_weights(initialization_seed=self.initialization_seed)
 
     # ---------------------------------------------------------- initialisation
@@ -297,6 +301,14 @@ class BankedDeltaMemory(nn.Module):
 
     def _output(self, hidden, reads, read_idx, gate, *, round_each):
         batch, time, _ = hidden.shape
+        if self.fused_output and ops.combine_project_supported(self.value_width, self.hidden_size,
+                                                              read_idx.shape[-1], reads.dtype):
+            # combine, norm, gate and o_proj in one tensor-core kernel; the o_proj input stays on chip
+            out = ops.combine_project(reads, read_idx, gate, self.output_norm_weight,
+                                      getattr(self, 'output_norm_bias', None), self.o_proj.weight, self.o_proj.bias,
+                                      eps=self.norm_eps, layer_norm=self.config.output_normalization == 'layer',
+                                      round_each=round_each)
+            return out.reshape(batch, time, self.hidden_size)
         normed = ops.combine_norm_gate(reads, read_idx, gate, self.output_norm_weight,
                                        getattr(self, 'output_norm_bias', None), eps=self.norm_eps,
                                        layer_norm=self.config.output_normalization == 'layer', round_each=round_each)

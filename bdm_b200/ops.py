@@ -11,6 +11,7 @@ Reference interfaces each op replaces (p0rc314in/bdm, implementation/bdm/):
   product_state    _parameters.py:40-67          materialize_initial_state
   bank_scan        routed_update.py:16-32, role_bank_kernel.py:177-202, inference.py:134-158
   combine_norm_gate role_bank_dispatch.py:219-231, _parameters.py:222-232
+  combine_project  role_bank_dispatch.py:201-216 + _parameters.py:222-232 (with o_proj)
   decode_step      inference.py:161-194
 Bank-sharded forward (no reference counterpart; the reference runs on one device):
   bank_histogram, bank_owners, dispatch_owned, combine_partial, norm_gate_f32
@@ -56,12 +57,14 @@ def _stream(device) -> int:
 
 # --------------------------------------------------------------- recurrence status
 class _ScanStatus:
-    """Sticky error bits of the bank recurrence on one device.
+    """Sticky error bits of the bank kernels on one device.
 
     Every bank_scan ORs its launch's status word into ``word`` on the launch stream (no host
-    sync).  A bit means a bounded wait inside the recurrence gave up (a producer / consumer
-    staging wait or a tensor-core completion wait); the reads and final states of that launch
-    are then unspecified.  The bits stay set until reset_scan_status.
+    sync), and combine_project ORs into it directly.  Bit 0x1: a bounded wait inside the
+    recurrence gave up (a producer / consumer staging wait or a tensor-core completion wait);
+    the reads and final states of that launch are then unspecified.  Bit 0x2: a bounded wait
+    inside the fused combine + output projection gave up; its outputs are unspecified.  The
+    bits stay set until reset_scan_status.
     """
 
     def __init__(self, device):
@@ -118,8 +121,9 @@ def check_scan_status(device=None, *, wait: bool = False) -> None:
         return
     bits = scan_status(device, wait=wait)
     if bits:
-        raise _lib.BDMError(f'bank recurrence: device status {bits:#x} (a bounded wait inside the kernel gave up; '
-                            f'outputs since then are unspecified; reset with ops.reset_scan_status)')
+        raise _lib.BDMError(f'bank kernels: device status {bits:#x} (a bounded wait inside a kernel gave up: 0x1 '
+                            f'recurrence, 0x2 combine + output projection; outputs since then are unspecified; '
+                            f'reset with ops.reset_scan_status)')
 
 
 def reset_scan_status(device=None) -> None:
@@ -372,6 +376,48 @@ def combine_norm_gate(reads, read_idx, gate, norm_weight, norm_bias, *, eps: flo
         _ptr(gate), ld_gate, _ptr(nw), _ptr(nb), float(eps),
         1 if layer_norm else 0, int(round_each), dtype_code(dt), _ptr(out), _stream(reads.device)),
         'bdm_combine_norm_gate')
+    return out
+
+
+def combine_project_supported(width: int, out_dim: int, kr: int, dtype) -> bool:
+    """Whether ``combine_project`` takes this geometry (BF16, 512 <= V <= 1024, V % 256 == 0,
+    D % 128 == 0 and <= 1024, 1 <= KR <= 16)."""
+    if dtype != torch.bfloat16:
+        return False
+    return bool(_lib.load().bdm_combine_project_supported(int(width), int(out_dim), int(kr), dtype_code(dtype)))
+
+
+def combine_project(reads, read_idx, gate, norm_weight, norm_bias, o_weight, o_bias, *, eps: float,
+                    layer_norm: bool, round_each: bool):
+    """Read combine, norm, gate and the output projection in one kernel -> [NT, D].
+
+    ``reads`` [NT, KR, V] with ``read_idx`` [NT, KR]; ``gate`` [NT, >=V] (row stride honoured);
+    ``o_weight`` [D, V] and ``o_bias`` [D] (or None) of o_proj.  The o_proj input equals
+    ``combine_norm_gate``'s output bit for bit; the product accumulates in FP32 on the tensor
+    cores.  Only shapes ``combine_project_supported`` accepts.
+    """
+    _cuda(reads, gate, norm_weight, o_weight)
+    dt = reads.dtype
+    nt, width = reads.shape[0], reads.shape[-1]
+    kr = read_idx.shape[-1]
+    out_dim = o_weight.shape[0]
+    if o_weight.shape != (out_dim, width):
+        raise ValueError(f'o_weight must be [out_dim, {width}], got {tuple(o_weight.shape)}')
+    if gate.stride(-1) != 1:
+        raise ValueError('gate rows must be contiguous')
+    out = torch.empty((nt, out_dim), dtype=dt, device=reads.device)
+    nw = norm_weight.detach().to(dt).contiguous()
+    nb = norm_bias.detach().to(dt).contiguous() if norm_bias is not None else None
+    w = o_weight.detach().to(dt).contiguous()
+    bo = o_bias.detach().to(dt).contiguous() if o_bias is not None else None
+    rd = reads.contiguous()
+    ri = read_idx.contiguous()
+    ld_gate = gate.stride(0) if nt > 1 else gate.shape[-1]
+    status = _scan_status_of(reads.device).word
+    _lib.check(_lib.load().bdm_combine_project(
+        _ptr(rd), _ptr(ri), nt, kr, width, _ptr(gate), ld_gate, _ptr(nw), _ptr(nb), float(eps),
+        1 if layer_norm else 0, int(round_each), _ptr(w), _ptr(bo), out_dim, dtype_code(dt), _ptr(out), out_dim,
+        _ptr(status), _stream(reads.device)), 'bdm_combine_project')
     return out
 
 

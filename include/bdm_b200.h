@@ -257,6 +257,28 @@ BDM_API int bdm_combine_norm_gate_save(const void *reads, const int64_t *read_id
                                        void *out, void *raw_out, void *stream);
 
 /*
+ * Read combine + output normalisation + sigmoid gate + output projection in one kernel: the
+ * whole output interface of the layer forward.  Replaces _readout (role_bank_dispatch.py:201-216)
+ * followed by _project_bank_output (_parameters.py:222-232: o_proj(norm(y) * sigmoid(gate)) + b).
+ *   reads, read_idx, gate, norm_*, eps, norm_mode, round_each: as bdm_combine_norm_gate.
+ *   o_weight [out_dim, width] (dtype, rows contiguous: nn.Linear.weight), o_bias [out_dim] or NULL.
+ *   out [ntok, ld_out] (dtype) = o_proj(dtype(norm(raw) * dtype(sigmoid(gate)))) + o_bias, FP32
+ *   accumulation, one rounding to dtype.  The normalised input of o_proj is bit-identical to
+ *   bdm_combine_norm_gate's output and is never written to memory.
+ *   status: optional device int; a bounded wait inside the kernel that gave up ORs in 0x2 (the
+ *   outputs of that launch are then unspecified).
+ * BF16 only, 512 <= width <= 1024 with width % 256 == 0, out_dim % 128 == 0 and <= 1024,
+ * 1 <= kr <= 16, reads / gate / norm_* / o_weight / out 16-byte aligned, ld_gate and ld_out multiples
+ * of 8; other shapes return BDM_ERR_UNSUPPORTED (run bdm_combine_norm_gate and a GEMM instead).
+ * bdm_combine_project_supported: 1 when (width, out_dim, kr, dtype) fits, else 0 (no launch).
+ */
+BDM_API int bdm_combine_project(const void *reads, const int64_t *read_idx, int64_t ntok, int kr, int64_t width,
+                                const void *gate, int64_t ld_gate, const void *norm_weight, const void *norm_bias,
+                                float eps, int norm_mode, int round_each, const void *o_weight, const void *o_bias,
+                                int64_t out_dim, int dtype, void *out, int64_t ld_out, int *status, void *stream);
+BDM_API int bdm_combine_project_supported(int64_t width, int64_t out_dim, int kr, int dtype);
+
+/*
  * Training backward.  Replaces the backward passes of RoutedUpdate /
  * RoleBankTraining / ProductRoutedUpdate (routed_update.py:31-49,
  * role_bank_kernel.py:76-150,204-215, product_routed_update.py:44-76) and, for the

@@ -58,6 +58,10 @@ def test_dispatch_workspace_sizing():
     lambda lib: lib.bdm_norm_gate_f32(None, 4, 64, None, 64, None, None, 1e-5, 1, 1, None, None),
     lambda lib: lib.bdm_combine_norm_gate_save(None, None, 4, 8, 64, None, 64, None, None, 1e-5, 1, 0, 1, None, None,
                                                None),
+    lambda lib: lib.bdm_combine_project(None, None, 4, 8, 1024, None, 1000, None, None, 1e-5, 1, 0, None, None,
+                                        1024, 1, None, 1024, None, None),                  # ld_gate < width
+    lambda lib: lib.bdm_combine_project(None, None, 4, 8, 1024, None, 1024, None, None, 1e-5, 1, 0, None, None,
+                                        1024, 1, None, 1024, None, None),                  # null inputs
     lambda lib: lib.bdm_norm_gate_backward(None, None, 4, 64, None, 32, None, None, 1e-5, 1, 1, None, None, 64, None,
                                            None, None, None),                          # ld_gate < width
     lambda lib: lib.bdm_scan_backward(*([None] * 10), 2, 4, 16, 1, 8, 32, 4, 4, 1, 1, 0.35, None, None, 0, 0, 0,
@@ -126,3 +130,20 @@ def test_scan_test_fault_validates_its_flag():
     lib = _lib.load()
     assert lib.bdm_scan_test_fault(2, 0) == _lib.BDM_ERR_INVALID
     assert lib.bdm_scan_test_fault(0, 0) == _lib.BDM_OK
+
+
+def test_combine_project_geometry_is_reported_without_a_launch():
+    lib = _lib.load()
+    bf, f32 = _lib.BDM_BF16, _lib.BDM_F32
+    assert lib.bdm_combine_project_supported(1024, 1024, 8, bf) == 1   # c2
+    assert lib.bdm_combine_project_supported(768, 768, 8, bf) == 1     # c5
+    assert lib.bdm_combine_project_supported(512, 128, 16, bf) == 1
+    for args in ((2048, 2048, 16, bf), (1024, 1024, 8, f32), (1024, 1088, 8, bf), (1024, 2048, 8, bf),
+                 (256, 256, 8, bf), (640, 256, 8, bf), (1024, 1024, 0, bf), (1024, 1024, 17, bf)):
+        assert lib.bdm_combine_project_supported(*args) == 0, args
+    dummy = ctypes.c_void_p(16)
+    # a geometry the kernel does not take is reported before any device work (c4: V = 2048)
+    assert lib.bdm_combine_project(dummy, dummy, 4, 16, 2048, dummy, 2048, dummy, None, 1e-5, 1, 0, dummy, None, 2048,
+                                   bf, dummy, 2048, None, None) == _lib.BDM_ERR_UNSUPPORTED
+    assert lib.bdm_combine_project(None, None, 0, 8, 1024, None, 1024, None, None, 1e-5, 1, 0, None, None, 1024, bf,
+                                   None, 1024, None, None) == _lib.BDM_OK  # no tokens: nothing to do

@@ -627,3 +627,92 @@ def test_captured_decode_step_matches_eager_step():
             y_eager, _ = m.step(toks[i], eager_state)
             assert torch.equal(y_graph, y_eager), i
             assert torch.equal(state, eager_state), i
+
+
+# ------------------------------------------------------- fused combine + output projection
+def _combine_project_case(ntok, kr, width, out_dim, norm_bias, o_bias, seed):
+    gen = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    reads = torch.randn(ntok, kr, width, generator=gen).to(bf).to(DEV)
+    banks = torch.randint(0, 64, (ntok, kr), generator=gen).to(DEV)  # repeats exercise the slot tie rule
+    proj = torch.randn(ntok, width + 40, generator=gen).to(bf).to(DEV)  # gate as a strided column block
+    gate = proj[:, 24:24 + width]
+    nw = (1 + 0.1 * torch.randn(width, generator=gen)).to(bf).to(DEV)
+    nb = (0.1 * torch.randn(width, generator=gen)).to(bf).to(DEV) if norm_bias else None
+    w = (torch.randn(out_dim, width, generator=gen) * width ** -0.5).to(bf).to(DEV)
+    b = (0.1 * torch.randn(out_dim, generator=gen)).to(bf).to(DEV) if o_bias else None
+    return reads, banks, gate, nw, nb, w, b
+
+
+@pytest.mark.parametrize('ntok,kr,width,out_dim,layer_norm,norm_bias,o_bias,round_each', [
+    (4096, 8, 1024, 1024, True, True, True, False),   # c2 output interface
+    (1000, 8, 1024, 1024, True, True, False, True),   # ragged last tile, no o_proj bias, round-each combine
+    (777, 16, 512, 256, False, False, True, False),   # RMS norm, 16 read slots
+    (130, 3, 768, 768, True, False, True, False),     # 3-warp token groups (V = 768), 6 accumulators
+    (64, 8, 1024, 128, True, True, True, False),      # one tile, one accumulator
+    (300, 8, 512, 1024, True, True, True, False),     # more features than columns: two staging chunks
+    (1, 1, 512, 1024, True, True, True, True),        # one token
+])
+def test_combine_project_matches_combine_then_exact_gemm(ntok, kr, width, out_dim, layer_norm, norm_bias, o_bias,
+                                                         round_each):
+    """The fused kernel's output is one BF16 rounding of the exact product of the
+    combine_norm_gate output with o_proj's weight (plus bias)."""
+    assert ops.combine_project_supported(width, out_dim, kr, torch.bfloat16)
+    reads, banks, gate, nw, nb, w, b = _combine_project_case(ntok, kr, width, out_dim, norm_bias, o_bias,
+                                                             seed=ntok + kr)
+    ops.reset_scan_status()
+    out = ops.combine_project(reads, banks, gate, nw, nb, w, b, eps=1e-5, layer_norm=layer_norm,
+                              round_each=round_each)
+    normed = ops.combine_norm_gate(reads, banks, gate, nw, nb, eps=1e-5, layer_norm=layer_norm,
+                                   round_each=round_each)
+    ref = normed.double() @ w.double().t()
+    if b is not None:
+        ref = ref + b.double()
+    got = out.double()
+    # BF16 rounding (half an ulp, 2^-9 relative) plus the FP32 accumulation-order difference
+    bound = 2.0 ** -8 * ref.abs() + 1e-5 * ref.abs().max()
+    assert bool(((got - ref).abs() <= bound).all()), float(((got - ref).abs() / (ref.abs() + 1e-6)).max())
+    assert ops.scan_status(wait=True) == 0
+
+
+def test_combine_project_rejects_shapes_it_does_not_take():
+    bf = torch.bfloat16
+    for width, out_dim, kr, dt in ((2048, 1024, 8, bf), (1024, 1152, 8, bf), (1024, 1000, 8, bf), (320, 256, 8, bf),
+                                   (1024, 1024, 17, bf), (1024, 1024, 8, torch.float32)):
+        assert not ops.combine_project_supported(width, out_dim, kr, dt)
+    reads = torch.zeros(4, 8, 2048, dtype=bf, device=DEV)
+    with pytest.raises(NotImplementedError):
+        ops.combine_project(reads, torch.zeros(4, 8, dtype=torch.int64, device=DEV), reads[:, 0],
+                            torch.ones(2048, dtype=bf, device=DEV), None, torch.zeros(1024, 2048, dtype=bf, device=DEV),
+                            None, eps=1e-5, layer_norm=True, round_each=False)
+
+
+def test_layer_fused_output_matches_unfused_and_oracle():
+    """A BF16 layer whose output interface fits the fused kernel: forward (FP32 combine) and
+    prefill (round-each combine) against the combine_norm_gate + cuBLAS path and the oracle."""
+    cfg = BSDMConfig(dim=512, bank_count=256, bank_size=8, selected_banks=8, value_width=512, num_heads=4)
+    torch.manual_seed(21)
+    m = BlockSparseDeltaMemory(cfg, seed=5)
+    with torch.no_grad():
+        m.output_norm_weight.add_(0.1 * torch.randn_like(m.output_norm_weight))
+        m.output_norm_bias.add_(0.1 * torch.randn_like(m.output_norm_bias))
+        if m.o_proj.bias is not None:
+            m.o_proj.bias.add_(0.1 * torch.randn_like(m.o_proj.bias))
+    m = m.to(torch.bfloat16).to(DEV)
+    assert ops.combine_project_supported(512, 512, 8, torch.bfloat16)
+    x = torch.randn(2, 300, 512).to(torch.bfloat16).to(DEV)
+    with torch.no_grad():
+        m.fused_output = True
+        y_fused = m(x)
+        yp_fused, st_fused = m.prefill(x)
+        m.fused_output = False
+        y_plain = m(x)
+        yp_plain, st_plain = m.prefill(x)
+        ctl, routes = _our_controls_routes(m, x)
+    for a, b in ((y_fused, y_plain), (yp_fused, yp_plain)):
+        d = (a.double() - b.double()).abs()
+        # one BF16 ulp where the two GEMMs' FP32 sums round to neighbouring values
+        assert bool((d <= 2.0 ** -7 * b.double().abs() + 1e-5).all()), float(d.max())
+    assert torch.equal(st_fused, st_plain)
+    oy = _oracle_layer(m).forward(npf(x), controls=ctl, routes=routes)
+    assert max_rel(npf(y_fused), oy) <= BF16_TOL, max_rel(npf(y_fused), oy)
