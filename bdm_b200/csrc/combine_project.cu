@@ -48,6 +48,7 @@ constexpr int kMaxFusedKR = 16;
 constexpr int kSmemMax = 232448;  // opt-in shared memory per CTA on sm_100
 constexpr unsigned long long kCpWaitNs = 2000000000ull;  // 2 s
 constexpr int BDM_CP_ERR_TIMEOUT = 2;
+constexpr unsigned kPhaseSleepNs = 256;  // poll interval of the waits that span a whole phase
 constexpr int kOrderBar = 9;  // named barrier of the combine warps (token groups use 1..8)
 
 struct CpParams {
@@ -82,11 +83,13 @@ constexpr int cp_smem_bytes(int width, int stages) {
 }
 
 // Bounded wait on a phase; gives up after kCpWaitNs (or once another thread of the CTA gave up),
-// recording the error.
-__device__ bool cp_wait(CpCtl &c, uint64_t *bar, unsigned parity, int *status) {
+// recording the error.  sleep_ns > 0 backs off between polls: long waits (a whole combine or MMA
+// phase) then leave the issue slots to the warps that do the work.
+__device__ bool cp_wait(CpCtl &c, uint64_t *bar, unsigned parity, int *status, unsigned sleep_ns = 0) {
     if (tc::mbar_test(bar, parity)) return true;
     const unsigned long long t0 = tc::global_ns();
     for (long long i = 0; i < (1ll << 32); ++i) {
+        if (sleep_ns) __nanosleep(sleep_ns);
         if (tc::mbar_test(bar, parity)) return true;
         if ((i & 63) == 63) {
             if (*reinterpret_cast<volatile int *>(&c.abort)) return false;
@@ -130,10 +133,11 @@ __device__ __forceinline__ void load_row(const CpParams &p, const CpCtl &c, int6
     const int64_t t = tile * kTileTok + r;
     if (t >= p.ntok) return;
     const bf16 *rrow = p.reads + t * p.kr * (int64_t)p.width + c0;
+    const uint64_t once = tc::l2_evict_first();  // read rows and gates are read once: keep W in L2
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-        if (j0 + j < p.kr) y[j] = __ldg(reinterpret_cast<const uint4 *>(rrow + (int64_t)c.order[r][j0 + j] * p.width));
-    if (j0 == 0) g = __ldg(reinterpret_cast<const uint4 *>(p.gate + t * p.ld_gate + c0));
+        if (j0 + j < p.kr) y[j] = tc::ldg_hint(rrow + (int64_t)c.order[r][j0 + j] * p.width, once);
+    if (j0 == 0) g = tc::ldg_hint(p.gate + t * p.ld_gate + c0, once);
 }
 
 // x += read rows j0 .. j0 + 7 (< kr) in order; round_each rounds to BF16 after every add.
@@ -241,6 +245,32 @@ __device__ __forceinline__ void combine_rows(const CpParams &p, CpCtl &c, unsign
     }
 }
 
+// Position in a CTA's sweep of the weight boxes: ring stage and how often the ring wrapped; the
+// column slice and feature block, both as a position in this CTA's order (kbi, mti) and rotated by
+// its starting box (kb, mt).  Feature blocks run fastest.
+struct Sweep {
+    int s = 0;
+    uint32_t round = 0;
+    int kbi = 0, mti = 0, kb, mt;
+    __device__ Sweep(int rot_kb, int rot_mt) : kb(rot_kb), mt(rot_mt) {}
+    __device__ __forceinline__ void next(int stages, int nkb, int nmt, int rot_kb, int rot_mt) {
+        if (++s == stages) {
+            s = 0;
+            ++round;
+        }
+        if (++mt == nmt) mt = 0;
+        if (++mti == nmt) {
+            mti = 0;
+            mt = rot_mt;
+            if (++kb == nkb) kb = 0;
+            if (++kbi == nkb) {
+                kbi = 0;
+                kb = rot_kb;
+            }
+        }
+    }
+};
+
 __global__ void __launch_bounds__(kCpThreads, 1)
 combine_project_kernel(const CpParams p, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ unsigned char cp_smem_raw[];
@@ -274,7 +304,7 @@ combine_project_kernel(const CpParams p, const __grid_constant__ CUtensorMap wma
     if (warp == 0) {
         // ------------------------------------------------- weight loads (TMA) + MMA issue
         // One thread: step q consumes weight box q (tile-major, then 64-column slice, then
-        // 128-feature block) from stage q % stages; box q + stages - 1 is loaded once step q - 1's
+        // 128-feature block) from ring stage q mod stages; box q + stages - 1 is loaded once step q - 1's
         // MMAs have released its stage, so stages - 1 boxes stay in flight and the tensor pipe keeps
         // step q queued while the thread waits.
         if (lane == 0) {
@@ -283,49 +313,50 @@ combine_project_kernel(const CpParams p, const __grid_constant__ CUtensorMap wma
             // CTAs start their sweep of W at different boxes (column slice and feature block), so
             // the SMs do not all request the same L2 lines at once
             const int rot_kb = (int)(blockIdx.x % nkb), rot_mt = (int)((blockIdx.x / nkb) % nmt);
+            const uint64_t keep = tc::l2_evict_last();  // every tile of every CTA reads all of W
             int64_t my_tiles = 0;
             for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) ++my_tiles;
             const uint32_t total = (uint32_t)my_tiles * per_tile;
-            auto load = [&](uint32_t ql) {
-                const int s = (int)(ql % stages);
-                const uint32_t r = ql % per_tile;
-                const int kb = ((int)(r / nmt) + rot_kb) % nkb, mt = ((int)(r % nmt) + rot_mt) % nmt;
-                tc::mbar_arrive_expect_tx(&c.full[s], kStageBytes);
-                tc::tma_load_2d(wbuf + s * kStageBytes, &wmap, kb * kAtomK, mt * kFeat, &c.full[s]);
-            };
+            // boxes are walked with incremental counters: one thread issues everything, and integer
+            // divisions by runtime values would dominate its loop
+            Sweep lc(rot_kb, rot_mt), qc(rot_kb, rot_mt);  // next box to load / to consume
             uint32_t loaded = 0;
-            for (; loaded < total && loaded + 1 < (uint32_t)stages; ++loaded) load(loaded);
+            auto load = [&]() {
+                tc::mbar_arrive_expect_tx(&c.full[lc.s], kStageBytes);
+                tc::tma_load_2d_hint(wbuf + lc.s * kStageBytes, &wmap, lc.kb * kAtomK, lc.mt * kFeat, &c.full[lc.s],
+                                     keep);
+                lc.next(stages, nkb, nmt, rot_kb, rot_mt);
+                ++loaded;
+            };
+            while (loaded < total && loaded + 1 < (uint32_t)stages) load();
             bool ok = true;
-            uint32_t q = 0;
             for (int it = 0; it < my_tiles && ok; ++it) {
-                ok = cp_wait(c, &c.a_full, it & 1, p.status);
+                ok = cp_wait(c, &c.a_full, it & 1, p.status, kPhaseSleepNs);
                 if (ok && it > 0) ok = cp_wait(c, &c.acc_empty, (it - 1) & 1, p.status);
                 if (!ok) break;
                 tc::fence_after_sync();
-                for (uint32_t r = 0; r < per_tile; ++r, ++q) {
-                    const int s = (int)(q % stages);
-                    if (!cp_wait(c, &c.full[s], (q / stages) & 1, p.status)) {
+                for (uint32_t r = 0; r < per_tile; ++r) {
+                    if (!cp_wait(c, &c.full[qc.s], qc.round & 1, p.status)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const int kbi = (int)(r / nmt);  // position in this CTA's column-slice order
-                    const int kb = (kbi + rot_kb) % nkb, mt = ((int)(r % nmt) + rot_mt) % nmt;
-                    const uint32_t wa = tc::smem_u32(wbuf + s * kStageBytes);
-                    const uint32_t ab = tc::smem_u32(abuf + kb * kAtomBytes);
+                    const uint32_t wa = tc::smem_u32(wbuf + qc.s * kStageBytes);
+                    const uint32_t ab = tc::smem_u32(abuf + qc.kb * kAtomBytes);
+                    const uint32_t d = tmem + (uint32_t)(qc.mt * kTileTok);
 #pragma unroll
                     for (int kk = 0; kk < kAtomK / 16; ++kk)
-                        tc::mma_bf16(tmem + (uint32_t)(mt * kTileTok), tc::smem_desc_sw128(wa + kk * 32),
-                                     tc::smem_desc_sw128(ab + kk * 32), idesc, (kbi | kk) != 0);
-                    tc::mma_commit(&c.empty[s]);  // the stage is free once these MMAs have read it
+                        tc::mma_bf16(d, tc::smem_desc_sw128(wa + kk * 32), tc::smem_desc_sw128(ab + kk * 32), idesc,
+                                     (qc.kbi | kk) != 0);
+                    tc::mma_commit(&c.empty[qc.s]);  // the stage is free once these MMAs have read it
+                    qc.next(stages, nkb, nmt, rot_kb, rot_mt);
                     if (loaded < total) {
-                        // box `loaded` reuses the stage of step loaded - stages (= q - 1 once primed)
-                        if (loaded >= (uint32_t)stages &&
-                            !cp_wait(c, &c.empty[loaded % stages], ((loaded / stages) - 1) & 1, p.status)) {
+                        // the next box reuses the stage of the step `stages` before it (step q - 1)
+                        if (lc.round > 0 && !cp_wait(c, &c.empty[lc.s], (lc.round - 1) & 1, p.status)) {
                             ok = false;
                             break;
                         }
-                        load(loaded++);
+                        load();
                     }
                 }
                 if (ok) tc::mma_commit(&c.acc_full);  // the tile's accumulators are complete
@@ -352,7 +383,7 @@ combine_project_kernel(const CpParams p, const __grid_constant__ CUtensorMap wma
         for (int64_t tile = blockIdx.x;; tile += gridDim.x, ++it) {
             if (it > 0) {
                 // the previous tile: its MMAs are done (token tile free), accumulators ready
-                if (!cp_wait(c, &c.acc_full, (it - 1) & 1, p.status)) break;
+                if (!cp_wait(c, &c.acc_full, (it - 1) & 1, p.status, kPhaseSleepNs)) break;
                 tc::fence_after_sync();
                 // The token tile is free: stage the output rows there in chunks of `fc` features
                 // (tokens x fc BF16), then store whole rows with 16-byte accesses.

@@ -69,6 +69,36 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, i
         : "memory");
 }
 
+// Same, with an L2 cache policy (createpolicy) for the box's lines.
+__device__ __forceinline__ void tma_load_2d_hint(void *dst, const void *map, int x, int y, uint64_t *bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;\n" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// L2 cache policies: keep lines (data read again soon) or drop them first (streamed once).
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+// 16-byte read-only global load under an L2 cache policy.
+__device__ __forceinline__ uint4 ldg_hint(const void *ptr, uint64_t policy) {
+    uint4 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(ptr), "l"(policy));
+    return v;
+}
+
 // ----------------------------------------------------------- tensor memory
 // Executed by one whole warp.  The allocated base address is written to *slot (shared).
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t cols) {

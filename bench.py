@@ -491,6 +491,11 @@ def run_ours(args, world, rank, local):
             line['scan_variants'] = run_scan_variants(layer, x, dev, args)
         except Exception as e:  # keep the headline line even if the extra workload fails
             line['scan_variants'] = {'error': repr(e)[:300]}
+    if not args.skip_output_variants:
+        try:
+            line['output_variants'] = run_output_variants(layer, x, dev, args)
+        except Exception as e:  # keep the headline line even if the extra workload fails
+            line['output_variants'] = {'error': repr(e)[:300]}
     if args.reference_gpu and rank == 0 and world == 1:
         line['reference_gpu'] = run_reference_gpu(dev, args)
     if not args.skip_c1 and world == 1:
@@ -572,6 +577,52 @@ def run_scan_variants(layer, x, dev, args):
         v['frac'] = v['achieved_gbs'] / hbm_peak
     return {'what': 'c2 recurrence alone (bdm_bank_scan vs bdm_bank_scan_chunked), same inputs, BF16 storage policy',
             **out}
+
+
+def run_output_variants(layer, x, dev, args):
+    """The c2 output interface alone on the layer's own read rows: bdm_combine_norm_gate followed by
+    the cuBLAS o_proj (the forward's default), and the fused tensor-core bdm_combine_project (the
+    o_proj input never written to memory); CUDA events around each, the 256 MiB L2 flush between."""
+    from bdm_b200 import ops, state_interval
+    from torch.nn import functional as F
+    batch, time_ = x.shape[0], x.shape[1]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    with torch.inference_mode():
+        controls, routes, gate = layer._controls_and_routes(x)
+        reads = layer._bank_pass(controls, routes, batch, time_, row_factor=layer.initial_row_factor,
+                                 col_factor=layer.initial_column_factor,
+                                 state_interval=state_interval(layer.bank_size))
+        ri = routes[3].reshape(batch * time_, -1)
+        rd = reads.reshape(batch * time_, ri.shape[-1], -1)
+        nb = getattr(layer, 'output_norm_bias', None)
+        ln = layer.config.output_normalization == 'layer'
+        w, b = layer.o_proj.weight, layer.o_proj.bias
+
+        def unfused():
+            n = ops.combine_norm_gate(rd, ri, gate, layer.output_norm_weight, nb, eps=layer.norm_eps, layer_norm=ln,
+                                      round_each=False)
+            return F.linear(n, w, b)
+
+        def fused():
+            return ops.combine_project(rd, ri, gate, layer.output_norm_weight, nb, w, b, eps=layer.norm_eps,
+                                       layer_norm=ln, round_each=False)
+        out = {}
+        for name, fn in (('combine_then_cublas', unfused), ('fused_combine_project', fused)):
+            for _ in range(3):
+                fn()
+            times = []
+            for _ in range(max(args.steps, 3)):
+                flush.zero_()
+                s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_.record()
+                fn()
+                e_.record()
+                torch.cuda.synchronize()
+                times.append(s_.elapsed_time(e_))
+            out[name] = {'ms': statistics.mean(times), 'min_ms': min(times)}
+        diff = (unfused().float() - fused().float()).abs().max().item()
+    return {'what': 'c2 read combine + norm + gate + o_proj, same inputs: two launches vs one fused kernel',
+            'max_abs_diff': diff, **out}
 
 
 def run_reference_gpu(dev, args):
@@ -974,6 +1025,7 @@ def main():
     ap.add_argument('--reference-gpu', action='store_true',
                     help="also time the reference's own Triton GPU path (installed in baseline/_ref)")
     ap.add_argument('--skip-scan-variants', action='store_true')
+    ap.add_argument('--skip-output-variants', action='store_true')
     ap.add_argument('--skip-cpu', action='store_true')
     ap.add_argument('--skip-c4', action='store_true')
     ap.add_argument('--c4-steps', type=int, default=5)
