@@ -175,6 +175,18 @@ template <int S> struct CtlLayout {
     static constexpr int c = 0, kd = S, p = 2 * S, dprev = 2 * S + 2, size = 3 * S + 2;
 };
 
+// Per-event record of a staged batch, written by the lane that staged the event: the event's row
+// offset in token storage (write: token * V for its value / write-gate rows; read: read id * V for
+// its output row) and its kind.  The event loop reads one record per event instead of decoding ids
+// and masks itself: the staging does that work one event per lane, the loop one event per warp
+// instruction.
+struct __align__(16) EvRec {
+    long long off;
+    int kind;
+    int pad;
+};
+constexpr int kEvWrite = 1, kEvRead = 2, kEvRound = 4, kEvCk = 8;
+
 #ifndef BDM_SCAN_EB_S16
 #define BDM_SCAN_EB_S16 16  // events per staged batch when S = 16 (32 otherwise)
 #endif
@@ -345,8 +357,8 @@ bank_scan_kernel(const ScanParams p) {
     __shared__ __align__(16) float2 ctl_all[kScanWarps][EB][Ctl::size];
     __shared__ __align__(16) float2 dend_all[kScanWarps][S];
     __shared__ __align__(16) unsigned char raw_all[kScanWarps][EB][Raw::size];
-    __shared__ int tok_all[kScanWarps][EB];
-    __shared__ int rid_all[kScanWarps][EB];
+    // EB records per batch plus PD empty ones, so prefetches past the batch need no bounds check
+    __shared__ EvRec ev_all[kScanWarps][EB + kPrefetch];
     __shared__ unsigned long long item_shared;
 
     const int warp = threadIdx.x >> 5;
@@ -354,8 +366,8 @@ bank_scan_kernel(const ScanParams p) {
     float2(*ctl)[Ctl::size] = ctl_all[warp];
     float2 *dend = dend_all[warp];
     unsigned char(*raw)[Raw::size] = raw_all[warp];
-    int *tok_s = tok_all[warp];
-    int *rid_s = rid_all[warp];
+    EvRec *ev_s = ev_all[warp];
+    if (lane < kPrefetch) ev_s[EB + lane] = EvRec{0, 0, 0};
     const int64_t per_seq = (int64_t)p.H * p.ctiles;
     int64_t total = 0;  // units of the classes this kernel runs (the long classes go to the long kernel)
 #pragma unroll
@@ -513,8 +525,14 @@ bank_scan_kernel(const ScanParams p) {
             if (lane == n - 1) dend[s] = dup(D[s]);
         }
         if (lane < EB) {
-            tok_s[lane] = use ? my_tok : -1;
-            rid_s[lane] = use ? my_rid : -1;
+            EvRec r{0, 0, 0};
+            if (use && my_tok >= 0) {
+                r.kind = my_write ? kEvWrite : kEvRead;
+                r.off = (long long)(my_write ? my_tok : my_rid) * V;
+            }
+            if (use && head) r.kind |= kEvRound;
+            if (use && ckp) r.kind |= kEvCk;
+            ev_s[lane] = r;
         }
         n_out = n;
         round_out = __ballot_sync(0xffffffffu, use && head);
@@ -538,11 +556,12 @@ bank_scan_kernel(const ScanParams p) {
     for (int64_t base = start; base < end;) {
         const int64_t nbase = base + n;
         const int nn = (int)min((int64_t)EB, end - nbase);
+        // events past n have empty records: no loads, and event_step does nothing for them
         auto prefetch = [&](int ev, int slot) {
-            if (ev < n && ((wmask >> ev) & 1u) && active) {
-                const int64_t o = (int64_t)tok_s[ev] * V;
-                load_row<T, NC>(vr[slot], vp + o);
-                load_row<T, NC>(wr[slot], wp + o);
+            const EvRec r = ev_s[ev];
+            if ((r.kind & kEvWrite) && active) {
+                load_row<T, NC>(vr[slot], vp + r.off);
+                load_row<T, NC>(wr[slot], wp + r.off);
             }
         };
 #pragma unroll
@@ -554,18 +573,18 @@ bank_scan_kernel(const ScanParams p) {
                 issued = true;
             }
 #pragma unroll
-            for (int j = 0; j < PD; ++j) {
+            for (int j = 0; j < PD; ++j) {  // a group past n runs empty records (no-ops)
                 const int ev = e0 + j;
-                if (ev >= n) break;
+                const EvRec r = ev_s[ev];
                 float *ck_row = nullptr;
-                const bool ck_here = CK && ((cmask >> ev) & 1u);
+                const bool ck_here = CK && (r.kind & kEvCk);
                 if (ck_here) {
                     const int64_t pos = base - start + ev;
                     ck_row = p.ckpt + ((start / p.ckpt_block + seq + pos / p.ckpt_block) * p.H + hh) * (int64_t)S * p.dv +
                              col0;
                 }
-                event_step<T, S, NC>(ctl[ev], (rmask >> ev) & 1u, (wmask >> ev) & 1u, tok_s[ev] >= 0, active, vr[j],
-                                     wr[j], p.scale, outp + (int64_t)rid_s[ev] * V, N, ck_here, ck_row, p.dv);
+                event_step<T, S, NC>(ctl[ev], r.kind & kEvRound, r.kind & kEvWrite, r.kind & (kEvWrite | kEvRead),
+                                     active, vr[j], wr[j], p.scale, outp + r.off, N, ck_here, ck_row, p.dv);
                 prefetch(ev + PD, j);
             }
         }
