@@ -34,6 +34,12 @@ namespace {
 #ifndef BDM_SCAN_MIN_BLOCKS
 #define BDM_SCAN_MIN_BLOCKS 4  // resident CTAs per SM the register allocation targets (measured best)
 #endif
+#ifndef BDM_SCAN_MIN_BLOCKS_G2
+#define BDM_SCAN_MIN_BLOCKS_G2 3  // the same with two heads per warp (twice the state registers per lane)
+#endif
+#ifndef BDM_SCAN_G2
+#define BDM_SCAN_G2 1  // 1: even head counts run two heads per warp in the short kernel
+#endif
 #ifndef BDM_SCAN_LONG
 #define BDM_SCAN_LONG 1  // 1: long sequences run on warp-specialised CTAs; 0: every unit on one warp
 #endif
@@ -49,6 +55,9 @@ namespace {
 
 constexpr int kScanWarps = 4;
 constexpr int kPrefetch = BDM_SCAN_PREFETCH;
+// With two heads per warp the value rows are twice as wide: two events ahead keep the registers
+// within 3 CTAs per SM (measured faster than four events at 3 CTAs or 4 CTAs with spills).
+constexpr int kPrefetchG2 = 2;
 
 // Lower bounds of classes 1..3; class 0 starts at the launch's long-sequence bound.
 __device__ __constant__ int kLenLower[kLenClasses] = {0, 2048, 512, 1};
@@ -340,35 +349,40 @@ __device__ __forceinline__ void event_step(const float2 *row, bool round_point, 
     }
 }
 
-// Short sequences: one warp per (sequence, head, column tile) unit, kScanWarps
+// Short sequences: one warp per (sequence, group of G heads, column tile) unit, kScanWarps
 // units per CTA; each warp stages and runs its own batches.  Takes the length
 // classes from p.ws_classes on (all of them when the long kernel does not run).
+// G = 2: the two halves of the warp run two heads of the same sequence (16 lanes x NC columns
+// each); the events, their records and the loop control are shared by both heads, and the
+// staging runs one (event, head) pair per lane over batches of 16 events.
 // CK: the launch writes the recurrence backward's state checkpoints (training forwards only;
 // the inference instantiation keeps none of that code).
-template <typename T, int S, int NC, bool CK>
-__global__ void __launch_bounds__(kScanWarps * 32, BDM_SCAN_MIN_BLOCKS)
+template <typename T, int S, int NC, bool CK, int G>
+__global__ void __launch_bounds__(kScanWarps * 32, G == 2 ? BDM_SCAN_MIN_BLOCKS_G2 : BDM_SCAN_MIN_BLOCKS)
 bank_scan_kernel(const ScanParams p) {
     constexpr int NP = NC / 2;
-    constexpr int EB = EvBatch<S>::value;
-    constexpr int PD = kPrefetch;
+    constexpr int LPG = 32 / G;  // lanes per head
+    constexpr int EB = EvBatch<S>::value < LPG ? EvBatch<S>::value : LPG;
+    constexpr int PD = G == 2 ? kPrefetchG2 : kPrefetch;
     using Raw = RawLayout<T, S>;
     using Ctl = CtlLayout<S>;
-    static_assert(EB % PD == 0 && 32 % EB == 0 && S % 2 == 0, "batch layout");
-    __shared__ __align__(16) float2 ctl_all[kScanWarps][EB][Ctl::size];
-    __shared__ __align__(16) float2 dend_all[kScanWarps][S];
-    __shared__ __align__(16) unsigned char raw_all[kScanWarps][EB][Raw::size];
+    static_assert(EB % PD == 0 && LPG % EB == 0 && S % 2 == 0 && (G == 1 || G == 2), "batch layout");
+    __shared__ __align__(16) float2 ctl_all[kScanWarps][EB][G][Ctl::size];
+    __shared__ __align__(16) float2 dend_all[kScanWarps][G][S];
+    __shared__ __align__(16) unsigned char raw_all[kScanWarps][G == 1 ? EB : 32][Raw::size];
     // EB records per batch plus PD empty ones, so prefetches past the batch need no bounds check
-    __shared__ EvRec ev_all[kScanWarps][EB + kPrefetch];
+    __shared__ EvRec ev_all[kScanWarps][EB + PD];
     __shared__ unsigned long long item_shared;
 
     const int warp = threadIdx.x >> 5;
     const int lane = (int)lane_id();
-    float2(*ctl)[Ctl::size] = ctl_all[warp];
-    float2 *dend = dend_all[warp];
+    const int el = lane % LPG, hl = lane / LPG;  // staging: event el of the batch, head hl of the group
+    float2(*ctl)[G][Ctl::size] = ctl_all[warp];
+    float2(*dend)[S] = dend_all[warp];
     unsigned char(*raw)[Raw::size] = raw_all[warp];
     EvRec *ev_s = ev_all[warp];
-    if (lane < kPrefetch) ev_s[EB + lane] = EvRec{0, 0, 0};
-    const int64_t per_seq = (int64_t)p.H * p.ctiles;
+    if (lane < PD) ev_s[EB + lane] = EvRec{0, 0, 0};
+    const int64_t per_seq = (int64_t)(p.H / G) * p.ctiles;
     int64_t total = 0;  // units of the classes this kernel runs (the long classes go to the long kernel)
 #pragma unroll
     for (int c = 0; c < kLenClasses; ++c) total += c >= p.ws_classes ? p.counts[c] : 0;
@@ -392,10 +406,10 @@ bank_scan_kernel(const ScanParams p) {
     while (cls < kLenClasses - 1 && local >= p.counts[cls]) local -= p.counts[cls++];
     const int64_t seq = p.lists[(int64_t)cls * p.nseq + local];
     const int64_t rem = (int64_t)item % per_seq;
-    const int hh = (int)(rem / p.ctiles);
+    const int hh = (int)(rem / p.ctiles) * G + hl;  // this lane's head
     const int ct = (int)(rem % p.ctiles);
     const int64_t bidx = seq / p.J, bank = seq % p.J;
-    const int col0 = ct * 32 * NC + lane * NC;
+    const int col0 = ct * LPG * NC + el * NC;
     const bool active = col0 < p.dv;
     const int HS = p.H * S;
     const int64_t V = (int64_t)p.H * p.dv;
@@ -431,8 +445,8 @@ bank_scan_kernel(const ScanParams p) {
         my_rid = -1;
         my_write = false;
         my_wt = 0.f;
-        if (lane < bn) {
-            const int64_t id = p.order[bbase + lane];
+        if (el < bn) {
+            const int64_t id = p.order[bbase + el];
             if (id >= 0 && id < nw) {
                 my_tok = (int)id / kw;
                 my_write = true;
@@ -465,8 +479,8 @@ bank_scan_kernel(const ScanParams p) {
     // storage-point mask, and returns the write mask.
     auto stage_finish = [&](int64_t pos0, int bn, int &n_out, unsigned &round_out, unsigned &ck_out) -> unsigned {
         cp_async_wait_all();
-        const bool valid = lane < bn;
-        const int64_t pos = pos0 + lane;
+        const bool valid = el < bn;
+        const int64_t pos = pos0 + el;
         const bool head = valid && p.interval > 0 && pos > 0 && (pos % p.interval) == 0;
         const bool ckp = CK && valid && pos > 0 && (pos % p.ckpt_block) == 0;
         const T *rk = reinterpret_cast<const T *>(raw[lane] + Raw::kOff);
@@ -479,25 +493,26 @@ bank_scan_kernel(const ScanParams p) {
             if (my_write && my_tok >= 0) ge = fmaxf(p.routed_decay ? rg[s] * my_wt : rg[s], kMinLogDecay);
             L[s] = ge;
         }
-        bool f = head || ckp || lane == 0;
+        bool f = head || ckp || el == 0;
 #pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-            const bool fu = __shfl_up_sync(0xffffffffu, f, d);
-            const bool take = lane >= d && !f;
+        for (int d = 1; d < LPG; d <<= 1) {
+            const bool fu = __shfl_up_sync(0xffffffffu, f, d, LPG);
+            const bool take = el >= d && !f;
 #pragma unroll
             for (int s = 0; s < S; ++s) {
-                const float lu = __shfl_up_sync(0xffffffffu, L[s], d);
+                const float lu = __shfl_up_sync(0xffffffffu, L[s], d, LPG);
                 if (take) L[s] += lu;
             }
-            f = f || (lane >= d && fu);
+            f = f || (el >= d && fu);
         }
         // cut the batch before the first event whose segment would leave the FP32 range
         float lmin = 0.f;
 #pragma unroll
         for (int s = 0; s < S; ++s) lmin = fminf(lmin, L[s]);
-        const unsigned over = __ballot_sync(0xffffffffu, valid && lmin < kMinLogDecay);
+        unsigned over = __ballot_sync(0xffffffffu, valid && lmin < kMinLogDecay);
+        if (G == 2) over = (over | (over >> 16)) & 0xffffu;  // either head's range ends the batch
         const int n = over ? (__ffs(over) - 1) : bn;  // >= 1: a single event is floored above
-        const bool use = lane < n;
+        const bool use = el < n;
         float D[S];
 #pragma unroll
         for (int s = 0; s < S; ++s) D[s] = expf(L[s]);
@@ -508,23 +523,24 @@ bank_scan_kernel(const ScanParams p) {
                 for (int s = 0; s < S; ++s) {
                     const float kk = Elem<T>::to_float(rk[s]);
                     const float a = rnd<T>(Elem<T>::to_float(rb[s]) * my_wt) * kk;
-                    ctl[lane][Ctl::c + s] = dup(a * D[s]);
-                    ctl[lane][Ctl::kd + s] = dup(kk * expf(-L[s]));
+                    ctl[el][hl][Ctl::c + s] = dup(a * D[s]);
+                    ctl[el][hl][Ctl::kd + s] = dup(kk * expf(-L[s]));
                 }
-                ctl[lane][Ctl::p] = weight_pair<T>(my_wt);
+                ctl[el][hl][Ctl::p] = weight_pair<T>(my_wt);
             } else {
 #pragma unroll
-                for (int s = 0; s < S; ++s) ctl[lane][Ctl::c + s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * my_wt) * D[s]);
+                for (int s = 0; s < S; ++s)
+                    ctl[el][hl][Ctl::c + s] = dup(rnd<T>(Elem<T>::to_float(rk[s]) * my_wt) * D[s]);
             }
         }
         // D before a storage point (materialise there), D after the last event (batch end)
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            const float before = __shfl_up_sync(0xffffffffu, D[s], 1);
-            if (use && (head || ckp)) ctl[lane][Ctl::dprev + s] = dup(lane == 0 ? 1.0f : before);
-            if (lane == n - 1) dend[s] = dup(D[s]);
+            const float before = __shfl_up_sync(0xffffffffu, D[s], 1, LPG);
+            if (use && (head || ckp)) ctl[el][hl][Ctl::dprev + s] = dup(el == 0 ? 1.0f : before);
+            if (el == n - 1) dend[hl][s] = dup(D[s]);
         }
-        if (lane < EB) {
+        if (hl == 0 && el < EB) {
             EvRec r{0, 0, 0};
             if (use && my_tok >= 0) {
                 r.kind = my_write ? kEvWrite : kEvRead;
@@ -532,12 +548,12 @@ bank_scan_kernel(const ScanParams p) {
             }
             if (use && head) r.kind |= kEvRound;
             if (use && ckp) r.kind |= kEvCk;
-            ev_s[lane] = r;
+            ev_s[el] = r;
         }
         n_out = n;
-        round_out = __ballot_sync(0xffffffffu, use && head);
-        ck_out = __ballot_sync(0xffffffffu, use && ckp);
-        const unsigned wm = __ballot_sync(0xffffffffu, use && my_write && my_tok >= 0);
+        round_out = __ballot_sync(0xffffffffu, hl == 0 && use && head);
+        ck_out = __ballot_sync(0xffffffffu, hl == 0 && use && ckp);
+        const unsigned wm = __ballot_sync(0xffffffffu, hl == 0 && use && my_write && my_tok >= 0);
         __syncwarp();
         return wm;
     };
@@ -583,7 +599,7 @@ bank_scan_kernel(const ScanParams p) {
                     ck_row = p.ckpt + ((start / p.ckpt_block + seq + pos / p.ckpt_block) * p.H + hh) * (int64_t)S * p.dv +
                              col0;
                 }
-                event_step<T, S, NC>(ctl[ev], r.kind & kEvRound, r.kind & kEvWrite, r.kind & (kEvWrite | kEvRead),
+                event_step<T, S, NC>(ctl[ev][hl], r.kind & kEvRound, r.kind & kEvWrite, r.kind & (kEvWrite | kEvRead),
                                      active, vr[j], wr[j], p.scale, outp + r.off, N, ck_here, ck_row, p.dv);
                 prefetch(ev + PD, j);
             }
@@ -591,7 +607,7 @@ bank_scan_kernel(const ScanParams p) {
         // segment end: materialise N = D * N for the next batch (or the final state)
 #pragma unroll
         for (int s = 0; s < S; ++s) {
-            const float2 d2 = dend[s];
+            const float2 d2 = dend[hl][s];
 #pragma unroll
             for (int c = 0; c < NP; ++c) N[s][c] = __fmul2_rn(N[s][c], d2);
         }
@@ -1252,11 +1268,18 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     // bdm_bank_scan_chunked: the remaining classes on the tensor-core chunked kernel
     // (chunk_scan.cu), as the long kernel's programmatic dependent.
     if (q.chunked) return launch_chunk_scan(q, S, st, long_mode);
+    // Even head counts run two heads per warp (twice the columns per lane): BF16 with S <= 8 and at
+    // most 8 columns per lane (the doubled state and value rows fit the registers of 3 CTAs per SM,
+    // the staging arrays the 48 KB of static shared memory), heads split into whole column tiles.
+    constexpr bool kG2Fits = sizeof(T) == 2 && S <= 8 && NC <= 4;
+    constexpr int NC2 = kG2Fits ? 2 * NC : NC, G2 = kG2Fits ? 2 : 1;
+    const bool g2 = BDM_SCAN_G2 && kG2Fits && p.H % 2 == 0 && p.dv % (32 * NC) == 0;
     int per_sm = 1;
-    auto sk = p.ckpt ? bank_scan_kernel<T, S, NC, true> : bank_scan_kernel<T, S, NC, false>;
+    void (*sk)(const ScanParams) = p.ckpt ? bank_scan_kernel<T, S, NC, true, 1> : bank_scan_kernel<T, S, NC, false, 1>;
+    if (g2) sk = p.ckpt ? bank_scan_kernel<T, S, NC2, true, G2> : bank_scan_kernel<T, S, NC2, false, G2>;
     rc = cuda_status(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sk, kScanWarps * 32, 0));
     if (rc) return rc;
-    const int64_t want = ceil_div(q.units, kScanWarps);
+    const int64_t want = ceil_div(q.units / (g2 ? 2 : 1), kScanWarps);
     const int64_t blocks = BDM_SCAN_DYNAMIC ? min((int64_t)sms * (per_sm > 0 ? per_sm : 1), want)
                                             : min(want, (int64_t)0x7fffffff);
     // With long units the short kernel is a programmatic dependent launch of the
