@@ -36,6 +36,14 @@ from .config import BDMConfig, near_square_factors, state_interval
 
 
 FUSED_F_MAX_TOKENS = 4096  # at most this many tokens: the controllers kernel computes f_proj.1 itself
+_COPY_STREAMS: dict = {}  # per device: (upload stream, download stream) of forward_host
+
+
+def _copy_streams(device):
+    st = _COPY_STREAMS.get(device.index)
+    if st is None:
+        st = _COPY_STREAMS[device.index] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+    return st
 
 
 class SharedResidualRouter(nn.Module):
@@ -346,6 +354,58 @@ class BankedDeltaMemory(nn.Module):
         ri = routes[3].reshape(batch * time, -1)
         out = self._output(hidden, reads, ri, gate, round_each=False)
         ops.check_scan_status(hidden.device)  # non-blocking: raises once an earlier timeout is seen
+        return out
+
+    @torch.no_grad()
+    def forward_host(self, hidden, out=None, *, chunks: int = 4):
+        """``forward`` of a batch held in host memory, returned in host memory.
+
+        The batch streams through the GPU in ``chunks`` groups of rows: every upload is queued on
+        one copy stream, each group's forward runs on the current stream once its rows have
+        landed, and its output goes back on a second copy stream, so the uploads, the downloads
+        (the two directions of the host link) and the compute of different groups overlap.  Batch
+        rows are independent (each bank sequence belongs to one row), so the result is
+        ``forward``'s up to the GEMMs' accumulation order at the smaller row count.  ``hidden``
+        should be pinned (pageable memory makes the copies synchronous); ``out`` (pinned, [B, T, D])
+        receives the result and is returned, else a new pinned tensor is.  The current stream
+        waits for the downloads before this returns; the host must synchronise before reading
+        ``out``.
+        """
+        if hidden.is_cuda or hidden.ndim != 3 or hidden.shape[-1] != self.hidden_size or hidden.shape[1] == 0:
+            raise ValueError('forward_host takes a host tensor [batch, positive time, dim]')
+        dev = self.q_proj.weight.device
+        if dev.type != 'cuda':
+            raise ValueError('bdm_b200 requires the layer on a CUDA device; there is no CPU path')
+        batch = hidden.shape[0]
+        if out is None:
+            out = torch.empty(hidden.shape[:2] + (self.hidden_size,), dtype=hidden.dtype, pin_memory=True)
+        elif out.shape != hidden.shape[:2] + (self.hidden_size,) or out.is_cuda:
+            raise ValueError('out must be a host tensor [batch, time, dim]')
+        groups = max(1, min(int(chunks), batch))
+        bounds = [(batch * i // groups, batch * (i + 1) // groups) for i in range(groups)]
+        cur = torch.cuda.current_stream(dev)
+        up, down = _copy_streams(dev)
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        inputs, landed = [], []
+        for a, b in bounds:
+            with torch.cuda.stream(up):
+                x = hidden[a:b].to(dev, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(up)
+            x.record_stream(cur)
+            inputs.append(x)
+            landed.append(ev)
+        for (a, b), x, ev in zip(bounds, inputs, landed):
+            cur.wait_event(ev)
+            y = self.forward(x)
+            done = torch.cuda.Event()
+            done.record(cur)
+            down.wait_event(done)
+            with torch.cuda.stream(down):
+                out[a:b].copy_(y, non_blocking=True)
+            y.record_stream(down)
+        cur.wait_stream(down)
         return out
 
     def _forward_train(self, hidden):

@@ -716,3 +716,24 @@ def test_layer_fused_output_matches_unfused_and_oracle():
     assert torch.equal(st_fused, st_plain)
     oy = _oracle_layer(m).forward(npf(x), controls=ctl, routes=routes)
     assert max_rel(npf(y_fused), oy) <= BF16_TOL, max_rel(npf(y_fused), oy)
+
+
+@pytest.mark.parametrize('dtype,chunks', [(torch.bfloat16, 4), (torch.float32, 3), (torch.bfloat16, 1)])
+def test_forward_host_streams_row_groups_like_forward(dtype, chunks):
+    """forward_host (host batch in, host result out, row groups with overlapped copies) against
+    forward on the device copy: the bank path is per row, so only the GEMMs' accumulation order
+    at a smaller row count may differ."""
+    cfg = BSDMConfig(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=256, num_heads=2)
+    torch.manual_seed(31)
+    m = BlockSparseDeltaMemory(cfg, seed=3).to(dtype).to(DEV)
+    x = torch.randn(5, 96, 256).to(dtype).pin_memory()
+    with torch.no_grad():
+        ref = m(x.to(DEV))
+        got = m.forward_host(x, chunks=chunks)
+        torch.cuda.synchronize()
+        again = m.forward_host(x, torch.empty_like(got).pin_memory(), chunks=chunks)
+        torch.cuda.synchronize()
+    assert not got.is_cuda and got.shape == ref.shape
+    tol = FP32_TOL if dtype == torch.float32 else BF16_TOL
+    assert max_rel(npf(got), npf(ref)) <= tol, max_rel(npf(got), npf(ref))
+    assert torch.equal(got, again)
