@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import hashlib
 import math
+import weakref
 
 import torch
 from torch import nn
@@ -37,6 +38,8 @@ from .config import BDMConfig, near_square_factors, state_interval
 
 FUSED_F_MAX_TOKENS = 4096  # at most this many tokens: the controllers kernel computes f_proj.1 itself
 _COPY_STREAMS: dict = {}  # per device: (upload stream, download stream) of forward_host
+# per layer: {(rows, time): (parameter key, [captured forwards])} for forward_host's row groups
+_HOST_GRAPHS: 'weakref.WeakKeyDictionary' = weakref.WeakKeyDictionary()
 
 
 def _copy_streams(device):
@@ -356,27 +359,73 @@ class BankedDeltaMemory(nn.Module):
         ops.check_scan_status(hidden.device)  # non-blocking: raises once an earlier timeout is seen
         return out
 
+    def capture_forward(self, batch: int, time: int, *, warmup: int = 2):
+        """CUDA-graph ``forward`` for inputs [batch, time, dim].
+
+        Returns ``run(hidden=None) -> out``: copies ``hidden`` (if given) into the graph's input
+        buffer ``run.input``, replays the forward and returns its output buffer ``run.output``,
+        which the next replay overwrites.  Parameters must not change afterwards (the graph holds
+        their fused copy); ``forward_host`` recaptures when they do.
+        """
+        if torch.is_grad_enabled():
+            raise RuntimeError('capture_forward requires no_grad or inference_mode')
+        dev, dt = self.q_proj.weight.device, self.q_proj.weight.dtype
+        x = torch.zeros(batch, time, self.hidden_size, dtype=dt, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.forward(x)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y = self.forward(x)
+
+        def run(hidden=None):
+            if hidden is not None:
+                x.copy_(hidden)
+            graph.replay()
+            return y
+
+        run.graph, run.input, run.output = graph, x, y  # keep the graph and its buffers alive
+        return run
+
+    def _host_graphs(self, rows: int, time: int, slots: int):
+        key = tuple((p.data_ptr(), p._version) for p in self.parameters())
+        per_layer = _HOST_GRAPHS.setdefault(self, {})
+        entry = per_layer.get((rows, time))
+        if entry is None or entry[0] != key or len(entry[1]) < slots:
+            per_layer.pop((rows, time), None)  # free stale graphs before capturing new ones
+            entry = (key, [self.capture_forward(rows, time) for _ in range(slots)])
+            per_layer[(rows, time)] = entry
+        return entry[1][:slots]
+
     @torch.no_grad()
-    def forward_host(self, hidden, out=None, *, chunks: int = 4):
+    def forward_host(self, hidden, out=None, *, chunks: int = 4, graphs: bool = True):
         """``forward`` of a batch held in host memory, returned in host memory.
 
-        The batch streams through the GPU in ``chunks`` groups of rows: every upload is queued on
-        one copy stream, each group's forward runs on the current stream once its rows have
-        landed, and its output goes back on a second copy stream, so the uploads, the downloads
-        (the two directions of the host link) and the compute of different groups overlap.  Batch
-        rows are independent (each bank sequence belongs to one row), so the result is
-        ``forward``'s up to the GEMMs' accumulation order at the smaller row count.  ``hidden``
-        should be pinned (pageable memory makes the copies synchronous); ``out`` (pinned, [B, T, D])
-        receives the result and is returned, else a new pinned tensor is.  The current stream
-        waits for the downloads before this returns; the host must synchronise before reading
-        ``out``.
+        The batch streams through the GPU in ``chunks`` groups of rows: each group is uploaded on
+        one copy stream, its forward runs on the current stream once its rows have landed, and
+        its output goes back on a second copy stream, so the uploads, the downloads (the two
+        directions of the host link) and the compute of different groups overlap.  With
+        ``graphs`` and equal groups, each group's forward is a replay of one of up to three
+        captured forwards (``capture_forward``, cached per layer and group shape, recaptured when
+        a parameter changes) used in rotation, which removes the per-group host launch cost; a
+        slot is refilled only once its previous output has been downloaded.  Batch rows are
+        independent (each bank sequence belongs to one row), so the result is ``forward``'s up to
+        the GEMMs' accumulation order at the smaller row count.  ``hidden`` should be pinned
+        (pageable memory makes the copies synchronous); ``out`` (pinned, [B, T, D]) receives the
+        result and is returned, else a new pinned tensor is.  The current stream waits for the
+        downloads before this returns; the host must synchronise before reading ``out``.
         """
         if hidden.is_cuda or hidden.ndim != 3 or hidden.shape[-1] != self.hidden_size or hidden.shape[1] == 0:
             raise ValueError('forward_host takes a host tensor [batch, positive time, dim]')
         dev = self.q_proj.weight.device
         if dev.type != 'cuda':
             raise ValueError('bdm_b200 requires the layer on a CUDA device; there is no CPU path')
-        batch = hidden.shape[0]
+        if hidden.dtype != self.q_proj.weight.dtype:
+            raise ValueError(f'hidden dtype {hidden.dtype} does not match the parameters ({self.q_proj.weight.dtype})')
+        batch, time = hidden.shape[0], hidden.shape[1]
         if out is None:
             out = torch.empty(hidden.shape[:2] + (self.hidden_size,), dtype=hidden.dtype, pin_memory=True)
         elif out.shape != hidden.shape[:2] + (self.hidden_size,) or out.is_cuda:
@@ -387,6 +436,30 @@ class BankedDeltaMemory(nn.Module):
         up, down = _copy_streams(dev)
         up.wait_stream(cur)
         down.wait_stream(cur)
+        if graphs and batch % groups == 0:
+            runs = self._host_graphs(batch // groups, time, min(groups, 3))
+            freed = [None] * len(runs)  # per slot: its last output has been downloaded
+            for i, (a, b) in enumerate(bounds):
+                slot = i % len(runs)
+                run = runs[slot]
+                with torch.cuda.stream(up):
+                    if freed[slot] is not None:
+                        up.wait_event(freed[slot])
+                    run.input.copy_(hidden[a:b], non_blocking=True)
+                    landed = torch.cuda.Event()
+                    landed.record(up)
+                cur.wait_event(landed)
+                run.graph.replay()
+                done = torch.cuda.Event()
+                done.record(cur)
+                with torch.cuda.stream(down):
+                    down.wait_event(done)
+                    out[a:b].copy_(run.output, non_blocking=True)
+                    freed[slot] = torch.cuda.Event()
+                    freed[slot].record(down)
+            cur.wait_stream(down)
+            ops.check_scan_status(dev)  # non-blocking: the replays skip the forward's own poll
+            return out
         inputs, landed = [], []
         for a, b in bounds:
             with torch.cuda.stream(up):

@@ -48,7 +48,7 @@ C1 = dict(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=64
 C1_BATCH, C1_TIME = 2, 512
 C2 = dict(dim=1024, bank_count=256, bank_size=8, selected_banks=8, value_width=1024, num_heads=8)
 C2_BATCH, C2_TIME, C2_CHUNK = 8, 4096, 64
-E2E_CHUNKS = 2  # row groups of BlockSparseDeltaMemory.forward_host in the e2e measurement (measured best of 1, 2, 4, 8)
+E2E_CHUNKS = 4  # row groups of BlockSparseDeltaMemory.forward_host (captured forwards) in the e2e measurement: measured best of 2, 4, 8
 C3 = dict(dim=1024, bank_count=2048, bank_size=8, selected_banks=8, value_width=128, num_heads=1)
 C3_BATCH, C3_PREFIX, C3_STEPS = 64, 2048, 1024
 C4 = dict(dim=2048, bank_count=16384, bank_size=16, selected_banks=16, value_width=2048, num_heads=16)
@@ -481,8 +481,8 @@ def run_ours(args, world, rank, local):
         'e2e': {'value': world * tokens * args.steps / (e2e_ms / 1000), 'unit': 'tokens/s',
                 'h2d_bytes_per_step': x_host.numel() * x_host.element_size(),
                 'd2h_bytes_per_step': y_host.numel() * y_host.element_size(),
-                'path': f'BlockSparseDeltaMemory.forward_host (pinned host in and out, {E2E_CHUNKS} row groups, '
-                        'uploads / downloads overlapped with compute)'},
+                'path': f'BlockSparseDeltaMemory.forward_host (pinned host in and out, {E2E_CHUNKS} row groups as '
+                        'replays of captured forwards, uploads / downloads overlapped with compute)'},
         'roofline': {'kernel': 'bdm_bank_scan (bank_scan_kernel<bf16, S=8, 8 columns/lane, 2 heads/warp>)',
                      'bound': 'hbm',
                      'achieved': achieved, 'peak': hbm_peak, 'unit': 'GB/s', 'frac': achieved / hbm_peak,

@@ -718,22 +718,28 @@ def test_layer_fused_output_matches_unfused_and_oracle():
     assert max_rel(npf(y_fused), oy) <= BF16_TOL, max_rel(npf(y_fused), oy)
 
 
-@pytest.mark.parametrize('dtype,chunks', [(torch.bfloat16, 4), (torch.float32, 3), (torch.bfloat16, 1)])
-def test_forward_host_streams_row_groups_like_forward(dtype, chunks):
-    """forward_host (host batch in, host result out, row groups with overlapped copies) against
-    forward on the device copy: the bank path is per row, so only the GEMMs' accumulation order
-    at a smaller row count may differ."""
+@pytest.mark.parametrize('dtype,chunks,graphs', [(torch.bfloat16, 4, False), (torch.float32, 3, False),
+                                                 (torch.bfloat16, 1, False), (torch.bfloat16, 2, True),
+                                                 (torch.float32, 4, True), (torch.bfloat16, 3, True)])
+def test_forward_host_streams_row_groups_like_forward(dtype, chunks, graphs):
+    """forward_host (host batch in, host result out, row groups with overlapped copies; with graphs,
+    replays of captured row-group forwards) against forward on the device copy: the bank path is
+    per row, so only the GEMMs' accumulation order at a smaller row count may differ.  After a
+    parameter update the captured forwards are recaptured."""
     cfg = BSDMConfig(dim=256, bank_count=256, bank_size=8, selected_banks=8, value_width=256, num_heads=2)
     torch.manual_seed(31)
     m = BlockSparseDeltaMemory(cfg, seed=3).to(dtype).to(DEV)
-    x = torch.randn(5, 96, 256).to(dtype).pin_memory()
-    with torch.no_grad():
-        ref = m(x.to(DEV))
-        got = m.forward_host(x, chunks=chunks)
-        torch.cuda.synchronize()
-        again = m.forward_host(x, torch.empty_like(got).pin_memory(), chunks=chunks)
-        torch.cuda.synchronize()
-    assert not got.is_cuda and got.shape == ref.shape
+    x = torch.randn(8, 96, 256).to(dtype).pin_memory()
     tol = FP32_TOL if dtype == torch.float32 else BF16_TOL
-    assert max_rel(npf(got), npf(ref)) <= tol, max_rel(npf(got), npf(ref))
-    assert torch.equal(got, again)
+    with torch.no_grad():
+        for update in (False, True):
+            if update:
+                m.o_proj.weight.mul_(1.5)  # in place: bumps the parameter's version
+            ref = m(x.to(DEV))
+            got = m.forward_host(x, chunks=chunks, graphs=graphs)
+            torch.cuda.synchronize()
+            again = m.forward_host(x, torch.empty_like(got).pin_memory(), chunks=chunks, graphs=graphs)
+            torch.cuda.synchronize()
+            assert not got.is_cuda and got.shape == ref.shape
+            assert max_rel(npf(got), npf(ref)) <= tol, (update, max_rel(npf(got), npf(ref)))
+            assert torch.equal(got, again)
