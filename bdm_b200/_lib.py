@@ -54,6 +54,7 @@ SIGNATURES = {
     'bdm_combine_project': (_int, [_vp, _vp, _i64, _int, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _vp, _vp,
                                    _i64, _int, _vp, _i64, _vp, _vp]),
     'bdm_combine_project_supported': (_int, [_i64, _i64, _int, _int]),
+    'bdm_status_or': (_int, [_vp, _vp, _vp]),
     'bdm_norm_gate_backward_partial_floats': (_i64, [_i64, _i64]),
     'bdm_norm_gate_backward': (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _flt, _int, _int, _vp, _vp, _i64,
                                       _vp, _vp, _vp, _vp]),

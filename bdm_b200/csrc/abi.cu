@@ -30,8 +30,20 @@ __global__ void product_state_kernel(const FT *__restrict__ U, const FT *__restr
     }
 }
 
+__global__ void status_or_kernel(int *dst, const int *src) {
+    const int bits = *src;
+    if (bits) atomicOr(dst, bits);
+}
+
 }  // namespace
 }  // namespace bdm
+
+extern "C" int bdm_status_or(int *dst, const int *src, void *stream) {
+    using namespace bdm;
+    if (!dst || !src) return BDM_ERR_INVALID;
+    status_or_kernel<<<1, 1, 0, as_stream(stream)>>>(dst, src);
+    return launch_status();
+}
 
 extern "C" const char *bdm_status_string(int status) {
     switch (status) {

@@ -37,7 +37,7 @@ from .config import BDMConfig, near_square_factors, state_interval
 
 
 FUSED_F_MAX_TOKENS = 4096  # at most this many tokens: the controllers kernel computes f_proj.1 itself
-_COPY_STREAMS: dict = {}  # per device: (upload stream, download stream) of forward_host
+_COPY_STREAMS: dict = {}  # per device: (upload, download, second compute) streams of forward_host
 # per layer: {(rows, time): (parameter key, [captured forwards])} for forward_host's row groups
 _HOST_GRAPHS: 'weakref.WeakKeyDictionary' = weakref.WeakKeyDictionary()
 
@@ -45,7 +45,7 @@ _HOST_GRAPHS: 'weakref.WeakKeyDictionary' = weakref.WeakKeyDictionary()
 def _copy_streams(device):
     st = _COPY_STREAMS.get(device.index)
     if st is None:
-        st = _COPY_STREAMS[device.index] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        st = _COPY_STREAMS[device.index] = tuple(torch.cuda.Stream(device) for _ in range(3))
     return st
 
 
@@ -411,7 +411,8 @@ class BankedDeltaMemory(nn.Module):
         ``graphs`` and equal groups, each group's forward is a replay of one of up to three
         captured forwards (``capture_forward``, cached per layer and group shape, recaptured when
         a parameter changes) used in rotation, which removes the per-group host launch cost; a
-        slot is refilled only once its previous output has been downloaded.  Batch rows are
+        slot is refilled only once its previous output has been downloaded, and consecutive
+        groups replay on two compute streams so that their kernels overlap.  Batch rows are
         independent (each bank sequence belongs to one row), so the result is ``forward``'s up to
         the GEMMs' accumulation order at the smaller row count.  ``hidden`` should be pinned
         (pageable memory makes the copies synchronous); ``out`` (pinned, [B, T, D]) receives the
@@ -433,30 +434,37 @@ class BankedDeltaMemory(nn.Module):
         groups = max(1, min(int(chunks), batch))
         bounds = [(batch * i // groups, batch * (i + 1) // groups) for i in range(groups)]
         cur = torch.cuda.current_stream(dev)
-        up, down = _copy_streams(dev)
+        up, down, comp2 = _copy_streams(dev)
         up.wait_stream(cur)
         down.wait_stream(cur)
         if graphs and batch % groups == 0:
             runs = self._host_graphs(batch // groups, time, min(groups, 3))
             freed = [None] * len(runs)  # per slot: its last output has been downloaded
+            # groups alternate between two compute streams, so one group's GEMMs fill the tail
+            # of the previous group's recurrence
+            comp2.wait_stream(cur)
+            computes = (cur, comp2)
             for i, (a, b) in enumerate(bounds):
                 slot = i % len(runs)
                 run = runs[slot]
+                cs = computes[i % 2]
                 with torch.cuda.stream(up):
                     if freed[slot] is not None:
                         up.wait_event(freed[slot])
                     run.input.copy_(hidden[a:b], non_blocking=True)
                     landed = torch.cuda.Event()
                     landed.record(up)
-                cur.wait_event(landed)
-                run.graph.replay()
-                done = torch.cuda.Event()
-                done.record(cur)
+                cs.wait_event(landed)
+                with torch.cuda.stream(cs):
+                    run.graph.replay()
+                    done = torch.cuda.Event()
+                    done.record(cs)
                 with torch.cuda.stream(down):
                     down.wait_event(done)
                     out[a:b].copy_(run.output, non_blocking=True)
                     freed[slot] = torch.cuda.Event()
                     freed[slot].record(down)
+            cur.wait_stream(comp2)
             cur.wait_stream(down)
             ops.check_scan_status(dev)  # non-blocking: the replays skip the forward's own poll
             return out

@@ -334,8 +334,10 @@ def bank_scan(q, k, v, g, b, w, write_idx, write_w, read_idx, read_w, order, cu_
         int(store_final), int(state_interval), _ptr(reads), _ptr(ws), nbytes, _ptr(checkpoints),
         int(checkpoint_block) if checkpoints is not None else 0, _stream(q.device)),
         'bdm_bank_scan_chunked' if chunked else 'bdm_bank_scan')
+    # atomic: recurrences on several streams (forward_host's row groups) share the sticky word
     sticky = _scan_status_of(q.device).word
-    sticky.bitwise_or_(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32))
+    _lib.check(_lib.load().bdm_status_or(_ptr(sticky), ws.data_ptr() + SCAN_STATUS_OFFSET, _stream(q.device)),
+               'bdm_status_or')
     if check_status:  # synchronises: the kernel's error bits (a bounded producer/consumer wait that gave up)
         status = int(ws[SCAN_STATUS_OFFSET:SCAN_STATUS_OFFSET + 4].view(torch.int32).item())
         if status:

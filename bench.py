@@ -55,6 +55,7 @@ C4 = dict(dim=2048, bank_count=16384, bank_size=16, selected_banks=16, value_wid
 C4_BATCH, C4_TIME, C4_ZIPF = 16, 8192, 1.1
 C5 = dict(dim=768, bank_count=512, bank_size=8, selected_banks=8, value_width=768, num_heads=12)
 C5_BATCH, C5_TIME = 32, 2048
+C4_WARMUP = C5_WARMUP = 3  # untimed steps before the c4 / c5 timed steps
 C5_METRIC = ('BDM layer training step (forward + backward) tokens/sec, c5 layer geometry (batch 32 x seq 2048, '
              'd_model 768, H=12, J=512, S=8, B=8, d_v=64)')
 C5_LM = dict(vocab_size=32000, layers=12)
@@ -652,7 +653,8 @@ def run_reference_gpu(dev, args):
         gen = torch.Generator().manual_seed(1)
         x = torch.randn(C2_BATCH, C2_TIME, cfg.dim, generator=gen).to(torch.bfloat16).to(dev)
         with torch.no_grad():
-            layer(x)
+            for _ in range(3):  # warm-up (Triton compilation and autotuning happen on the first call)
+                layer(x)
             torch.cuda.synchronize()
             n = 3
             s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -663,7 +665,7 @@ def run_reference_gpu(dev, args):
             torch.cuda.synchronize()
         ms = s_.elapsed_time(e_) / n
         out['c2_forward'] = {'ms_per_step': ms, 'value': C2_BATCH * C2_TIME / (ms / 1000), 'unit': 'tokens/s',
-                             'steps': n, 'warmup': 1}
+                             'steps': n, 'warmup': 3}
         del layer, x
     except Exception as e:  # noqa: BLE001
         out['c2_forward'] = {'error': repr(e)[:300]}
@@ -874,7 +876,7 @@ def run_c5(dev, rank, world, args):
         return loss
 
     clocks = ClockSampler(dev.index).start()
-    for _ in range(2):
+    for _ in range(C5_WARMUP):
         step()
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -897,7 +899,7 @@ def run_c5(dev, rank, world, args):
     dense_flops = 6 * gemm_params * tokens_step  # every GEMM weight: forward + two backward products
     floor_ms = dense_flops / world / (bf16_peak * 1e12) * 1000
     out = {'metric': C5_LM_METRIC, 'value': tokens_step / (ms / 1000), 'unit': 'tokens/s', 'n_gpus': world,
-           'steps': steps, 'warmup': 2, 'ms_per_step': ms, 'scaling': 'strong', 'dtype': 'bf16',
+           'steps': steps, 'warmup': C5_WARMUP, 'ms_per_step': ms, 'scaling': 'strong', 'dtype': 'bf16',
            'loss': float(loss.item()),
            'path': 'bdm_b200.lm.BDMLanguageModel (B200 BDM layers, cuBLAS SwiGLU/head), fused AdamW'
                    + (', DistributedDataParallel over NCCL' if world > 1 else ''),
@@ -941,7 +943,7 @@ def run_c4(dev, rank, world, args):
     steps = args.c4_steps
     clocks = ClockSampler(dev.index).start()
     with torch.inference_mode():
-        for _ in range(2):
+        for _ in range(C4_WARMUP):
             fwd(x)
         torch.cuda.synchronize()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -964,7 +966,7 @@ def run_c4(dev, rank, world, args):
     _, layer_bytes = c4_bytes_per_token()
     roof_ms = layer_bytes * tokens / (hbm_peak * 1e9 * world) * 1000
     out = {'metric': C4_METRIC, 'value': tokens / (ms / 1000), 'unit': 'tokens/s', 'n_gpus': world,
-           'steps': steps, 'warmup': 2, 'ms_per_step': ms, 'scaling': 'strong',
+           'steps': steps, 'warmup': C4_WARMUP, 'ms_per_step': ms, 'scaling': 'strong',
            'path': 'BlockSparseDeltaMemory.forward' if world == 1 else
                    f'BankShardedMemory (bank-sharded, {args.c4_ownership} partition, NCCL all-gather/reduce-scatter)',
            'config': {'workload': 'c4: BSDMConfig(dim=2048, bank_count=16384, bank_size=16, selected_banks=16, '
@@ -1038,7 +1040,7 @@ def main():
     ap.add_argument('--skip-train', action='store_true')
     ap.add_argument('--cpu-train-batch', type=int, default=2, help='rows (x 2048 tokens) of the training CPU sample')
     ap.add_argument('--skip-c5', action='store_true')
-    ap.add_argument('--c5-steps', type=int, default=2)
+    ap.add_argument('--c5-steps', type=int, default=3)
     ap.add_argument('--c5-batch', type=int, default=32, help='c5 global batch (32 is the benchmark)')
     ap.add_argument('--train-steps', type=int, default=3)
     ap.add_argument('--train-batch', type=int, default=C5_BATCH, help='c5 batch (32 is the benchmark)')

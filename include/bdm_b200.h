@@ -51,6 +51,9 @@ enum bdm_status {
 enum bdm_dtype { BDM_F32 = 0, BDM_BF16 = 1 };
 
 /* Human-readable status text (static storage). */
+/* *dst |= *src (device ints) as an atomic OR on `stream`: folds a launch's error bits into a word
+ * that launches on other streams may update at the same time.  Utility; no reference counterpart. */
+BDM_API int bdm_status_or(int *dst, const int *src, void *stream);
 BDM_API const char *bdm_status_string(int status);
 /* cudaError_t of the last call that returned BDM_ERR_CUDA on this host thread. */
 BDM_API int bdm_last_cuda_error(void);

@@ -50,6 +50,7 @@ def test_dispatch_workspace_sizing():
     lambda lib: lib.bdm_route(None, 4, 8, 16, 16, 8, 1, None, None, None),        # ld < j1 + j2
     lambda lib: lib.bdm_dispatch(None, None, 2, 4, 8, 8, 256, None, None, None, None, None, None, 0, None),
     lambda lib: lib.bdm_combine_norm_gate(None, None, 4, 8, 0, None, 0, None, None, 1e-5, 1, 0, 1, None, None),
+    lambda lib: lib.bdm_status_or(None, None, None),                                  # null words
     lambda lib: lib.bdm_bank_owners(None, 256, 4, 1, None, None, None, None),          # balanced needs counts
     lambda lib: lib.bdm_bank_owners(None, 256, 0, 0, None, None, None, None),          # world 0
     lambda lib: lib.bdm_dispatch_owned(None, None, 2, 4, 8, 8, 256, None, None, 0, 64, None, None, None, None, None,
