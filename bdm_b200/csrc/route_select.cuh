@@ -4,8 +4,9 @@
 // (value desc, index asc), so equal scores resolve to the lower index -- the tie rule the
 // reference leaves to torch.topk.  Short lists (factor widths <= 128, the pair "staircase") are
 // sorted in registers (warp bitonic network over 64-bit keys: order-preserving value bits above
-// the inverted index); wide factors use warp arg-max rounds over the same keys.  Shared by the
-// router kernel (router.cu) and the fused decode step (decode.cu).
+// the inverted index; both factors in one sort when together they fit 128 keys); wide factors use
+// warp arg-max rounds over the same keys.  Shared by the router kernel (router.cu) and the fused
+// decode step (decode.cu).
 #pragma once
 
 #include "common.cuh"
@@ -130,6 +131,49 @@ __device__ __forceinline__ void warp_sort_select(const float *vals, int n, int k
     else warp_sort_select_m<4>(vals, n, k, out_v, out_i);
 }
 
+// Top-sub of both factors at once: z[0, j1) and z[j1, j1 + j2), j1 + j2 <= 32 * M, in one sort.
+// A key carries its factor above the selection key (value bits, inverted index within the
+// factor), so factor 1 sorts ahead of factor 2 and each keeps the (value desc, index asc) order:
+// factor 1's top-sub end at flat positions [0, sub), factor 2's at [j1, j1 + sub).
+template <int M>
+__device__ __forceinline__ void warp_sort_select_pair_m(const float *z, int j1, int j2, int sub, float *fv, int *fi,
+                                                        float *sv, int *si) {
+    const int lane = (int)lane_id();
+    unsigned long long key[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const int e = lane + 32 * m;
+        if (e < j1 + j2) {
+            const bool first = e < j1;
+            const int i = first ? e : e - j1;
+            float v = z[e];
+            if (v == 0.f) v = 0.f;
+            key[m] = ((unsigned long long)(first ? 1u : 0u) << 63) | ((unsigned long long)ordered_bits(v) << 31) |
+                     (unsigned long long)(~(uint32_t)i & 0x7fffffffu);
+        } else {
+            key[m] = 0ull;
+        }
+    }
+    warp_bitonic_desc<M>(key);
+    // factor 2's l-th key sits at flat position j1 + l: lane (j1 + l) % 32, register (j1 + l) / 32
+    const int e2 = j1 + lane;
+    unsigned long long k2 = 0ull;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        const unsigned long long t = __shfl_sync(0xffffffffu, key[m], e2 & 31);
+        if ((e2 >> 5) == m) k2 = t;
+    }
+    if (lane < sub) {
+        const int i1 = (int)(~(uint32_t)(key[0] & 0x7fffffffull) & 0x7fffffffu);
+        const int i2 = (int)(~(uint32_t)(k2 & 0x7fffffffull) & 0x7fffffffu);
+        fv[lane] = z[i1];
+        fi[lane] = i1;
+        sv[lane] = z[j1 + i2];
+        si[lane] = i2;
+    }
+    __syncwarp();
+}
+
 // Pairs (i, l) that can reach the top `count`: a pair is outranked by every
 // (i', l') <= (i, l) componentwise (sums of descending lists, lower pair index),
 // so only pairs with (i + 1) * (l + 1) <= count are candidates.  Returns the
@@ -168,10 +212,18 @@ __device__ __forceinline__ bool route_token(float *scratch, int j1, int j2, int 
     float *cv = pv + sub * sub;
     int *ci = reinterpret_cast<int *>(cv + count);
     __syncwarp();
-    if (j1 <= kRankMax) warp_sort_select(z, j1, sub, fv, fi);
-    else warp_topk(z, j1, sub, fv, fi);
-    if (j2 <= kRankMax) warp_sort_select(z + j1, j2, sub, sv, si);
-    else warp_topk(z + j1, j2, sub, sv, si);
+    if (j1 + j2 <= 32) {  // both factors in one register sort
+        warp_sort_select_pair_m<1>(z, j1, j2, sub, fv, fi, sv, si);
+    } else if (j1 + j2 <= 64) {
+        warp_sort_select_pair_m<2>(z, j1, j2, sub, fv, fi, sv, si);
+    } else if (j1 + j2 <= kRankMax) {
+        warp_sort_select_pair_m<4>(z, j1, j2, sub, fv, fi, sv, si);
+    } else {
+        if (j1 <= kRankMax) warp_sort_select(z, j1, sub, fv, fi);
+        else warp_topk(z, j1, sub, fv, fi);
+        if (j2 <= kRankMax) warp_sort_select(z + j1, j2, sub, sv, si);
+        else warp_topk(z + j1, j2, sub, sv, si);
+    }
     // Pair scores in the logits dtype, pair p = i*sub + l (gdn2_banks.py:106-110).
     if (fast_pairs) {
         for (int c = lane; c < ncand; c += 32) {
