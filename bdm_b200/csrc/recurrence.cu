@@ -363,11 +363,14 @@ __global__ void __launch_bounds__(kScanWarps * 32, G == 2 ? BDM_SCAN_MIN_BLOCKS_
 bank_scan_kernel(const ScanParams p) {
     constexpr int NP = NC / 2;
     constexpr int LPG = 32 / G;  // lanes per head
-    constexpr int EB = EvBatch<S>::value < LPG ? EvBatch<S>::value : LPG;
+    // two heads per warp: 16 events per batch (one (event, head) pair per lane), 8 at S = 16 (its
+    // coefficient rows are twice as long; 48 KB of static shared memory)
+    constexpr int EBG = G == 2 ? (S >= 16 ? 8 : 16) : 32;
+    constexpr int EB = EvBatch<S>::value < EBG ? EvBatch<S>::value : EBG;
     constexpr int PD = G == 2 ? kPrefetchG2 : kPrefetch;
     using Raw = RawLayout<T, S>;
     using Ctl = CtlLayout<S>;
-    static_assert(EB % PD == 0 && LPG % EB == 0 && S % 2 == 0 && (G == 1 || G == 2), "batch layout");
+    static_assert(EB % PD == 0 && LPG % EB == 0 && EB <= LPG && S % 2 == 0 && (G == 1 || G == 2), "batch layout");
     __shared__ __align__(16) float2 ctl_all[kScanWarps][EB][G][Ctl::size];
     __shared__ __align__(16) float2 dend_all[kScanWarps][G][S];
     __shared__ __align__(16) unsigned char raw_all[kScanWarps][G == 1 ? EB : 32][Raw::size];
@@ -1271,10 +1274,10 @@ int launch_scan(const ScanParams &p, cudaStream_t st) {
     // bdm_bank_scan_chunked: the remaining classes on the tensor-core chunked kernel
     // (chunk_scan.cu), as the long kernel's programmatic dependent.
     if (q.chunked) return launch_chunk_scan(q, S, st, long_mode);
-    // Even head counts run two heads per warp (twice the columns per lane): BF16 with S <= 8 and at
-    // most 8 columns per lane (the doubled state and value rows fit the registers of 3 CTAs per SM,
-    // the staging arrays the 48 KB of static shared memory), heads split into whole column tiles.
-    constexpr bool kG2Fits = sizeof(T) == 2 && S <= 8 && NC <= 4;
+    // Even head counts run two heads per warp (twice the columns per lane): BF16 with at most 8
+    // columns per lane (the doubled state and value rows fit the registers of 3 CTAs per SM, the
+    // staging arrays the 48 KB of static shared memory), heads split into whole column tiles.
+    constexpr bool kG2Fits = sizeof(T) == 2 && NC <= 4 && S * NC <= 32;
     constexpr int NC2 = kG2Fits ? 2 * NC : NC, G2 = kG2Fits ? 2 : 1;
     const bool g2 = BDM_SCAN_G2 && kG2Fits && p.H % 2 == 0 && p.dv % (32 * NC) == 0;
     int per_sm = 1;
