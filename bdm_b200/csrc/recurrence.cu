@@ -57,7 +57,10 @@ constexpr int kScanWarps = 4;
 constexpr int kPrefetch = BDM_SCAN_PREFETCH;
 // With two heads per warp the value rows are twice as wide: two events ahead keep the registers
 // within 3 CTAs per SM (measured faster than four events at 3 CTAs or 4 CTAs with spills).
-constexpr int kPrefetchG2 = 2;
+#ifndef BDM_SCAN_PREFETCH_G2
+#define BDM_SCAN_PREFETCH_G2 2
+#endif
+constexpr int kPrefetchG2 = BDM_SCAN_PREFETCH_G2;
 
 // Lower bounds of classes 1..3; class 0 starts at the launch's long-sequence bound.
 __device__ __constant__ int kLenLower[kLenClasses] = {0, 2048, 512, 1};
