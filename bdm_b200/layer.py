@@ -391,14 +391,18 @@ class BankedDeltaMemory(nn.Module):
         return run
 
     def _host_graphs(self, rows: int, time: int, slots: int):
+        """(captured forwards, their download events, fresh): up to ``slots`` captured forwards of
+        [rows, time] inputs, recaptured when a parameter changes; ``freed[i]`` is the event after
+        slot i's last output download (None before its first use), kept across calls."""
         key = tuple((p.data_ptr(), p._version) for p in self.parameters())
         per_layer = _HOST_GRAPHS.setdefault(self, {})
         entry = per_layer.get((rows, time))
-        if entry is None or entry[0] != key or len(entry[1]) < slots:
+        fresh = entry is None or entry[0] != key or len(entry[1]) < slots
+        if fresh:
             per_layer.pop((rows, time), None)  # free stale graphs before capturing new ones
-            entry = (key, [self.capture_forward(rows, time) for _ in range(slots)])
+            entry = (key, [self.capture_forward(rows, time) for _ in range(slots)], [None] * slots)
             per_layer[(rows, time)] = entry
-        return entry[1][:slots]
+        return entry[1][:slots], entry[2], fresh
 
     @torch.no_grad()
     def forward_host(self, hidden, out=None, *, chunks: int = 4, graphs: bool = True):
@@ -408,11 +412,12 @@ class BankedDeltaMemory(nn.Module):
         one copy stream, its forward runs on the current stream once its rows have landed, and
         its output goes back on a second copy stream, so the uploads, the downloads (the two
         directions of the host link) and the compute of different groups overlap.  With
-        ``graphs`` and equal groups, each group's forward is a replay of one of up to three
+        ``graphs`` and equal groups, each group's forward is a replay of one of up to four
         captured forwards (``capture_forward``, cached per layer and group shape, recaptured when
         a parameter changes) used in rotation, which removes the per-group host launch cost; a
-        slot is refilled only once its previous output has been downloaded, and consecutive
-        groups replay on two compute streams so that their kernels overlap.  Batch rows are
+        slot is refilled only once its previous output has been downloaded (tracked across calls,
+        so back-to-back calls overlap too), and consecutive groups replay on two compute streams
+        so that their kernels overlap.  Batch rows are
         independent (each bank sequence belongs to one row), so the result is ``forward``'s up to
         the GEMMs' accumulation order at the smaller row count.  ``hidden`` should be pinned
         (pageable memory makes the copies synchronous); ``out`` (pinned, [B, T, D]) receives the
@@ -435,11 +440,14 @@ class BankedDeltaMemory(nn.Module):
         bounds = [(batch * i // groups, batch * (i + 1) // groups) for i in range(groups)]
         cur = torch.cuda.current_stream(dev)
         up, down, comp2 = _copy_streams(dev)
-        up.wait_stream(cur)
         down.wait_stream(cur)
         if graphs and batch % groups == 0:
-            runs = self._host_graphs(batch // groups, time, min(groups, 3))
-            freed = [None] * len(runs)  # per slot: its last output has been downloaded
+            runs, freed, fresh = self._host_graphs(batch // groups, time, min(groups, 4))
+            # A slot's input is rewritten only after its previous output went down (``freed``, kept
+            # across calls), so this call's first uploads may overlap the previous call's last
+            # groups; right after a capture the uploads wait for everything before.
+            if fresh:
+                up.wait_stream(cur)
             # groups alternate between two compute streams, so one group's GEMMs fill the tail
             # of the previous group's recurrence
             comp2.wait_stream(cur)
@@ -468,6 +476,7 @@ class BankedDeltaMemory(nn.Module):
             cur.wait_stream(down)
             ops.check_scan_status(dev)  # non-blocking: the replays skip the forward's own poll
             return out
+        up.wait_stream(cur)
         inputs, landed = [], []
         for a, b in bounds:
             with torch.cuda.stream(up):

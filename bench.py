@@ -449,21 +449,22 @@ def run_ours(args, world, rank, local):
         total_ms = max_over_ranks(sum(step_ms), world)
         scan_mean = max_over_ranks(statistics.mean(scan_ms), world)
         # --------------------------------------------------------- e2e
-        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         for _ in range(args.warmup):  # the row groups run the forward at their own shapes: warm those too
             layer.forward_host(x_host, y_host, chunks=E2E_CHUNKS)
         barrier(world)
         torch.cuda.synchronize()
+        # K back-to-back calls timed as one interval (a call's first uploads overlap the previous
+        # call's last groups, as in a serving loop); no L2 flush: the forward's working set (read
+        # outputs alone 0.5 GB) is far larger than L2, and every call's data comes from the host
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record()
         for i in range(args.steps):
-            flush.zero_()
-            e_starts[i].record()
             # host in, host out: the layer streams the batch through in row groups, copies overlapped
             layer.forward_host(x_host, y_host, chunks=E2E_CHUNKS)
-            e_ends[i].record()
+        e_end.record()
         torch.cuda.synchronize()
         barrier(world)
-        e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)), world)
+        e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
 
     value = world * tokens * args.steps / (total_ms / 1000)
     kernel_bytes, layer_bytes = c2_bytes_per_token(batch=args.batch)
@@ -483,7 +484,8 @@ def run_ours(args, world, rank, local):
                 'h2d_bytes_per_step': x_host.numel() * x_host.element_size(),
                 'd2h_bytes_per_step': y_host.numel() * y_host.element_size(),
                 'path': f'BlockSparseDeltaMemory.forward_host (pinned host in and out, {E2E_CHUNKS} row groups as '
-                        'replays of captured forwards, uploads / downloads overlapped with compute)'},
+                        'replays of captured forwards, uploads / downloads overlapped with compute)',
+                'timing': f'{args.steps} back-to-back calls as one CUDA-event interval, no L2 flush between calls'},
         'roofline': {'kernel': 'bdm_bank_scan (bank_scan_kernel<bf16, S=8, 8 columns/lane, 2 heads/warp>)',
                      'bound': 'hbm',
                      'achieved': achieved, 'peak': hbm_peak, 'unit': 'GB/s', 'frac': achieved / hbm_peak,
