@@ -442,11 +442,18 @@ struct VjpParams {
 };
 
 constexpr int kVjpWarps = 4;
+#ifndef BDM_VJP_BATCH
+#define BDM_VJP_BATCH 4  // slots per load batch of the event VJP at <= 2 value columns per lane
+#endif
 
 // One warp per (token, head).  Mirrors _vjp's per-token loop over the write slots,
 // then the read slots, with its rounding points.  The route-weight gradients stay
 // per head (the reference runs one routed update per head); the router backward
 // sums them over heads.  CPL = value columns per lane (lane l: l, l+32, ...).
+// The loads of a batch of JB slots (event gradient rows, tile-0 records, route
+// weights) are all issued before any of that batch's arithmetic, so a warp keeps
+// a batch of independent requests in flight instead of one dependent round trip
+// per slot; the arithmetic itself runs slot by slot in the reference's order.
 template <typename T, int S, int CPL>
 __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpParams p) {
     const int64_t item = (int64_t)blockIdx.x * kVjpWarps + (threadIdx.x >> 5);
@@ -459,6 +466,10 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     const int64_t hs0 = (t * p.H + h) * S;
     const bool nl = lane < S;
     constexpr int R = 3 * S;
+    constexpr int JB = CPL <= 2 ? BDM_VJP_BATCH : (CPL == 4 ? 4 : 2);  // slots per load batch
+    const T *__restrict__ ww = static_cast<const T *>(p.ww);
+    const T *__restrict__ rwp = static_cast<const T *>(p.rw);
+    const float *__restrict__ evg = p.evg;
     float k0 = 0.f, b0 = 0.f, g0 = 0.f, q0 = 0.f;
     if (nl) {
         k0 = ld_f(static_cast<const T *>(p.k), hs0 + lane);
@@ -479,67 +490,105 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     float dk_acc = 0.f, db_acc = 0.f, dg_acc = 0.f, dq_acc = 0.f;
     T *dwwh = static_cast<T *>(p.dww_h) + (t * p.H + h) * p.kw;
     T *drwh = static_cast<T *>(p.drw_h) + (t * p.H + h) * p.kr;
-#pragma unroll 2
-    for (int j = 0; j < p.kw; ++j) {
-        const int64_t id = t * p.kw + j;
-        const float pw = ld_f(static_cast<const T *>(p.ww), id);
-        float wvp = 0.f;
-        const float *durow = p.du + id * V + (int64_t)h * dv;
+    for (int j0 = 0; j0 < p.kw; j0 += JB) {
+        float dub[JB][CPL], pwb[JB], ra[JB], rc[JB], rg[JB];
 #pragma unroll
-        for (int i = 0; i < CPL; ++i) {
-            const int c = lane + 32 * i;
-            if (c < dv) {
-                const float du = durow[c];
-                const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
-                const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
-                accv[i] = rnd<T>(accv[i] + dve);
-                accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
-                wvp += rnd<T>(dwe * w0[i]);
+        for (int u = 0; u < JB; ++u) {
+            const int j = j0 + u;
+            const bool js = j < p.kw;
+            const int64_t id = t * p.kw + j;
+            pwb[u] = js ? ld_f(ww, id) : 0.f;
+            const float *durow = p.du + id * V + (int64_t)h * dv;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = lane + 32 * i;
+                dub[u][i] = (js && c < dv) ? __ldg(durow + c) : 0.f;
             }
+            const float *rec = evg + (id * p.H + h) * R;
+            const bool rs = js && nl;
+            ra[u] = rs ? __ldg(rec + lane) : 0.f;
+            rc[u] = rs ? __ldg(rec + S + lane) : 0.f;
+            rg[u] = rs ? __ldg(rec + 2 * S + lane) : 0.f;
         }
-        float wbp = 0.f, dec = 0.f;
-        if (nl) {
-            float A = 0.f, C = 0.f, Gs = 0.f;
-            for (int tile = 0; tile < p.tiles; ++tile) {
-                const float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * R;
-                A += rec[lane];
-                C += rec[S + lane];
-                Gs += rec[2 * S + lane];
+#pragma unroll
+        for (int u = 0; u < JB; ++u) {
+            const int j = j0 + u;
+            if (j >= p.kw) break;
+            const int64_t id = t * p.kw + j;
+            const float pw = pwb[u];
+            float wvp = 0.f;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = lane + 32 * i;
+                if (c < dv) {
+                    const float du = dub[u][i];
+                    const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
+                    const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
+                    accv[i] = rnd<T>(accv[i] + dve);
+                    accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
+                    wvp += rnd<T>(dwe * w0[i]);
+                }
             }
-            const float be = rnd<T>(b0 * pw);
-            const float dke = rnd<T>(A - be * C);
-            const float dbe = rnd<T>(-k0 * C);
-            dk_acc += dke;
-            db_acc += rnd<T>(dbe * pw);
-            if (p.routed_decay) {
-                dg_acc += Gs * pw;
-                dec = Gs * g0;
-            } else {
-                dg_acc += Gs;
+            float wbp = 0.f, dec = 0.f;
+            if (nl) {
+                float A = 0.f, C = 0.f, Gs = 0.f;
+                A += ra[u];
+                C += rc[u];
+                Gs += rg[u];
+                for (int tile = 1; tile < p.tiles; ++tile) {
+                    const float *rec = evg + (((int64_t)tile * p.E + id) * p.H + h) * R;
+                    A += rec[lane];
+                    C += rec[S + lane];
+                    Gs += rec[2 * S + lane];
+                }
+                const float be = rnd<T>(b0 * pw);
+                const float dke = rnd<T>(A - be * C);
+                const float dbe = rnd<T>(-k0 * C);
+                dk_acc += dke;
+                db_acc += rnd<T>(dbe * pw);
+                if (p.routed_decay) {
+                    dg_acc += Gs * pw;
+                    dec = Gs * g0;
+                } else {
+                    dg_acc += Gs;
+                }
+                wbp = rnd<T>(dbe * b0);
             }
-            wbp = rnd<T>(dbe * b0);
+            const float wv = rnd<T>(warp_sum(wvp));
+            const float wb = rnd<T>(warp_sum(wbp));
+            const float decs = warp_sum(dec);
+            if (lane == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
         }
-        const float wv = rnd<T>(warp_sum(wvp));
-        const float wb = rnd<T>(warp_sum(wbp));
-        const float decs = warp_sum(dec);
-        if (lane == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
     }
-#pragma unroll 2
-    for (int j = 0; j < p.kr; ++j) {
-        const int64_t rid = t * p.kr + j;
-        const int64_t id = p.nw + rid;
-        const float r = ld_f(static_cast<const T *>(p.rw), rid);
-        float wrp = 0.f;
-        if (nl) {
-            float o = 0.f;
-            for (int tile = 0; tile < p.tiles; ++tile)
-                o += p.evg[(((int64_t)tile * p.E + id) * p.H + h) * R + lane] * p.scale;
-            const float dqe = rnd<T>(o);
-            dq_acc += rnd<T>(dqe * r);
-            wrp = rnd<T>(dqe * q0);
+    for (int j0 = 0; j0 < p.kr; j0 += JB) {
+        float ob[JB], rb[JB];
+#pragma unroll
+        for (int u = 0; u < JB; ++u) {
+            const int j = j0 + u;
+            const bool js = j < p.kr;
+            const int64_t rid = t * p.kr + j;
+            rb[u] = js ? ld_f(rwp, rid) : 0.f;
+            ob[u] = (js && nl) ? __ldg(evg + ((p.nw + rid) * p.H + h) * R + lane) : 0.f;
         }
-        const float wr = warp_sum(wrp);
-        if (lane == 0) drwh[j] = Elem<T>::from_float(wr);
+#pragma unroll
+        for (int u = 0; u < JB; ++u) {
+            const int j = j0 + u;
+            if (j >= p.kr) break;
+            const int64_t id = p.nw + t * p.kr + j;
+            const float r = rb[u];
+            float wrp = 0.f;
+            if (nl) {
+                float o = 0.f;
+                o += ob[u] * p.scale;
+                for (int tile = 1; tile < p.tiles; ++tile)
+                    o += evg[(((int64_t)tile * p.E + id) * p.H + h) * R + lane] * p.scale;
+                const float dqe = rnd<T>(o);
+                dq_acc += rnd<T>(dqe * r);
+                wrp = rnd<T>(dqe * q0);
+            }
+            const float wr = warp_sum(wrp);
+            if (lane == 0) drwh[j] = Elem<T>::from_float(wr);
+        }
     }
     if (nl) {
         st_f(static_cast<T *>(p.dq), hs0 + lane, dq_acc);
