@@ -128,15 +128,21 @@ template <int S, int COLS> struct BwdGeom {
 // lane-uniform rows [k | a | e] per event (a = dtype(b*p)*k, e = exp(g_e); a read
 // keeps q_e = dtype(q*r) in the k slot), the lane's column values per event
 // (write: dtype(w*p)*v; read: the output gradient), the event ids, and the
-// lane-private history of the states before each event of the block.
+// lane-private history of the states before each event of the block.  States are
+// held as (s, s+1) pairs: every per-row operation of the recurrence and of its
+// reverse runs along s, so one packed FP32x2 instruction does two rows with the
+// same per-component rounding as the scalar instruction.
 template <int S, int COLS> struct BlockStage {
     using G = BwdGeom<S, COLS>;
-    float hist[G::kBlock][S][COLS][32];
+    float2 hist[G::kBlock][S / 2][COLS][32];
     alignas(16) float uni[G::kBlock][3 * S];
     float col[G::kBlock][COLS][32];
     int64_t id[G::kBlock];
     int tok[G::kBlock];
 };
+
+__device__ __forceinline__ float2 pair(float x) { return make_float2(x, x); }
+__device__ __forceinline__ float2 upair(const float *u, int s) { return *reinterpret_cast<const float2 *>(u + s); }
 
 template <typename T, int S, int COLS>
 __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S, COLS> &st, int64_t pos0, int n,
@@ -198,47 +204,49 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
 
 // Replays events [0, n) of the staged block from hs.  With `save` the state before each
 // event (after its storage rounding) goes to the block history; `rpos` = position of
-// event 0 modulo the storage interval.
+// event 0 modulo the storage interval.  hs[sp][c] = (state[2sp][c], state[2sp+1][c]);
+// the even / odd halves of the a.h sum are the two components of er[c].
 template <int S, int COLS>
 __device__ __forceinline__ void replay_block(const ScanBwdParams &p, BlockStage<S, COLS> &st, int n, int rpos,
-                                             bool save, float (&hs)[S][COLS]) {
+                                             bool save, float2 (&hs)[S / 2][COLS]) {
     const unsigned lane = lane_id();
 #pragma unroll 1
     for (int i = 0; i < n; ++i) {
         if (p.interval > 0) {
             if (rpos == 0) {
 #pragma unroll
-                for (int s = 0; s < S; ++s)
+                for (int sp = 0; sp < S / 2; ++sp)
 #pragma unroll
-                    for (int c = 0; c < COLS; ++c) hs[s][c] = bf16_round(hs[s][c]);
+                    for (int c = 0; c < COLS; ++c)
+                        hs[sp][c] = make_float2(bf16_round(hs[sp][c].x), bf16_round(hs[sp][c].y));
             }
             rpos = rpos + 1 == p.interval ? 0 : rpos + 1;
         }
         if (save) {
 #pragma unroll
-            for (int s = 0; s < S; ++s)
+            for (int sp = 0; sp < S / 2; ++sp)
 #pragma unroll
-                for (int c = 0; c < COLS; ++c) st.hist[i][s][c][lane] = hs[s][c];
+                for (int c = 0; c < COLS; ++c) st.hist[i][sp][c][lane] = hs[sp][c];
         }
         if (st.id[i] >= p.nw) continue;  // reads leave the state unchanged
         const float *u = st.uni[i];
-        float er[COLS][2];
+        float2 er[COLS];
 #pragma unroll
-        for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = 0.f;
+        for (int c = 0; c < COLS; ++c) er[c] = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
-            const float e = u[2 * S + s], a = u[S + s];
+        for (int sp = 0; sp < S / 2; ++sp) {
+            const float2 e = upair(u, 2 * S + 2 * sp), a = upair(u, S + 2 * sp);
 #pragma unroll
             for (int c = 0; c < COLS; ++c) {
-                hs[s][c] *= e;
-                er[c][s & 1] = fmaf(a, hs[s][c], er[c][s & 1]);
+                hs[sp][c] = __fmul2_rn(hs[sp][c], e);
+                er[c] = __ffma2_rn(a, hs[sp][c], er[c]);
             }
         }
 #pragma unroll
         for (int c = 0; c < COLS; ++c) {
-            const float uu = st.col[i][c][lane] - (er[c][0] + er[c][1]);
+            const float2 uu = pair(st.col[i][c][lane] - (er[c].x + er[c].y));
 #pragma unroll
-            for (int s = 0; s < S; ++s) hs[s][c] = fmaf(u[s], uu, hs[s][c]);
+            for (int sp = 0; sp < S / 2; ++sp) hs[sp][c] = __ffma2_rn(upair(u, 2 * sp), uu, hs[sp][c]);
         }
     }
 }
@@ -247,7 +255,7 @@ __device__ __forceinline__ void replay_block(const ScanBwdParams &p, BlockStage<
 // zero; rounded to BF16 under the training storage policy.
 template <int S, int COLS>
 __device__ __forceinline__ void initial_columns(const ScanBwdParams &p, int64_t seq, int h, int col0,
-                                                float (&hs)[S][COLS]) {
+                                                float2 (&hs)[S / 2][COLS]) {
     const int64_t bank = seq % p.J;
 #pragma unroll
     for (int s = 0; s < S; ++s) {
@@ -265,7 +273,8 @@ __device__ __forceinline__ void initial_columns(const ScanBwdParams &p, int64_t 
                     x = static_cast<const float *>(p.row_factor)[ou] + static_cast<const float *>(p.col_factor)[oz];
                 if (p.interval > 0) x = bf16_round(x);
             }
-            hs[s][c] = x;
+            if (s & 1) hs[s / 2][c].y = x;
+            else hs[s / 2][c].x = x;
         }
     }
 }
@@ -273,8 +282,9 @@ __device__ __forceinline__ void initial_columns(const ScanBwdParams &p, int64_t 
 // Reverse pass over events [0, n) of the staged block (descending), from the history.
 template <int S, int COLS>
 __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const BlockStage<S, COLS> &st, int n, int tile,
-                                              int h, int col0, float (&dh)[S][COLS]) {
+                                              int h, int col0, float2 (&dh)[S / 2][COLS]) {
     using G = BwdGeom<S, COLS>;
+    constexpr int P = S / 2;
     const unsigned lane = lane_id();
 #pragma unroll 1
     for (int i = n - 1; i >= 0; --i) {
@@ -282,38 +292,46 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
         const float *u = st.uni[i];
         float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
         if (id < p.nw) {
-            float hd[S][COLS], er[COLS][2], du[COLS][2], uu[COLS], dus[COLS];
+            float2 hd[P][COLS], er[COLS], du[COLS];
+            float uu[COLS], dus[COLS];
 #pragma unroll
-            for (int c = 0; c < COLS; ++c) er[c][0] = er[c][1] = du[c][0] = du[c][1] = 0.f;
+            for (int c = 0; c < COLS; ++c) er[c] = du[c] = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int s = 0; s < S; ++s) {
+            for (int sp = 0; sp < P; ++sp) {
+                const float2 e = upair(u, 2 * S + 2 * sp), a = upair(u, S + 2 * sp), k = upair(u, 2 * sp);
 #pragma unroll
                 for (int c = 0; c < COLS; ++c) {
-                    hd[s][c] = st.hist[i][s][c][lane] * u[2 * S + s];
-                    er[c][s & 1] = fmaf(u[S + s], hd[s][c], er[c][s & 1]);
-                    du[c][s & 1] = fmaf(dh[s][c], u[s], du[c][s & 1]);
+                    hd[sp][c] = __fmul2_rn(st.hist[i][sp][c][lane], e);
+                    er[c] = __ffma2_rn(a, hd[sp][c], er[c]);
+                    du[c] = __ffma2_rn(dh[sp][c], k, du[c]);
                 }
             }
 #pragma unroll
             for (int c = 0; c < COLS; ++c) {
-                uu[c] = st.col[i][c][lane] - (er[c][0] + er[c][1]);
-                dus[c] = du[c][0] + du[c][1];
+                uu[c] = st.col[i][c][lane] - (er[c].x + er[c].y);
+                dus[c] = du[c].x + du[c].y;
             }
             float red[G::kRedW];
 #pragma unroll
-            for (int s = 0; s < S; ++s) {
-                float A = 0.f, C = 0.f, Gs = 0.f;
+            for (int sp = 0; sp < P; ++sp) {
+                const float2 e = upair(u, 2 * S + 2 * sp), a = upair(u, S + 2 * sp);
+                const float2 na = make_float2(-a.x, -a.y);
+                float2 A = make_float2(0.f, 0.f), C = A, Gs = A;
 #pragma unroll
                 for (int c = 0; c < COLS; ++c) {
-                    A = fmaf(dh[s][c], uu[c], A);
-                    C = fmaf(hd[s][c], dus[c], C);
-                    const float dp = fmaf(-u[S + s], dus[c], dh[s][c]);
-                    Gs = fmaf(dp, hd[s][c], Gs);
-                    dh[s][c] = dp * u[2 * S + s];
+                    const float2 ds = pair(dus[c]);
+                    A = __ffma2_rn(dh[sp][c], pair(uu[c]), A);
+                    C = __ffma2_rn(hd[sp][c], ds, C);
+                    const float2 dp = __ffma2_rn(na, ds, dh[sp][c]);
+                    Gs = __ffma2_rn(dp, hd[sp][c], Gs);
+                    dh[sp][c] = __fmul2_rn(dp, e);
                 }
-                red[s] = A;
-                red[S + s] = C;
-                red[2 * S + s] = Gs;
+                red[2 * sp] = A.x;
+                red[2 * sp + 1] = A.y;
+                red[S + 2 * sp] = C.x;
+                red[S + 2 * sp + 1] = C.y;
+                red[2 * S + 2 * sp] = Gs.x;
+                red[2 * S + 2 * sp + 1] = Gs.y;
             }
 #pragma unroll
             for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
@@ -325,16 +343,19 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
             reduce_store<G::kRedW>(red, 3 * S, rec);
         } else {
             float red[S];
+            const float2 sc = pair(p.scale);
 #pragma unroll
-            for (int s = 0; s < S; ++s) {
-                float o = 0.f;
+            for (int sp = 0; sp < P; ++sp) {
+                const float2 k = upair(u, 2 * sp);
+                float2 o = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int c = 0; c < COLS; ++c) {
-                    const float cv = st.col[i][c][lane];
-                    o = fmaf(st.hist[i][s][c][lane], cv, o);
-                    dh[s][c] = fmaf(u[s] * cv, p.scale, dh[s][c]);
+                    const float2 cv = pair(st.col[i][c][lane]);
+                    o = __ffma2_rn(st.hist[i][sp][c][lane], cv, o);
+                    dh[sp][c] = __ffma2_rn(__fmul2_rn(k, cv), sc, dh[sp][c]);
                 }
-                red[s] = o;
+                red[2 * sp] = o.x;
+                red[2 * sp + 1] = o.y;
             }
             reduce_store<S>(red, S, rec);
         }
@@ -345,6 +366,7 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
 template <typename T, int S, int COLS>
 __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p) {
     using G = BwdGeom<S, COLS>;
+    constexpr int P = S / 2;
     __shared__ BlockStage<S, COLS> st;
     const unsigned lane = lane_id();
     const int64_t unit = blockIdx.x;
@@ -354,17 +376,17 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
     const int64_t seq = unit / ((int64_t)p.tiles * p.H);
     const int col0 = tile * G::kTileCols + (int)lane;
     const int64_t start = p.cu[seq], L = p.cu[seq + 1] - start;
-    float dh[S][COLS];
+    float2 dh[P][COLS];
 #pragma unroll
-    for (int s = 0; s < S; ++s)
+    for (int sp = 0; sp < P; ++sp)
 #pragma unroll
-        for (int c = 0; c < COLS; ++c) dh[s][c] = 0.f;
+        for (int c = 0; c < COLS; ++c) dh[sp][c] = make_float2(0.f, 0.f);
     const int64_t stride_state = (int64_t)S * p.dv;
     const int interval = p.interval > 0 ? p.interval : 1;
     if (L > 0) {
         const int64_t nblk = (L + G::kBlock - 1) / G::kBlock;
         const int64_t slot0 = start / G::kBlock + seq;  // disjoint slot ranges across sequences
-        float hs[S][COLS];
+        float2 hs[P][COLS];
         if (nblk > 1 && (!p.ckpt_ready || L >= kLongSeq)) {  // sweep 1: checkpoints at blocks 1 .. nblk-1
             initial_columns<S, COLS>(p, seq, h, col0, hs);
 #pragma unroll 1
@@ -374,10 +396,13 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
                 replay_block<S, COLS>(p, st, G::kBlock, (int)(e0 % interval), false, hs);
                 float *ck = p.ckpt + ((slot0 + m + 1) * p.H + h) * stride_state;
 #pragma unroll
-                for (int s = 0; s < S; ++s)
+                for (int sp = 0; sp < P; ++sp)
 #pragma unroll
                     for (int c = 0; c < COLS; ++c)
-                        if (col0 + 32 * c < p.dv) ck[(int64_t)s * p.dv + col0 + 32 * c] = hs[s][c];
+                        if (col0 + 32 * c < p.dv) {
+                            ck[(int64_t)(2 * sp) * p.dv + col0 + 32 * c] = hs[sp][c].x;
+                            ck[(int64_t)(2 * sp + 1) * p.dv + col0 + 32 * c] = hs[sp][c].y;
+                        }
             }
         }
 #pragma unroll 1
@@ -387,10 +412,14 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
             } else {
                 const float *ck = p.ckpt + ((slot0 + m) * p.H + h) * stride_state;
 #pragma unroll
-                for (int s = 0; s < S; ++s)
+                for (int sp = 0; sp < P; ++sp)
 #pragma unroll
-                    for (int c = 0; c < COLS; ++c)
-                        hs[s][c] = col0 + 32 * c < p.dv ? ck[(int64_t)s * p.dv + col0 + 32 * c] : 0.f;
+                    for (int c = 0; c < COLS; ++c) {
+                        const bool on = col0 + 32 * c < p.dv;
+                        hs[sp][c] = on ? make_float2(ck[(int64_t)(2 * sp) * p.dv + col0 + 32 * c],
+                                                     ck[(int64_t)(2 * sp + 1) * p.dv + col0 + 32 * c])
+                                       : make_float2(0.f, 0.f);
+                    }
             }
             const int64_t e0 = m * G::kBlock;
             const int blen = (int)min((int64_t)G::kBlock, L - e0);
@@ -401,10 +430,13 @@ __global__ void __launch_bounds__(32) scan_backward_kernel(const ScanBwdParams p
     }
     float *di = p.dinit + (seq * p.H + h) * stride_state;
 #pragma unroll
-    for (int s = 0; s < S; ++s)
+    for (int sp = 0; sp < P; ++sp)
 #pragma unroll
         for (int c = 0; c < COLS; ++c)
-            if (col0 + 32 * c < p.dv) di[(int64_t)s * p.dv + col0 + 32 * c] = dh[s][c];
+            if (col0 + 32 * c < p.dv) {
+                di[(int64_t)(2 * sp) * p.dv + col0 + 32 * c] = dh[sp][c].x;
+                di[(int64_t)(2 * sp + 1) * p.dv + col0 + 32 * c] = dh[sp][c].y;
+            }
 }
 
 template <typename T, int S, int COLS>
