@@ -37,52 +37,75 @@ constexpr unsigned kFull = 0xffffffffu;
 
 // ------------------------------------------------------------ warp reductions
 
-template <int N> struct Pow2Ceil {
-    static constexpr int value = N <= 1 ? 1 : 2 * Pow2Ceil<(N + 1) / 2>::value;
-};
-template <> struct Pow2Ceil<1> { static constexpr int value = 1; };
+// Sums N per-lane values across the warp.  While the live count is even, a butterfly
+// level halves it: a lane keeps one half of its live values (the upper half on lanes
+// whose OFF bit is set) and adds the partner's copy of that half.  Once it is odd, the
+// remaining levels add the partner's copy of every live value.  Every value is summed
+// over the same tree (lane bits 16, 8, 4, 2, 1 in that order) whatever N is, so padding
+// N to a power of two would change only the cost.  Independent adds run as FP32x2 pairs.
+constexpr int reduce_live(int live, int off) { return (off >= 1 && live % 2 == 0) ? reduce_live(live / 2, off / 2) : live; }
+constexpr unsigned reduce_bfly(int live, int off) {
+    return off < 1 ? 0u : (live % 2 == 0 ? reduce_bfly(live / 2, off / 2) : (unsigned)(2 * off - 1));
+}
 
-constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
-
-// Sums N (a power of two) per-lane values across the warp by recursive halving:
-// at each of the five butterfly levels a lane keeps one half of its live values
-// and adds the partner's copy of that half.  Afterwards, for N >= 32, live value i
-// of lane l is the warp total of value l*(N/32) + i; for N < 32, value 0 of lane l
-// is the total of value l >> (5 - log2 N), held by 32/N lanes.
-template <int LIVE, int OFF, int N> struct HalvingReduce {
-    static __device__ __forceinline__ void run(float (&v)[N], unsigned lane) {
-        if constexpr (LIVE >= 2) {
-            constexpr int H = LIVE / 2;
-            const bool up = (lane & OFF) != 0;
+template <int H, int N>
+__device__ __forceinline__ void add_pairs(float (&v)[N], const float (&a)[H], const float (&b)[H]) {
 #pragma unroll
-            for (int i = 0; i < H; ++i) {
-                const float send = up ? v[i] : v[i + H];
-                const float keep = up ? v[i + H] : v[i];
-                v[i] = keep + __shfl_xor_sync(kFull, send, OFF);
+    for (int i = 0; i + 1 < H; i += 2) {
+        const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+        v[i] = r.x;
+        v[i + 1] = r.y;
+    }
+    if constexpr (H % 2 == 1) v[H - 1] = a[H - 1] + b[H - 1];
+}
+
+template <int LIVE, int OFF, int N> struct SplitReduce {
+    static __device__ __forceinline__ void run(float (&v)[N], unsigned lane, int &base) {
+        if constexpr (OFF >= 1) {
+            if constexpr (LIVE % 2 == 0) {
+                constexpr int H = LIVE / 2;
+                const bool up = (lane & OFF) != 0;
+                float keep[H], recv[H];
+#pragma unroll
+                for (int i = 0; i < H; ++i) {
+                    const float send = up ? v[i] : v[i + H];
+                    keep[i] = up ? v[i + H] : v[i];
+                    recv[i] = __shfl_xor_sync(kFull, send, OFF);
+                }
+                add_pairs<H, N>(v, keep, recv);
+                if (up) base += H;
+                SplitReduce<H, OFF / 2, N>::run(v, lane, base);
+            } else {
+                float own[LIVE], recv[LIVE];
+#pragma unroll
+                for (int i = 0; i < LIVE; ++i) {
+                    own[i] = v[i];
+                    recv[i] = __shfl_xor_sync(kFull, v[i], OFF);
+                }
+                add_pairs<LIVE, N>(v, own, recv);
+                SplitReduce<LIVE, OFF / 2, N>::run(v, lane, base);
             }
-            if constexpr (OFF > 1) HalvingReduce<H, OFF / 2, N>::run(v, lane);
-        } else {
-            v[0] += __shfl_xor_sync(kFull, v[0], OFF);
-            if constexpr (OFF > 1) HalvingReduce<1, OFF / 2, N>::run(v, lane);
         }
     }
 };
 
-// Store the first `used` of N reduced values to out[0..used).
+// Sums the N per-lane values across the warp and stores the N totals to out[0..N).
 template <int N>
-__device__ __forceinline__ void reduce_store(float (&v)[N], int used, float *out) {
+__device__ __forceinline__ void reduce_store(float (&v)[N], float *out) {
+    constexpr int kLive = reduce_live(N, 16);
+    constexpr unsigned kBfly = reduce_bfly(N, 16);
     const unsigned lane = lane_id();
-    HalvingReduce<N, 16, N>::run(v, lane);
-    if constexpr (N >= 32) {
+    int base = 0;
+    SplitReduce<N, 16, N>::run(v, lane, base);
+    if constexpr (kBfly + 1 >= kLive) {  // the lanes holding one window store one total each
+        const int q = (int)(lane & kBfly);
+        float x = v[0];
 #pragma unroll
-        for (int i = 0; i < N / 32; ++i) {
-            const int idx = (int)lane * (N / 32) + i;
-            if (idx < used) out[idx] = v[i];
-        }
-    } else {
-        constexpr int shift = 5 - ilog2(N);
-        const int idx = (int)(lane >> shift);
-        if ((lane & ((1u << shift) - 1u)) == 0 && idx < used) out[idx] = v[0];
+        for (int i = 1; i < kLive; ++i) x = q == i ? v[i] : x;
+        if (q < kLive) out[base + q] = x;
+    } else if ((lane & kBfly) == 0) {
+#pragma unroll
+        for (int i = 0; i < kLive; ++i) out[base + i] = v[i];
     }
 }
 
@@ -120,7 +143,6 @@ constexpr int64_t kLongSeq = kLongEvents;
 template <int S, int COLS> struct BwdGeom {
     static constexpr int kBlock = 128 / (S * COLS);  // events between HBM checkpoints (16 KB of history)
     static constexpr int kRec = 3 * S;               // floats per (event, head) record
-    static constexpr int kRedW = Pow2Ceil<3 * S>::value;
     static constexpr int kTileCols = 32 * COLS;      // value columns per warp (lane l: l, l+32, ...)
 };
 
@@ -137,7 +159,7 @@ template <int S, int COLS> struct BlockStage {
     float2 hist[G::kBlock][S / 2][COLS][32];
     alignas(16) float uni[G::kBlock][3 * S];
     float col[G::kBlock][COLS][32];
-    int64_t id[G::kBlock];
+    int id[G::kBlock];  // event ids < 2^31 (checked on the host)
     int tok[G::kBlock];
 };
 
@@ -152,7 +174,7 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
     __syncwarp();
     for (int i = (int)lane; i < n; i += 32) {  // lanes over events: ids and the lane-uniform rows
         const int64_t id = __ldg(p.order + pos0 + i);
-        st.id[i] = id;
+        st.id[i] = (int)id;
         float *u = st.uni[i];
         if (id < p.nw) {
             const int64_t tok = (uint32_t)id / (uint32_t)p.kw;  // event ids < 2^31 (checked on the host)
@@ -178,23 +200,26 @@ __device__ __forceinline__ void stage_block(const ScanBwdParams &p, BlockStage<S
         }
     }
     __syncwarp();
+    const int64_t hc = (int64_t)h * p.dv + col0;  // the lane's first column within a token row
+    const T *wl = static_cast<const T *>(p.w) + hc, *vl = static_cast<const T *>(p.v) + hc;
+    const T *dl = static_cast<const T *>(p.dread) + hc;
+    const int nw = (int)p.nw;
 #pragma unroll 4
     for (int i = 0; i < n; ++i) {  // every lane over the events: its own columns
-        const int64_t id = st.id[i];
-        const bool wr = id < p.nw;
+        const int id = st.id[i];
+        const bool wr = id < nw;
         if (!wr && !want_dout) continue;
-        const int64_t row = (int64_t)st.tok[i] * V;
+        const uint64_t row = (uint64_t)(uint32_t)st.tok[i] * (uint32_t)V;
         const float pw = wr ? ld_f(static_cast<const T *>(p.ww), id) : 0.f;
 #pragma unroll
         for (int c = 0; c < COLS; ++c) {
-            const int cc = col0 + 32 * c;
             float val = 0.f;
-            if (cc < p.dv) {
-                const int64_t o = row + (int64_t)h * p.dv + cc;
+            if (col0 + 32 * c < p.dv) {
+                const uint64_t o = row + 32 * c;
                 if (wr)
-                    val = rnd<T>(ld_f(static_cast<const T *>(p.w), o) * pw) * ld_f(static_cast<const T *>(p.v), o);
+                    val = rnd<T>(ld_f(wl, o) * pw) * ld_f(vl, o);
                 else if (want_dout)
-                    val = ld_f(static_cast<const T *>(p.dread), o);
+                    val = ld_f(dl, o);
             }
             st.col[i][c][lane] = val;
         }
@@ -228,7 +253,7 @@ __device__ __forceinline__ void replay_block(const ScanBwdParams &p, BlockStage<
 #pragma unroll
                 for (int c = 0; c < COLS; ++c) st.hist[i][sp][c][lane] = hs[sp][c];
         }
-        if (st.id[i] >= p.nw) continue;  // reads leave the state unchanged
+        if (st.id[i] >= (int)p.nw) continue;  // reads leave the state unchanged
         const float *u = st.uni[i];
         float2 er[COLS];
 #pragma unroll
@@ -286,12 +311,17 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
     using G = BwdGeom<S, COLS>;
     constexpr int P = S / 2;
     const unsigned lane = lane_id();
+    float *const rec0 = p.evg + ((int64_t)tile * p.E * p.H + h) * G::kRec;  // record of event 0
+    const uint32_t rec_stride = (uint32_t)p.H * G::kRec;
+    const uint32_t V = (uint32_t)p.H * (uint32_t)p.dv;
+    float *const du0 = p.du + (int64_t)h * p.dv + col0;
+    const int nw = (int)p.nw;
 #pragma unroll 1
     for (int i = n - 1; i >= 0; --i) {
-        const int64_t id = st.id[i];
+        const int id = st.id[i];
         const float *u = st.uni[i];
-        float *rec = p.evg + (((int64_t)tile * p.E + id) * p.H + h) * G::kRec;
-        if (id < p.nw) {
+        float *rec = rec0 + (uint64_t)(uint32_t)id * rec_stride;
+        if (id < nw) {
             float2 hd[P][COLS], er[COLS], du[COLS];
             float uu[COLS], dus[COLS];
 #pragma unroll
@@ -311,7 +341,7 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
                 uu[c] = st.col[i][c][lane] - (er[c].x + er[c].y);
                 dus[c] = du[c].x + du[c].y;
             }
-            float red[G::kRedW];
+            float red[3 * S];
 #pragma unroll
             for (int sp = 0; sp < P; ++sp) {
                 const float2 e = upair(u, 2 * S + 2 * sp), a = upair(u, S + 2 * sp);
@@ -333,14 +363,11 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
                 red[2 * S + 2 * sp] = Gs.x;
                 red[2 * S + 2 * sp + 1] = Gs.y;
             }
+            float *dur = du0 + (uint64_t)(uint32_t)id * V;
 #pragma unroll
-            for (int k = 3 * S; k < G::kRedW; ++k) red[k] = 0.f;
-#pragma unroll
-            for (int c = 0; c < COLS; ++c) {
-                const int cc = col0 + 32 * c;
-                if (cc < p.dv) p.du[id * ((int64_t)p.H * p.dv) + (int64_t)h * p.dv + cc] = dus[c];
-            }
-            reduce_store<G::kRedW>(red, 3 * S, rec);
+            for (int c = 0; c < COLS; ++c)
+                if (col0 + 32 * c < p.dv) dur[32 * c] = dus[c];
+            reduce_store<3 * S>(red, rec);
         } else {
             float red[S];
             const float2 sc = pair(p.scale);
@@ -357,7 +384,7 @@ __device__ __forceinline__ void reverse_block(const ScanBwdParams &p, const Bloc
                 red[2 * sp] = o.x;
                 red[2 * sp + 1] = o.y;
             }
-            reduce_store<S>(red, S, rec);
+            reduce_store<S>(red, rec);
         }
     }
 }
