@@ -27,6 +27,7 @@
 // pass over a block first stages the block's event controls in shared memory (all
 // of the block's loads in flight at once), so replay and reverse read only shared
 // memory, and the loops stay rolled (compact code, no instruction-cache misses).
+#include <type_traits>
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -500,6 +501,16 @@ struct VjpParams {
     float *dg;
 };
 
+// Warp total of x when only lanes < W (a power of two, at most 16) can hold non-zero values:
+// warp_sum's levels at offsets >= W only add +0 there, which turns -0 into +0 and changes
+// nothing else, so one add of +0 and the levels below W give the same value on lane 0.
+template <int W> __device__ __forceinline__ float warp_sum_low(float x) {
+    x = __fadd_rn(x, 0.f);
+#pragma unroll
+    for (int o = W / 2; o > 0; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
+    return x;
+}
+
 constexpr int kVjpWarps = 4;
 #ifndef BDM_VJP_BATCH
 #define BDM_VJP_BATCH 4  // slots per load batch of the event VJP at <= 2 value columns per lane
@@ -546,6 +557,24 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
         w0[i] = on ? ld_f(static_cast<const T *>(p.w), vrow + c) : 0.f;
         accv[i] = accw[i] = 0.f;
     }
+    // BF16 with an even number of columns per lane: the lane's columns (i, i+1) run as BF16x2
+    // pairs.  Each BF16 result below is the same value as the FP32 expression rounded once:
+    // a product of two BF16 values is exact in FP32; a sum of two BF16 values is exact in
+    // FP32 unless their exponents differ by more than 16, and then both roundings return the
+    // larger operand.  The FP32 x BF16 products stay FP32 (packed FP32x2) and are rounded by
+    // one paired conversion.  The _rn forms never contract into a fused multiply-add.
+    constexpr bool kPair = std::is_same<T, bf16>::value && CPL % 2 == 0;
+    constexpr int NQ = CPL / 2 > 0 ? CPL / 2 : 1;
+    __nv_bfloat162 w2[NQ], accv2[NQ], accw2[NQ];
+    float2 v2[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+        if constexpr (kPair) {
+            w2[q] = __floats2bfloat162_rn(w0[2 * q], w0[2 * q + 1]);  // exact: BF16 values
+            v2[q] = make_float2(v0[2 * q], v0[2 * q + 1]);
+            accv2[q] = accw2[q] = __floats2bfloat162_rn(0.f, 0.f);
+        }
+    }
     float dk_acc = 0.f, db_acc = 0.f, dg_acc = 0.f, dq_acc = 0.f;
     T *dwwh = static_cast<T *>(p.dww_h) + (t * p.H + h) * p.kw;
     T *drwh = static_cast<T *>(p.drw_h) + (t * p.H + h) * p.kr;
@@ -576,16 +605,32 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
             const int64_t id = t * p.kw + j;
             const float pw = pwb[u];
             float wvp = 0.f;
+            if constexpr (kPair) {
+                const __nv_bfloat162 pw2 = __float2bfloat162_rn(pw);  // exact: a BF16 route weight
 #pragma unroll
-            for (int i = 0; i < CPL; ++i) {
-                const int c = lane + 32 * i;
-                if (c < dv) {
-                    const float du = dub[u][i];
-                    const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
-                    const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
-                    accv[i] = rnd<T>(accv[i] + dve);
-                    accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
-                    wvp += rnd<T>(dwe * w0[i]);
+                for (int q = 0; q < NQ; ++q) {
+                    const float2 du = make_float2(dub[u][2 * q], dub[u][2 * q + 1]);
+                    const float2 a = __bfloat1622float2(__hmul2_rn(w2[q], pw2));                  // dtype(w*p)
+                    const __nv_bfloat162 dve = __float22bfloat162_rn(__fmul2_rn(du, a));      // dv of the event
+                    const __nv_bfloat162 dwe = __float22bfloat162_rn(__fmul2_rn(du, v2[q]));  // dw of the event
+                    accv2[q] = __hadd2_rn(accv2[q], dve);
+                    accw2[q] = __hadd2_rn(accw2[q], __hmul2_rn(dwe, pw2));
+                    const float2 x = __bfloat1622float2(__hmul2_rn(dwe, w2[q]));
+                    if (lane + 64 * q < dv) wvp += x.x;
+                    if (lane + 64 * q + 32 < dv) wvp += x.y;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < CPL; ++i) {
+                    const int c = lane + 32 * i;
+                    if (c < dv) {
+                        const float du = dub[u][i];
+                        const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
+                        const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
+                        accv[i] = rnd<T>(accv[i] + dve);
+                        accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
+                        wvp += rnd<T>(dwe * w0[i]);
+                    }
                 }
             }
             float wbp = 0.f, dec = 0.f;
@@ -614,8 +659,8 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
                 wbp = rnd<T>(dbe * b0);
             }
             const float wv = rnd<T>(warp_sum(wvp));
-            const float wb = rnd<T>(warp_sum(wbp));
-            const float decs = warp_sum(dec);
+            const float wb = rnd<T>(warp_sum_low<S>(wbp));  // wbp, dec: non-zero on lanes < S only
+            const float decs = warp_sum_low<S>(dec);
             if (lane == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
         }
     }
@@ -645,7 +690,7 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
                 dq_acc += rnd<T>(dqe * r);
                 wrp = rnd<T>(dqe * q0);
             }
-            const float wr = warp_sum(wrp);
+            const float wr = warp_sum_low<S>(wrp);  // non-zero on lanes < S only
             if (lane == 0) drwh[j] = Elem<T>::from_float(wr);
         }
     }
@@ -659,8 +704,14 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     for (int i = 0; i < CPL; ++i) {
         const int c = lane + 32 * i;
         if (c < dv) {
-            st_f(static_cast<T *>(p.dv_out), vrow + c, accv[i]);
-            st_f(static_cast<T *>(p.dw_out), vrow + c, accw[i]);
+            if constexpr (kPair) {
+                const __nv_bfloat162 av = accv2[i / 2], aw = accw2[i / 2];
+                static_cast<bf16 *>(p.dv_out)[vrow + c] = i % 2 ? __high2bfloat16(av) : __low2bfloat16(av);
+                static_cast<bf16 *>(p.dw_out)[vrow + c] = i % 2 ? __high2bfloat16(aw) : __low2bfloat16(aw);
+            } else {
+                st_f(static_cast<T *>(p.dv_out), vrow + c, accv[i]);
+                st_f(static_cast<T *>(p.dw_out), vrow + c, accw[i]);
+            }
         }
     }
 }
