@@ -37,7 +37,9 @@ from .config import BDMConfig, near_square_factors, state_interval
 
 
 FUSED_F_MAX_TOKENS = 4096  # at most this many tokens: the controllers kernel computes f_proj.1 itself
-_COPY_STREAMS: dict = {}  # per device: (upload, download, second compute) streams of forward_host
+_COPY_STREAMS: dict = {}  # per device: (upload, download, (extra compute streams)) of forward_host
+HOST_COMPUTE_STREAMS = 2  # compute streams forward_host's row groups rotate over (current + extras)
+_MAX_HOST_COMPUTE_STREAMS = 4
 # per layer: {(rows, time): (parameter key, [captured forwards])} for forward_host's row groups
 _HOST_GRAPHS: 'weakref.WeakKeyDictionary' = weakref.WeakKeyDictionary()
 
@@ -45,7 +47,9 @@ _HOST_GRAPHS: 'weakref.WeakKeyDictionary' = weakref.WeakKeyDictionary()
 def _copy_streams(device):
     st = _COPY_STREAMS.get(device.index)
     if st is None:
-        st = _COPY_STREAMS[device.index] = tuple(torch.cuda.Stream(device) for _ in range(3))
+        st = _COPY_STREAMS[device.index] = (torch.cuda.Stream(device), torch.cuda.Stream(device),
+                                            tuple(torch.cuda.Stream(device)
+                                                  for _ in range(_MAX_HOST_COMPUTE_STREAMS - 1)))
     return st
 
 
@@ -439,7 +443,7 @@ class BankedDeltaMemory(nn.Module):
         groups = max(1, min(int(chunks), batch))
         bounds = [(batch * i // groups, batch * (i + 1) // groups) for i in range(groups)]
         cur = torch.cuda.current_stream(dev)
-        up, down, comp2 = _copy_streams(dev)
+        up, down, extra = _copy_streams(dev)
         down.wait_stream(cur)
         if graphs and batch % groups == 0:
             runs, freed, fresh = self._host_graphs(batch // groups, time, min(groups, 4))
@@ -448,14 +452,16 @@ class BankedDeltaMemory(nn.Module):
             # groups; right after a capture the uploads wait for everything before.
             if fresh:
                 up.wait_stream(cur)
-            # groups alternate between two compute streams, so one group's GEMMs fill the tail
-            # of the previous group's recurrence
-            comp2.wait_stream(cur)
-            computes = (cur, comp2)
+            # groups rotate over the compute streams, so the recurrences of neighbouring groups
+            # (each latency-bound on its own: a group keeps the full sequence length) overlap
+            n_comp = max(1, min(HOST_COMPUTE_STREAMS, _MAX_HOST_COMPUTE_STREAMS))
+            computes = (cur,) + extra[:n_comp - 1]
+            for cs in computes[1:]:
+                cs.wait_stream(cur)
             for i, (a, b) in enumerate(bounds):
                 slot = i % len(runs)
                 run = runs[slot]
-                cs = computes[i % 2]
+                cs = computes[i % len(computes)]
                 with torch.cuda.stream(up):
                     if freed[slot] is not None:
                         up.wait_event(freed[slot])
@@ -472,7 +478,8 @@ class BankedDeltaMemory(nn.Module):
                     out[a:b].copy_(run.output, non_blocking=True)
                     freed[slot] = torch.cuda.Event()
                     freed[slot].record(down)
-            cur.wait_stream(comp2)
+            for cs in computes[1:]:
+                cur.wait_stream(cs)
             cur.wait_stream(down)
             ops.check_scan_status(dev)  # non-blocking: the replays skip the forward's own poll
             return out
