@@ -524,17 +524,28 @@ constexpr int kVjpWarps = 4;
 // weights) are all issued before any of that batch's arithmetic, so a warp keeps
 // a batch of independent requests in flight instead of one dependent round trip
 // per slot; the arithmetic itself runs slot by slot in the reference's order.
-template <typename T, int S, int CPL>
-__global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpParams p) {
+// G = 2: the two half-warps take two heads of the token (16 lanes each, lane el:
+// columns el, el+16, ...), so the per-slot work of the S lanes and the reductions
+// serve two heads at once.  Columns el + 32i (even positions) and el + 16 + 32i (odd
+// positions) are what lanes el and el + 16 hold at G = 1; their two partial sums,
+// added, are warp_sum's first level, so every total keeps warp_sum's tree.
+// Minimum CTAs per SM: the register budgets that measured fastest (no spills).
+template <int G, int CPL> constexpr int vjp_min_blocks() { return G == 2 ? 5 : (CPL <= 2 ? 6 : 5); }
+
+template <typename T, int S, int CPL, int G>
+__global__ void __launch_bounds__(32 * kVjpWarps, (vjp_min_blocks<G, CPL>())) event_vjp_kernel(const VjpParams p) {
+    constexpr int LPH = 32 / G;  // lanes per head
     const int64_t item = (int64_t)blockIdx.x * kVjpWarps + (threadIdx.x >> 5);
-    if (item >= p.items) return;
-    const int64_t t = item / p.H;
-    const int h = (int)(item % p.H);
+    const int HG = p.H / G;
+    if (item >= p.nt * HG) return;
+    const int64_t t = item / HG;
     const int lane = (int)lane_id();
+    const int el = G == 2 ? (lane & 15) : lane;
+    const int h = (int)(item % HG) * G + (G == 2 ? (lane >> 4) : 0);
     const int dv = p.dv;
     const int64_t V = (int64_t)p.H * dv;
     const int64_t hs0 = (t * p.H + h) * S;
-    const bool nl = lane < S;
+    const bool nl = el < S;
     constexpr int R = 3 * S;
     constexpr int JB = CPL <= 2 ? BDM_VJP_BATCH : (CPL == 4 ? 4 : 2);  // slots per load batch
     const T *__restrict__ ww = static_cast<const T *>(p.ww);
@@ -542,16 +553,16 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     const float *__restrict__ evg = p.evg;
     float k0 = 0.f, b0 = 0.f, g0 = 0.f, q0 = 0.f;
     if (nl) {
-        k0 = ld_f(static_cast<const T *>(p.k), hs0 + lane);
-        b0 = ld_f(static_cast<const T *>(p.b), hs0 + lane);
-        g0 = p.g[hs0 + lane];
-        q0 = ld_f(static_cast<const T *>(p.q), hs0 + lane);
+        k0 = ld_f(static_cast<const T *>(p.k), hs0 + el);
+        b0 = ld_f(static_cast<const T *>(p.b), hs0 + el);
+        g0 = p.g[hs0 + el];
+        q0 = ld_f(static_cast<const T *>(p.q), hs0 + el);
     }
     const int64_t vrow = t * V + (int64_t)h * dv;
     float v0[CPL], w0[CPL], accv[CPL], accw[CPL];
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
-        const int c = lane + 32 * i;
+        const int c = el + LPH * i;
         const bool on = c < dv;
         v0[i] = on ? ld_f(static_cast<const T *>(p.v), vrow + c) : 0.f;
         w0[i] = on ? ld_f(static_cast<const T *>(p.w), vrow + c) : 0.f;
@@ -589,14 +600,14 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
             const float *durow = p.du + id * V + (int64_t)h * dv;
 #pragma unroll
             for (int i = 0; i < CPL; ++i) {
-                const int c = lane + 32 * i;
+                const int c = el + LPH * i;
                 dub[u][i] = (js && c < dv) ? __ldg(durow + c) : 0.f;
             }
             const float *rec = evg + (id * p.H + h) * R;
             const bool rs = js && nl;
-            ra[u] = rs ? __ldg(rec + lane) : 0.f;
-            rc[u] = rs ? __ldg(rec + S + lane) : 0.f;
-            rg[u] = rs ? __ldg(rec + 2 * S + lane) : 0.f;
+            ra[u] = rs ? __ldg(rec + el) : 0.f;
+            rc[u] = rs ? __ldg(rec + S + el) : 0.f;
+            rg[u] = rs ? __ldg(rec + 2 * S + el) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < JB; ++u) {
@@ -604,7 +615,8 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
             if (j >= p.kw) break;
             const int64_t id = t * p.kw + j;
             const float pw = pwb[u];
-            float wvp = 0.f;
+            float wvp = 0.f, wvp_odd = 0.f;  // G = 2: sums of the even / odd column positions
+            float &wvp2 = G == 2 ? wvp_odd : wvp;
             if constexpr (kPair) {
                 const __nv_bfloat162 pw2 = __float2bfloat162_rn(pw);  // exact: a BF16 route weight
 #pragma unroll
@@ -616,20 +628,20 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
                     accv2[q] = __hadd2_rn(accv2[q], dve);
                     accw2[q] = __hadd2_rn(accw2[q], __hmul2_rn(dwe, pw2));
                     const float2 x = __bfloat1622float2(__hmul2_rn(dwe, w2[q]));
-                    if (lane + 64 * q < dv) wvp += x.x;
-                    if (lane + 64 * q + 32 < dv) wvp += x.y;
+                    if (el + 2 * LPH * q < dv) wvp += x.x;
+                    if (el + 2 * LPH * q + LPH < dv) wvp2 += x.y;
                 }
             } else {
 #pragma unroll
                 for (int i = 0; i < CPL; ++i) {
-                    const int c = lane + 32 * i;
+                    const int c = el + LPH * i;
                     if (c < dv) {
                         const float du = dub[u][i];
                         const float dve = rnd<T>(du * rnd<T>(w0[i] * pw));  // dv of the event (stored as dtype)
                         const float dwe = rnd<T>(du * v0[i]);                // dw of the event (stored as dtype)
                         accv[i] = rnd<T>(accv[i] + dve);
                         accw[i] = rnd<T>(accw[i] + rnd<T>(dwe * pw));
-                        wvp += rnd<T>(dwe * w0[i]);
+                        (i % 2 ? wvp2 : wvp) += rnd<T>(dwe * w0[i]);
                     }
                 }
             }
@@ -641,9 +653,9 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
                 Gs += rg[u];
                 for (int tile = 1; tile < p.tiles; ++tile) {
                     const float *rec = evg + (((int64_t)tile * p.E + id) * p.H + h) * R;
-                    A += rec[lane];
-                    C += rec[S + lane];
-                    Gs += rec[2 * S + lane];
+                    A += rec[el];
+                    C += rec[S + el];
+                    Gs += rec[2 * S + el];
                 }
                 const float be = rnd<T>(b0 * pw);
                 const float dke = rnd<T>(A - be * C);
@@ -658,10 +670,18 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
                 }
                 wbp = rnd<T>(dbe * b0);
             }
-            const float wv = rnd<T>(warp_sum(wvp));
+            float wv;
+            if constexpr (G == 2) {
+                float x = wvp + wvp_odd;  // warp_sum's level 16
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
+                wv = rnd<T>(x);
+            } else {
+                wv = rnd<T>(warp_sum(wvp));
+            }
             const float wb = rnd<T>(warp_sum_low<S>(wbp));  // wbp, dec: non-zero on lanes < S only
             const float decs = warp_sum_low<S>(dec);
-            if (lane == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
+            if (el == 0) dwwh[j] = Elem<T>::from_float(rnd<T>(wb + wv) + decs);
         }
     }
     for (int j0 = 0; j0 < p.kr; j0 += JB) {
@@ -672,7 +692,7 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
             const bool js = j < p.kr;
             const int64_t rid = t * p.kr + j;
             rb[u] = js ? ld_f(rwp, rid) : 0.f;
-            ob[u] = (js && nl) ? __ldg(evg + ((p.nw + rid) * p.H + h) * R + lane) : 0.f;
+            ob[u] = (js && nl) ? __ldg(evg + ((p.nw + rid) * p.H + h) * R + el) : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < JB; ++u) {
@@ -685,24 +705,24 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
                 float o = 0.f;
                 o += ob[u] * p.scale;
                 for (int tile = 1; tile < p.tiles; ++tile)
-                    o += evg[(((int64_t)tile * p.E + id) * p.H + h) * R + lane] * p.scale;
+                    o += evg[(((int64_t)tile * p.E + id) * p.H + h) * R + el] * p.scale;
                 const float dqe = rnd<T>(o);
                 dq_acc += rnd<T>(dqe * r);
                 wrp = rnd<T>(dqe * q0);
             }
             const float wr = warp_sum_low<S>(wrp);  // non-zero on lanes < S only
-            if (lane == 0) drwh[j] = Elem<T>::from_float(wr);
+            if (el == 0) drwh[j] = Elem<T>::from_float(wr);
         }
     }
     if (nl) {
-        st_f(static_cast<T *>(p.dq), hs0 + lane, dq_acc);
-        st_f(static_cast<T *>(p.dk), hs0 + lane, dk_acc);
-        st_f(static_cast<T *>(p.db), hs0 + lane, db_acc);
-        p.dg[hs0 + lane] = dg_acc;
+        st_f(static_cast<T *>(p.dq), hs0 + el, dq_acc);
+        st_f(static_cast<T *>(p.dk), hs0 + el, dk_acc);
+        st_f(static_cast<T *>(p.db), hs0 + el, db_acc);
+        p.dg[hs0 + el] = dg_acc;
     }
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
-        const int c = lane + 32 * i;
+        const int c = el + LPH * i;
         if (c < dv) {
             if constexpr (kPair) {
                 const __nv_bfloat162 av = accv2[i / 2], aw = accw2[i / 2];
@@ -716,12 +736,24 @@ __global__ void __launch_bounds__(32 * kVjpWarps) event_vjp_kernel(const VjpPara
     }
 }
 
+#ifndef BDM_VJP_G2
+#define BDM_VJP_G2 1  // two heads per warp in the event VJP when the head count is even
+#endif
+
 template <typename T, int S>
-void launch_vjp(const VjpParams &p, int cpl, unsigned blocks, cudaStream_t st) {
-    if (cpl <= 1) event_vjp_kernel<T, S, 1><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
-    else if (cpl == 2) event_vjp_kernel<T, S, 2><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
-    else if (cpl <= 4) event_vjp_kernel<T, S, 4><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
-    else event_vjp_kernel<T, S, 8><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+void launch_vjp(const VjpParams &p, int cpl, cudaStream_t st) {
+    if (BDM_VJP_G2 && p.H % 2 == 0 && cpl <= 4) {  // two heads per warp: 2 x cpl columns per lane
+        const unsigned blocks = (unsigned)ceil_div(p.nt * (p.H / 2), kVjpWarps);
+        if (cpl <= 1) event_vjp_kernel<T, S, 2, 2><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+        else if (cpl == 2) event_vjp_kernel<T, S, 4, 2><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+        else event_vjp_kernel<T, S, 8, 2><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+        return;
+    }
+    const unsigned blocks = (unsigned)ceil_div(p.items, kVjpWarps);
+    if (cpl <= 1) event_vjp_kernel<T, S, 1, 1><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+    else if (cpl == 2) event_vjp_kernel<T, S, 2, 1><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+    else if (cpl <= 4) event_vjp_kernel<T, S, 4, 1><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
+    else event_vjp_kernel<T, S, 8, 1><<<blocks, 32 * kVjpWarps, 0, st>>>(p);
 }
 
 // ------------------------------------------------------- initial-state factors
@@ -1201,9 +1233,9 @@ extern "C" int bdm_event_vjp(const void *q, const void *k, const void *v, const 
     const int cpl = (int)ceil_div(head_value_width, 32);
     const cudaStream_t st = as_stream(stream);
     BDM_DISPATCH_DTYPE(dtype, T, {
-        if (bank_size == 4) launch_vjp<T, 4>(p, cpl, (unsigned)blocks, st);
-        else if (bank_size == 8) launch_vjp<T, 8>(p, cpl, (unsigned)blocks, st);
-        else launch_vjp<T, 16>(p, cpl, (unsigned)blocks, st);
+        if (bank_size == 4) launch_vjp<T, 4>(p, cpl, st);
+        else if (bank_size == 8) launch_vjp<T, 8>(p, cpl, st);
+        else launch_vjp<T, 16>(p, cpl, st);
     });
     return launch_status();
 }
