@@ -1019,15 +1019,28 @@ __global__ void norm_gate_backward_kernel(const NgBwdArgs a) {
     }
     const int64_t t0 = (int64_t)blockIdx.x * kNgTokens;
     const int64_t t1 = min(a.ntok, t0 + kNgTokens);
+    // a token's loads are issued one token ahead, so they overlap the previous token's reductions
+    float xn[kNgCols], dyn[kNgCols], gln[kNgCols];
+    auto load_token = [&](int64_t t) {
+#pragma unroll
+        for (int i = 0; i < kNgCols; ++i) {
+            const bool on = act && c0 + i < a.width;
+            xn[i] = on ? ld_f(static_cast<const T *>(a.raw), t * a.width + c0 + i) : 0.f;
+            dyn[i] = on ? ld_f(static_cast<const T *>(a.dout), t * a.width + c0 + i) : 0.f;
+            gln[i] = on ? ld_f(static_cast<const T *>(a.gate), t * a.ld_gate + c0 + i) : 0.f;
+        }
+    };
+    if (t0 < t1) load_token(t0);
     for (int64_t t = t0; t < t1; ++t) {
         float x[kNgCols], dy[kNgCols], gt[kNgCols];
 #pragma unroll
         for (int i = 0; i < kNgCols; ++i) {
             const bool on = act && c0 + i < a.width;
-            x[i] = on ? ld_f(static_cast<const T *>(a.raw), t * a.width + c0 + i) : 0.f;
-            dy[i] = on ? ld_f(static_cast<const T *>(a.dout), t * a.width + c0 + i) : 0.f;
-            gt[i] = on ? rnd<T>(gate_sigmoid<T>(ld_f(static_cast<const T *>(a.gate), t * a.ld_gate + c0 + i))) : 0.f;
+            x[i] = xn[i];
+            dy[i] = dyn[i];
+            gt[i] = on ? rnd<T>(gate_sigmoid<T>(gln[i])) : 0.f;
         }
+        if (t + 1 < t1) load_token(t + 1);
         float n[kNgCols], dn[kNgCols], dx[kNgCols];
         if (a.norm_mode == 1) {
             float s = 0.f;
